@@ -1,0 +1,287 @@
+"""The chip stack as sparse host tensors: every projection of every GDN + SwiGLU layer as CSR
+with bf16 values, the embedding, the output head and the final norm.
+
+This is the host-side description the table builder (``linuxformer_b200.tables``), the CPU
+oracle (``oracle/``) and the stock-forward materialiser (``to_hf``) all start from. Shapes follow
+the reference's chip layers (``lx/lx/hf.py:25-38, 113-118``; ``lx/lx/emit.py:216-224``):
+
+    in_proj_qkv  (2*16*256 + 128*128 = 24576) x 2560     conv1d taps   24576 x 4
+    in_proj_z    16384 x 2560                            in_proj_b/a   128 x 2560
+    out_proj     2560 x 16384
+    gate/up      9216 x 2560                             down          2560 x 9216
+
+Values are bf16 bit patterns (uint16). CSR rows hold only nonzero entries, in ascending column
+order; that order is the summation order every kernel and the oracle use.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import hashlib
+from dataclasses import dataclass, field
+
+import numpy as np
+
+H = 2560          # hidden
+KD, VD = 256, 128  # key / value head dims
+NK, NV = 16, 128   # key / value heads
+R = NV // NK       # value heads per key head
+CONV = 2 * NK * KD + NV * VD  # 24576 conv channels: q | k | v
+ZD = NV * VD       # 16384 value dims
+INTER = 9216       # SwiGLU width
+TAPS = 4
+
+
+# --- bf16 helpers -------------------------------------------------------------------------------
+def bf16_bits(x) -> np.ndarray:
+    """float32 values -> bf16 bit patterns, round to nearest even (NaN kept quiet)."""
+    u = np.ascontiguousarray(np.asarray(x, dtype=np.float32)).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    r = np.where(nan, (u >> 16) | 0x40, r)
+    return r.astype(np.uint16)
+
+
+def bf16_float(b) -> np.ndarray:
+    """bf16 bit patterns -> float32."""
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def round_bf16(x) -> np.ndarray:
+    return bf16_float(bf16_bits(x))
+
+
+# --- sparse matrices ----------------------------------------------------------------------------
+@dataclass
+class Sparse:
+    """CSR with bf16 values: row r holds indices[indptr[r]:indptr[r+1]] (ascending columns)."""
+    shape: tuple
+    indptr: np.ndarray   # int64 [rows + 1]
+    indices: np.ndarray  # int32 [nnz]
+    data: np.ndarray     # uint16 [nnz], bf16 bits, never +-0
+
+    @property
+    def nnz(self) -> int:
+        return int(self.indices.shape[0])
+
+    @staticmethod
+    def from_coo(shape, rows, cols, bits) -> "Sparse":
+        rows = np.asarray(rows, np.int64)
+        cols = np.asarray(cols, np.int64)
+        bits = np.asarray(bits, np.uint16)
+        keep = (bits & 0x7FFF) != 0
+        rows, cols, bits = rows[keep], cols[keep], bits[keep]
+        key = rows * shape[1] + cols
+        key, first = np.unique(key, return_index=True)  # sorted, duplicates dropped
+        rows, cols, bits = key // shape[1], key % shape[1], bits[first]
+        indptr = np.zeros(shape[0] + 1, np.int64)
+        np.cumsum(np.bincount(rows, minlength=shape[0]), out=indptr[1:])
+        return Sparse(tuple(shape), indptr, cols.astype(np.int32), bits)
+
+    @staticmethod
+    def from_dense(bits2d) -> "Sparse":
+        b = np.asarray(bits2d, np.uint16)
+        r, c = np.nonzero(b & 0x7FFF)
+        return Sparse.from_coo(b.shape, r, c, b[r, c])
+
+    def to_dense(self) -> np.ndarray:
+        out = np.zeros(self.shape, np.uint16)
+        rows = np.repeat(np.arange(self.shape[0]), np.diff(self.indptr))
+        out[rows, self.indices] = self.data
+        return out
+
+    def row_nnz(self) -> np.ndarray:
+        return np.diff(self.indptr)
+
+    def transpose(self) -> "Sparse":
+        rows = np.repeat(np.arange(self.shape[0], dtype=np.int64), np.diff(self.indptr))
+        return Sparse.from_coo((self.shape[1], self.shape[0]), self.indices, rows, self.data)
+
+    def rows_subset(self, rows) -> "Sparse":
+        rows = np.asarray(rows, np.int64)
+        cnt = self.indptr[rows + 1] - self.indptr[rows]
+        idx = _ranges(self.indptr[rows], cnt)
+        indptr = np.zeros(len(rows) + 1, np.int64)
+        np.cumsum(cnt, out=indptr[1:])
+        return Sparse((len(rows), self.shape[1]), indptr, self.indices[idx], self.data[idx])
+
+
+def _ranges(starts, counts) -> np.ndarray:
+    """concatenation of arange(s, s + c) over the pairs (s, c)."""
+    starts = np.asarray(starts, np.int64)
+    counts = np.asarray(counts, np.int64)
+    tot = int(counts.sum())
+    if tot == 0:
+        return np.zeros(0, np.int64)
+    first = np.repeat(np.cumsum(counts) - counts, counts)
+    return np.repeat(starts, counts) + np.arange(tot) - first
+
+
+# --- the stack ----------------------------------------------------------------------------------
+@dataclass
+class Layer:
+    """One chip layer (Qwen3_5DecoderLayer with linear_attention): GDN then SwiGLU."""
+    qkv: Sparse
+    conv: np.ndarray      # uint16 [CONV, 4]: conv1d.weight[:, 0, :]
+    z: Sparse
+    b: Sparse
+    a: Sparse
+    out: Sparse
+    A_log: np.ndarray     # uint16 [NV]
+    dt_bias: np.ndarray   # uint16 [NV]
+    gnorm: np.ndarray     # uint16 [VD]: Qwen3_5RMSNormGated.weight
+    ln_in: np.ndarray     # uint16 [H]: input_layernorm.weight
+    ln_post: np.ndarray   # uint16 [H]: post_attention_layernorm.weight
+    gate: Sparse
+    up: Sparse
+    down: Sparse
+
+
+@dataclass
+class Chip:
+    name: str
+    layers: list
+    embed: np.ndarray     # uint16 [V_embed, H] (dense)
+    head: Sparse          # [V, H]
+    final_norm: np.ndarray  # uint16 [H]
+    eps: float = 1e-6     # rms_norm_eps (also the gated norm's)
+    offset: int = 0       # chip token t embeds row offset + t
+    meta: dict = field(default_factory=dict)
+
+    @property
+    def n_layers(self) -> int:
+        return len(self.layers)
+
+    @property
+    def n_vocab(self) -> int:
+        return self.head.shape[0]
+
+    def digest(self) -> str:
+        """A hash of every tensor, to pin generated models against fixtures."""
+        h = hashlib.sha256()
+        for L in self.layers:
+            for f in dataclasses.fields(L):
+                v = getattr(L, f.name)
+                if isinstance(v, Sparse):
+                    for a in (v.indptr, v.indices, v.data):
+                        h.update(np.ascontiguousarray(a).tobytes())
+                else:
+                    h.update(np.ascontiguousarray(v).tobytes())
+        for a in (self.embed, self.head.indptr, self.head.indices, self.head.data,
+                  self.final_norm):
+            h.update(np.ascontiguousarray(a).tobytes())
+        h.update(np.float64(self.eps).tobytes())
+        return h.hexdigest()[:16]
+
+
+@dataclass
+class State:
+    """One machine's state, in the HF cache layout (lx/lx/mega.py:506-516):
+    recurrent [L][NV][KD][VD] fp32, conv [L][CONV][4] bf16 bits (oldest tap first)."""
+    recurrent: np.ndarray  # float32 [L, NV, KD, VD]
+    conv: np.ndarray       # uint16 [L, CONV, 4]
+
+    def copy(self) -> "State":
+        return State(self.recurrent.copy(), self.conv.copy())
+
+
+# --- seeded synthetic stacks --------------------------------------------------------------------
+def _sparse_random(rng, shape, density, values) -> Sparse:
+    """~density * rows * cols nonzeros at uniform positions, values from values(n)."""
+    n = int(round(density * shape[0] * shape[1]))
+    flat = rng.integers(0, shape[0] * shape[1], size=n, dtype=np.int64)
+    bits = bf16_bits(values(n))
+    return Sparse.from_coo(shape, flat // shape[1], flat % shape[1], bits)
+
+
+def c1(seed: int = 0, n_layers: int = 2, vocab: int = 4096, density: float = 1e-3) -> Chip:
+    """Config 1: the 2-layer synthetic sparse stack. Every projection and the conv taps at
+    `density` nonzeros (uniform positions), values N(0, 0.02) in bf16; embedding dense
+    N(0, 0.02); output head `vocab` x 2560 at `density`. The scalar parameters are the stock
+    module's own initialisation (transformers Qwen3_5GatedDeltaNet.__init__): dt_bias = 1,
+    A_log = log(U(0, 16)), gated-norm weight 1, RMSNorm weights 0 (gain 1)."""
+    rng = np.random.default_rng(seed)
+    nrm = lambda n: rng.normal(0.0, 0.02, n)  # noqa: E731
+    layers = []
+    for _ in range(n_layers):
+        conv = _sparse_random(rng, (CONV, TAPS), density, nrm).to_dense()
+        layers.append(Layer(
+            qkv=_sparse_random(rng, (CONV, H), density, nrm),
+            conv=conv,
+            z=_sparse_random(rng, (ZD, H), density, nrm),
+            b=_sparse_random(rng, (NV, H), density, nrm),
+            a=_sparse_random(rng, (NV, H), density, nrm),
+            out=_sparse_random(rng, (H, ZD), density, nrm),
+            A_log=bf16_bits(np.log(rng.uniform(0.0, 16.0, NV)).astype(np.float32)),
+            dt_bias=bf16_bits(np.ones(NV, np.float32)),
+            gnorm=bf16_bits(np.ones(VD, np.float32)),
+            ln_in=np.zeros(H, np.uint16),
+            ln_post=np.zeros(H, np.uint16),
+            gate=_sparse_random(rng, (INTER, H), density, nrm),
+            up=_sparse_random(rng, (INTER, H), density, nrm),
+            down=_sparse_random(rng, (H, INTER), density, nrm),
+        ))
+    embed = bf16_bits(rng.normal(0.0, 0.02, (vocab, H)).astype(np.float32))
+    head = _sparse_random(rng, (vocab, H), density, nrm)
+    return Chip(name=f"c1(seed={seed},layers={n_layers},vocab={vocab},density={density})",
+                layers=layers, embed=embed, head=head, final_norm=np.zeros(H, np.uint16),
+                eps=1e-6, meta={"config": 1, "seed": seed})
+
+
+def c1_state(chip: Chip, seed: int = 0, std: float = 1e-3) -> State:
+    """Config 1's initial state: recurrent N(0, std) fp32, conv windows zero."""
+    rng = np.random.default_rng(seed + 1_000_003)
+    rec = rng.normal(0.0, std, (chip.n_layers, NV, KD, VD)).astype(np.float32)
+    return State(rec, np.zeros((chip.n_layers, CONV, TAPS), np.uint16))
+
+
+# --- the stock model (transformers), for the reference's own forward ----------------------------
+def hf_config(chip: Chip):
+    from transformers import Qwen3_5TextConfig
+
+    n = chip.n_layers
+    return Qwen3_5TextConfig(
+        hidden_size=H, num_hidden_layers=n, layer_types=["linear_attention"] * n,
+        vocab_size=chip.n_vocab, linear_key_head_dim=KD, linear_value_head_dim=VD,
+        linear_num_key_heads=NK, linear_num_value_heads=NV, intermediate_size=INTER,
+        linear_conv_kernel_dim=TAPS, hidden_act="silu", rms_norm_eps=chip.eps,
+        tie_word_embeddings=False, num_attention_heads=16, num_key_value_heads=4, head_dim=256)
+
+
+def to_hf(chip: Chip):
+    """The chip as a stock Qwen3_5ForCausalLM (bf16, CPU): the model the reference's
+    hf.chip_forward / hf.head_argmax run (lx/lx/hf.py:169-184)."""
+    import torch
+    from transformers import Qwen3_5ForCausalLM
+
+    cfg = hf_config(chip)
+    with torch.device("meta"):
+        model = Qwen3_5ForCausalLM(cfg)
+
+    def t(bits, shape=None):
+        x = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16)
+        return x.reshape(shape) if shape is not None else x
+
+    sd = {}
+    for i, L in enumerate(chip.layers):
+        p = f"model.layers.{i}."
+        sd[p + "linear_attn.in_proj_qkv.weight"] = t(L.qkv.to_dense())
+        sd[p + "linear_attn.conv1d.weight"] = t(L.conv, (CONV, 1, TAPS))
+        sd[p + "linear_attn.in_proj_z.weight"] = t(L.z.to_dense())
+        sd[p + "linear_attn.in_proj_b.weight"] = t(L.b.to_dense())
+        sd[p + "linear_attn.in_proj_a.weight"] = t(L.a.to_dense())
+        sd[p + "linear_attn.out_proj.weight"] = t(L.out.to_dense())
+        sd[p + "linear_attn.A_log"] = t(L.A_log)
+        sd[p + "linear_attn.dt_bias"] = t(L.dt_bias)
+        sd[p + "linear_attn.norm.weight"] = t(L.gnorm)
+        sd[p + "input_layernorm.weight"] = t(L.ln_in)
+        sd[p + "post_attention_layernorm.weight"] = t(L.ln_post)
+        sd[p + "mlp.gate_proj.weight"] = t(L.gate.to_dense())
+        sd[p + "mlp.up_proj.weight"] = t(L.up.to_dense())
+        sd[p + "mlp.down_proj.weight"] = t(L.down.to_dense())
+    sd["model.embed_tokens.weight"] = t(chip.embed)
+    sd["model.norm.weight"] = t(chip.final_norm)
+    sd["lm_head.weight"] = t(chip.head.to_dense())
+    missing, unexpected = model.load_state_dict(sd, strict=False, assign=True)
+    assert not unexpected and not missing, (missing[:5], unexpected[:5])
+    return model.eval()

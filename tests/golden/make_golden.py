@@ -1,0 +1,126 @@
+"""Golden vectors from the reference's own stock forward, run on CPU in the build container.
+
+The reference's decode and verify paths call ``lx.hf.chip_forward`` (the stock
+``Qwen3_5DecoderLayer`` modules, layer by layer) and ``lx.hf.head_argmax``
+(lx/lx/hf.py:169-184; lx/lx/session.py:95-100, 140-146). Without fla/causal_conv1d (the CPU case)
+transformers runs its torch paths: ``torch_causal_conv1d_update``, ``torch_recurrent_gated_delta_rule``
+(decode) and ``torch_chunk_gated_delta_rule`` (prefill). This script imports the reference from
+its checkout, builds the seeded config-1 stack as a stock model, seeds fp32 recurrent states as
+``Fast.init_cache`` does (lx/lx/fast.py:420-430), and records:
+
+- ``c1_decode.npz``: 512 greedy tokens from token 0 (the reference's model-alone decode, one
+  token per call as ``Session.step`` runs it), each step's top-2 bf16 logit margin, the final conv
+  windows, per-value-head checksums of the final recurrent states plus two full value heads, and
+  the residual after the chip layers for the first 8 steps;
+- ``c1_prefill.npz``: two 256-token chunks of seeded random ids run as chunked prefill (the
+  verified mode), the argmax at every position, the same state summaries after each chunk.
+
+Run here (needs /root/reference); the GPU box only reads the .npz files:
+
+    python tests/golden/make_golden.py
+"""
+
+import os
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1]))
+REF = os.environ.get("LXB_REFERENCE", "/root/reference") + "/lx"
+
+from linuxformer_b200 import chip as C  # noqa: E402
+
+N_DEC = 512
+PRE_T = 256
+
+
+def new_cache(model, st: C.State):
+    from transformers import DynamicCache
+
+    cache = DynamicCache(config=model.config)
+    for L in range(st.recurrent.shape[0]):
+        conv = torch.from_numpy(st.conv[L].view(np.int16).copy()).view(torch.bfloat16)[None]
+        cache.update_conv_state(conv, L)
+        lay = cache.layers[L]
+        # fp32 recurrent state (this transformers' lazy init would make it bf16)
+        lay.recurrent_states = torch.from_numpy(st.recurrent[L].copy())[None]
+        lay.is_recurrent_states_initialized = True
+    return cache
+
+
+def summarize(cache, n_layers):
+    conv = np.stack([cache.layers[L].conv_states[0].view(torch.int16).numpy().view(np.uint16)
+                     for L in range(n_layers)])
+    rec = np.stack([cache.layers[L].recurrent_states[0].float().numpy() for L in range(n_layers)])
+    sums = rec.astype(np.float64).sum(axis=(2, 3))           # [L, NV]
+    abss = np.abs(rec.astype(np.float64)).sum(axis=(2, 3))
+    heads = rec[:, [5, 77]]                                   # two full value heads per layer
+    return conv, sums, abss, heads
+
+
+def margins(logits: torch.Tensor) -> np.ndarray:
+    top = torch.topk(logits.float(), 2, dim=-1).values
+    return (top[..., 0] - top[..., 1]).numpy()
+
+
+@torch.no_grad()
+def main():
+    sys.path.insert(0, REF)
+    from lx import hf as ref_hf  # the reference's stock forward
+
+    torch.manual_seed(0)
+    torch.set_num_threads(os.cpu_count())
+    chip = C.c1(0)
+    model = C.to_hf(chip)
+    st0 = C.c1_state(chip, 0)
+    n = chip.n_layers
+    emb = model.model.embed_tokens
+
+    # --- model-alone decode --------------------------------------------------------------
+    cache = new_cache(model, st0)
+    tok, toks, preds, marg, resid = 0, [], [], [], []
+    t0 = time.time()
+    for i in range(N_DEC):
+        h = ref_hf.chip_forward(model, emb(torch.tensor([[tok]])), cache, n)[0]
+        logits = torch.nn.functional.linear(model.model.norm(h), model.lm_head.weight)
+        p = int(ref_hf.head_argmax(model, h)[0])
+        assert p == int(logits.argmax(-1)[0])
+        toks.append(tok)
+        preds.append(p)
+        marg.append(float(margins(logits)[0]))
+        if i < 8:
+            resid.append(h[0].view(torch.int16).numpy().view(np.uint16).copy())
+        tok = p
+    dt = time.time() - t0
+    conv, sums, abss, heads = summarize(cache, n)
+    np.savez_compressed(HERE / "c1_decode.npz", digest=chip.digest(), inputs=np.array(toks),
+                        preds=np.array(preds), margin=np.array(marg, np.float32),
+                        resid=np.stack(resid), conv=conv, rec_sum=sums, rec_abs=abss,
+                        rec_heads=heads, cpu_s=dt)
+    print(f"decode: {N_DEC} tokens in {dt:.1f}s, min margin {min(marg):.3g}")
+
+    # --- verified-mode prefill (chunked) -------------------------------------------------
+    cache = new_cache(model, st0)
+    rng = np.random.default_rng(2)
+    out = {}
+    for c in range(2):
+        ids = rng.integers(0, chip.n_vocab, PRE_T)
+        t0 = time.time()
+        h = ref_hf.chip_forward(model, emb(torch.from_numpy(ids)[None]), cache, n)[0]
+        logits = torch.nn.functional.linear(model.model.norm(h), model.lm_head.weight)
+        p = ref_hf.head_argmax(model, h).numpy()
+        dt = time.time() - t0
+        conv, sums, abss, heads = summarize(cache, n)
+        out.update({f"ids{c}": ids, f"preds{c}": p, f"margin{c}": margins(logits),
+                    f"conv{c}": conv, f"rec_sum{c}": sums, f"rec_abs{c}": abss,
+                    f"rec_heads{c}": heads, f"cpu_s{c}": dt})
+        print(f"prefill chunk {c}: {PRE_T} tokens in {dt:.1f}s")
+    np.savez_compressed(HERE / "c1_prefill.npz", digest=chip.digest(), **out)
+
+
+if __name__ == "__main__":
+    main()
