@@ -1,0 +1,97 @@
+/* linuxformer-b200: the C ABI of the sparse chip decode (B200, sm_100a).
+ *
+ * One shared library, liblxb.so, replaces the reference's megakernel boundary: the ctypes
+ * interface of lx/csrc/mega.cu (mk_run, mk_smem_base, mk_max_ctas, mk_max_smem,
+ * mk_last_error: mega.cu:864-893), which lx/lx/mega.py loads through lx/lx/mk_build.py:40-57.
+ * Plain pointers and sizes only; every call returns 0 or an error code (a positive cudaError
+ * value, or a negative LXB_E_* value); nothing throws across the boundary. Launches are
+ * asynchronous on the stream given. A plan is not thread-safe: one launch at a time per plan.
+ *
+ * Buffer ownership follows the reference (lx/lx/mega.py:506-574): the caller owns the machine
+ * state (HF cache layout: recurrent [128][256][128] fp32 and conv [24576][4] bf16 per layer,
+ * updated in place), the embedding, and the forced/preds/inputs arrays; the plan owns the
+ * weight tables it uploads.
+ */
+#ifndef LXB_ABI_H_
+#define LXB_ABI_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LXB_ABI_VERSION 1
+
+/* error codes (negative; positive values are cudaError_t) */
+#define LXB_OK 0
+#define LXB_E_INVAL (-1)     /* a bad argument */
+#define LXB_E_IMAGE (-2)     /* a malformed plan image (an offset, count or index out of range) */
+#define LXB_E_DEVICE (-3)    /* the device cannot run the plan (arch, cluster size, shared memory) */
+#define LXB_E_STATUS (-4)    /* the kernel reported an error: read it with lxb_status */
+
+/* device status bits (lxb_status) */
+#define LXB_S_TOKEN 1u       /* a token id outside the embedding: clamped, the stream is invalid */
+
+typedef struct lxb_plan lxb_plan;
+
+typedef struct {
+  int device;
+  int cc_major, cc_minor;
+  int sm_count;
+  int max_smem_optin;   /* bytes per block */
+  int cluster_launch;   /* cudaDevAttrClusterLaunch */
+  int max_clusters;     /* co-resident clusters of the plan's size (0 before a plan exists) */
+} lxb_caps;
+
+typedef struct {
+  uint32_t status;      /* LXB_S_* bits, sticky until lxb_status_clear */
+  int32_t first_stream; /* the first stream that set a bit */
+  int32_t first_step;
+} lxb_error;
+
+/* ABI version of the library (LXB_ABI_VERSION). Replaces nothing: the reference's ctypes loader
+ * trusted the .so it had just compiled (lx/lx/mk_build.py:40-57). */
+int lxb_abi_version(void);
+
+/* Device capabilities. Replaces mk_max_smem / mk_max_ctas (mega.cu:876-890). */
+int lxb_query(int device, lxb_caps* caps);
+
+/* Upload a plan image (the packed weight tables, format in lxb_plan.h, built by
+ * linuxformer_b200.tables) to the current device, validating every offset and index. cluster is
+ * the number of CTAs that run one stream (8 or 16). Replaces Mega.__init__'s uploads
+ * (lx/lx/mega.py:458-504) and the launch setup of mk_run (mega.cu:867-874). */
+int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb_plan** out);
+
+/* Decode n_tokens steps of n_streams independent machines (one thread-block cluster each).
+ * Stream s: step i embeds forced[s * n_forced + i] for i < n_forced, else its own step i-1
+ * prediction; preds[s * n_tokens + i] receives step i's argmax, inputs (optional, may be NULL)
+ * the token each step embedded. state_ptrs: a DEVICE array of n_streams * n_layers * 2 uint64,
+ * (recurrent, conv) device pointers per stream and layer. bitmaps: a DEVICE array of
+ * n_streams * n_layers * 128 * 8 uint32, the nonzero-row bitmaps of the recurrent states; with
+ * sync_bitmaps != 0 they are rebuilt from the states first (the reference's sync_bitmaps,
+ * mega.py:518-526). embed: DEVICE bf16 [n_embed_rows][2560]; token t embeds row offset + t.
+ * Replaces mk_run (mega.cu:867-874) as called by Mega.run (mega.py:529-574). */
+int lxb_decode(lxb_plan* plan, const uint64_t* state_ptrs, uint32_t* bitmaps, int sync_bitmaps,
+               const uint16_t* embed, int n_streams, const int32_t* forced, int n_forced,
+               int n_tokens, int32_t* preds, int32_t* inputs, void* cuda_stream);
+
+/* The device status word (after the stream has synchronised). Replaces mk_last_error
+ * (mega.cu:892) for kernel-side errors. */
+int lxb_status(lxb_plan* plan, lxb_error* err);
+int lxb_status_clear(lxb_plan* plan);
+
+/* Bytes of the plan's device tables; the number of co-resident clusters for this plan. */
+size_t lxb_plan_bytes(const lxb_plan* plan);
+int lxb_plan_max_clusters(const lxb_plan* plan);
+
+void lxb_plan_destroy(lxb_plan* plan);
+
+/* A short text for an error code. */
+const char* lxb_error_string(int code);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LXB_ABI_H_ */

@@ -1,0 +1,64 @@
+"""ctypes binding of liblxb.so (the C ABI in include/lxb.h). There is no fallback: if the
+library is missing or fails to load, every entry point raises."""
+
+from __future__ import annotations
+
+import ctypes
+
+from . import build as _build
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+
+_lib = None
+
+
+class LxbError(RuntimeError):
+    pass
+
+
+class Caps(ctypes.Structure):
+    _fields_ = [("device", I), ("cc_major", I), ("cc_minor", I), ("sm_count", I),
+                ("max_smem_optin", I), ("cluster_launch", I), ("max_clusters", I)]
+
+
+class Err(ctypes.Structure):
+    _fields_ = [("status", ctypes.c_uint32), ("first_stream", ctypes.c_int32),
+                ("first_step", ctypes.c_int32)]
+
+
+SIGNATURES = {
+    "lxb_abi_version": (I, []),
+    "lxb_query": (I, [I, P]),
+    "lxb_plan_create": (I, [P, ctypes.c_size_t, I, P]),
+    "lxb_decode": (I, [P, P, P, I, P, I, P, I, I, P, P, P]),
+    "lxb_status": (I, [P, P]),
+    "lxb_status_clear": (I, [P]),
+    "lxb_plan_bytes": (ctypes.c_size_t, [P]),
+    "lxb_plan_max_clusters": (I, [P]),
+    "lxb_plan_destroy": (None, [P]),
+    "lxb_error_string": (ctypes.c_char_p, [I]),
+}
+
+
+def lib():
+    """The loaded library (built first if it is missing or older than its sources)."""
+    global _lib
+    if _lib is None:
+        path = _build.LIB
+        if not path.exists():
+            raise LxbError(f"{path} is not built: run `python -m linuxformer_b200.build`")
+        L = ctypes.CDLL(str(path))
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype, f.argtypes = res, args
+        if L.lxb_abi_version() != 1:
+            raise LxbError("liblxb.so has another ABI version than this binding")
+        _lib = L
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc:
+        msg = lib().lxb_error_string(rc).decode()
+        raise LxbError(f"{what}: error {rc} ({msg})")

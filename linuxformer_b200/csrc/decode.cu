@@ -1,0 +1,944 @@
+// The chip decode on B200 (sm_100a): one thread-block cluster per machine (stream), the whole
+// token loop inside one launch, the next token chosen and embedded on the device.
+//
+// What it computes is the reference's stock decode step (lx/lx/hf.py:169-184), as its
+// megakernel does (lx/csrc/mega.cu:653-862): per token, every chip layer's Gated DeltaNet step
+// and SwiGLU over their nonzero parts, then the output head's argmax. The arithmetic follows the
+// CPU restatement in oracle/oracle.c operation for operation (the same lxb_math.h functions, the
+// same fixed reduction orders), so the two agree bit for bit.
+//
+// How it maps to the hardware (the reference instead runs one 132-CTA persistent grid with a
+// global-memory barrier per phase and fp32 atomics into a global accumulator):
+//   - A cluster of C CTAs (C = 8 or 16, one per SM) runs one stream. Every CTA keeps a replica of
+//     the residual row in shared memory. Cluster barriers (barrier.cluster, in hardware) separate
+//     the steps; data crosses CTAs only through distributed shared memory (DSMEM).
+//   - Residual rows are owned in contiguous blocks of 2560 / C. The owner computes every sum that
+//     lands in its rows (down_proj and out_proj rows, sequentially in CSR order), re-evaluating
+//     the few MLP units it needs itself, so no sum is split across CTAs and no atomic is used:
+//     the results do not depend on timing. After a barrier every CTA pulls the C blocks back
+//     into its replica with 16-byte DSMEM loads.
+//   - One step per layer: the layer's GDN items (one live key head each) and its MLP (assuming
+//     the GDN leaves the residual as it is) run side by side; if any item did write, an
+//     out_proj step and the MLP again follow (two more barriers). The reference pairs only the
+//     layers it measured (PAIR_LAYERS, lx/lx/mega.py:97); here every layer is paired.
+//   - Independent streams are independent clusters: no inter-cluster communication at all.
+// No device-wide barrier exists, so nothing spins on global memory; the only waits are
+// hardware cluster barriers, which every CTA of a cluster reaches on the same cluster-uniform
+// control path.
+#include <cooperative_groups.h>
+#include <cuda_runtime.h>
+
+#include <new>
+#include <stddef.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/lxb.h"
+#include "lxb_math.h"
+#include "lxb_plan.h"
+
+namespace cg = cooperative_groups;
+
+#define NT 512
+#define H LXB_H
+#define KD LXB_KD
+#define VD LXB_VD
+#define R LXB_R
+#define BLKMAX (LXB_H / LXB_MINC)
+
+struct Dev {
+  const lxb_layer* layers;
+  const lxb_item* items;
+  const lxb_chan* chans;
+  const uint32_t* ent;
+  const lxb_unit* units;
+  const lxb_owner* owners;
+  const int32_t* i32;
+  const uint16_t* u16;
+  const lxb_headcta* headcta;
+  const uint64_t* hcodes;
+  int n_layers, C, blk, n_vocab, n_dense, final_norm;
+  float eps;
+  int64_t n_embed_rows;
+  int offset;
+  float htab[4];
+  int dense_cols[LXB_MAXDENSE];
+  uint32_t* status;  // [0] bits, [1] first stream, [2] first step
+};
+
+struct Run {
+  const uint64_t* state_ptrs;  // [stream][layer][2]
+  uint32_t* bitmaps;           // [stream][layer][128][8]
+  const uint16_t* embed;
+  const int32_t* forced;
+  int n_forced, n_tokens;
+  int32_t* preds;
+  int32_t* inputs;
+};
+
+struct __align__(16) Smem {
+  alignas(16) float x[H];          // the residual replica (bf16 values)
+  float xn[H];                     // input_layernorm(x) (bf16 values)
+  float xm[H];                     // post_attention_layernorm(x) or the final norm
+  alignas(16) float own[2][BLKMAX];  // this CTA's rows after the step, by step parity
+  float buf[LXB_NSLOT];            // an item's q | k | v
+  float qval[KD], kval[KD];        // nonzero l2-normed query (x 1/16) and key values
+  int qidx[KD], kidx[KD];
+  float ob[R][VD];                 // o per value head (bf16 values)
+  float beta[R], g[R];
+  float red[40];
+  int nq, nk;
+  uint32_t vhmask[LXB_ITEMSLOTS];  // value heads with output, per item slot
+  int wflag[2];                    // some item of the step wrote (pushed by the writer)
+  int kmask[LXB_NK];               // out_proj step: active value heads per key head
+  alignas(16) uint16_t on[LXB_ITEMSLOTS][R * VD];  // the gated norm's output per item slot
+  alignas(16) uint16_t onall[LXB_NK][R * VD];  // gathered for the out_proj step
+  float hbuf[LXB_MAXUNITS];        // MLP unit outputs
+  float htg[LXB_MAXDENSE / 4][256];  // head: per group of 4 dense columns, each code's sum
+  float bestv;
+  int besti;
+  int tok;
+};
+
+// --- block reductions in the canonical orders -------------------------------------------------
+__device__ __forceinline__ float warp_xor_sum(float s) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s = lx_add(s, __shfl_xor_sync(0xffffffffu, s, off));
+  return s;
+}
+
+// lane t sums x[t + 512 i]^2 (i = 0..4), butterfly per warp, butterfly over the 16 warp sums
+__device__ float block_ssq(Smem& sm, const float* x) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  float s = lx_mul(x[t], x[t]);
+#pragma unroll
+  for (int i = 1; i < 5; i++) s = lx_add(s, lx_mul(x[t + 512 * i], x[t + 512 * i]));
+  s = warp_xor_sum(s);
+  if (lane == 0) sm.red[warp] = s;
+  __syncthreads();
+  if (warp == 0) {
+    float v = lane < 16 ? sm.red[lane] : 0.0f;
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) v = lx_add(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if (lane == 0) sm.red[32] = v;
+  }
+  __syncthreads();
+  const float r = sm.red[32];
+  __syncthreads();
+  return r;
+}
+
+// Qwen3_5RMSNorm: out[c] = bf16(x[c] * rsqrt(ss / 2560 + eps) * (1 + w[c]))
+__device__ void norm_into(const Dev& P, float* out, const float* x, int w_off, float ss) {
+  const float r = lx_rsqrt(lx_add(lx_div(ss, (float)H), P.eps));
+  const uint16_t* w = P.u16 + w_off;
+  for (int c = threadIdx.x; c < H; c += NT)
+    out[c] = lx_rbf(lx_mul(lx_mul(x[c], r), lx_add(1.0f, lx_f(__ldg(w + c)))));
+}
+
+__device__ __forceinline__ float row_dot(const uint32_t* ent, uint32_t e0, int n, const float* x) {
+  float s = 0.0f;
+  for (int e = 0; e < n; e++) {
+    const uint32_t w = __ldg(ent + e0 + e);
+    s = lx_add(s, lx_mul(x[w & 0xffffu], lx_f((uint16_t)(w >> 16))));
+  }
+  return s;
+}
+
+__device__ __forceinline__ void set_status(const Dev& P, uint32_t bit, int stream, int step) {
+  if (atomicOr(P.status, bit) == 0) {
+    P.status[1] = (uint32_t)stream;
+    P.status[2] = (uint32_t)step;
+  }
+}
+
+// --- a GDN item: one live key head of one layer --------------------------------------------------
+// Returns whether it wrote (some value head has output and the head has out_proj entries).
+__device__ bool gdn_item(const Dev& P, Smem& sm, const lxb_item& it, float* rec, uint16_t* conv,
+                         uint32_t* bm) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  uint16_t* on = sm.on[it.slot];
+  for (int k = t; k < LXB_NSLOT; k += NT) sm.buf[k] = 0.0f;
+  for (int k = t; k < R * VD; k += NT) on[k] = 0;
+  if (t == 0) sm.vhmask[it.slot] = 0;
+  __syncthreads();
+  // in_proj_qkv rows, the conv window shift and the conv output with silu (bf16), per channel
+  for (int c = t; c < it.n_ch; c += NT) {
+    const lxb_chan* cp = P.chans + it.ch0 + c;
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(cp));  // ent, n|slot, conv_ch, t01
+    const uint32_t t23 = __ldg(reinterpret_cast<const uint4*>(cp) + 1).x;
+    const uint16_t Pv = lx_rb(row_dot(P.ent, a.x, (int)(a.y & 0xffffu), sm.xn));
+    uint2* wp = reinterpret_cast<uint2*>(conv + (size_t)a.z * 4);
+    const uint2 win = *wp;
+    const uint16_t n0 = (uint16_t)(win.x >> 16), n1 = (uint16_t)(win.y & 0xffffu),
+                   n2 = (uint16_t)(win.y >> 16);
+    *wp = make_uint2((uint32_t)n0 | ((uint32_t)n1 << 16), (uint32_t)n2 | ((uint32_t)Pv << 16));
+    const uint32_t slot = a.y >> 16;
+    if (slot != LXB_NOSLOT) {
+      float y = 0.0f;
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(n0)));
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(n1)));
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 & 0xffffu)), lx_f(n2)));
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(Pv)));
+      sm.buf[slot] = lx_rbf(lx_silu(lx_rbf(y)));
+    }
+  }
+  const int32_t* rows = P.i32 + it.rows;
+  const uint16_t* prm = P.u16 + it.params;
+  if (t < R) {  // g = -exp(A_log) * softplus(bf16(a . x) + dt_bias)
+    const float a = lx_rbf(row_dot(P.ent, (uint32_t)rows[16 + 2 * t], rows[17 + 2 * t], sm.xn));
+    const float A = -lx_exp(lx_f(prm[t]));
+    sm.g[t] = lx_mul(A, lx_softplus(lx_add(a, lx_f(prm[R + t]))));
+  } else if (t < 2 * R) {  // beta = bf16(sigmoid(bf16(b . x)))
+    const int r = t - R;
+    const float b = lx_rbf(row_dot(P.ent, (uint32_t)rows[2 * r], rows[2 * r + 1], sm.xn));
+    sm.beta[r] = lx_rbf(lx_sigmoid(b));
+  }
+  const int qa = __syncthreads_or(t < KD && sm.buf[t] != 0.0f);
+  const int ka = __syncthreads_or(t >= KD && t < 2 * KD && sm.buf[t] != 0.0f);
+  int anyg = 0;
+#pragma unroll
+  for (int r = 0; r < R; r++) anyg |= sm.g[r] != 0.0f;
+  if (!qa && !ka && !anyg) return false;  // the state stays as it is and o = 0
+  // transformers' l2norm in bf16 on q (warp 0) and k (warp 1): the nonzero entries in
+  // ascending order, their bf16 squares summed sequentially from +0
+  if (warp < 2) {
+    const float* xv = sm.buf + warp * KD;
+    int* idx = warp ? sm.kidx : sm.qidx;
+    float* val = warp ? sm.kval : sm.qval;
+    int n = 0;
+    for (int base = 0; base < KD; base += 32) {
+      const float v = xv[base + lane];
+      const unsigned m = __ballot_sync(0xffffffffu, v != 0.0f);
+      if (v != 0.0f) {
+        const int k = n + __popc(m & ((1u << lane) - 1u));
+        idx[k] = base + lane;
+        val[k] = v;
+      }
+      n += __popc(m);
+    }
+    __syncwarp();
+    float inv = 0.0f;
+    if (lane == 0) {
+      float s = 0.0f;
+      for (int i = 0; i < n; i++) s = lx_add(s, lx_rbf(lx_mul(val[i], val[i])));
+      inv = lx_rbf(lx_rsqrt(lx_rbf(lx_add(lx_rbf(s), 1e-6f))));
+    }
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    for (int i = lane; i < n; i += 32) {
+      const float vn = lx_rbf(lx_mul(val[i], inv));
+      val[i] = warp ? vn : lx_mul(vn, 0.0625f);  // the query times 256^-0.5
+    }
+    if (lane == 0) (warp ? sm.nk : sm.nq) = n;
+  }
+  __syncthreads();
+  // the delta rule, thread = (value head, state column)
+  const int nq = sm.nq, nk = sm.nk;
+  {
+    const int j = t & (VD - 1);
+    for (int r = t >> 7; r < R; r += NT / VD) {
+      const int vh = it.kh * R + r;
+      float* S = rec + (size_t)vh * KD * VD + j;
+      const float g = sm.g[r];
+      if (g != 0.0f) {  // decay the rows that may be nonzero (the others stay zero)
+        const float e = lx_exp(g);
+        const uint32_t* b = bm + vh * 8;
+#pragma unroll 1
+        for (int w = 0; w < 8; w++) {
+          uint32_t m = b[w];
+          while (m) {
+            int ix[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              ix[q] = m ? (w * 32 + __ffs(m) - 1) : -1;
+              m &= m - 1;
+            }
+            float v[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) v[q] = ix[q] >= 0 ? S[ix[q] * VD] : 0.0f;
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+              if (ix[q] >= 0) S[ix[q] * VD] = lx_mul(v[q], e);
+          }
+        }
+      }
+      if (nk) {
+        float kv = 0.0f;
+        for (int a = 0; a < nk; a++) kv = lx_add(kv, lx_mul(S[sm.kidx[a] * VD], sm.kval[a]));
+        const float delta = lx_mul(lx_sub(sm.buf[2 * KD + r * VD + j], kv), sm.beta[r]);
+        for (int a = 0; a < nk; a++) {
+          float* hp = S + sm.kidx[a] * VD;
+          *hp = lx_add(*hp, lx_mul(sm.kval[a], delta));
+        }
+      }
+      float o = 0.0f;
+      for (int a = 0; a < nq; a++) o = lx_add(o, lx_mul(S[sm.qidx[a] * VD], sm.qval[a]));
+      sm.ob[r][j] = lx_rbf(o);
+    }
+  }
+  __syncthreads();
+  if ((it.flags & LXB_IT_DECAYS) && t < R) {  // rows the key wrote may now be nonzero
+    uint32_t* b = bm + (it.kh * R + t) * 8;
+    for (int a = 0; a < nk; a++) b[sm.kidx[a] >> 5] |= 1u << (sm.kidx[a] & 31);
+  }
+  // Qwen3_5RMSNormGated per value head with output (warp r): bf16(bf16(w * bf16(o * rsqrt(
+  // mean(o^2) + eps))) * silu(z)), z = bf16(in_proj_z . x)
+  if (warp < R) {
+    const int r = warp;
+    const float* o = sm.ob[r];
+    const float o0 = o[4 * lane], o1 = o[4 * lane + 1], o2 = o[4 * lane + 2],
+                o3 = o[4 * lane + 3];
+    const bool nz = __any_sync(0xffffffffu, o0 != 0.0f || o1 != 0.0f || o2 != 0.0f || o3 != 0.0f);
+    if (nz) {
+      float s = lx_mul(o0, o0);
+      s = lx_add(s, lx_mul(o1, o1));
+      s = lx_add(s, lx_mul(o2, o2));
+      s = lx_add(s, lx_mul(o3, o3));
+      s = warp_xor_sum(s);
+      const float rr = lx_rsqrt(lx_add(lx_div(s, 128.0f), P.eps));
+      const uint16_t* gw = prm + 2 * R;
+      const int vh = it.kh * R + r;
+      for (int j = lane; j < VD; j += 32) {
+        const float hn = lx_rbf(lx_mul(o[j], rr));
+        const float u = lx_rbf(lx_mul(lx_f(gw[j]), hn));
+        const int zr = 32 + 2 * (r * VD + j);
+        const float z = lx_rbf(row_dot(P.ent, (uint32_t)rows[zr], rows[zr + 1], sm.xn));
+        on[r * VD + j] = lx_rb(lx_mul(u, lx_silu(z)));
+      }
+      if (lane == 0) atomicOr(&sm.vhmask[it.slot], 1u << r);
+      (void)vh;
+    }
+  }
+  __syncthreads();
+  return sm.vhmask[it.slot] != 0 && (it.flags & LXB_IT_OUT);
+}
+
+// --- the owned rows ---------------------------------------------------------------------------
+// The MLP over this CTA's rows: own[row] = bf16(x + bf16(sum_u h_u w_d)), h_u re-evaluated here.
+__device__ void mlp_owner(const Dev& P, Smem& sm, const lxb_owner& ow, int rank, float* own) {
+  const int t = threadIdx.x;
+  for (int u = t; u < ow.n_units; u += NT) {
+    const lxb_unit un = P.units[ow.unit0 + u];
+    const float gg = lx_rbf(row_dot(P.ent, un.g, un.ng, sm.xm));
+    const float uu = lx_rbf(row_dot(P.ent, un.u, un.nu, sm.xm));
+    const float act = lx_rbf(lx_silu(gg));
+    sm.hbuf[u] = lx_rbf(lx_mul(act, uu));
+  }
+  __syncthreads();
+  const int r0 = rank * P.blk;
+  const int32_t* rp = ow.mrow >= 0 ? P.i32 + ow.mrow : nullptr;
+  for (int k = t; k < P.blk; k += NT) {
+    const float xv = sm.x[r0 + k];
+    float res = xv;
+    if (rp) {
+      const int a = rp[k], b = rp[k + 1];
+      float s = 0.0f;
+      bool any = false;
+      for (int e = a; e < b; e++) {
+        const uint32_t w = __ldg(P.ent + e);
+        const float hv = sm.hbuf[w & 0xffffu];
+        if (hv != 0.0f) {
+          s = lx_add(s, lx_mul(hv, lx_f((uint16_t)(w >> 16))));
+          any = true;
+        }
+      }
+      if (any) res = lx_rbf(lx_add(xv, lx_rbf(s)));
+    }
+    own[k] = res;
+  }
+}
+
+// out_proj over this CTA's rows, from the layer's items' outputs (gathered over DSMEM)
+__device__ void out_owner(const Dev& P, Smem& sm, const lxb_layer& ly, const lxb_owner& ow,
+                          int rank, float* own, cg::cluster_group& cluster) {
+  const int t = threadIdx.x;
+  const int32_t* itemof = P.i32 + ly.itemof;
+  if (t < LXB_NK) {
+    const int ii = itemof[t];
+    uint32_t m = 0;
+    if (ii >= 0) {
+      const lxb_item it = P.items[ii];
+      const uint32_t* rm = cluster.map_shared_rank(&sm.vhmask[it.slot], it.cta);
+      m = *rm;
+    }
+    sm.kmask[t] = (int)m;
+  }
+  __syncthreads();
+  // copy the active items' outputs: 16 key heads x 128 uint4
+  for (int k = t; k < LXB_NK * (R * VD / 8); k += NT) {
+    const int kh = k / (R * VD / 8), q = k % (R * VD / 8);
+    if (!sm.kmask[kh]) continue;
+    const lxb_item it = P.items[itemof[kh]];
+    const uint4* src = reinterpret_cast<const uint4*>(cluster.map_shared_rank(&sm.on[it.slot][0], it.cta));
+    reinterpret_cast<uint4*>(&sm.onall[kh][0])[q] = src[q];
+  }
+  __syncthreads();
+  const int r0 = rank * P.blk;
+  const int32_t* rp = ow.orow >= 0 ? P.i32 + ow.orow : nullptr;
+  for (int k = t; k < P.blk; k += NT) {
+    const float xv = sm.x[r0 + k];
+    float res = xv;
+    if (rp) {
+      const int a = rp[k], b = rp[k + 1];
+      float s = 0.0f;
+      bool any = false;
+      for (int e = a; e < b; e++) {
+        const uint32_t w = __ldg(P.ent + e);
+        const uint32_t vd = w & 0xffffu;
+        const int kh = (int)(vd >> 10);
+        if (!((sm.kmask[kh] >> ((vd >> 7) & 7)) & 1)) continue;
+        const float ov = lx_f(sm.onall[kh][vd & 1023u]);
+        if (ov != 0.0f) {
+          s = lx_add(s, lx_mul(ov, lx_f((uint16_t)(w >> 16))));
+          any = true;
+        }
+      }
+      if (any) res = lx_rbf(lx_add(xv, lx_rbf(s)));
+    }
+    own[k] = res;
+  }
+}
+
+// every CTA's replica from the owners' blocks (16-byte DSMEM loads)
+__device__ void pull(const Dev& P, Smem& sm, int par, cg::cluster_group& cluster) {
+  const int per = P.blk / 4;  // uint4 per owner
+  for (int k = threadIdx.x; k < H / 4; k += NT) {
+    const int c = k / per, q = k % per;
+    const uint4* src = reinterpret_cast<const uint4*>(cluster.map_shared_rank(&sm.own[par][0], c));
+    reinterpret_cast<uint4*>(sm.x)[k] = src[q];
+  }
+  __syncthreads();
+}
+
+__device__ void load_embed(const Run& run, const Dev& P, Smem& sm, int tok) {
+  const uint4* e = reinterpret_cast<const uint4*>(run.embed + ((int64_t)tok + P.offset) * H);
+  for (int k = threadIdx.x; k < H / 8; k += NT) {
+    const uint4 v = __ldg(e + k);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      sm.x[8 * k + 2 * q] = lx_f((uint16_t)(w[q] & 0xffffu));
+      sm.x[8 * k + 2 * q + 1] = lx_f((uint16_t)(w[q] >> 16));
+    }
+  }
+  __syncthreads();
+}
+
+// the head over this CTA's rows: the first maximum of the bf16 logits
+__device__ void head_part(const Dev& P, Smem& sm, int rank) {
+  const int t = threadIdx.x;
+  const int nd = P.n_dense, ng = (nd + 3) / 4;
+  for (int k = t; k < ng * 256; k += NT) {
+    const int g = k >> 8, code = k & 255;
+    float s = 0.0f;
+    for (int j = 0; j < 4 && 4 * g + j < nd; j++)
+      s = lx_add(s, lx_mul(P.htab[(code >> (2 * j)) & 3], sm.xm[P.dense_cols[4 * g + j]]));
+    sm.htg[g][code] = s;
+  }
+  __syncthreads();
+  const lxb_headcta hc = P.headcta[rank];
+  const int32_t* rp = P.i32 + hc.rowptr;
+  float bv = -LXB_INF;
+  int bi = 0x7fffffff;
+  for (int row = hc.r0 + t; row < hc.r1; row += NT) {
+    float D = 0.0f;
+    if (nd) {
+      const uint64_t code = __ldg(P.hcodes + row);
+      for (int g = 0; g < ng; g++) D = lx_add(D, sm.htg[g][(code >> (8 * g)) & 255u]);
+    }
+    float S = 0.0f;
+    const int a = rp[row - hc.r0], b = rp[row - hc.r0 + 1];
+    for (int e = a; e < b; e++) {
+      const uint32_t w = __ldg(P.ent + e);
+      S = lx_add(S, lx_mul(lx_f((uint16_t)(w >> 16)), sm.xm[w & 0xffffu]));
+    }
+    const float lg = lx_rbf(lx_add(D, S));
+    if (lg > bv) {
+      bv = lg;
+      bi = row;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_down_sync(0xffffffffu, bv, off);
+    const int oi = __shfl_down_sync(0xffffffffu, bi, off);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int lane = t & 31, warp = t >> 5;
+  __syncthreads();
+  if (lane == 0) {
+    sm.red[warp] = bv;
+    reinterpret_cast<int*>(sm.hbuf)[warp] = bi;
+  }
+  __syncthreads();
+  if (t == 0) {
+    for (int w = 1; w < NT / 32; w++) {
+      const float ov = sm.red[w];
+      const int oi = reinterpret_cast<int*>(sm.hbuf)[w];
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    sm.bestv = bv;
+    sm.besti = bi;
+  }
+}
+
+__global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
+  extern __shared__ __align__(16) unsigned char dsm[];
+  Smem& sm = *reinterpret_cast<Smem*>(dsm);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int C = P.C;
+  const int s = blockIdx.x / C;
+  const int t = threadIdx.x;
+  if (t < 2) sm.wflag[t] = 0;
+  if (t == 0) {
+    int tok = run.forced[(size_t)s * run.n_forced];
+    if (tok < 0 || (int64_t)tok + P.offset >= P.n_embed_rows) {
+      set_status(P, LXB_S_TOKEN, s, 0);
+      tok = 0;
+    }
+    sm.tok = tok;
+  }
+  __syncthreads();
+  cluster.sync();  // every CTA's flags are initialised before anyone may push one
+  int ph = 0;
+  load_embed(run, P, sm, sm.tok);
+  for (int i = 0; i < run.n_tokens; i++) {
+    if (rank == 0 && t == 0 && run.inputs) run.inputs[(size_t)s * run.n_tokens + i] = sm.tok;
+    for (int L = 0; L < P.n_layers; L++) {
+      const lxb_layer ly = P.layers[L];
+      const uint64_t* sp = run.state_ptrs + ((size_t)s * P.n_layers + L) * 2;
+      float* rec = reinterpret_cast<float*>(sp[0]);
+      uint16_t* conv = reinterpret_cast<uint16_t*>(sp[1]);
+      uint32_t* bm = run.bitmaps + ((size_t)s * P.n_layers + L) * LXB_NV * 8;
+      const lxb_owner ow = P.owners[ly.owner0 + rank];
+      const float ss = block_ssq(sm, sm.x);
+      if (ly.has_gdn) norm_into(P, sm.xn, sm.x, ly.ln_in, ss);
+      if (ly.has_mlp) norm_into(P, sm.xm, sm.x, ly.ln_post, ss);
+      __syncthreads();
+      bool wrote = false;
+      if (ly.has_gdn) {
+        for (int k = 0; k < ly.n_items; k++) {
+          const lxb_item it = P.items[ly.item0 + k];
+          if (it.cta == rank) wrote |= gdn_item(P, sm, it, rec, conv, bm);
+        }
+      }
+      if (wrote && t < C) *cluster.map_shared_rank(&sm.wflag[ph & 1], t) = 1;
+      if (ly.has_mlp) mlp_owner(P, sm, ow, rank, sm.own[ph & 1]);
+      cluster.sync();
+      const int fl = *reinterpret_cast<volatile int*>(&sm.wflag[ph & 1]);
+      __syncthreads();
+      if (fl) {
+        if (t == 0) sm.wflag[ph & 1] = 0;
+        ph++;
+        out_owner(P, sm, ly, ow, rank, sm.own[ph & 1], cluster);
+        cluster.sync();
+        pull(P, sm, ph & 1, cluster);
+        ph++;
+        if (ly.has_mlp) {
+          const float ss2 = block_ssq(sm, sm.x);
+          norm_into(P, sm.xm, sm.x, ly.ln_post, ss2);
+          __syncthreads();
+          mlp_owner(P, sm, ow, rank, sm.own[ph & 1]);
+          cluster.sync();
+          pull(P, sm, ph & 1, cluster);
+          ph++;
+        }
+      } else {
+        if (ly.has_mlp) pull(P, sm, ph & 1, cluster);
+        ph++;
+      }
+    }
+    // the output head: every CTA its rows, then the first maximum over the cluster
+    {
+      const float ss = block_ssq(sm, sm.x);
+      norm_into(P, sm.xm, sm.x, P.final_norm, ss);
+      __syncthreads();
+      head_part(P, sm, rank);
+      cluster.sync();
+      if (t < 32) {
+        float bv = -LXB_INF;
+        int bi = 0x7fffffff;
+        if (t < C) {
+          bv = *cluster.map_shared_rank(&sm.bestv, t);
+          bi = *cluster.map_shared_rank(&sm.besti, t);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          const float ov = __shfl_down_sync(0xffffffffu, bv, off);
+          const int oi = __shfl_down_sync(0xffffffffu, bi, off);
+          if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if (t == 0) {
+          if (rank == 0) run.preds[(size_t)s * run.n_tokens + i] = bi;
+          int nt = (i + 1 < run.n_forced) ? run.forced[(size_t)s * run.n_forced + i + 1] : bi;
+          if (nt < 0 || (int64_t)nt + P.offset >= P.n_embed_rows) {
+            if (i + 1 < run.n_tokens) set_status(P, LXB_S_TOKEN, s, i + 1);
+            nt = 0;
+          }
+          sm.tok = nt;
+        }
+      }
+      __syncthreads();
+      if (i + 1 < run.n_tokens) load_embed(run, P, sm, sm.tok);
+    }
+  }
+  cluster.sync();  // no CTA leaves while another may still read its shared memory
+}
+
+// the nonzero-row bitmaps of the decaying layers' states: one warp per state row
+__global__ void lxb_bitmap_kernel(const uint64_t* state_ptrs, uint32_t* bitmaps,
+                                  const lxb_layer* layers, int n_layers) {
+  const int s = blockIdx.z, L = blockIdx.y, vh = blockIdx.x;
+  if (!layers[L].decays) return;
+  const float* S = reinterpret_cast<const float*>(state_ptrs[((size_t)s * n_layers + L) * 2]) +
+                   (size_t)vh * KD * VD;
+  uint32_t* b = bitmaps + (((size_t)s * n_layers + L) * LXB_NV + vh) * 8;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;  // 8 warps
+  for (int w = warp; w < 8; w += 8) {
+    uint32_t word = 0;
+    for (int i = 0; i < 32; i++) {
+      const float4 v = reinterpret_cast<const float4*>(S + (size_t)(w * 32 + i) * VD)[lane];
+      const bool nz = v.x != 0.0f || v.y != 0.0f || v.z != 0.0f || v.w != 0.0f;
+      if (__any_sync(0xffffffffu, nz)) word |= 1u << i;
+    }
+    if (lane == 0) b[w] = word;
+  }
+}
+
+// =============================================================================================
+// The C ABI
+// =============================================================================================
+struct lxb_plan {
+  int device;
+  int cluster;
+  void* dimage;
+  size_t bytes;
+  lxb_image_header hdr;
+  Dev dev;
+  uint32_t* status;
+  int max_clusters;
+};
+
+static_assert(offsetof(Smem, own) % 16 == 0 && offsetof(Smem, on) % 16 == 0 &&
+                  offsetof(Smem, onall) % 16 == 0 && sizeof(Smem) < 200 * 1024,
+              "shared memory layout");
+
+static int cuda_rc(cudaError_t e) { return e == cudaSuccess ? LXB_OK : (int)e; }
+
+extern "C" int lxb_abi_version(void) { return LXB_ABI_VERSION; }
+
+extern "C" int lxb_query(int device, lxb_caps* caps) {
+  if (!caps) return LXB_E_INVAL;
+  memset(caps, 0, sizeof(*caps));
+  caps->device = device;
+  cudaError_t e;
+  if ((e = cudaDeviceGetAttribute(&caps->cc_major, cudaDevAttrComputeCapabilityMajor, device)))
+    return cuda_rc(e);
+  cudaDeviceGetAttribute(&caps->cc_minor, cudaDevAttrComputeCapabilityMinor, device);
+  cudaDeviceGetAttribute(&caps->sm_count, cudaDevAttrMultiProcessorCount, device);
+  cudaDeviceGetAttribute(&caps->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  cudaDeviceGetAttribute(&caps->cluster_launch, cudaDevAttrClusterLaunch, device);
+  return LXB_OK;
+}
+
+const char* lxb_error_string_c(int code) {
+  switch (code) {
+    case LXB_OK: return "ok";
+    case LXB_E_INVAL: return "invalid argument";
+    case LXB_E_IMAGE: return "malformed plan image";
+    case LXB_E_DEVICE: return "device cannot run this plan";
+    case LXB_E_STATUS: return "kernel reported an error (lxb_status)";
+    default: return code > 0 ? cudaGetErrorString((cudaError_t)code) : "unknown error";
+  }
+}
+extern "C" const char* lxb_error_string(int code) { return lxb_error_string_c(code); }
+
+// --- image validation: every offset, count and index the kernel will follow ------------------
+namespace {
+struct View {
+  const unsigned char* base;
+  size_t bytes;
+  const lxb_image_header* h;
+  template <class T>
+  const T* sec(int k) const { return reinterpret_cast<const T*>(base + h->sec[k].off); }
+  int64_t n(int k) const { return h->sec[k].count; }
+};
+
+bool ent_range(const View& v, int64_t off, int64_t cnt) {
+  return off >= 0 && cnt >= 0 && off + cnt <= v.n(LXB_SEC_ENT);
+}
+bool i32_range(const View& v, int64_t off, int64_t cnt) {
+  return off >= 0 && cnt >= 0 && off + cnt <= v.n(LXB_SEC_I32);
+}
+bool u16_range(const View& v, int64_t off, int64_t cnt) {
+  return off >= 0 && cnt >= 0 && off + cnt <= v.n(LXB_SEC_U16);
+}
+// entries [off, off + cnt) whose low 16 bits must be < lim
+bool ent_idx(const View& v, int64_t off, int64_t cnt, uint32_t lim) {
+  if (!ent_range(v, off, cnt)) return false;
+  const uint32_t* e = v.sec<uint32_t>(LXB_SEC_ENT) + off;
+  for (int64_t i = 0; i < cnt; i++)
+    if ((e[i] & 0xffffu) >= lim) return false;
+  return true;
+}
+// a row-pointer block: n + 1 monotone pointers into ent, entries' indices < lim
+bool rowptr_ok(const View& v, int32_t p, int n, uint32_t lim) {
+  if (!i32_range(v, p, (int64_t)n + 1)) return false;
+  const int32_t* rp = v.sec<int32_t>(LXB_SEC_I32) + p;
+  for (int k = 0; k < n; k++)
+    if (rp[k + 1] < rp[k]) return false;
+  return ent_idx(v, rp[0], (int64_t)rp[n] - rp[0], lim);
+}
+
+int validate(const View& v, int cluster) {
+  const lxb_image_header* h = v.h;
+  if (v.bytes < sizeof(lxb_image_header)) return LXB_E_IMAGE;
+  if (h->magic != LXB_MAGIC || h->version != LXB_IMAGE_VERSION) return LXB_E_IMAGE;
+  if (h->hidden != H || h->cluster != cluster || h->n_layers < 1 || h->n_vocab < 1)
+    return LXB_E_IMAGE;
+  const size_t esz[LXB_SEC_COUNT] = {sizeof(lxb_layer), sizeof(lxb_item), sizeof(lxb_chan), 4,
+                                     sizeof(lxb_unit), sizeof(lxb_owner), 4, 2,
+                                     sizeof(lxb_headcta), 8};
+  for (int k = 0; k < LXB_SEC_COUNT; k++) {
+    const lxb_sec& s = h->sec[k];
+    if (s.off < (int64_t)sizeof(lxb_image_header) || s.off % 16 || s.count < 0 ||
+        (size_t)s.off + (size_t)s.count * esz[k] > v.bytes)
+      return LXB_E_IMAGE;
+  }
+  const int C = cluster, blk = H / C;
+  if (v.n(LXB_SEC_LAYERS) != h->n_layers || v.n(LXB_SEC_OWNERS) != (int64_t)h->n_layers * C ||
+      v.n(LXB_SEC_HEADCTA) != C || v.n(LXB_SEC_ITEMS) != h->n_items)
+    return LXB_E_IMAGE;
+  if (h->n_dense < 0 || h->n_dense > LXB_MAXDENSE) return LXB_E_IMAGE;
+  if (h->n_dense && v.n(LXB_SEC_HCODES) != h->n_vocab) return LXB_E_IMAGE;
+  for (int j = 0; j < h->n_dense; j++)
+    if (h->dense_cols[j] < 0 || h->dense_cols[j] >= H) return LXB_E_IMAGE;
+  if (!u16_range(v, h->final_norm, H) || h->n_embed_rows < 1 || h->offset < 0) return LXB_E_IMAGE;
+  const lxb_layer* layers = v.sec<lxb_layer>(LXB_SEC_LAYERS);
+  const lxb_item* items = v.sec<lxb_item>(LXB_SEC_ITEMS);
+  const lxb_chan* chans = v.sec<lxb_chan>(LXB_SEC_CHANS);
+  const lxb_owner* owners = v.sec<lxb_owner>(LXB_SEC_OWNERS);
+  const lxb_unit* units = v.sec<lxb_unit>(LXB_SEC_UNITS);
+  for (int L = 0; L < h->n_layers; L++) {
+    const lxb_layer& ly = layers[L];
+    if (!u16_range(v, ly.ln_in, H) || !u16_range(v, ly.ln_post, H)) return LXB_E_IMAGE;
+    if (ly.item0 < 0 || ly.n_items < 0 || ly.item0 + ly.n_items > h->n_items) return LXB_E_IMAGE;
+    if (ly.owner0 != L * C) return LXB_E_IMAGE;
+    if (!i32_range(v, ly.itemof, LXB_NK)) return LXB_E_IMAGE;
+    const int32_t* io = v.sec<int32_t>(LXB_SEC_I32) + ly.itemof;
+    for (int kh = 0; kh < LXB_NK; kh++)
+      if (io[kh] != -1 && (io[kh] < ly.item0 || io[kh] >= ly.item0 + ly.n_items ||
+                           items[io[kh]].kh != kh))
+        return LXB_E_IMAGE;
+    int per_cta[LXB_MAXC] = {0};
+    for (int k = 0; k < ly.n_items; k++) {
+      const lxb_item& it = items[ly.item0 + k];
+      if (it.layer != L || it.kh < 0 || it.kh >= LXB_NK || it.cta < 0 || it.cta >= C ||
+          it.slot < 0 || it.slot >= LXB_ITEMSLOTS || io[it.kh] != ly.item0 + k)
+        return LXB_E_IMAGE;
+      if (per_cta[it.cta] & (1 << it.slot)) return LXB_E_IMAGE;  // one item per (cta, slot)
+      per_cta[it.cta] |= 1 << it.slot;
+      if (it.ch0 < 0 || it.n_ch < 0 || it.n_ch > LXB_NSLOT * 2 ||
+          (int64_t)it.ch0 + it.n_ch > v.n(LXB_SEC_CHANS))
+        return LXB_E_IMAGE;
+      for (int c = 0; c < it.n_ch; c++) {
+        const lxb_chan& ch = chans[it.ch0 + c];
+        if (ch.conv_ch >= LXB_CONV || (ch.slot != LXB_NOSLOT && ch.slot >= LXB_NSLOT) ||
+            !ent_idx(v, ch.ent, ch.n, H))
+          return LXB_E_IMAGE;
+      }
+      if (!i32_range(v, it.rows, 2 * (2 * R + R * VD)) || !u16_range(v, it.params, 2 * R + VD))
+        return LXB_E_IMAGE;
+      const int32_t* rr = v.sec<int32_t>(LXB_SEC_I32) + it.rows;
+      for (int q = 0; q < 2 * R + R * VD; q++)
+        if (!ent_idx(v, rr[2 * q], rr[2 * q + 1], H)) return LXB_E_IMAGE;
+      if ((it.flags & LXB_IT_DECAYS) && !ly.decays) return LXB_E_IMAGE;
+    }
+    for (int c = 0; c < C; c++) {
+      const lxb_owner& ow = owners[L * C + c];
+      if (ow.unit0 < 0 || ow.n_units < 0 || ow.n_units > LXB_MAXUNITS ||
+          (int64_t)ow.unit0 + ow.n_units > v.n(LXB_SEC_UNITS))
+        return LXB_E_IMAGE;
+      for (int u = 0; u < ow.n_units; u++) {
+        const lxb_unit& un = units[ow.unit0 + u];
+        if (!ent_idx(v, un.g, un.ng, H) || !ent_idx(v, un.u, un.nu, H)) return LXB_E_IMAGE;
+      }
+      if (ow.mrow >= 0 && !rowptr_ok(v, ow.mrow, blk, (uint32_t)ow.n_units)) return LXB_E_IMAGE;
+      if (ow.orow >= 0 && !rowptr_ok(v, ow.orow, blk, LXB_NV * LXB_VD)) return LXB_E_IMAGE;
+      if (ly.has_mlp && ow.mrow < 0 && ow.n_units) return LXB_E_IMAGE;
+    }
+  }
+  const lxb_headcta* hc = v.sec<lxb_headcta>(LXB_SEC_HEADCTA);
+  int prev = 0;
+  for (int c = 0; c < C; c++) {
+    if (hc[c].r0 != prev || hc[c].r1 < hc[c].r0 || hc[c].r1 > h->n_vocab) return LXB_E_IMAGE;
+    prev = hc[c].r1;
+    if (!rowptr_ok(v, hc[c].rowptr, hc[c].r1 - hc[c].r0, H)) return LXB_E_IMAGE;
+  }
+  if (prev != h->n_vocab) return LXB_E_IMAGE;
+  if (h->n_dense) {
+    const uint64_t* codes = v.sec<uint64_t>(LXB_SEC_HCODES);
+    const int bits = 2 * h->n_dense;
+    for (int64_t r = 0; r < h->n_vocab; r++)
+      if (bits < 64 && (codes[r] >> bits)) return LXB_E_IMAGE;
+  }
+  return LXB_OK;
+}
+}  // namespace
+
+extern "C" int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb_plan** out) {
+  if (!image || !out || bytes < sizeof(lxb_image_header)) return LXB_E_INVAL;
+  *out = nullptr;
+  if (cluster < LXB_MINC || cluster > LXB_MAXC || H % cluster || (H / cluster) % 4)
+    return LXB_E_INVAL;
+  View v{static_cast<const unsigned char*>(image), bytes,
+         static_cast<const lxb_image_header*>(image)};
+  int rc = validate(v, cluster);
+  if (rc) return rc;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e) return cuda_rc(e);
+  int major = 0, cl = 0, optin = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&cl, cudaDevAttrClusterLaunch, dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (major < 10 || !cl || optin < (int)sizeof(Smem)) return LXB_E_DEVICE;
+  lxb_plan* p = new (std::nothrow) lxb_plan();
+  if (!p) return LXB_E_INVAL;
+  p->device = dev;
+  p->cluster = cluster;
+  p->bytes = bytes;
+  p->hdr = *v.h;
+  if ((e = cudaMalloc(&p->dimage, bytes))) {
+    delete p;
+    return cuda_rc(e);
+  }
+  if ((e = cudaMalloc(&p->status, 16)) || (e = cudaMemset(p->status, 0, 16)) ||
+      (e = cudaMemcpy(p->dimage, image, bytes, cudaMemcpyHostToDevice))) {
+    cudaFree(p->dimage);
+    if (p->status) cudaFree(p->status);
+    delete p;
+    return cuda_rc(e);
+  }
+  const unsigned char* b = static_cast<const unsigned char*>(p->dimage);
+  const lxb_image_header* h = &p->hdr;
+  Dev& d = p->dev;
+  d.layers = reinterpret_cast<const lxb_layer*>(b + h->sec[LXB_SEC_LAYERS].off);
+  d.items = reinterpret_cast<const lxb_item*>(b + h->sec[LXB_SEC_ITEMS].off);
+  d.chans = reinterpret_cast<const lxb_chan*>(b + h->sec[LXB_SEC_CHANS].off);
+  d.ent = reinterpret_cast<const uint32_t*>(b + h->sec[LXB_SEC_ENT].off);
+  d.units = reinterpret_cast<const lxb_unit*>(b + h->sec[LXB_SEC_UNITS].off);
+  d.owners = reinterpret_cast<const lxb_owner*>(b + h->sec[LXB_SEC_OWNERS].off);
+  d.i32 = reinterpret_cast<const int32_t*>(b + h->sec[LXB_SEC_I32].off);
+  d.u16 = reinterpret_cast<const uint16_t*>(b + h->sec[LXB_SEC_U16].off);
+  d.headcta = reinterpret_cast<const lxb_headcta*>(b + h->sec[LXB_SEC_HEADCTA].off);
+  d.hcodes = reinterpret_cast<const uint64_t*>(b + h->sec[LXB_SEC_HCODES].off);
+  d.n_layers = h->n_layers;
+  d.C = cluster;
+  d.blk = H / cluster;
+  d.n_vocab = h->n_vocab;
+  d.n_dense = h->n_dense;
+  d.final_norm = h->final_norm;
+  d.eps = h->eps;
+  d.n_embed_rows = h->n_embed_rows;
+  d.offset = h->offset;
+  memcpy(d.htab, h->htab, sizeof(d.htab));
+  memcpy(d.dense_cols, h->dense_cols, sizeof(d.dense_cols));
+  d.status = p->status;
+  // launch attributes, and how many clusters fit at once
+  const int smem = (int)sizeof(Smem);
+  cudaFuncSetAttribute(lxb_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (cluster > 8)
+    cudaFuncSetAttribute(lxb_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = cluster;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(cluster);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int ncl = 0;
+  e = cudaOccupancyMaxActiveClusters(&ncl, (void*)lxb_decode_kernel, &cfg);
+  if (e || ncl < 1) {
+    cudaGetLastError();
+    lxb_plan_destroy(p);
+    return e ? cuda_rc(e) : LXB_E_DEVICE;
+  }
+  p->max_clusters = ncl;
+  *out = p;
+  return LXB_OK;
+}
+
+extern "C" int lxb_decode(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitmaps,
+                          int sync_bitmaps, const uint16_t* embed, int n_streams,
+                          const int32_t* forced, int n_forced, int n_tokens, int32_t* preds,
+                          int32_t* inputs, void* cuda_stream) {
+  if (!p || !state_ptrs || !bitmaps || !embed || !forced || !preds || n_streams < 1 ||
+      n_forced < 1 || n_tokens < 1 || n_streams > 65535)
+    return LXB_E_INVAL;
+  if ((reinterpret_cast<uintptr_t>(embed) & 15) || (reinterpret_cast<uintptr_t>(bitmaps) & 15))
+    return LXB_E_INVAL;
+  cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+  cudaError_t e;
+  if (sync_bitmaps) {
+    lxb_bitmap_kernel<<<dim3(LXB_NV, p->hdr.n_layers, n_streams), 256, 0, st>>>(
+        state_ptrs, bitmaps, p->dev.layers, p->hdr.n_layers);
+    if ((e = cudaGetLastError())) return cuda_rc(e);
+  }
+  Run run{state_ptrs, bitmaps, embed, forced, n_forced, n_tokens, preds, inputs};
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = p->cluster;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(p->cluster * n_streams);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = sizeof(Smem);
+  cfg.stream = st;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, lxb_decode_kernel, p->dev, run);
+  return cuda_rc(e);
+}
+
+extern "C" int lxb_status(lxb_plan* p, lxb_error* err) {
+  if (!p || !err) return LXB_E_INVAL;
+  uint32_t s[3];
+  cudaError_t e = cudaMemcpy(s, p->status, 12, cudaMemcpyDeviceToHost);
+  if (e) return cuda_rc(e);
+  err->status = s[0];
+  err->first_stream = (int32_t)s[1];
+  err->first_step = (int32_t)s[2];
+  return LXB_OK;
+}
+
+extern "C" int lxb_status_clear(lxb_plan* p) {
+  if (!p) return LXB_E_INVAL;
+  return cuda_rc(cudaMemset(p->status, 0, 16));
+}
+
+extern "C" size_t lxb_plan_bytes(const lxb_plan* p) { return p ? p->bytes : 0; }
+extern "C" int lxb_plan_max_clusters(const lxb_plan* p) { return p ? p->max_clusters : 0; }
+
+extern "C" void lxb_plan_destroy(lxb_plan* p) {
+  if (!p) return;
+  if (p->dimage) cudaFree(p->dimage);
+  if (p->status) cudaFree(p->status);
+  delete p;
+}

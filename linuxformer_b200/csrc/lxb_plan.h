@@ -1,0 +1,125 @@
+// The plan image: every weight table the decode kernel reads, packed by
+// linuxformer_b200/tables.py into one byte image that lxb_plan_create validates and uploads
+// whole. All offsets are byte offsets from the image start (sections) or element indices into
+// a section; all structs are plain 4/8-byte fields, little-endian, no padding surprises.
+//
+// The tables restate what the reference packs in lx/lx/mega.py:199-504 (its CSR rows, the CSC
+// of out_proj/down_proj, per-item channel lists, the head's dense codes and sparse columns), laid
+// out for a thread-block cluster per stream instead of one persistent grid:
+//   - a GDN item (one live key head of one layer) runs on one CTA of the cluster;
+//   - the residual rows are split in C contiguous blocks of 2560 / C; the CTA owning a block
+//     computes every sum that lands in it (down_proj and out_proj rows, in CSR order), so no
+//     sum is ever split across CTAs and none needs an atomic;
+//   - the head's rows are split in C contiguous ranges.
+#pragma once
+#include <stdint.h>
+
+#define LXB_MAGIC 0x50425a4cu  // "LZBP"
+#define LXB_IMAGE_VERSION 2
+
+#define LXB_H 2560
+#define LXB_KD 256
+#define LXB_VD 128
+#define LXB_NK 16
+#define LXB_NV 128
+#define LXB_R 8
+#define LXB_CONV 24576
+#define LXB_NSLOT 1536  // an item's q | k | v: q 0..255, k 256..511, v 512 + r * 128 + j
+#define LXB_NOSLOT 0xffffu
+#define LXB_MAXC 16     // CTAs per cluster
+#define LXB_MINC 4
+#define LXB_ITEMSLOTS 4 // items one CTA may run in one layer
+#define LXB_MAXDENSE 32
+#define LXB_MAXUNITS 4096  // MLP units one CTA evaluates in one layer
+
+// item flags
+#define LXB_IT_DECAYS 1  // some value head's g may be nonzero
+#define LXB_IT_OUT 2     // the key head's value dims have out_proj entries
+
+enum {
+  LXB_SEC_LAYERS = 0,  // lxb_layer[n_layers]
+  LXB_SEC_ITEMS,       // lxb_item[n_items]
+  LXB_SEC_CHANS,       // lxb_chan[]
+  LXB_SEC_ENT,         // uint32 entries: low 16 bits an index, high 16 bits a bf16 weight
+  LXB_SEC_UNITS,       // lxb_unit[]
+  LXB_SEC_OWNERS,      // lxb_owner[n_layers * cluster]
+  LXB_SEC_I32,         // int32 pool: row pointers, row refs, item-of tables
+  LXB_SEC_U16,         // uint16 pool: bf16 parameters (norm weights, A_log, dt_bias, gated norm)
+  LXB_SEC_HEADCTA,     // lxb_headcta[cluster]
+  LXB_SEC_HCODES,      // uint64 per vocabulary row: the dense columns' 2-bit codes
+  LXB_SEC_COUNT
+};
+
+typedef struct {
+  int64_t off;    // bytes from the image start (16-aligned)
+  int64_t count;  // elements
+} lxb_sec;
+
+typedef struct {
+  uint32_t magic, version;
+  int32_t n_layers, cluster;
+  int32_t n_vocab, hidden;
+  int32_t n_items, n_dense;
+  int64_t n_embed_rows;  // rows the embedding must have
+  int32_t offset;        // chip token t embeds row offset + t
+  float eps;             // rms_norm_eps (every RMSNorm and the gated norm)
+  int32_t final_norm;    // u16 pool offset of the final norm weight [2560]
+  int32_t pad0;
+  float htab[4];         // the dense head columns' values, by code
+  int32_t dense_cols[LXB_MAXDENSE];
+  lxb_sec sec[LXB_SEC_COUNT];
+} lxb_image_header;
+
+typedef struct {
+  int32_t has_gdn, has_mlp;
+  int32_t ln_in, ln_post;  // u16 pool offsets of input_layernorm / post_attention_layernorm [2560]
+  int32_t item0, n_items;  // items [item0, item0 + n_items)
+  int32_t owner0;          // owners[owner0 + rank]
+  int32_t itemof;          // i32 pool offset: item index of key head kh (16 entries, -1 none)
+  int32_t decays;          // some item of the layer decays (its bitmaps are kept)
+  int32_t pad[3];
+} lxb_layer;  // 48 bytes
+
+typedef struct {
+  int32_t layer, kh, cta, slot;
+  int32_t ch0, n_ch;       // chans[ch0, ch0 + n_ch)
+  int32_t rows;            // i32 pool: (entry offset, count) pairs: 8 beta, 8 a, 1024 z rows
+  int32_t params;          // u16 pool: A_log[8], dt_bias[8], gated-norm weight[128]
+  int32_t flags;           // LXB_IT_*
+  int32_t pad[3];
+} lxb_item;  // 48 bytes
+
+typedef struct {
+  uint32_t ent;            // entries [ent, ent + n): column | bf16 << 16
+  uint16_t n, slot;        // entry count; place in q | k | v (LXB_NOSLOT: window only)
+  uint32_t conv_ch;        // the channel's index in the layer's conv state
+  uint32_t t01, t23;       // conv taps 0..3, bf16 pairs (low half first)
+  uint32_t pad[3];
+} lxb_chan;  // 32 bytes: two aligned 16-byte loads
+
+typedef struct {
+  uint32_t g, u;           // gate / up row entries
+  uint16_t ng, nu;
+  uint32_t pad;
+} lxb_unit;  // 16 bytes
+
+typedef struct {
+  int32_t unit0, n_units;  // units[unit0, unit0 + n_units): every unit with a down weight here
+  int32_t mrow;            // i32 pool: blk + 1 entry pointers of the owned rows' down_proj
+                           // entries (local unit index | bf16 << 16), or -1
+  int32_t orow;            // i32 pool: blk + 1 entry pointers of the owned rows' out_proj
+                           // entries (value dim | bf16 << 16), or -1
+} lxb_owner;  // 16 bytes
+
+typedef struct {
+  int32_t r0, r1;          // head rows [r0, r1)
+  int32_t rowptr;          // i32 pool: r1 - r0 + 1 entry pointers (the rows' sparse entries)
+  int32_t pad;
+} lxb_headcta;  // 16 bytes
+
+#ifdef __cplusplus
+static_assert(sizeof(lxb_image_header) == 360, "lxb_image_header layout");
+static_assert(sizeof(lxb_layer) == 48 && sizeof(lxb_item) == 48, "layer/item layout");
+static_assert(sizeof(lxb_chan) == 32 && sizeof(lxb_unit) == 16, "chan/unit layout");
+static_assert(sizeof(lxb_owner) == 16 && sizeof(lxb_headcta) == 16, "owner/headcta layout");
+#endif

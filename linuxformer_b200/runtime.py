@@ -1,0 +1,137 @@
+"""The device-side runtime: a chip's plan on the GPU, machine states in device memory, and the
+decode launch through the C ABI.
+
+    dec = Decoder(chip, cluster=16)               # tables built and uploaded once
+    st = dec.states([state0, state1])             # device copies of chip.State (HF cache layout)
+    preds, inputs = dec.run(st, forced=[[0], [7]], n=4096)   # [streams, n] int32, on the device
+
+PyTorch is used for device memory and streams only; all compute is in liblxb.so.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import chip as C
+from . import tables
+from ._lib import Caps, Err, LxbError, check, lib
+
+
+def _u16(t: np.ndarray, dev) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(t).view(np.int16)).to(dev)
+
+
+@dataclass
+class DeviceStates:
+    """n_streams machines: recurrent [S, L, 128, 256, 128] fp32, conv [S, L, 24576, 4] bf16 bits
+    (int16 storage), the per-(stream, layer) pointer table and the nonzero-row bitmaps."""
+    recurrent: torch.Tensor
+    conv: torch.Tensor
+    ptrs: torch.Tensor      # int64 [S, L, 2]
+    bitmaps: torch.Tensor   # int32 [S, L, 128, 8]
+
+    @property
+    def n_streams(self) -> int:
+        return self.recurrent.shape[0]
+
+    def host(self, s: int) -> C.State:
+        return C.State(self.recurrent[s].cpu().numpy().copy(),
+                       self.conv[s].cpu().numpy().view(np.uint16).copy())
+
+
+def state_pointers(rec_list, conv_list, dev) -> torch.Tensor:
+    """[S][L][2] device pointers from per-(stream, layer) tensors (lists of lists)."""
+    rows = [[(r.data_ptr(), c.data_ptr()) for r, c in zip(rs, cs)]
+            for rs, cs in zip(rec_list, conv_list)]
+    return torch.tensor(rows, dtype=torch.int64, device=dev)
+
+
+class Decoder:
+    def __init__(self, chip: C.Chip, cluster: int = 16, device=None, embed=None) -> None:
+        self.dev = torch.device(device or "cuda")
+        if self.dev.type != "cuda":
+            raise LxbError("the chip decode runs on a CUDA device only")
+        if self.dev.index is None:
+            self.dev = torch.device("cuda", torch.cuda.current_device())
+        torch.cuda.set_device(self.dev)
+        self.chip, self.cluster = chip, cluster
+        self.image, self.stats = tables.build_image(chip, cluster)
+        self._img = np.frombuffer(self.image, np.uint8)
+        p = ctypes.c_void_p()
+        check(lib().lxb_plan_create(self._img.ctypes.data, len(self.image), cluster,
+                                    ctypes.byref(p)), "lxb_plan_create")
+        self.plan = p
+        self.max_clusters = lib().lxb_plan_max_clusters(p)
+        self.embed = embed if embed is not None else _u16(chip.embed, self.dev)
+        assert self.embed.is_contiguous() and self.embed.shape[1] == C.H
+
+    def __del__(self):
+        p = getattr(self, "plan", None)
+        if p is not None and p.value:
+            lib().lxb_plan_destroy(p)
+            self.plan = None
+
+    def caps(self) -> Caps:
+        c = Caps()
+        check(lib().lxb_query(self.dev.index or 0, ctypes.byref(c)), "lxb_query")
+        c.max_clusters = self.max_clusters
+        return c
+
+    def states(self, init) -> DeviceStates:
+        """Device copies of chip.State objects (or an int: that many zero states)."""
+        nl = self.chip.n_layers
+        if isinstance(init, int):
+            S = init
+            rec = torch.zeros((S, nl, C.NV, C.KD, C.VD), dtype=torch.float32, device=self.dev)
+            conv = torch.zeros((S, nl, C.CONV, C.TAPS), dtype=torch.int16, device=self.dev)
+        else:
+            S = len(init)
+            rec = torch.empty((S, nl, C.NV, C.KD, C.VD), dtype=torch.float32, device=self.dev)
+            conv = torch.empty((S, nl, C.CONV, C.TAPS), dtype=torch.int16, device=self.dev)
+            for s, st in enumerate(init):
+                rec[s].copy_(torch.from_numpy(st.recurrent))
+                conv[s].copy_(torch.from_numpy(st.conv.view(np.int16)))
+        ptrs = state_pointers([[rec[s, L] for L in range(nl)] for s in range(S)],
+                              [[conv[s, L] for L in range(nl)] for s in range(S)], self.dev)
+        bm = torch.zeros((S, nl, C.NV, 8), dtype=torch.int32, device=self.dev)
+        return DeviceStates(rec, conv, ptrs, bm)
+
+    def launch(self, ptrs: torch.Tensor, bitmaps: torch.Tensor, forced: torch.Tensor, n: int,
+               preds: torch.Tensor, inputs: torch.Tensor | None, sync_bitmaps: bool = True,
+               stream=None) -> None:
+        """Raw launch on device tensors (no host sync): forced int32 [S, nf], preds [S, n]."""
+        S = forced.shape[0]
+        assert forced.dtype == torch.int32 and forced.is_contiguous() and forced.dim() == 2
+        assert preds.dtype == torch.int32 and preds.shape == (S, n) and preds.is_contiguous()
+        assert ptrs.shape == (S, self.chip.n_layers, 2) and bitmaps.shape[0] == S
+        st = (stream or torch.cuda.current_stream(self.dev)).cuda_stream
+        check(lib().lxb_decode(self.plan, ptrs.data_ptr(), bitmaps.data_ptr(), int(sync_bitmaps),
+                               self.embed.data_ptr(), S, forced.data_ptr(), forced.shape[1], n,
+                               preds.data_ptr(),
+                               inputs.data_ptr() if inputs is not None else None, st),
+              "lxb_decode")
+
+    def status(self) -> Err:
+        e = Err()
+        check(lib().lxb_status(self.plan, ctypes.byref(e)), "lxb_status")
+        return e
+
+    def run(self, states: DeviceStates, forced, n: int):
+        """n steps of every stream; forced: one list of ints per stream (equal lengths >= 1).
+        Returns (preds, inputs) as int32 device tensors [S, n]; raises on a device error."""
+        f = torch.as_tensor(np.asarray(forced, np.int32).reshape(states.n_streams, -1),
+                            device=self.dev)
+        preds = torch.empty((states.n_streams, n), dtype=torch.int32, device=self.dev)
+        inputs = torch.empty_like(preds)
+        self.launch(states.ptrs, states.bitmaps, f, n, preds, inputs)
+        torch.cuda.synchronize(self.dev)
+        e = self.status()
+        if e.status:
+            check(lib().lxb_status_clear(self.plan), "lxb_status_clear")
+            raise LxbError(f"device status {e.status:#x} (stream {e.first_stream}, "
+                           f"step {e.first_step})")
+        return preds, inputs

@@ -1,0 +1,277 @@
+"""Host-side table builder: a chip (linuxformer_b200.chip.Chip) -> one plan image for the C ABI
+(layout in csrc/lxb_plan.h; lxb_plan_create validates every offset and index in it).
+
+This is the B200 counterpart of the reference's Fast._gdn/_mlp/_dec (which find the nonzero rows
+and columns, lx/lx/fast.py:187-248, 432-469) and Mega.__init__ (which packs them into CSR/CSC
+tables, per-CTA blobs and a phase schedule, lx/lx/mega.py:199-504). What is kept:
+
+- live channels: rows of in_proj_qkv with any weight (their conv windows are state);
+- items: key heads with a live channel, or whose value heads can decay;
+- live MLP units: gate, up and down all nonzero (fast.py:240-245);
+- the head: the columns nonzero in every row (at most 32, at most 4 distinct values) as 2-bit
+  codes, the rest as sparse rows (mega.py:354-395).
+
+What differs: the layout is for a cluster of C CTAs per stream. Residual rows are owned in
+blocks of 2560 / C; each owner gets the down_proj and out_proj entries of its rows in CSR order
+(so every sum is taken by one thread, in column order) and the list of MLP units those rows
+need. Items are spread over the CTAs, at most LXB_ITEMSLOTS per CTA per layer.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import chip as C
+
+MAGIC = 0x50425A4C
+VERSION = 2
+NSLOT, NOSLOT = 1536, 0xFFFF
+ITEMSLOTS, MAXDENSE, MAXUNITS = 4, 32, 4096
+IT_DECAYS, IT_OUT = 1, 2
+SEC = ("layers", "items", "chans", "ent", "units", "owners", "i32", "u16", "headcta", "hcodes")
+
+LAYER = np.dtype([(n, "<i4") for n in ("has_gdn", "has_mlp", "ln_in", "ln_post", "item0",
+                                       "n_items", "owner0", "itemof", "decays", "p0", "p1",
+                                       "p2")])
+ITEM = np.dtype([(n, "<i4") for n in ("layer", "kh", "cta", "slot", "ch0", "n_ch", "rows",
+                                      "params", "flags", "p0", "p1", "p2")])
+CHAN = np.dtype([("ent", "<u4"), ("n", "<u2"), ("slot", "<u2"), ("conv_ch", "<u4"),
+                 ("t01", "<u4"), ("t23", "<u4"), ("p0", "<u4"), ("p1", "<u4"), ("p2", "<u4")])
+UNIT = np.dtype([("g", "<u4"), ("u", "<u4"), ("ng", "<u2"), ("nu", "<u2"), ("pad", "<u4")])
+OWNER = np.dtype([("unit0", "<i4"), ("n_units", "<i4"), ("mrow", "<i4"), ("orow", "<i4")])
+HEADCTA = np.dtype([("r0", "<i4"), ("r1", "<i4"), ("rowptr", "<i4"), ("pad", "<i4")])
+HEADER = np.dtype([("magic", "<u4"), ("version", "<u4"), ("n_layers", "<i4"), ("cluster", "<i4"),
+                   ("n_vocab", "<i4"), ("hidden", "<i4"), ("n_items", "<i4"), ("n_dense", "<i4"),
+                   ("n_embed_rows", "<i8"), ("offset", "<i4"), ("eps", "<f4"),
+                   ("final_norm", "<i4"), ("pad0", "<i4"), ("htab", "<f4", (4,)),
+                   ("dense_cols", "<i4", (MAXDENSE,)), ("sec", "<i8", (len(SEC), 2))])
+assert LAYER.itemsize == 48 and ITEM.itemsize == 48 and CHAN.itemsize == 32
+assert UNIT.itemsize == 16 and OWNER.itemsize == 16 and HEADCTA.itemsize == 16
+assert HEADER.itemsize == 360
+
+
+class _Pool:
+    """A growing flat array (entries, int32, uint16)."""
+
+    def __init__(self, dtype):
+        self.dtype, self.parts, self.n = dtype, [], 0
+
+    def add(self, a) -> int:
+        a = np.ascontiguousarray(a, self.dtype).reshape(-1)
+        off = self.n
+        if a.size:
+            self.parts.append(a)
+            self.n += a.size
+        return off
+
+    def array(self) -> np.ndarray:
+        return np.concatenate(self.parts) if self.parts else np.zeros(0, self.dtype)
+
+
+def _pack(idx, bits) -> np.ndarray:
+    """(index < 2^16, bf16 bits) -> uint32 entries."""
+    idx = np.asarray(idx, np.int64)
+    assert idx.size == 0 or (idx.min() >= 0 and idx.max() < 1 << 16)
+    return (idx.astype(np.uint32) | (np.asarray(bits, np.uint32) << 16)).astype(np.uint32)
+
+
+def _f32(bits) -> np.ndarray:
+    return C.bf16_float(bits)
+
+
+def _may_decay(layer: C.Layer, vh: np.ndarray) -> np.ndarray:
+    """Whether g = -exp(A_log) * softplus(a + dt_bias) can ever be nonzero, per value head:
+    with an empty in_proj_a row a is always 0, and exp(x) is 0 in fp32 below -103.97, so
+    softplus(dt_bias) (and -exp(A_log)) is then exactly zero."""
+    a_nnz = layer.a.row_nnz()[vh]
+    return ((a_nnz > 0) | (_f32(layer.dt_bias[vh]) >= -103.98)) & \
+        (_f32(layer.A_log[vh]) >= -103.98)
+
+
+def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
+    """The plan image for `chip` on clusters of `cluster` CTAs, and build statistics."""
+    Cn = cluster
+    assert Cn in (4, 8, 16) and C.H % Cn == 0
+    blk = C.H // Cn
+    ent, i32, u16 = _Pool(np.uint32), _Pool(np.int32), _Pool(np.uint16)
+    layers = np.zeros(chip.n_layers, LAYER)
+    items, chans, units, owners = [], [], [], []
+    stats = {"cluster": Cn, "items": 0, "chans": 0, "csr_nnz": 0, "units": 0, "unit_evals": 0,
+             "down_nnz": 0, "out_nnz": 0}
+    for L, ly in enumerate(chip.layers):
+        rec = layers[L]
+        rec["ln_in"] = u16.add(ly.ln_in)
+        rec["ln_post"] = u16.add(ly.ln_post)
+        rec["owner0"] = L * Cn
+        # --- GDN items ---------------------------------------------------------------------
+        qkv = ly.qkv
+        cnt = qkv.row_nnz()
+        live = np.nonzero(cnt > 0)[0]
+        if len(live):
+            assert cnt.max() < 1 << 16
+        kh_of = np.where(live < C.NK * C.KD, live // C.KD,
+                         np.where(live < 2 * C.NK * C.KD, (live - C.NK * C.KD) // C.KD,
+                                  (live - 2 * C.NK * C.KD) // C.VD // C.R))
+        slot_of = np.where(live < C.NK * C.KD, live % C.KD,
+                           np.where(live < 2 * C.NK * C.KD, C.KD + (live - C.NK * C.KD) % C.KD,
+                                    2 * C.KD + (live - 2 * C.NK * C.KD) % (C.R * C.VD)))
+        decays_vh = _may_decay(ly, np.arange(C.NV))
+        heads = sorted(set(kh_of.tolist()) |
+                       set(np.nonzero(decays_vh.reshape(C.NK, C.R).any(1))[0].tolist()))
+        assert len(heads) <= ITEMSLOTS * Cn, "more key heads in a layer than the cluster holds"
+        rec["item0"] = len(items)
+        rec["n_items"] = len(heads)
+        itemof = np.full(C.NK, -1, np.int32)
+        out_cols = ly.out.transpose()  # CSC by value dim
+        out_has = out_cols.row_nnz().reshape(C.NK, C.R * C.VD).any(1)
+        # the row entries of the whole in_proj_qkv, packed once
+        qkv_ent0 = ent.add(_pack(qkv.indices, qkv.data))
+        stats["csr_nnz"] += qkv.nnz
+        rot = (3 * L) % Cn
+        for k, kh in enumerate(heads):
+            pos = k + rot
+            sel = np.nonzero(kh_of == kh)[0]
+            chs = live[sel]
+            ch = np.zeros(len(chs), CHAN)
+            ch["ent"] = qkv_ent0 + qkv.indptr[chs]
+            ch["n"] = cnt[chs]
+            ch["slot"] = slot_of[sel]
+            ch["conv_ch"] = chs
+            taps = ly.conv[chs].astype(np.uint32)
+            ch["t01"] = taps[:, 0] | (taps[:, 1] << 16)
+            ch["t23"] = taps[:, 2] | (taps[:, 3] << 16)
+            assert len(chs) <= 2 * NSLOT
+            ch0 = sum(len(c) for c in chans)
+            chans.append(ch)
+            vh = kh * C.R + np.arange(C.R)
+            refs = np.zeros((2 * C.R + C.R * C.VD, 2), np.int32)
+            zrows = (vh[:, None] * C.VD + np.arange(C.VD)).reshape(-1)
+            for q0, m, rr in ((0, ly.b, vh), (C.R, ly.a, vh), (2 * C.R, ly.z, zrows)):
+                sub = m.rows_subset(rr)
+                n = sub.row_nnz()
+                base = ent.add(_pack(sub.indices, sub.data))
+                refs[q0:q0 + len(rr), 0] = np.where(n > 0, base + sub.indptr[:-1], 0)
+                refs[q0:q0 + len(rr), 1] = n
+            it = np.zeros(1, ITEM)[0]
+            it["layer"], it["kh"], it["cta"], it["slot"] = L, kh, pos % Cn, pos // Cn
+            it["ch0"], it["n_ch"] = ch0, len(chs)
+            it["rows"] = i32.add(refs)
+            it["params"] = u16.add(np.concatenate([ly.A_log[vh], ly.dt_bias[vh], ly.gnorm]))
+            it["flags"] = (IT_DECAYS if decays_vh[vh].any() else 0) | \
+                (IT_OUT if out_has[kh] else 0)
+            itemof[kh] = len(items)
+            items.append(it)
+            stats["chans"] += len(chs)
+        stats["items"] += len(heads)
+        rec["itemof"] = i32.add(itemof)
+        rec["has_gdn"] = int(len(heads) > 0)
+        rec["decays"] = int(any(items[i]["flags"] & IT_DECAYS for i in
+                                range(rec["item0"], rec["item0"] + len(heads))))
+        # --- owners: MLP units and the rows' down_proj / out_proj entries --------------------
+        g_cnt, u_cnt = ly.gate.row_nnz(), ly.up.row_nnz()
+        d_cols = ly.down.transpose()
+        unit_live = (g_cnt > 0) & (u_cnt > 0) & (d_cols.row_nnz() > 0)
+        assert g_cnt.max(initial=0) < 1 << 16 and u_cnt.max(initial=0) < 1 << 16
+        rec["has_mlp"] = int(unit_live.any())
+        stats["units"] += int(unit_live.sum())
+        g_ent = ent.add(_pack(ly.gate.indices, ly.gate.data))
+        u_ent = ent.add(_pack(ly.up.indices, ly.up.data))
+        item_heads = np.zeros(C.NK, bool)
+        item_heads[heads] = True
+        for c in range(Cn):
+            ow = np.zeros(1, OWNER)[0]
+            ow["unit0"], ow["mrow"], ow["orow"] = sum(len(u) for u in units), -1, -1
+            rows = np.arange(c * blk, (c + 1) * blk)
+            if rec["has_mlp"]:
+                sub = ly.down.rows_subset(rows)
+                keep = unit_live[sub.indices]
+                rowid = np.repeat(np.arange(blk), sub.row_nnz())[keep]
+                uidx, w = sub.indices[keep], sub.data[keep]
+                need = np.unique(uidx)
+                assert len(need) <= MAXUNITS, "too many MLP units for one CTA: use a larger cluster"
+                loc = np.searchsorted(need, uidx)
+                un = np.zeros(len(need), UNIT)
+                un["g"] = g_ent + ly.gate.indptr[need]
+                un["u"] = u_ent + ly.up.indptr[need]
+                un["ng"], un["nu"] = g_cnt[need], u_cnt[need]
+                ow["unit0"] = sum(len(u) for u in units)
+                ow["n_units"] = len(need)
+                units.append(un)
+                ptr = np.zeros(blk + 1, np.int64)
+                np.cumsum(np.bincount(rowid, minlength=blk), out=ptr[1:])
+                base = ent.add(_pack(loc, w))
+                ow["mrow"] = i32.add((ptr + base).astype(np.int32))
+                stats["unit_evals"] += len(need)
+                stats["down_nnz"] += int(keep.sum())
+            if rec["has_gdn"] and out_has[item_heads].any():
+                sub = ly.out.rows_subset(rows)
+                keep = item_heads[sub.indices // (C.R * C.VD)]
+                rowid = np.repeat(np.arange(blk), sub.row_nnz())[keep]
+                ptr = np.zeros(blk + 1, np.int64)
+                np.cumsum(np.bincount(rowid, minlength=blk), out=ptr[1:])
+                base = ent.add(_pack(sub.indices[keep], sub.data[keep]))
+                ow["orow"] = i32.add((ptr + base).astype(np.int32))
+                stats["out_nnz"] += int(keep.sum())
+            owners.append(ow)
+    # --- the head ----------------------------------------------------------------------------
+    hd = chip.head
+    V = hd.shape[0]
+    col_cnt = np.bincount(hd.indices, minlength=C.H)
+    dense = np.nonzero(col_cnt == V)[0] if V else np.zeros(0, np.int64)
+    htab = np.zeros(4, np.float32)
+    dense_ok = 0 < len(dense) <= MAXDENSE
+    if dense_ok:
+        isd = np.isin(hd.indices, dense)
+        vals = np.unique(_f32(hd.data[isd]))
+        dense_ok = len(vals) <= 4
+    if not dense_ok:
+        dense = dense[:0]
+    rows_of = np.repeat(np.arange(V), hd.row_nnz())
+    hcodes = np.zeros(V if len(dense) else 0, np.uint64)
+    if len(dense):
+        htab[:len(vals)] = vals
+        isd = np.isin(hd.indices, dense)
+        code = np.searchsorted(vals, _f32(hd.data[isd])).astype(np.uint64)
+        j = np.searchsorted(dense, hd.indices[isd]).astype(np.uint64)
+        np.bitwise_or.at(hcodes, rows_of[isd], code << (np.uint64(2) * j))
+        sp = ~isd
+    else:
+        sp = np.ones(hd.nnz, bool)
+    sp_rows, sp_cols, sp_bits = rows_of[sp], hd.indices[sp], hd.data[sp]
+    sp_ptr = np.zeros(V + 1, np.int64)
+    np.cumsum(np.bincount(sp_rows, minlength=V), out=sp_ptr[1:])
+    sp_base = ent.add(_pack(sp_cols, sp_bits))
+    headcta = np.zeros(Cn, HEADCTA)
+    for c in range(Cn):
+        r0, r1 = V * c // Cn, V * (c + 1) // Cn
+        headcta[c]["r0"], headcta[c]["r1"] = r0, r1
+        headcta[c]["rowptr"] = i32.add((sp_ptr[r0:r1 + 1] + sp_base).astype(np.int32))
+    final_norm = u16.add(chip.final_norm)
+    assert ent.n < 1 << 31 and i32.n < 1 << 31 and u16.n < 1 << 31
+    stats.update(head_dense=len(dense), head_sparse_nnz=int(sp.sum()), ent=ent.n)
+    # --- the image ---------------------------------------------------------------------------
+    secs = [layers, np.array(items, ITEM) if items else np.zeros(0, ITEM),
+            np.concatenate(chans) if chans else np.zeros(0, CHAN), ent.array(),
+            np.concatenate(units) if units else np.zeros(0, UNIT),
+            np.array(owners, OWNER), i32.array(), u16.array(), headcta, hcodes]
+    hdr = np.zeros(1, HEADER)[0]
+    hdr["magic"], hdr["version"] = MAGIC, VERSION
+    hdr["n_layers"], hdr["cluster"], hdr["n_vocab"], hdr["hidden"] = chip.n_layers, Cn, V, C.H
+    hdr["n_items"], hdr["n_dense"] = len(items), len(dense)
+    hdr["n_embed_rows"], hdr["offset"], hdr["eps"] = chip.embed.shape[0], chip.offset, chip.eps
+    hdr["final_norm"] = final_norm
+    hdr["htab"] = htab
+    hdr["dense_cols"][:len(dense)] = dense
+    blobs, pos = [], HEADER.itemsize
+    for k, a in enumerate(secs):
+        pos = -(-pos // 16) * 16
+        b = np.ascontiguousarray(a).tobytes()
+        hdr["sec"][k] = (pos, len(a))
+        blobs.append((pos, b))
+        pos += len(b)
+    image = bytearray(-(-pos // 16) * 16)
+    image[:HEADER.itemsize] = np.array([hdr], HEADER).tobytes()
+    for p, b in blobs:
+        image[p:p + len(b)] = b
+    stats["image_bytes"] = len(image)
+    return bytes(image), stats

@@ -1,0 +1,83 @@
+"""The CUDA decode (liblxb.so through its C ABI) against the CPU oracle and the reference's own
+stock stream. Bit-exact: token streams, conv windows and recurrent states (values compared as
+floats, so -0 and +0 agree: the stock forward itself differs from the sparse path only in a
+zero's sign, lx/csrc/mega.cu:276)."""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from linuxformer_b200 import chip as C  # noqa: E402
+from oracle.oracle import Oracle  # noqa: E402
+
+GOLD = __import__("pathlib").Path(__file__).parent / "golden"
+
+
+def _decoder(chip, cluster):
+    from linuxformer_b200.runtime import Decoder
+
+    return Decoder(chip, cluster=cluster)
+
+
+def _same_state(dev_states, s, host_state):
+    got = dev_states.host(s)
+    assert np.array_equal(got.conv, host_state.conv), "conv windows differ"
+    diff = got.recurrent != host_state.recurrent
+    assert not diff.any(), f"{int(diff.sum())} recurrent values differ"
+
+
+@pytest.mark.parametrize("cluster", [16, 8])
+def test_c1_matches_oracle(c1_chip, cluster):
+    n = 40
+    dec = _decoder(c1_chip, cluster)
+    st0 = C.c1_state(c1_chip, 0)
+    ds = dec.states([st0])
+    preds, inputs = dec.run(ds, [[0]], n)
+    host = st0.copy()
+    p, i, _ = Oracle(c1_chip).decode(host, [0], n)
+    assert (preds[0].cpu().numpy() == p).all()
+    assert (inputs[0].cpu().numpy() == i).all()
+    _same_state(ds, 0, host)
+
+
+def test_c1_stock_stream_512(c1_chip):
+    """512 greedy tokens equal the reference's stock forward (tests/golden/c1_decode.npz)."""
+    g = np.load(GOLD / "c1_decode.npz")
+    dec = _decoder(c1_chip, 16)
+    ds = dec.states([C.c1_state(c1_chip, 0)])
+    preds, inputs = dec.run(ds, [[0]], 512)
+    assert (preds[0].cpu().numpy() == g["preds"]).all()
+    got = ds.host(0)
+    assert np.array_equal(got.conv, g["conv"])
+    assert np.abs(got.recurrent[:, [5, 77]] - g["rec_heads"]).max() <= 1e-9
+
+
+def test_streams_are_independent(c1_chip):
+    """Three machines with their own states and forced prefixes, one launch: each equals its
+    own oracle run."""
+    n = 24
+    dec = _decoder(c1_chip, 16)
+    sts = [C.c1_state(c1_chip, s) for s in (0, 3, 4)]
+    forced = [[0, 5, 9], [17, 17, 3], [4095, 1, 2]]
+    ds = dec.states(sts)
+    preds, _ = dec.run(ds, forced, n)
+    o = Oracle(c1_chip)
+    for s in range(3):
+        host = sts[s].copy()
+        p, _, _ = o.decode(host, forced[s], n)
+        assert (preds[s].cpu().numpy() == p).all()
+        _same_state(ds, s, host)
+
+
+def test_bad_token_sets_status(c1_chip):
+    """A forced token outside the embedding is clamped and reported, not read out of bounds."""
+    from linuxformer_b200._lib import LxbError
+
+    dec = _decoder(c1_chip, 16)
+    ds = dec.states([C.c1_state(c1_chip, 0)])
+    with pytest.raises(LxbError, match="device status"):
+        dec.run(ds, [[0, 5000]], 4)
+    preds, _ = dec.run(ds, [[0]], 2)  # the plan stays usable
+    assert preds.shape == (1, 2)
