@@ -285,3 +285,195 @@ def to_hf(chip: Chip):
     missing, unexpected = model.load_state_dict(sd, strict=False, assign=True)
     assert not unexpected and not missing, (missing[:5], unexpected[:5])
     return model.eval()
+
+
+# --- config 2: the full 37-layer chip-shaped stack ------------------------------------------
+C2_LAYERS = 37
+C2_LOGIC = 15            # layers 0..14 carry the SwiGLU units; 15..36 are GDN-only (memory)
+C2_HEADS = 497           # live key heads
+C2_UNITS = 36716         # live SwiGLU units
+C2_VOCAB = 459982
+C2_RAM, C2_ROM = 4718592, 1009088
+N_BALLAST, N_SEL = 8, 1024
+SEL0 = N_BALLAST                      # select columns [8, 1032)
+DATA0 = SEL0 + N_SEL                  # data columns [1032, 2560)
+N_CODE = 31                           # the head's dense code columns: the last 31 data columns
+
+
+def _pow2_values(rng, n):
+    """values uniform in {-1, -0.5, 0.5, 1} x 2^k, k in [-4, 4] (all exact in bf16)."""
+    m = rng.choice(np.array([-1.0, -0.5, 0.5, 1.0], np.float32), n)
+    return (m * np.exp2(rng.integers(-4, 5, n)).astype(np.float32)).astype(np.float32)
+
+
+def c2(seed: int = 1, vocab: int = C2_VOCAB, n_layers: int = C2_LAYERS) -> Chip:
+    """Config 2: a 37-layer chip-shaped stack with the real circuit's sizes and a per-token
+    activity shaped like the measured one (lx/results/summary.md:81: of the live value heads
+    ~375 get a nonzero query or key, ~4.5 change state, ~21 produce output).
+
+    Residual columns: 8 ballast columns (a constant 2.0 in every embedding row, never written,
+    so every RMSNorm sees a stable scale), 1024 select columns (set by the embedding only), 1528
+    data columns (embedding features, written by out_proj and down_proj). Every live key head
+    reads its queries from one select column and its keys from another (one in_proj entry per
+    channel, one conv tap on the newest input), so whether a head is active is decided by which
+    select columns the current token sets: memory heads' queries fire for ~1.7% of tokens, the
+    other heads' for ~13%, keys for ~0.65%. Value channels read 15 data columns each (every
+    token, as in the real circuit, since their conv windows are state); only memory heads
+    have in_proj_z rows. Query and key rows of
+    the non-memory heads are disjoint, so only memory heads (whose states hold the RAM and ROM
+    bytes, see c2_state) produce output. Layers 0..14 carry the 36,716 SwiGLU units (8 gate and
+    8 up entries, one down weight each); layers 15..36 are GDN only, as the real circuit's
+    last 22 layers. Two logic layers decay (dt_bias 1, in_proj_a entries); the rest have
+    dt_bias -110 and empty in_proj_a rows, so their g is exactly 0. The head: 31 dense code
+    columns with 2-bit codes over {-1/8, -1/16, 1/16, 1/8}. All weights are in
+    {+-1, +-0.5} x 2^k, k in [-4, 4], drawn from `seed`."""
+    rng = np.random.default_rng(seed)
+    data_cols = np.arange(DATA0, H)
+    heads_per_layer = np.full(n_layers, C2_HEADS // n_layers)
+    heads_per_layer[:C2_HEADS - heads_per_layer.sum()] += 1
+    n_logic = min(C2_LOGIC, n_layers)
+    units_per_layer = np.zeros(n_layers, np.int64)
+    units_per_layer[:n_logic] = C2_UNITS // n_logic
+    units_per_layer[:C2_UNITS - units_per_layer.sum()] += 1
+    decay_layers = {4, 9} & set(range(n_logic))
+    sel_free = list(rng.permutation(N_SEL) + SEL0)
+    meta = {"config": 2, "seed": seed, "memory_heads": [], "q_sel": {}, "k_sel": {}}
+    layers = []
+    mem_budget = -(-(C2_RAM // 15) // KD) + -(-(C2_ROM // 64) // KD)  # value heads of RAM+ROM
+    mem_vh_left = mem_budget
+    for L in range(n_layers):
+        nkh = int(heads_per_layer[L])
+        khs = np.sort(rng.choice(NK, nkh, replace=False))
+        rows, cols, vals = [], [], []
+        taps = np.zeros((CONV, TAPS), np.uint16)
+        b_r, b_c, a_r, a_c, z_r, z_c, o_r, o_c = [], [], [], [], [], [], [], []
+        decays = L in decay_layers
+        for kh in khs:
+            memory = L >= n_logic and mem_vh_left > 0
+            if memory:
+                mem_vh_left -= R
+                meta["memory_heads"].append((L, int(kh)))
+            qs, ks = sel_free.pop(), sel_free.pop()
+            meta["q_sel"][(L, int(kh))] = qs
+            meta["k_sel"][(L, int(kh))] = ks
+            qrows = rng.choice(KD, 8, replace=False)
+            krows = qrows if memory else rng.choice(np.setdiff1d(np.arange(KD), qrows), 8,
+                                                    replace=False)
+            for base, rr, sc in ((kh * KD, qrows, qs), (NK * KD + kh * KD, krows, ks)):
+                ch = base + rr
+                rows.append(ch)
+                cols.append(np.full(len(ch), sc))
+                vals.append(_pow2_values(rng, len(ch)))
+                taps[ch, 3] = bf16_bits(_pow2_values(rng, len(ch)))
+            vch = 2 * NK * KD + kh * R * VD + rng.choice(R * VD, 700, replace=False)
+            rows.append(np.repeat(vch, 15))
+            cols.append(rng.integers(DATA0, H, len(vch) * 15))
+            vals.append(_pow2_values(rng, len(vch) * 15))
+            single = rng.random(len(vch)) < 0.8
+            taps[vch[single], 3] = bf16_bits(_pow2_values(rng, int(single.sum())))
+            multi = vch[~single]
+            taps[multi] = bf16_bits(_pow2_values(rng, len(multi) * TAPS)).reshape(-1, TAPS)
+            vh = kh * R + np.arange(R)
+            for v in vh:
+                b_r.append(np.full(4, v))
+                b_c.append(rng.choice(data_cols, 4, replace=False))
+                if decays:
+                    a_r.append(np.full(2, v))
+                    a_c.append(rng.choice(data_cols, 2, replace=False))
+            dims = (vh[:, None] * VD + np.arange(VD)).reshape(-1)
+            if memory:  # only memory heads can produce output
+                z_r.append(dims)
+                z_c.append(rng.choice(data_cols, len(dims)))
+                od = rng.choice(dims, 330, replace=False)
+                o_r.append(rng.choice(data_cols, len(od)))
+                o_c.append(od)
+        cat = lambda x: np.concatenate(x) if x else np.zeros(0, np.int64)  # noqa: E731
+        qkv = Sparse.from_coo((CONV, H), cat(rows), cat(cols), bf16_bits(cat(vals)))
+        mk = lambda r, c, shape: Sparse.from_coo(shape, cat(r), cat(c), bf16_bits(  # noqa: E731
+            _pow2_values(rng, len(cat(r)))))
+        nu = int(units_per_layer[L])
+        if nu:
+            u = np.sort(rng.choice(INTER, nu, replace=False))
+            gr, gc = np.repeat(u, 8), rng.choice(data_cols, nu * 8)
+            gate = Sparse.from_coo((INTER, H), gr, gc, bf16_bits(_pow2_values(rng, nu * 8)))
+            up = Sparse.from_coo((INTER, H), gr, rng.choice(data_cols, nu * 8),
+                                 bf16_bits(_pow2_values(rng, nu * 8)))
+            down = Sparse.from_coo((H, INTER), rng.choice(data_cols, nu), u,
+                                   bf16_bits(_pow2_values(rng, nu)))
+        else:
+            gate = up = Sparse.from_coo((INTER, H), [], [], [])
+            down = Sparse.from_coo((H, INTER), [], [], [])
+        layers.append(Layer(
+            qkv=qkv, conv=taps,
+            z=mk(z_r, z_c, (ZD, H)),
+            b=mk(b_r, b_c, (NV, H)),
+            a=mk(a_r, a_c, (NV, H)),
+            out=mk(o_r, o_c, (H, ZD)),
+            A_log=np.zeros(NV, np.uint16),  # A = -exp(0) = -1
+            dt_bias=bf16_bits(np.where(np.isin(np.arange(NV) // R, khs) & decays, 1.0,
+                                       -110.0).astype(np.float32)),
+            gnorm=bf16_bits(np.ones(VD, np.float32)),
+            ln_in=np.zeros(H, np.uint16), ln_post=np.zeros(H, np.uint16),
+            gate=gate, up=up, down=down))
+    # the embedding: ballast, select columns by head kind, ~48 data features
+    emb = np.zeros((vocab, H), np.uint16)
+    emb[:, :N_BALLAST] = bf16_bits(np.float32(2.0))
+    mem = set(meta["memory_heads"])
+    for (L, kh), qs in meta["q_sel"].items():
+        p = 0.017 if (L, kh) in mem else 0.13
+        on = np.nonzero(rng.random(vocab) < p)[0]
+        emb[on, qs] = bf16_bits(_pow2_values(rng, len(on)))
+    for (L, kh), ks in meta["k_sel"].items():
+        on = np.nonzero(rng.random(vocab) < 0.0065)[0]
+        emb[on, ks] = bf16_bits(_pow2_values(rng, len(on)))
+    nf = 48
+    fr = np.repeat(np.arange(vocab), nf)
+    fc = rng.integers(DATA0, H - N_CODE, vocab * nf)
+    emb[fr, fc] = bf16_bits(rng.choice(np.array([-1.0, 1.0], np.float32), vocab * nf))
+    # every token carries a +-1 pattern in the code columns (the head reads them back)
+    emb[:, H - N_CODE:] = bf16_bits(rng.choice(np.array([-1.0, 1.0], np.float32),
+                                               (vocab, N_CODE)))
+    # the head: 31 dense code columns, 2-bit codes
+    code_cols = np.arange(H - N_CODE, H)
+    hv = np.array([-0.125, -0.0625, 0.0625, 0.125], np.float32)
+    codes = rng.integers(0, 4, (vocab, N_CODE))
+    head = Sparse((vocab, H), np.arange(vocab + 1, dtype=np.int64) * N_CODE,
+                  np.tile(code_cols.astype(np.int32), vocab), bf16_bits(hv[codes]).reshape(-1))
+    meta["memory_value_heads"] = (mem_budget - mem_vh_left)
+    meta["q_sel"] = {f"{k[0]}.{k[1]}": int(v) for k, v in meta["q_sel"].items()}
+    meta["k_sel"] = {f"{k[0]}.{k[1]}": int(v) for k, v in meta["k_sel"].items()}
+    return Chip(name=f"c2(seed={seed},layers={n_layers},vocab={vocab})", layers=layers,
+                embed=emb, head=head, final_norm=np.zeros(H, np.uint16), eps=1e-6, meta=meta)
+
+
+def c2_state(chip: Chip, seed: int = 1) -> State:
+    """Config 2's initial state: 5.5 MB of uniform random bytes in the memory heads' rows.
+    RAM (4,718,592 bytes): 15 bytes per state row as 120 bit columns (0 or 128) in columns
+    2..121, with ballast 2^24 in columns 0 and 1; ROM (1,009,088 bytes): 64 bytes per row as 128
+    nibble columns (integers 0..15). Filled in order over the memory heads' value heads."""
+    rng = np.random.default_rng(seed + 7_000_003)
+    L_n = chip.n_layers
+    rec = np.zeros((L_n, NV, KD, VD), np.float32)
+    ram = rng.integers(0, 256, C2_RAM, dtype=np.uint8)
+    rom = rng.integers(0, 256, C2_ROM, dtype=np.uint8)
+    ram_rows = -(-C2_RAM // 15)
+    rbuf = np.zeros(ram_rows * 15, np.uint8)
+    rbuf[:C2_RAM] = ram
+    bits = np.unpackbits(rbuf.reshape(ram_rows, 15), axis=1)            # [rows, 120]
+    ram_f = np.zeros((ram_rows, VD), np.float32)
+    ram_f[:, 0:2] = 2.0 ** 24
+    ram_f[:, 2:122] = bits * 128.0
+    rom_rows = -(-C2_ROM // 64)
+    obuf = np.zeros(rom_rows * 64, np.uint8)
+    obuf[:C2_ROM] = rom
+    nib = np.stack([obuf >> 4, obuf & 15], 1).reshape(rom_rows, VD).astype(np.float32)
+    all_rows = np.concatenate([ram_f, nib])
+    vhs = [(L, kh * R + r) for (L, kh) in chip.meta["memory_heads"] for r in range(R)]
+    k = 0
+    for L, vh in vhs:
+        if k >= len(all_rows):
+            break
+        n = min(KD, len(all_rows) - k)
+        rec[L, vh, :n] = all_rows[k:k + n]
+        k += n
+    return State(rec, np.zeros((L_n, CONV, TAPS), np.uint16))

@@ -120,6 +120,36 @@ class Decoder:
         check(lib().lxb_status(self.plan, ctypes.byref(e)), "lxb_status")
         return e
 
+    def _pinned(self, key, shape) -> torch.Tensor:
+        buf = getattr(self, "_pin", {})
+        self._pin = buf
+        t = buf.get(key)
+        if t is None or t.numel() < int(np.prod(shape)):
+            t = torch.empty(int(np.prod(shape)), dtype=torch.int32).pin_memory()
+            buf[key] = t
+        return t[:int(np.prod(shape))].view(shape)
+
+    def run_host(self, states: DeviceStates, forced: np.ndarray, n: int,
+                 sync_bitmaps: bool = True) -> np.ndarray:
+        """The host-buffer call: forced tokens from host memory in, predictions [S, n] back in
+        host memory (copies through pinned buffers on the current stream)."""
+        forced = np.ascontiguousarray(forced, np.int32).reshape(states.n_streams, -1)
+        S = states.n_streams
+        fh = self._pinned("f", forced.shape)
+        fh.numpy()[...] = forced
+        fd = fh.to(self.dev, non_blocking=True)
+        preds = torch.empty((S, n), dtype=torch.int32, device=self.dev)
+        self.launch(states.ptrs, states.bitmaps, fd, n, preds, None, sync_bitmaps)
+        ph = self._pinned("p", (S, n))
+        ph.copy_(preds, non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        e = self.status()
+        if e.status:
+            check(lib().lxb_status_clear(self.plan), "lxb_status_clear")
+            raise LxbError(f"device status {e.status:#x} (stream {e.first_stream}, "
+                           f"step {e.first_step})")
+        return ph.numpy().copy()
+
     def run(self, states: DeviceStates, forced, n: int):
         """n steps of every stream; forced: one list of ints per stream (equal lengths >= 1).
         Returns (preds, inputs) as int32 device tensors [S, n]; raises on a device error."""

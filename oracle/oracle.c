@@ -147,7 +147,27 @@ typedef struct {
   float on[ZD];
   int dense_cols[32];
   int n_dense;
+  int64_t* cnt;  // this step's counters (LXO_C_*), or NULL
 } lxo_run;
+
+// per-step activity counters: what the step logically reads and writes (the bench's algorithmic
+// bytes per token are computed from them)
+enum {
+  LXO_C_CHANS,     // live conv channels (window read + write: 16 bytes each)
+  LXO_C_QKV_ENT,   // in_proj_qkv entries of the live channels
+  LXO_C_BA_ENT,    // in_proj_b / in_proj_a entries of the value heads evaluated
+  LXO_C_Z_ENT,     // in_proj_z entries of the value heads with output
+  LXO_C_ROWS,      // recurrent-state rows touched (decayed or keyed or queried; 512 B each)
+  LXO_C_OUT_ENT,   // out_proj entries with a nonzero input
+  LXO_C_GU_ENT,    // gate / up entries of the live units
+  LXO_C_DOWN_ENT,  // down_proj entries with a nonzero input
+  LXO_C_HEAD_B,    // head bytes (8 per row of dense codes, 4 per sparse entry)
+  LXO_C_VH_ACTIVE, // value heads with a nonzero query or key
+  LXO_C_VH_WRITE,  // value heads whose state took a key update
+  LXO_C_VH_OUT,    // value heads with output
+  LXO_C_GDN_WRITE, // layers whose GDN changed the residual
+  LXO_C_N
+};
 
 // one GDN layer on the residual x (in place)
 static void gdn_layer(lxo_run* st, int L) {
@@ -159,6 +179,8 @@ static void gdn_layer(lxo_run* st, int L) {
   // in_proj_qkv, then torch_causal_conv1d_update: window [w0 w1 w2 w3] -> [w1 w2 w3 P],
   // out = silu(conv over the new window) in bf16
   uint16_t* cw = st->conv + (size_t)L * CONV * 4;
+  int64_t n_ch = 0, n_ent = 0;
+#pragma omp parallel for schedule(static) reduction(+ : n_ch, n_ent)
   for (int ch = 0; ch < CONV; ch++) {
     const bool live = ly->qkv.indptr[ch + 1] > ly->qkv.indptr[ch];
     if (!live) {  // a zero row: P = 0 every step; its window only ever holds what it held
@@ -168,6 +190,8 @@ static void gdn_layer(lxo_run* st, int L) {
       if (!any) continue;
     }
     const uint16_t P = lx_rb(row_dot(&ly->qkv, ch, xn));
+    n_ch++;
+    n_ent += ly->qkv.indptr[ch + 1] - ly->qkv.indptr[ch];
     uint16_t* w = cw + (size_t)ch * 4;
     const uint16_t n0 = w[1], n1 = w[2], n2 = w[3];
     w[0] = n0;
@@ -184,6 +208,9 @@ static void gdn_layer(lxo_run* st, int L) {
   }
   memset(st->on, 0, sizeof(st->on));
   int any_out = 0;
+  int64_t c_ba = 0, c_z = 0, c_rows = 0, c_act = 0, c_wr = 0, c_out = 0;
+#pragma omp parallel for schedule(dynamic, 1) reduction(| : any_out) \
+    reduction(+ : c_ba, c_z, c_rows, c_act, c_wr, c_out)
   for (int kh = 0; kh < NK; kh++) {
     const float* q = st->qkv + kh * KD;
     const float* k = st->qkv + NK * KD + kh * KD;
@@ -203,8 +230,18 @@ static void gdn_layer(lxo_run* st, int L) {
       const float a = lx_rbf(row_dot(&ly->a, vh, xn));
       const float A = -lx_exp(lx_f(ly->A_log[vh]));
       const float g = lx_mul(A, lx_softplus(lx_add(a, lx_f(ly->dt_bias[vh]))));
+      c_ba += ly->a.indptr[vh + 1] - ly->a.indptr[vh];
       if (!qa && !ka && g == 0.0f) continue;  // the state stays, o = 0
+      c_ba += ly->b.indptr[vh + 1] - ly->b.indptr[vh];
+      c_act += qa || ka;
+      c_wr += ka;
       float* S = st->rec + (((size_t)L * NV + vh) * KD) * VD;
+      for (int i = 0; i < KD; i++) {  // rows touched: nonzero rows decayed, keyed or queried
+        int nzr = 0;
+        if (g != 0.0f)
+          for (int j = 0; j < VD; j++) nzr |= S[i * VD + j] != 0.0f;
+        c_rows += nzr || (ka && kn[i] != 0.0f) || (qa && qn[i] != 0.0f);
+      }
       if (g != 0.0f) {
         const float e = lx_exp(g);
         for (int i = 0; i < KD * VD; i++) S[i] = lx_mul(S[i], e);
@@ -236,13 +273,27 @@ static void gdn_layer(lxo_run* st, int L) {
         const float hn = lx_rbf(lx_mul(o[j], rr));
         const float u = lx_rbf(lx_mul(lx_f(ly->gnorm[j]), hn));
         const float z = lx_rbf(row_dot(&ly->z, (int64_t)vh * VD + j, xn));
+        c_z += ly->z.indptr[(int64_t)vh * VD + j + 1] - ly->z.indptr[(int64_t)vh * VD + j];
         st->on[vh * VD + j] = lx_rbf(lx_mul(u, lx_silu(z)));
       }
       any_out = 1;
+      c_out++;
     }
+  }
+  if (st->cnt) {
+    st->cnt[LXO_C_CHANS] += n_ch;
+    st->cnt[LXO_C_QKV_ENT] += n_ent;
+    st->cnt[LXO_C_BA_ENT] += c_ba;
+    st->cnt[LXO_C_Z_ENT] += c_z;
+    st->cnt[LXO_C_ROWS] += c_rows;
+    st->cnt[LXO_C_VH_ACTIVE] += c_act;
+    st->cnt[LXO_C_VH_WRITE] += c_wr;
+    st->cnt[LXO_C_VH_OUT] += c_out;
   }
   if (!any_out) return;
   // out_proj (bf16 linear) added to the residual in bf16
+  int64_t c_oe = 0, c_chg = 0;
+#pragma omp parallel for schedule(static) reduction(+ : c_oe, c_chg)
   for (int rr = 0; rr < H; rr++) {
     const lxo_csr* m = &ly->out;
     if (m->indptr[rr + 1] == m->indptr[rr]) continue;
@@ -253,10 +304,20 @@ static void gdn_layer(lxo_run* st, int L) {
       if (o != 0.0f) {
         s = lx_add(s, lx_mul(o, lx_f(m->data[e])));
         any = 1;
+        c_oe++;
       }
     }
-    if (any) x[rr] = lx_rbf(lx_add(x[rr], lx_rbf(s)));
+    if (any) {
+      const float nx = lx_rbf(lx_add(x[rr], lx_rbf(s)));
+      c_chg += nx != x[rr];
+      x[rr] = nx;
+    }
   }
+  if (st->cnt) {
+    st->cnt[LXO_C_OUT_ENT] += c_oe;
+    st->cnt[LXO_C_GDN_WRITE] += c_oe > 0;
+  }
+  (void)c_chg;
 }
 
 static void mlp_layer(lxo_run* st, int L) {
@@ -267,15 +328,19 @@ static void mlp_layer(lxo_run* st, int L) {
   rms_norm(x, ly->ln_post, chip->eps, xn);
   const int64_t nu = ly->gate.rows;
   float* h = (float*)calloc((size_t)nu, sizeof(float));
+  int64_t c_gu = 0, c_dn = 0;
+#pragma omp parallel for schedule(static) reduction(+ : c_gu)
   for (int64_t u = 0; u < nu; u++) {
     if (ly->gate.indptr[u + 1] == ly->gate.indptr[u] || ly->up.indptr[u + 1] == ly->up.indptr[u])
       continue;
+    c_gu += ly->gate.indptr[u + 1] - ly->gate.indptr[u] + ly->up.indptr[u + 1] - ly->up.indptr[u];
     // down_proj(silu(gate(x)) * up(x)), every product of bf16 tensors rounded to bf16
     const float gg = lx_rbf(row_dot(&ly->gate, u, xn));
     const float uu = lx_rbf(row_dot(&ly->up, u, xn));
     const float act = lx_rbf(lx_silu(gg));
     h[u] = lx_rbf(lx_mul(act, uu));
   }
+#pragma omp parallel for schedule(static) reduction(+ : c_dn)
   for (int rr = 0; rr < H; rr++) {
     const lxo_csr* m = &ly->down;
     float s = 0.0f;
@@ -285,11 +350,16 @@ static void mlp_layer(lxo_run* st, int L) {
       if (hv != 0.0f) {
         s = lx_add(s, lx_mul(hv, lx_f(m->data[e])));
         any = 1;
+        c_dn++;
       }
     }
     if (any) x[rr] = lx_rbf(lx_add(x[rr], lx_rbf(s)));
   }
   free(h);
+  if (st->cnt) {
+    st->cnt[LXO_C_GU_ENT] += c_gu;
+    st->cnt[LXO_C_DOWN_ENT] += c_dn;
+  }
 }
 
 // the head's dense columns (see the header comment); returns their count (0: none)
@@ -331,39 +401,60 @@ static int head_argmax(lxo_run* st, float* margin_out) {
   const lxo_csr* hd = &chip->head;
   float xf[H];
   rms_norm(st->x, chip->final_norm, chip->eps, xf);
-  float best = -LXB_INF, second = -LXB_INF;
-  int bi = 0;
-  for (int64_t t = 0; t < hd->rows; t++) {
-    float D = 0.0f, S = 0.0f;
-    int di = 0;
-    float grp = 0.0f;
-    int in_grp = 0;
-    for (int64_t e = hd->indptr[t]; e < hd->indptr[t + 1]; e++) {
-      const int c = hd->indices[e];
-      const float p = lx_mul(lx_f(hd->data[e]), xf[c]);
-      if (di < st->n_dense && st->dense_cols[di] == c) {
-        grp = lx_add(grp, p);
-        di++;
-        if (++in_grp == 4 || di == st->n_dense) {
-          D = lx_add(D, grp);
-          grp = 0.0f;
-          in_grp = 0;
+  enum { NCH = 64 };  // row chunks, combined in row order (the first maximum wins)
+  float cb[NCH], cs[NCH];
+  int ci[NCH];
+  const int64_t V = hd->rows;
+#pragma omp parallel for schedule(static)
+  for (int k = 0; k < NCH; k++) {
+    float best = -LXB_INF, second = -LXB_INF;
+    int bi = -1;
+    for (int64_t t = V * k / NCH; t < V * (k + 1) / NCH; t++) {
+      float D = 0.0f, S = 0.0f;
+      int di = 0;
+      float grp = 0.0f;
+      int in_grp = 0;
+      for (int64_t e = hd->indptr[t]; e < hd->indptr[t + 1]; e++) {
+        const int c = hd->indices[e];
+        const float p = lx_mul(lx_f(hd->data[e]), xf[c]);
+        if (di < st->n_dense && st->dense_cols[di] == c) {
+          grp = lx_add(grp, p);
+          di++;
+          if (++in_grp == 4 || di == st->n_dense) {
+            D = lx_add(D, grp);
+            grp = 0.0f;
+            in_grp = 0;
+          }
+        } else {
+          S = lx_add(S, p);
         }
-      } else {
-        S = lx_add(S, p);
+      }
+      const float lg = lx_rbf(lx_add(D, S));
+      if (bi < 0 || lg > best) {  // the first maximum: a later equal logit does not replace it
+        second = bi < 0 ? -LXB_INF : best;
+        best = lg;
+        bi = (int)t;
+      } else if (lg > second) {
+        second = lg;
       }
     }
-    const float lg = lx_rbf(lx_add(D, S));
-    if (lg > best) {  // the first maximum: a later equal logit does not replace it
-      second = best;
-      best = lg;
-      bi = (int)t;
-    } else if (lg > second) {
-      second = lg;
-    }
+    cb[k] = best;
+    cs[k] = second;
+    ci[k] = bi;
   }
-  if (margin_out) *margin_out = lx_sub(best, second);
-  return bi;
+  int w = -1;
+  for (int k = 0; k < NCH; k++)
+    if (ci[k] >= 0 && (w < 0 || cb[k] > cb[w])) w = k;
+  float second = -LXB_INF;
+  for (int k = 0; k < NCH; k++) {
+    if (ci[k] < 0) continue;
+    if (cs[k] > second) second = cs[k];
+    if (k != w && cb[k] > second) second = cb[k];
+  }
+  if (margin_out) *margin_out = lx_sub(cb[w], second);
+  if (st->cnt)
+    st->cnt[LXO_C_HEAD_B] += (st->n_dense ? 8 * V : 0) + 4 * (hd->indptr[V] - (st->n_dense ? V * st->n_dense : 0));
+  return ci[w];
 }
 
 // n_tokens steps of the model alone: step i embeds forced[i] (i < n_forced) or step i-1's
@@ -373,7 +464,7 @@ static int head_argmax(lxo_run* st, float* margin_out) {
 // token id.
 int lxo_decode(const lxo_chip* chip, float* rec, uint16_t* conv, const int32_t* forced,
                int n_forced, int n_tokens, int32_t* preds, int32_t* inputs, float* margins,
-               float* resid) {
+               float* resid, int64_t* counts) {
   lxo_run* st = (lxo_run*)calloc(1, sizeof(lxo_run));
   st->chip = chip;
   st->rec = rec;
@@ -388,6 +479,7 @@ int lxo_decode(const lxo_chip* chip, float* rec, uint16_t* conv, const int32_t* 
       break;
     }
     if (inputs) inputs[i] = tok;
+    st->cnt = counts ? counts + (size_t)i * LXO_C_N : NULL;
     const uint16_t* e = chip->embed + ((int64_t)tok + chip->offset) * H;
     for (int c = 0; c < H; c++) st->x[c] = lx_f(e[c]);
     for (int L = 0; L < chip->n_layers; L++) {
@@ -404,6 +496,7 @@ int lxo_decode(const lxo_chip* chip, float* rec, uint16_t* conv, const int32_t* 
 }
 
 // the canonical sums, exposed for the kernels' unit tests
+int lxo_n_counters(void) { return LXO_C_N; }
 float lxo_ssq2560(const float* x) { return ssq2560(x); }
 float lxo_sumsq128(const float* x) { return sumsq128(x); }
 void lxo_l2norm_bf16(const float* x, int n, float* out) { l2norm_bf16(x, n, out); }

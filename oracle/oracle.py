@@ -53,7 +53,7 @@ def lib():
             build()
         _lib = ctypes.CDLL(str(LIB))
         _lib.lxo_decode.restype = ctypes.c_int
-        _lib.lxo_decode.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, P, P, P, P]
+        _lib.lxo_decode.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, P, P, P, P, P]
         for f in ("lxo_exp", "lxo_log1p", "lxo_silu", "lxo_sigmoid", "lxo_softplus"):
             getattr(_lib, f).restype = ctypes.c_float
             getattr(_lib, f).argtypes = [ctypes.c_float]
@@ -61,6 +61,7 @@ def lib():
         _lib.lxo_ssq2560.argtypes = [P]
         _lib.lxo_sumsq128.restype = ctypes.c_float
         _lib.lxo_sumsq128.argtypes = [P]
+        assert _lib.lxo_n_counters() == len(Oracle.COUNTERS)
     return _lib
 
 
@@ -98,9 +99,12 @@ class Oracle:
         return _Csr(rows=m.shape[0], cols=m.shape[1], indptr=_ptr(ip), indices=_ptr(ix),
                     data=_ptr(da))
 
-    def decode(self, state, forced, n: int, resid: bool = False):
+    COUNTERS = ("chans", "qkv_ent", "ba_ent", "z_ent", "rows", "out_ent", "gu_ent", "down_ent",
+                "head_bytes", "vh_active", "vh_write", "vh_out", "gdn_write")
+
+    def decode(self, state, forced, n: int, resid: bool = False, counts: bool = False):
         """n steps of the model alone from `state` (a chip.State, updated in place). Returns
-        (preds, inputs, margins[, resid])."""
+        (preds, inputs, margins[, resid][, counts]); counts: int64 [n, len(COUNTERS)]."""
         assert state.recurrent.dtype == np.float32 and state.conv.dtype == np.uint16
         assert state.recurrent.flags["C_CONTIGUOUS"] and state.conv.flags["C_CONTIGUOUS"]
         f = np.ascontiguousarray(forced, np.int32)
@@ -108,9 +112,16 @@ class Oracle:
         inputs = np.zeros(n, np.int32)
         margins = np.zeros(n, np.float32)
         rs = np.zeros((n, 2560), np.float32) if resid else None
+        cn = np.zeros((n, len(self.COUNTERS)), np.int64) if counts else None
         rc = lib().lxo_decode(ctypes.addressof(self._chip), _ptr(state.recurrent),
                               _ptr(state.conv), _ptr(f), len(f), n, _ptr(preds), _ptr(inputs),
-                              _ptr(margins), _ptr(rs) if resid else None)
+                              _ptr(margins), _ptr(rs) if resid else None,
+                              _ptr(cn) if counts else None)
         if rc:
             raise ValueError("oracle: token id out of the embedding's range")
-        return (preds, inputs, margins, rs) if resid else (preds, inputs, margins)
+        out = (preds, inputs, margins)
+        if resid:
+            out += (rs,)
+        if counts:
+            out += (cn,)
+        return out

@@ -81,3 +81,18 @@ def test_bad_token_sets_status(c1_chip):
         dec.run(ds, [[0, 5000]], 4)
     preds, _ = dec.run(ds, [[0]], 2)  # the plan stays usable
     assert preds.shape == (1, 2)
+
+
+def test_c2_matches_oracle():
+    """The 37-layer chip-shaped stack (a 20,000-row head to keep the oracle quick): streams,
+    conv windows and recurrent states bit-identical."""
+    chip = C.c2(1, vocab=20000)
+    st0 = C.c2_state(chip, 1)
+    n = 48
+    dec = _decoder(chip, 16)
+    ds = dec.states([st0])
+    preds, _ = dec.run(ds, [[0]], n)
+    host = st0.copy()
+    p, _, _ = Oracle(chip).decode(host, [0], n)
+    assert (preds[0].cpu().numpy() == p).all()
+    _same_state(ds, 0, host)
