@@ -233,7 +233,7 @@ def main():
     # warm-up: W launches, the stream chained
     for w in range(a.warmup):
         dec.launch(states.ptrs, states.bitmaps, forced, T, preds, None, sync_bitmaps=(w == 0),
-                   stream=stream)
+                   stream=stream, scratch=states.scratch)
         forced = preds[:, -1:].clone()
     torch.cuda.synchronize(dev)
     if world > 1:
@@ -246,7 +246,7 @@ def main():
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             dec.launch(states.ptrs, states.bitmaps, forced, T, preds, None, sync_bitmaps=False,
-                       stream=stream)
+                       stream=stream, scratch=states.scratch)
             e1.record(stream)
             forced = preds[:, -1:].clone()
             e1.synchronize()

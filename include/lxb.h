@@ -74,8 +74,13 @@ int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb_plan** out
  * mega.py:518-526). embed: DEVICE bf16 [n_embed_rows][2560]; token t embeds row offset + t.
  * Replaces mk_run (mega.cu:867-874) as called by Mega.run (mega.py:529-574). */
 int lxb_decode(lxb_plan* plan, const uint64_t* state_ptrs, uint32_t* bitmaps, int sync_bitmaps,
-               const uint16_t* embed, int n_streams, const int32_t* forced, int n_forced,
-               int n_tokens, int32_t* preds, int32_t* inputs, void* cuda_stream);
+               void* scratch, const uint16_t* embed, int n_streams, const int32_t* forced,
+               int n_forced, int n_tokens, int32_t* preds, int32_t* inputs, void* cuda_stream);
+
+/* Device scratch lxb_decode needs for n_streams streams (a ring of the last 4 steps' residual
+ * rows per layer, from which the lazily kept conv windows are recomputed). The caller allocates
+ * it (16-byte aligned); its contents need no initialisation and do not outlive a call. */
+size_t lxb_scratch_bytes(const lxb_plan* plan, int n_streams);
 
 /* The device status word (after the stream has synchronised). Replaces mk_last_error
  * (mega.cu:892) for kernel-side errors. */

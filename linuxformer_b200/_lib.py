@@ -31,7 +31,8 @@ SIGNATURES = {
     "lxb_abi_version": (I, []),
     "lxb_query": (I, [I, P]),
     "lxb_plan_create": (I, [P, ctypes.c_size_t, I, P]),
-    "lxb_decode": (I, [P, P, P, I, P, I, P, I, I, P, P, P]),
+    "lxb_decode": (I, [P, P, P, I, P, P, I, P, I, I, P, P, P]),
+    "lxb_scratch_bytes": (ctypes.c_size_t, [P, I]),
     "lxb_status": (I, [P, P]),
     "lxb_status_clear": (I, [P]),
     "lxb_plan_bytes": (ctypes.c_size_t, [P]),

@@ -317,7 +317,7 @@ def c2(seed: int = 1, vocab: int = C2_VOCAB, n_layers: int = C2_LAYERS) -> Chip:
     reads its queries from one select column and its keys from another (one in_proj entry per
     channel, one conv tap on the newest input), so whether a head is active is decided by which
     select columns the current token sets: memory heads' queries fire for ~1.7% of tokens, the
-    other heads' for ~13%, keys for ~0.65%. Value channels read 15 data columns each (every
+    other heads' for ~13%, keys for ~0.15%. Value channels read 15 data columns each (every
     token, as in the real circuit, since their conv windows are state); only memory heads
     have in_proj_z rows. Query and key rows of
     the non-memory heads are disjoint, so only memory heads (whose states hold the RAM and ROM
@@ -424,7 +424,7 @@ def c2(seed: int = 1, vocab: int = C2_VOCAB, n_layers: int = C2_LAYERS) -> Chip:
         on = np.nonzero(rng.random(vocab) < p)[0]
         emb[on, qs] = bf16_bits(_pow2_values(rng, len(on)))
     for (L, kh), ks in meta["k_sel"].items():
-        on = np.nonzero(rng.random(vocab) < 0.0065)[0]
+        on = np.nonzero(rng.random(vocab) < 0.0015)[0]
         emb[on, ks] = bf16_bits(_pow2_values(rng, len(on)))
     nf = 48
     fr = np.repeat(np.arange(vocab), nf)

@@ -21,6 +21,12 @@
 //     the GDN leaves the residual as it is) run side by side; if any item did write, an
 //     out_proj step and the MLP again follow (two more barriers). The reference pairs only the
 //     layers it measured (PAIR_LAYERS, lx/lx/mega.py:97); here every layer is paired.
+//   - Value channels are kept lazily: their projections only matter on the steps a key of
+//     their head fires (the delta rule's v) and for the conv windows the launch leaves behind.
+//     Each step stores its GDN input row in a 4-step ring (device scratch); a firing key's
+//     head recomputes its value channels' last four projections from it, and at the launch's
+//     end every lazy window is rebuilt the same way. The reference evaluates every channel on
+//     every step (lx/csrc/mega.cu:318-336); the results are the same bits.
 //   - Independent streams are independent clusters: no inter-cluster communication at all.
 // No device-wide barrier exists, so nothing spins on global memory; the only waits are
 // hardware cluster barriers, which every CTA of a cluster reaches on the same cluster-uniform
@@ -28,6 +34,7 @@
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <new>
 #include <stddef.h>
 #include <stdint.h>
@@ -70,6 +77,8 @@ struct Dev {
 struct Run {
   const uint64_t* state_ptrs;  // [stream][layer][2]
   uint32_t* bitmaps;           // [stream][layer][128][8]
+  uint16_t* ring;              // [stream][layer][4][2560]: the GDN input rows of the last 4 steps
+  float* ring_r;               // [stream][layer][4]: their RMSNorm factors
   const uint16_t* embed;
   const int32_t* forced;
   int n_forced, n_tokens;
@@ -81,6 +90,7 @@ struct __align__(16) Smem {
   alignas(16) float x[H];          // the residual replica (bf16 values)
   float xn[H];                     // input_layernorm(x) (bf16 values)
   float xm[H];                     // post_attention_layernorm(x) or the final norm
+  float xr[H];                     // input_layernorm of an earlier step's residual (lazy windows)
   alignas(16) float own[2][BLKMAX];  // this CTA's rows after the step, by step parity
   float buf[LXB_NSLOT];            // an item's q | k | v
   float qval[KD], kval[KD];        // nonzero l2-normed query (x 1/16) and key values
@@ -93,7 +103,10 @@ struct __align__(16) Smem {
   int wflag[2];                    // some item of the step wrote (pushed by the writer)
   int kmask[LXB_NK];               // out_proj step: active value heads per key head
   alignas(16) uint16_t on[LXB_ITEMSLOTS][R * VD];  // the gated norm's output per item slot
-  alignas(16) uint16_t onall[LXB_NK][R * VD];  // gathered for the out_proj step
+  union {
+    alignas(16) uint16_t onall[LXB_NK][R * VD];  // gathered for the out_proj step
+    uint16_t pw[4][LXB_NSLOT];     // lazy channels: their projections at 4 steps
+  };
   float hbuf[LXB_MAXUNITS];        // MLP unit outputs
   float htg[LXB_MAXDENSE / 4][256];  // head: per group of 4 dense columns, each code's sum
   float bestv;
@@ -129,21 +142,54 @@ __device__ float block_ssq(Smem& sm, const float* x) {
   return r;
 }
 
-// Qwen3_5RMSNorm: out[c] = bf16(x[c] * rsqrt(ss / 2560 + eps) * (1 + w[c]))
-__device__ void norm_into(const Dev& P, float* out, const float* x, int w_off, float ss) {
-  const float r = lx_rsqrt(lx_add(lx_div(ss, (float)H), P.eps));
+__device__ __forceinline__ float norm_factor(const Dev& P, float ss) {
+  return lx_rsqrt(lx_add(lx_div(ss, (float)H), P.eps));
+}
+
+// Qwen3_5RMSNorm with the factor r: out[c] = bf16(x[c] * r * (1 + w[c]))
+__device__ void norm_into(const Dev& P, float* out, const float* x, int w_off, float r) {
   const uint16_t* w = P.u16 + w_off;
   for (int c = threadIdx.x; c < H; c += NT)
     out[c] = lx_rbf(lx_mul(lx_mul(x[c], r), lx_add(1.0f, lx_f(__ldg(w + c)))));
 }
 
-__device__ __forceinline__ float row_dot(const uint32_t* ent, uint32_t e0, int n, const float* x) {
+// sequential dot over entries [e0, e0 + n) (column | bf16 << 16), loads issued 8 at a time
+__device__ __forceinline__ float dotb(const uint32_t* __restrict__ ent, uint32_t e0, int n,
+                                      const float* x) {
   float s = 0.0f;
-  for (int e = 0; e < n; e++) {
-    const uint32_t w = __ldg(ent + e0 + e);
-    s = lx_add(s, lx_mul(x[w & 0xffffu], lx_f((uint16_t)(w >> 16))));
+  for (int e = 0; e < n; e += 8) {
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) w[k] = e + k < n ? __ldg(ent + e0 + e + k) : 0u;
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      if (e + k < n) s = lx_add(s, lx_mul(x[w[k] & 0xffffu], lx_f((uint16_t)(w[k] >> 16))));
   }
   return s;
+}
+
+// two sequential dots with their loads interleaved (a unit's gate and up rows)
+__device__ __forceinline__ void dot2b(const uint32_t* __restrict__ ent, uint32_t ga, int gn,
+                                      uint32_t ua, int un, const float* x, float& sg,
+                                      float& su) {
+  float a = 0.0f, b = 0.0f;
+  const int m = gn > un ? gn : un;
+  for (int e = 0; e < m; e += 8) {
+    uint32_t wg[8], wu[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      wg[k] = e + k < gn ? __ldg(ent + ga + e + k) : 0u;
+      wu[k] = e + k < un ? __ldg(ent + ua + e + k) : 0u;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      if (e + k < gn) a = lx_add(a, lx_mul(x[wg[k] & 0xffffu], lx_f((uint16_t)(wg[k] >> 16))));
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      if (e + k < un) b = lx_add(b, lx_mul(x[wu[k] & 0xffffu], lx_f((uint16_t)(wu[k] >> 16))));
+  }
+  sg = a;
+  su = b;
 }
 
 __device__ __forceinline__ void set_status(const Dev& P, uint32_t bit, int stream, int step) {
@@ -153,46 +199,101 @@ __device__ __forceinline__ void set_status(const Dev& P, uint32_t bit, int strea
   }
 }
 
+// sm.xr = input_layernorm of step tau's residual at layer L, from the ring
+__device__ void build_xr(const Dev& P, const Run& run, Smem& sm, int s, int L, int tau,
+                         int w_off) {
+  const size_t slot = ((size_t)s * P.n_layers + L) * 4 + (tau & 3);
+  const uint4* xs = reinterpret_cast<const uint4*>(run.ring + slot * H);
+  const float r = __ldcg(run.ring_r + slot);
+  for (int k = threadIdx.x; k < H / 8; k += NT) {
+    const uint4 v = __ldcg(xs + k);
+    const uint32_t xw[4] = {v.x, v.y, v.z, v.w};
+    const uint16_t* wv = P.u16 + w_off + 8 * k;
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const float xv = lx_f((uint16_t)(q & 1 ? xw[q >> 1] >> 16 : xw[q >> 1] & 0xffffu));
+      sm.xr[8 * k + q] = lx_rbf(lx_mul(lx_mul(xv, r), lx_add(1.0f, lx_f(__ldg(wv + q)))));
+    }
+  }
+  __syncthreads();
+}
+
+// Lazily kept channels [c0, c1) of an item: their projections P at the steps tau = base + p
+// (p = 0..3) into sm.pw[p][c - c0]. P of a step before the launch comes from the channel's conv
+// window as the launch found it (a lazy channel's window is not written until the launch ends).
+// `cur` is the current step (its input norm is sm.xn already), or a value no step has.
+// taps_only: compute P only where the channel's tap p is nonzero (0 elsewhere: a zero tap's
+// product is a signed zero, which leaves the conv sum as it is).
+__device__ void lazy_proj(const Dev& P, const Run& run, Smem& sm, const lxb_item& it,
+                          const uint16_t* conv, int s, int L, int base, int cur, bool taps_only,
+                          int c0, int c1, int w_off) {
+  const int t = threadIdx.x;
+  for (int p = 0; p < 4; p++) {
+    const int tau = base + p;
+    const float* xsrc = nullptr;
+    if (tau == cur) {
+      xsrc = sm.xn;
+    } else if (tau >= 0) {
+      build_xr(P, run, sm, s, L, tau, w_off);
+      xsrc = sm.xr;
+    }
+    for (int c = c0 + t; c < c1; c += NT) {
+      const lxb_chan* cp = P.chans + it.ch0 + c;
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(cp));
+      uint16_t v = 0;
+      if (taps_only && !((__ldg(reinterpret_cast<const uint4*>(cp) + 1).y >> p) & 1)) {
+        v = 0;
+      } else if (xsrc) {
+        v = lx_rb(dotb(P.ent, a.x, (int)(a.y & 0xffffu), xsrc));
+      } else {  // before the launch: the window holds P of steps -4..-1 at positions 0..3
+        const uint2 win = *reinterpret_cast<const uint2*>(conv + (size_t)a.z * 4);
+        const int pos = tau + 4;
+        const uint32_t wd = pos < 2 ? win.x : win.y;
+        v = (uint16_t)((pos & 1) ? wd >> 16 : wd & 0xffffu);
+      }
+      sm.pw[p][c - c0] = v;
+    }
+    __syncthreads();
+  }
+}
+
 // --- a GDN item: one live key head of one layer --------------------------------------------------
 // Returns whether it wrote (some value head has output and the head has out_proj entries).
-__device__ bool gdn_item(const Dev& P, Smem& sm, const lxb_item& it, float* rec, uint16_t* conv,
-                         uint32_t* bm) {
+__device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const lxb_item& it, float* rec,
+                         uint16_t* conv, uint32_t* bm, int s, int L, int step, int ln_in) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   uint16_t* on = sm.on[it.slot];
   for (int k = t; k < LXB_NSLOT; k += NT) sm.buf[k] = 0.0f;
   for (int k = t; k < R * VD; k += NT) on[k] = 0;
   if (t == 0) sm.vhmask[it.slot] = 0;
   __syncthreads();
-  // in_proj_qkv rows, the conv window shift and the conv output with silu (bf16), per channel
-  for (int c = t; c < it.n_ch; c += NT) {
+  // query / key channels: in_proj_qkv row, conv window shift, conv output with silu (bf16)
+  for (int c = t; c < it.n_eager; c += NT) {
     const lxb_chan* cp = P.chans + it.ch0 + c;
     const uint4 a = __ldg(reinterpret_cast<const uint4*>(cp));  // ent, n|slot, conv_ch, t01
     const uint32_t t23 = __ldg(reinterpret_cast<const uint4*>(cp) + 1).x;
-    const uint16_t Pv = lx_rb(row_dot(P.ent, a.x, (int)(a.y & 0xffffu), sm.xn));
     uint2* wp = reinterpret_cast<uint2*>(conv + (size_t)a.z * 4);
     const uint2 win = *wp;
+    const uint16_t Pv = lx_rb(dotb(P.ent, a.x, (int)(a.y & 0xffffu), sm.xn));
     const uint16_t n0 = (uint16_t)(win.x >> 16), n1 = (uint16_t)(win.y & 0xffffu),
                    n2 = (uint16_t)(win.y >> 16);
     *wp = make_uint2((uint32_t)n0 | ((uint32_t)n1 << 16), (uint32_t)n2 | ((uint32_t)Pv << 16));
-    const uint32_t slot = a.y >> 16;
-    if (slot != LXB_NOSLOT) {
-      float y = 0.0f;
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(n0)));
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(n1)));
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 & 0xffffu)), lx_f(n2)));
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(Pv)));
-      sm.buf[slot] = lx_rbf(lx_silu(lx_rbf(y)));
-    }
+    float y = 0.0f;
+    y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(n0)));
+    y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(n1)));
+    y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 & 0xffffu)), lx_f(n2)));
+    y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(Pv)));
+    sm.buf[a.y >> 16] = lx_rbf(lx_silu(lx_rbf(y)));
   }
   const int32_t* rows = P.i32 + it.rows;
   const uint16_t* prm = P.u16 + it.params;
   if (t < R) {  // g = -exp(A_log) * softplus(bf16(a . x) + dt_bias)
-    const float a = lx_rbf(row_dot(P.ent, (uint32_t)rows[16 + 2 * t], rows[17 + 2 * t], sm.xn));
+    const float a = lx_rbf(dotb(P.ent, (uint32_t)rows[16 + 2 * t], rows[17 + 2 * t], sm.xn));
     const float A = -lx_exp(lx_f(prm[t]));
     sm.g[t] = lx_mul(A, lx_softplus(lx_add(a, lx_f(prm[R + t]))));
   } else if (t < 2 * R) {  // beta = bf16(sigmoid(bf16(b . x)))
     const int r = t - R;
-    const float b = lx_rbf(row_dot(P.ent, (uint32_t)rows[2 * r], rows[2 * r + 1], sm.xn));
+    const float b = lx_rbf(dotb(P.ent, (uint32_t)rows[2 * r], rows[2 * r + 1], sm.xn));
     sm.beta[r] = lx_rbf(lx_sigmoid(b));
   }
   const int qa = __syncthreads_or(t < KD && sm.buf[t] != 0.0f);
@@ -201,8 +302,27 @@ __device__ bool gdn_item(const Dev& P, Smem& sm, const lxb_item& it, float* rec,
 #pragma unroll
   for (int r = 0; r < R; r++) anyg |= sm.g[r] != 0.0f;
   if (!qa && !ka && !anyg) return false;  // the state stays as it is and o = 0
+  // a key fired: the value channels' conv outputs at this step, from their projections at
+  // the last four steps (the window a stock step would hold)
+  if (ka && it.n_vneed) {
+    const int c0 = it.n_eager, c1 = it.n_eager + it.n_vneed;
+    lazy_proj(P, run, sm, it, conv, s, L, step - 3, step, true, c0, c1, ln_in);
+    for (int c = c0 + t; c < c1; c += NT) {
+      const lxb_chan* cp = P.chans + it.ch0 + c;
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(cp));
+      const uint32_t t23 = __ldg(reinterpret_cast<const uint4*>(cp) + 1).x;
+      const int i = c - c0;
+      float y = 0.0f;
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(sm.pw[0][i])));
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(sm.pw[1][i])));
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 & 0xffffu)), lx_f(sm.pw[2][i])));
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(sm.pw[3][i])));
+      sm.buf[a.y >> 16] = lx_rbf(lx_silu(lx_rbf(y)));
+    }
+  }
   // transformers' l2norm in bf16 on q (warp 0) and k (warp 1): the nonzero entries in
   // ascending order, their bf16 squares summed sequentially from +0
+  __syncthreads();
   if (warp < 2) {
     const float* xv = sm.buf + warp * KD;
     int* idx = warp ? sm.kidx : sm.qidx;
@@ -221,9 +341,9 @@ __device__ bool gdn_item(const Dev& P, Smem& sm, const lxb_item& it, float* rec,
     __syncwarp();
     float inv = 0.0f;
     if (lane == 0) {
-      float s = 0.0f;
-      for (int i = 0; i < n; i++) s = lx_add(s, lx_rbf(lx_mul(val[i], val[i])));
-      inv = lx_rbf(lx_rsqrt(lx_rbf(lx_add(lx_rbf(s), 1e-6f))));
+      float sq = 0.0f;
+      for (int i = 0; i < n; i++) sq = lx_add(sq, lx_rbf(lx_mul(val[i], val[i])));
+      inv = lx_rbf(lx_rsqrt(lx_rbf(lx_add(lx_rbf(sq), 1e-6f))));
     }
     inv = __shfl_sync(0xffffffffu, inv, 0);
     for (int i = lane; i < n; i += 32) {
@@ -265,7 +385,14 @@ __device__ bool gdn_item(const Dev& P, Smem& sm, const lxb_item& it, float* rec,
       }
       if (nk) {
         float kv = 0.0f;
-        for (int a = 0; a < nk; a++) kv = lx_add(kv, lx_mul(S[sm.kidx[a] * VD], sm.kval[a]));
+        for (int a0 = 0; a0 < nk; a0 += 8) {
+          float hv[8];
+#pragma unroll
+          for (int q = 0; q < 8; q++) hv[q] = a0 + q < nk ? S[sm.kidx[a0 + q] * VD] : 0.0f;
+#pragma unroll
+          for (int q = 0; q < 8; q++)
+            if (a0 + q < nk) kv = lx_add(kv, lx_mul(hv[q], sm.kval[a0 + q]));
+        }
         const float delta = lx_mul(lx_sub(sm.buf[2 * KD + r * VD + j], kv), sm.beta[r]);
         for (int a = 0; a < nk; a++) {
           float* hp = S + sm.kidx[a] * VD;
@@ -273,7 +400,14 @@ __device__ bool gdn_item(const Dev& P, Smem& sm, const lxb_item& it, float* rec,
         }
       }
       float o = 0.0f;
-      for (int a = 0; a < nq; a++) o = lx_add(o, lx_mul(S[sm.qidx[a] * VD], sm.qval[a]));
+      for (int a0 = 0; a0 < nq; a0 += 8) {
+        float hv[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) hv[q] = a0 + q < nq ? S[sm.qidx[a0 + q] * VD] : 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; q++)
+          if (a0 + q < nq) o = lx_add(o, lx_mul(hv[q], sm.qval[a0 + q]));
+      }
       sm.ob[r][j] = lx_rbf(o);
     }
   }
@@ -291,23 +425,27 @@ __device__ bool gdn_item(const Dev& P, Smem& sm, const lxb_item& it, float* rec,
                 o3 = o[4 * lane + 3];
     const bool nz = __any_sync(0xffffffffu, o0 != 0.0f || o1 != 0.0f || o2 != 0.0f || o3 != 0.0f);
     if (nz) {
-      float s = lx_mul(o0, o0);
-      s = lx_add(s, lx_mul(o1, o1));
-      s = lx_add(s, lx_mul(o2, o2));
-      s = lx_add(s, lx_mul(o3, o3));
-      s = warp_xor_sum(s);
-      const float rr = lx_rsqrt(lx_add(lx_div(s, 128.0f), P.eps));
+      float sq = lx_mul(o0, o0);
+      sq = lx_add(sq, lx_mul(o1, o1));
+      sq = lx_add(sq, lx_mul(o2, o2));
+      sq = lx_add(sq, lx_mul(o3, o3));
+      sq = warp_xor_sum(sq);
+      const float rr = lx_rsqrt(lx_add(lx_div(sq, 128.0f), P.eps));
       const uint16_t* gw = prm + 2 * R;
-      const int vh = it.kh * R + r;
-      for (int j = lane; j < VD; j += 32) {
+      float z[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int zr = 32 + 2 * (r * VD + lane + 32 * q);
+        z[q] = lx_rbf(dotb(P.ent, (uint32_t)rows[zr], rows[zr + 1], sm.xn));
+      }
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int j = lane + 32 * q;
         const float hn = lx_rbf(lx_mul(o[j], rr));
         const float u = lx_rbf(lx_mul(lx_f(gw[j]), hn));
-        const int zr = 32 + 2 * (r * VD + j);
-        const float z = lx_rbf(row_dot(P.ent, (uint32_t)rows[zr], rows[zr + 1], sm.xn));
-        on[r * VD + j] = lx_rb(lx_mul(u, lx_silu(z)));
+        on[r * VD + j] = lx_rb(lx_mul(u, lx_silu(z[q])));
       }
       if (lane == 0) atomicOr(&sm.vhmask[it.slot], 1u << r);
-      (void)vh;
     }
   }
   __syncthreads();
@@ -319,9 +457,10 @@ __device__ bool gdn_item(const Dev& P, Smem& sm, const lxb_item& it, float* rec,
 __device__ void mlp_owner(const Dev& P, Smem& sm, const lxb_owner& ow, int rank, float* own) {
   const int t = threadIdx.x;
   for (int u = t; u < ow.n_units; u += NT) {
-    const lxb_unit un = P.units[ow.unit0 + u];
-    const float gg = lx_rbf(row_dot(P.ent, un.g, un.ng, sm.xm));
-    const float uu = lx_rbf(row_dot(P.ent, un.u, un.nu, sm.xm));
+    const uint4 un = __ldg(reinterpret_cast<const uint4*>(P.units + ow.unit0 + u));
+    float gs, us;
+    dot2b(P.ent, un.x, (int)(un.z & 0xffffu), un.y, (int)(un.z >> 16), sm.xm, gs, us);
+    const float gg = lx_rbf(gs), uu = lx_rbf(us);
     const float act = lx_rbf(lx_silu(gg));
     sm.hbuf[u] = lx_rbf(lx_mul(act, uu));
   }
@@ -332,15 +471,21 @@ __device__ void mlp_owner(const Dev& P, Smem& sm, const lxb_owner& ow, int rank,
     const float xv = sm.x[r0 + k];
     float res = xv;
     if (rp) {
-      const int a = rp[k], b = rp[k + 1];
+      const int a = __ldg(rp + k), b = __ldg(rp + k + 1);
       float s = 0.0f;
       bool any = false;
-      for (int e = a; e < b; e++) {
-        const uint32_t w = __ldg(P.ent + e);
-        const float hv = sm.hbuf[w & 0xffffu];
-        if (hv != 0.0f) {
-          s = lx_add(s, lx_mul(hv, lx_f((uint16_t)(w >> 16))));
-          any = true;
+      for (int e = a; e < b; e += 8) {
+        uint32_t w[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) w[q] = e + q < b ? __ldg(P.ent + e + q) : 0u;
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          if (e + q >= b) continue;
+          const float hv = sm.hbuf[w[q] & 0xffffu];
+          if (hv != 0.0f) {
+            s = lx_add(s, lx_mul(hv, lx_f((uint16_t)(w[q] >> 16))));
+            any = true;
+          }
         }
       }
       if (any) res = lx_rbf(lx_add(xv, lx_rbf(s)));
@@ -370,7 +515,8 @@ __device__ void out_owner(const Dev& P, Smem& sm, const lxb_layer& ly, const lxb
     const int kh = k / (R * VD / 8), q = k % (R * VD / 8);
     if (!sm.kmask[kh]) continue;
     const lxb_item it = P.items[itemof[kh]];
-    const uint4* src = reinterpret_cast<const uint4*>(cluster.map_shared_rank(&sm.on[it.slot][0], it.cta));
+    const uint4* src =
+        reinterpret_cast<const uint4*>(cluster.map_shared_rank(&sm.on[it.slot][0], it.cta));
     reinterpret_cast<uint4*>(&sm.onall[kh][0])[q] = src[q];
   }
   __syncthreads();
@@ -383,15 +529,21 @@ __device__ void out_owner(const Dev& P, Smem& sm, const lxb_layer& ly, const lxb
       const int a = rp[k], b = rp[k + 1];
       float s = 0.0f;
       bool any = false;
-      for (int e = a; e < b; e++) {
-        const uint32_t w = __ldg(P.ent + e);
-        const uint32_t vd = w & 0xffffu;
-        const int kh = (int)(vd >> 10);
-        if (!((sm.kmask[kh] >> ((vd >> 7) & 7)) & 1)) continue;
-        const float ov = lx_f(sm.onall[kh][vd & 1023u]);
-        if (ov != 0.0f) {
-          s = lx_add(s, lx_mul(ov, lx_f((uint16_t)(w >> 16))));
-          any = true;
+      for (int e = a; e < b; e += 8) {
+        uint32_t w[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) w[q] = e + q < b ? __ldg(P.ent + e + q) : 0u;
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          if (e + q >= b) continue;
+          const uint32_t vd = w[q] & 0xffffu;
+          const int kh = (int)(vd >> 10);
+          if (!((sm.kmask[kh] >> ((vd >> 7) & 7)) & 1)) continue;
+          const float ov = lx_f(sm.onall[kh][vd & 1023u]);
+          if (ov != 0.0f) {
+            s = lx_add(s, lx_mul(ov, lx_f((uint16_t)(w[q] >> 16))));
+            any = true;
+          }
         }
       }
       if (any) res = lx_rbf(lx_add(xv, lx_rbf(s)));
@@ -441,22 +593,34 @@ __device__ void head_part(const Dev& P, Smem& sm, int rank) {
   const int32_t* rp = P.i32 + hc.rowptr;
   float bv = -LXB_INF;
   int bi = 0x7fffffff;
-  for (int row = hc.r0 + t; row < hc.r1; row += NT) {
-    float D = 0.0f;
-    if (nd) {
-      const uint64_t code = __ldg(P.hcodes + row);
-      for (int g = 0; g < ng; g++) D = lx_add(D, sm.htg[g][(code >> (8 * g)) & 255u]);
+  constexpr int U = 8;  // rows in flight per thread
+  for (int row0 = hc.r0 + t; row0 < hc.r1; row0 += NT * U) {
+    uint64_t code[U];
+    int ea[U], eb[U];
+#pragma unroll
+    for (int q = 0; q < U; q++) {
+      const int row = row0 + q * NT;
+      const bool ok = row < hc.r1;
+      code[q] = (ok && nd) ? __ldg(P.hcodes + row) : 0ull;
+      ea[q] = ok ? __ldg(rp + row - hc.r0) : 0;
+      eb[q] = ok ? __ldg(rp + row - hc.r0 + 1) : 0;
     }
-    float S = 0.0f;
-    const int a = rp[row - hc.r0], b = rp[row - hc.r0 + 1];
-    for (int e = a; e < b; e++) {
-      const uint32_t w = __ldg(P.ent + e);
-      S = lx_add(S, lx_mul(lx_f((uint16_t)(w >> 16)), sm.xm[w & 0xffffu]));
-    }
-    const float lg = lx_rbf(lx_add(D, S));
-    if (lg > bv) {
-      bv = lg;
-      bi = row;
+#pragma unroll
+    for (int q = 0; q < U; q++) {
+      const int row = row0 + q * NT;
+      if (row >= hc.r1) continue;
+      float D = 0.0f;
+      for (int g = 0; g < ng; g++) D = lx_add(D, sm.htg[g][(code[q] >> (8 * g)) & 255u]);
+      float S = 0.0f;
+      for (int e = ea[q]; e < eb[q]; e++) {
+        const uint32_t w = __ldg(P.ent + e);
+        S = lx_add(S, lx_mul(lx_f((uint16_t)(w >> 16)), sm.xm[w & 0xffffu]));
+      }
+      const float lg = lx_rbf(lx_add(D, S));
+      if (lg > bv) {
+        bv = lg;
+        bi = row;
+      }
     }
   }
 #pragma unroll
@@ -486,6 +650,33 @@ __device__ void head_part(const Dev& P, Smem& sm, int rank) {
     }
     sm.bestv = bv;
     sm.besti = bi;
+  }
+}
+
+// At the launch's end: every lazily kept conv window of this CTA's items becomes what the stock
+// steps would have left, [P(n-4), P(n-3), P(n-2), P(n-1)].
+__device__ void materialize(const Dev& P, const Run& run, Smem& sm, int s, int rank, int n) {
+  for (int L = 0; L < P.n_layers; L++) {
+    const lxb_layer ly = P.layers[L];
+    if (!ly.has_gdn) continue;
+    uint16_t* conv =
+        reinterpret_cast<uint16_t*>(run.state_ptrs[((size_t)s * P.n_layers + L) * 2 + 1]);
+    for (int k = 0; k < ly.n_items; k++) {
+      const lxb_item it = P.items[ly.item0 + k];
+      if (it.cta != rank) continue;
+      for (int c0 = it.n_eager; c0 < it.n_ch; c0 += LXB_NSLOT) {
+        const int c1 = min(it.n_ch, c0 + LXB_NSLOT);
+        lazy_proj(P, run, sm, it, conv, s, L, n - 4, INT_MIN, false, c0, c1, ly.ln_in);
+        for (int c = c0 + threadIdx.x; c < c1; c += NT) {
+          const uint32_t cc = __ldg(reinterpret_cast<const uint32_t*>(P.chans + it.ch0 + c) + 2);
+          const int i = c - c0;
+          *reinterpret_cast<uint2*>(conv + (size_t)cc * 4) =
+              make_uint2((uint32_t)sm.pw[0][i] | ((uint32_t)sm.pw[1][i] << 16),
+                         (uint32_t)sm.pw[2][i] | ((uint32_t)sm.pw[3][i] << 16));
+        }
+        __syncthreads();
+      }
+    }
   }
 }
 
@@ -519,15 +710,25 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       uint16_t* conv = reinterpret_cast<uint16_t*>(sp[1]);
       uint32_t* bm = run.bitmaps + ((size_t)s * P.n_layers + L) * LXB_NV * 8;
       const lxb_owner ow = P.owners[ly.owner0 + rank];
-      const float ss = block_ssq(sm, sm.x);
-      if (ly.has_gdn) norm_into(P, sm.xn, sm.x, ly.ln_in, ss);
-      if (ly.has_mlp) norm_into(P, sm.xm, sm.x, ly.ln_post, ss);
+      const float r = norm_factor(P, block_ssq(sm, sm.x));
+      if (ly.has_gdn) {
+        norm_into(P, sm.xn, sm.x, ly.ln_in, r);
+        // this step's GDN input row into the ring (each CTA its block; rank 0 the factor)
+        const size_t slot = ((size_t)s * P.n_layers + L) * 4 + (i & 3);
+        uint16_t* rg = run.ring + slot * H + rank * P.blk;
+        for (int k = t; k < P.blk / 2; k += NT) {
+          const float* xv = sm.x + rank * P.blk + 2 * k;
+          reinterpret_cast<uint32_t*>(rg)[k] = (uint32_t)lx_rb(xv[0]) | ((uint32_t)lx_rb(xv[1]) << 16);
+        }
+        if (rank == 0 && t == 0) run.ring_r[slot] = r;
+      }
+      if (ly.has_mlp) norm_into(P, sm.xm, sm.x, ly.ln_post, r);
       __syncthreads();
       bool wrote = false;
       if (ly.has_gdn) {
         for (int k = 0; k < ly.n_items; k++) {
           const lxb_item it = P.items[ly.item0 + k];
-          if (it.cta == rank) wrote |= gdn_item(P, sm, it, rec, conv, bm);
+          if (it.cta == rank) wrote |= gdn_item(P, run, sm, it, rec, conv, bm, s, L, i, ly.ln_in);
         }
       }
       if (wrote && t < C) *cluster.map_shared_rank(&sm.wflag[ph & 1], t) = 1;
@@ -543,8 +744,8 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         pull(P, sm, ph & 1, cluster);
         ph++;
         if (ly.has_mlp) {
-          const float ss2 = block_ssq(sm, sm.x);
-          norm_into(P, sm.xm, sm.x, ly.ln_post, ss2);
+          const float r2 = norm_factor(P, block_ssq(sm, sm.x));
+          norm_into(P, sm.xm, sm.x, ly.ln_post, r2);
           __syncthreads();
           mlp_owner(P, sm, ow, rank, sm.own[ph & 1]);
           cluster.sync();
@@ -558,8 +759,8 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     }
     // the output head: every CTA its rows, then the first maximum over the cluster
     {
-      const float ss = block_ssq(sm, sm.x);
-      norm_into(P, sm.xm, sm.x, P.final_norm, ss);
+      const float r = norm_factor(P, block_ssq(sm, sm.x));
+      norm_into(P, sm.xm, sm.x, P.final_norm, r);
       __syncthreads();
       head_part(P, sm, rank);
       cluster.sync();
@@ -593,6 +794,8 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       if (i + 1 < run.n_tokens) load_embed(run, P, sm, sm.tok);
     }
   }
+  cluster.sync();  // every ring write of the launch is visible cluster-wide
+  materialize(P, run, sm, s, rank, run.n_tokens);
   cluster.sync();  // no CTA leaves while another may still read its shared memory
 }
 
@@ -749,12 +952,15 @@ int validate(const View& v, int cluster) {
         return LXB_E_IMAGE;
       if (per_cta[it.cta] & (1 << it.slot)) return LXB_E_IMAGE;  // one item per (cta, slot)
       per_cta[it.cta] |= 1 << it.slot;
-      if (it.ch0 < 0 || it.n_ch < 0 || it.n_ch > LXB_NSLOT * 2 ||
+      if (it.ch0 < 0 || it.n_ch < 0 || it.n_ch > LXB_NSLOT || it.n_eager < 0 ||
+          it.n_vneed < 0 || it.n_eager + it.n_vneed > it.n_ch ||
           (int64_t)it.ch0 + it.n_ch > v.n(LXB_SEC_CHANS))
         return LXB_E_IMAGE;
       for (int c = 0; c < it.n_ch; c++) {
         const lxb_chan& ch = chans[it.ch0 + c];
-        if (ch.conv_ch >= LXB_CONV || (ch.slot != LXB_NOSLOT && ch.slot >= LXB_NSLOT) ||
+        const bool computed = c < it.n_eager + it.n_vneed;  // these write their q|k|v slot
+        if (ch.conv_ch >= LXB_CONV || ch.tapmask > 15 ||
+            (computed ? ch.slot >= LXB_NSLOT : (ch.slot != LXB_NOSLOT && ch.slot >= LXB_NSLOT)) ||
             !ent_idx(v, ch.ent, ch.n, H))
           return LXB_E_IMAGE;
       }
@@ -884,14 +1090,24 @@ extern "C" int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb
   return LXB_OK;
 }
 
+static size_t ring_bytes(const lxb_plan* p, int n_streams) {
+  return (size_t)n_streams * p->hdr.n_layers * 4 * H * sizeof(uint16_t);
+}
+
+extern "C" size_t lxb_scratch_bytes(const lxb_plan* p, int n_streams) {
+  if (!p || n_streams < 1) return 0;
+  return ring_bytes(p, n_streams) + (size_t)n_streams * p->hdr.n_layers * 4 * sizeof(float);
+}
+
 extern "C" int lxb_decode(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitmaps,
-                          int sync_bitmaps, const uint16_t* embed, int n_streams,
+                          int sync_bitmaps, void* scratch, const uint16_t* embed, int n_streams,
                           const int32_t* forced, int n_forced, int n_tokens, int32_t* preds,
                           int32_t* inputs, void* cuda_stream) {
-  if (!p || !state_ptrs || !bitmaps || !embed || !forced || !preds || n_streams < 1 ||
-      n_forced < 1 || n_tokens < 1 || n_streams > 65535)
+  if (!p || !state_ptrs || !bitmaps || !scratch || !embed || !forced || !preds ||
+      n_streams < 1 || n_forced < 1 || n_tokens < 1 || n_streams > 65535)
     return LXB_E_INVAL;
-  if ((reinterpret_cast<uintptr_t>(embed) & 15) || (reinterpret_cast<uintptr_t>(bitmaps) & 15))
+  if ((reinterpret_cast<uintptr_t>(embed) & 15) || (reinterpret_cast<uintptr_t>(bitmaps) & 15) ||
+      (reinterpret_cast<uintptr_t>(scratch) & 15))
     return LXB_E_INVAL;
   cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
   cudaError_t e;
@@ -900,7 +1116,10 @@ extern "C" int lxb_decode(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bit
         state_ptrs, bitmaps, p->dev.layers, p->hdr.n_layers);
     if ((e = cudaGetLastError())) return cuda_rc(e);
   }
-  Run run{state_ptrs, bitmaps, embed, forced, n_forced, n_tokens, preds, inputs};
+  uint16_t* ring = static_cast<uint16_t*>(scratch);
+  float* ring_r = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) +
+                                           ring_bytes(p, n_streams));
+  Run run{state_ptrs, bitmaps, ring, ring_r, embed, forced, n_forced, n_tokens, preds, inputs};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;

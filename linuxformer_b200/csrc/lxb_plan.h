@@ -15,7 +15,7 @@
 #include <stdint.h>
 
 #define LXB_MAGIC 0x50425a4cu  // "LZBP"
-#define LXB_IMAGE_VERSION 2
+#define LXB_IMAGE_VERSION 3
 
 #define LXB_H 2560
 #define LXB_KD 256
@@ -86,7 +86,12 @@ typedef struct {
   int32_t rows;            // i32 pool: (entry offset, count) pairs: 8 beta, 8 a, 1024 z rows
   int32_t params;          // u16 pool: A_log[8], dt_bias[8], gated-norm weight[128]
   int32_t flags;           // LXB_IT_*
-  int32_t pad[3];
+  int32_t n_eager;         // chans [ch0, ch0 + n_eager): query/key channels with a nonzero tap,
+                           // evaluated every step
+  int32_t n_vneed;         // then value channels with a nonzero tap: evaluated on the steps a key
+                           // fires; every channel from n_eager on keeps its conv window lazily
+                           // (recomputed from the residual ring at the launch's end)
+  int32_t pad;
 } lxb_item;  // 48 bytes
 
 typedef struct {
@@ -94,7 +99,8 @@ typedef struct {
   uint16_t n, slot;        // entry count; place in q | k | v (LXB_NOSLOT: window only)
   uint32_t conv_ch;        // the channel's index in the layer's conv state
   uint32_t t01, t23;       // conv taps 0..3, bf16 pairs (low half first)
-  uint32_t pad[3];
+  uint32_t tapmask;        // bit j: tap j is nonzero
+  uint32_t pad[2];
 } lxb_chan;  // 32 bytes: two aligned 16-byte loads
 
 typedef struct {

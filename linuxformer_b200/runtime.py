@@ -33,6 +33,7 @@ class DeviceStates:
     conv: torch.Tensor
     ptrs: torch.Tensor      # int64 [S, L, 2]
     bitmaps: torch.Tensor   # int32 [S, L, 128, 8]
+    scratch: torch.Tensor   # uint8, lxb_scratch_bytes(plan, S)
 
     @property
     def n_streams(self) -> int:
@@ -98,19 +99,28 @@ class Decoder:
         ptrs = state_pointers([[rec[s, L] for L in range(nl)] for s in range(S)],
                               [[conv[s, L] for L in range(nl)] for s in range(S)], self.dev)
         bm = torch.zeros((S, nl, C.NV, 8), dtype=torch.int32, device=self.dev)
-        return DeviceStates(rec, conv, ptrs, bm)
+        return DeviceStates(rec, conv, ptrs, bm, self.scratch(S))
+
+    def scratch(self, n_streams: int) -> torch.Tensor:
+        """The device scratch one launch of n_streams streams needs."""
+        nb = lib().lxb_scratch_bytes(self.plan, n_streams)
+        return torch.empty(nb, dtype=torch.uint8, device=self.dev)
 
     def launch(self, ptrs: torch.Tensor, bitmaps: torch.Tensor, forced: torch.Tensor, n: int,
                preds: torch.Tensor, inputs: torch.Tensor | None, sync_bitmaps: bool = True,
-               stream=None) -> None:
+               stream=None, scratch: torch.Tensor | None = None) -> None:
         """Raw launch on device tensors (no host sync): forced int32 [S, nf], preds [S, n]."""
         S = forced.shape[0]
         assert forced.dtype == torch.int32 and forced.is_contiguous() and forced.dim() == 2
         assert preds.dtype == torch.int32 and preds.shape == (S, n) and preds.is_contiguous()
         assert ptrs.shape == (S, self.chip.n_layers, 2) and bitmaps.shape[0] == S
+        if scratch is None:
+            scratch = self.scratch(S)
+        assert scratch.numel() >= lib().lxb_scratch_bytes(self.plan, S)
         st = (stream or torch.cuda.current_stream(self.dev)).cuda_stream
         check(lib().lxb_decode(self.plan, ptrs.data_ptr(), bitmaps.data_ptr(), int(sync_bitmaps),
-                               self.embed.data_ptr(), S, forced.data_ptr(), forced.shape[1], n,
+                               scratch.data_ptr(), self.embed.data_ptr(), S, forced.data_ptr(),
+                               forced.shape[1], n,
                                preds.data_ptr(),
                                inputs.data_ptr() if inputs is not None else None, st),
               "lxb_decode")
@@ -139,7 +149,8 @@ class Decoder:
         fh.numpy()[...] = forced
         fd = fh.to(self.dev, non_blocking=True)
         preds = torch.empty((S, n), dtype=torch.int32, device=self.dev)
-        self.launch(states.ptrs, states.bitmaps, fd, n, preds, None, sync_bitmaps)
+        self.launch(states.ptrs, states.bitmaps, fd, n, preds, None, sync_bitmaps,
+                    scratch=states.scratch)
         ph = self._pinned("p", (S, n))
         ph.copy_(preds, non_blocking=True)
         torch.cuda.current_stream(self.dev).synchronize()
@@ -157,7 +168,7 @@ class Decoder:
                             device=self.dev)
         preds = torch.empty((states.n_streams, n), dtype=torch.int32, device=self.dev)
         inputs = torch.empty_like(preds)
-        self.launch(states.ptrs, states.bitmaps, f, n, preds, inputs)
+        self.launch(states.ptrs, states.bitmaps, f, n, preds, inputs, scratch=states.scratch)
         torch.cuda.synchronize(self.dev)
         e = self.status()
         if e.status:

@@ -24,7 +24,7 @@ import numpy as np
 from . import chip as C
 
 MAGIC = 0x50425A4C
-VERSION = 2
+VERSION = 3
 NSLOT, NOSLOT = 1536, 0xFFFF
 ITEMSLOTS, MAXDENSE, MAXUNITS = 4, 32, 4096
 IT_DECAYS, IT_OUT = 1, 2
@@ -34,9 +34,10 @@ LAYER = np.dtype([(n, "<i4") for n in ("has_gdn", "has_mlp", "ln_in", "ln_post",
                                        "n_items", "owner0", "itemof", "decays", "p0", "p1",
                                        "p2")])
 ITEM = np.dtype([(n, "<i4") for n in ("layer", "kh", "cta", "slot", "ch0", "n_ch", "rows",
-                                      "params", "flags", "p0", "p1", "p2")])
+                                      "params", "flags", "n_eager", "n_vneed", "p0")])
 CHAN = np.dtype([("ent", "<u4"), ("n", "<u2"), ("slot", "<u2"), ("conv_ch", "<u4"),
-                 ("t01", "<u4"), ("t23", "<u4"), ("p0", "<u4"), ("p1", "<u4"), ("p2", "<u4")])
+                 ("t01", "<u4"), ("t23", "<u4"), ("tapmask", "<u4"), ("p1", "<u4"),
+                 ("p2", "<u4")])
 UNIT = np.dtype([("g", "<u4"), ("u", "<u4"), ("ng", "<u2"), ("nu", "<u2"), ("pad", "<u4")])
 OWNER = np.dtype([("unit0", "<i4"), ("n_units", "<i4"), ("mrow", "<i4"), ("orow", "<i4")])
 HEADCTA = np.dtype([("r0", "<i4"), ("r1", "<i4"), ("rowptr", "<i4"), ("pad", "<i4")])
@@ -131,6 +132,12 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
         for k, kh in enumerate(heads):
             pos = k + rot
             sel = np.nonzero(kh_of == kh)[0]
+            # order: eager (query/key with a tap) | value with a tap | the rest (window only)
+            tapped = (ly.conv[live[sel]] & 0x7FFF).any(1)
+            isqk = slot_of[sel] < 2 * C.KD
+            cls = np.where(tapped & isqk, 0, np.where(tapped, 1, 2))
+            order = np.argsort(cls, kind="stable")
+            sel, cls = sel[order], cls[order]
             chs = live[sel]
             ch = np.zeros(len(chs), CHAN)
             ch["ent"] = qkv_ent0 + qkv.indptr[chs]
@@ -140,6 +147,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
             taps = ly.conv[chs].astype(np.uint32)
             ch["t01"] = taps[:, 0] | (taps[:, 1] << 16)
             ch["t23"] = taps[:, 2] | (taps[:, 3] << 16)
+            ch["tapmask"] = ((taps & 0x7FFF) != 0).astype(np.uint32) @ (1 << np.arange(4))
             assert len(chs) <= 2 * NSLOT
             ch0 = sum(len(c) for c in chans)
             chans.append(ch)
@@ -155,6 +163,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
             it = np.zeros(1, ITEM)[0]
             it["layer"], it["kh"], it["cta"], it["slot"] = L, kh, pos % Cn, pos // Cn
             it["ch0"], it["n_ch"] = ch0, len(chs)
+            it["n_eager"], it["n_vneed"] = int((cls == 0).sum()), int((cls == 1).sum())
             it["rows"] = i32.add(refs)
             it["params"] = u16.add(np.concatenate([ly.A_log[vh], ly.dt_bias[vh], ly.gnorm]))
             it["flags"] = (IT_DECAYS if decays_vh[vh].any() else 0) | \

@@ -66,5 +66,5 @@ def test_invalid_arguments():
     L = lib()
     p = ctypes.c_void_p()
     assert L.lxb_plan_create(None, 0, 16, ctypes.byref(p)) == -1
-    assert L.lxb_decode(None, None, None, 0, None, 1, None, 1, 1, None, None, None) == -1
+    assert L.lxb_decode(None, None, None, 0, None, None, 1, None, 1, 1, None, None, None) == -1
     assert L.lxb_error_string(-2) == b"malformed plan image"

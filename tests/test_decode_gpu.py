@@ -96,3 +96,24 @@ def test_c2_matches_oracle():
     p, _, _ = Oracle(chip).decode(host, [0], n)
     assert (preds[0].cpu().numpy() == p).all()
     _same_state(ds, 0, host)
+
+
+@pytest.mark.parametrize("which", ["c1", "c2"])
+def test_chained_short_launches(c1_chip, which):
+    """Launches of 1, 2, 5, 3 and 7 steps, each continuing from the last prediction (as
+    Linux.run_alone chains Mega.run): the lazily kept conv windows are rebuilt at every launch's
+    end, including launches shorter than the window; the whole equals one continuous run."""
+    chip = c1_chip if which == "c1" else C.c2(1, vocab=20000)
+    st0 = C.c1_state(chip, 0) if which == "c1" else C.c2_state(chip, 1)
+    dec = _decoder(chip, 16)
+    ds = dec.states([st0])
+    got, last = [], 0
+    for n in (1, 2, 5, 3, 7):
+        preds, _ = dec.run(ds, [[last]], n)
+        p = preds[0].cpu().numpy().tolist()
+        got += p
+        last = p[-1]
+    host = st0.copy()
+    want, _, _ = Oracle(chip).decode(host, [0], len(got))
+    assert got == want.tolist()
+    _same_state(ds, 0, host)
