@@ -296,6 +296,7 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const lxb_item&
     const float b = lx_rbf(dotb(P.ent, (uint32_t)rows[2 * r], rows[2 * r + 1], sm.xn));
     sm.beta[r] = lx_rbf(lx_sigmoid(b));
   }
+  __syncthreads();  // the predicates below read other threads' slots: evaluated before the barrier
   const int qa = __syncthreads_or(t < KD && sm.buf[t] != 0.0f);
   const int ka = __syncthreads_or(t >= KD && t < 2 * KD && sm.buf[t] != 0.0f);
   int anyg = 0;

@@ -148,6 +148,8 @@ typedef struct {
   int dense_cols[32];
   int n_dense;
   int64_t* cnt;  // this step's counters (LXO_C_*), or NULL
+  float* xin;    // this step's GDN input rows [n_layers][H], or NULL
+  int32_t* act;  // this step's per-(layer, key head) activity bits, [n_layers][16], or NULL
 } lxo_run;
 
 // per-step activity counters: what the step logically reads and writes (the bench's algorithmic
@@ -175,6 +177,7 @@ static void gdn_layer(lxo_run* st, int L) {
   const lxo_layer* ly = &chip->layers[L];
   float* x = st->x;
   float* xn = st->xn;
+  if (st->xin) memcpy(st->xin + (size_t)L * H, x, sizeof(float) * H);
   rms_norm(x, ly->ln_in, chip->eps, xn);
   // in_proj_qkv, then torch_causal_conv1d_update: window [w0 w1 w2 w3] -> [w1 w2 w3 P],
   // out = silu(conv over the new window) in bf16
@@ -222,6 +225,7 @@ static void gdn_layer(lxo_run* st, int L) {
     float qn[KD], kn[KD];
     if (qa) l2norm_bf16(q, KD, qn);
     if (ka) l2norm_bf16(k, KD, kn);
+    int anyg_h = 0, out_h = 0;
     for (int r = 0; r < RR; r++) {
       const int vh = kh * RR + r;
       // beta = sigmoid(in_proj_b(x)) in bf16; g = -exp(A_log) * softplus(a + dt_bias) in fp32
@@ -230,6 +234,7 @@ static void gdn_layer(lxo_run* st, int L) {
       const float a = lx_rbf(row_dot(&ly->a, vh, xn));
       const float A = -lx_exp(lx_f(ly->A_log[vh]));
       const float g = lx_mul(A, lx_softplus(lx_add(a, lx_f(ly->dt_bias[vh]))));
+      anyg_h |= g != 0.0f;
       c_ba += ly->a.indptr[vh + 1] - ly->a.indptr[vh];
       if (!qa && !ka && g == 0.0f) continue;  // the state stays, o = 0
       c_ba += ly->b.indptr[vh + 1] - ly->b.indptr[vh];
@@ -278,7 +283,10 @@ static void gdn_layer(lxo_run* st, int L) {
       }
       any_out = 1;
       c_out++;
+      out_h |= 1 << r;
     }
+    if (st->act)
+      st->act[(size_t)L * NK + kh] = qa | (ka << 1) | (anyg_h << 2) | (out_h << 8);
   }
   if (st->cnt) {
     st->cnt[LXO_C_CHANS] += n_ch;
@@ -464,7 +472,7 @@ static int head_argmax(lxo_run* st, float* margin_out) {
 // token id.
 int lxo_decode(const lxo_chip* chip, float* rec, uint16_t* conv, const int32_t* forced,
                int n_forced, int n_tokens, int32_t* preds, int32_t* inputs, float* margins,
-               float* resid, int64_t* counts) {
+               float* resid, int64_t* counts, float* xin, int32_t* act) {
   lxo_run* st = (lxo_run*)calloc(1, sizeof(lxo_run));
   st->chip = chip;
   st->rec = rec;
@@ -480,6 +488,8 @@ int lxo_decode(const lxo_chip* chip, float* rec, uint16_t* conv, const int32_t* 
     }
     if (inputs) inputs[i] = tok;
     st->cnt = counts ? counts + (size_t)i * LXO_C_N : NULL;
+    st->xin = xin ? xin + (size_t)i * chip->n_layers * H : NULL;
+    st->act = act ? act + (size_t)i * chip->n_layers * NK : NULL;
     const uint16_t* e = chip->embed + ((int64_t)tok + chip->offset) * H;
     for (int c = 0; c < H; c++) st->x[c] = lx_f(e[c]);
     for (int L = 0; L < chip->n_layers; L++) {

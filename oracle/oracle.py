@@ -53,7 +53,7 @@ def lib():
             build()
         _lib = ctypes.CDLL(str(LIB))
         _lib.lxo_decode.restype = ctypes.c_int
-        _lib.lxo_decode.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, P, P, P, P, P]
+        _lib.lxo_decode.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, P, P, P, P, P, P, P]
         for f in ("lxo_exp", "lxo_log1p", "lxo_silu", "lxo_sigmoid", "lxo_softplus"):
             getattr(_lib, f).restype = ctypes.c_float
             getattr(_lib, f).argtypes = [ctypes.c_float]
@@ -102,9 +102,12 @@ class Oracle:
     COUNTERS = ("chans", "qkv_ent", "ba_ent", "z_ent", "rows", "out_ent", "gu_ent", "down_ent",
                 "head_bytes", "vh_active", "vh_write", "vh_out", "gdn_write")
 
-    def decode(self, state, forced, n: int, resid: bool = False, counts: bool = False):
+    def decode(self, state, forced, n: int, resid: bool = False, counts: bool = False,
+               xin: bool = False, act: bool = False):
         """n steps of the model alone from `state` (a chip.State, updated in place). Returns
-        (preds, inputs, margins[, resid][, counts]); counts: int64 [n, len(COUNTERS)]."""
+        (preds, inputs, margins[, resid][, counts][, xin]); counts: int64 [n, len(COUNTERS)];
+        xin: each step's GDN input rows, float32 [n, n_layers, 2560]; act: per (step, layer,
+        key head) bits: 1 query, 2 key, 4 decay, value heads with output << 8."""
         assert state.recurrent.dtype == np.float32 and state.conv.dtype == np.uint16
         assert state.recurrent.flags["C_CONTIGUOUS"] and state.conv.flags["C_CONTIGUOUS"]
         f = np.ascontiguousarray(forced, np.int32)
@@ -113,10 +116,13 @@ class Oracle:
         margins = np.zeros(n, np.float32)
         rs = np.zeros((n, 2560), np.float32) if resid else None
         cn = np.zeros((n, len(self.COUNTERS)), np.int64) if counts else None
+        xi = np.zeros((n, self.chip.n_layers, 2560), np.float32) if xin else None
+        ac = np.zeros((n, self.chip.n_layers, 16), np.int32) if act else None
         rc = lib().lxo_decode(ctypes.addressof(self._chip), _ptr(state.recurrent),
                               _ptr(state.conv), _ptr(f), len(f), n, _ptr(preds), _ptr(inputs),
                               _ptr(margins), _ptr(rs) if resid else None,
-                              _ptr(cn) if counts else None)
+                              _ptr(cn) if counts else None, _ptr(xi) if xin else None,
+                              _ptr(ac) if act else None)
         if rc:
             raise ValueError("oracle: token id out of the embedding's range")
         out = (preds, inputs, margins)
@@ -124,4 +130,8 @@ class Oracle:
             out += (rs,)
         if counts:
             out += (cn,)
+        if xin:
+            out += (xi,)
+        if act:
+            out += (ac,)
         return out
