@@ -87,6 +87,14 @@ size_t lxb_scratch_bytes(const lxb_plan* plan, int n_streams);
 int lxb_status(lxb_plan* plan, lxb_error* err);
 int lxb_status_clear(lxb_plan* plan);
 
+/* Per-section cycle counters (the reference's Mega.run(prof=...), lx/csrc/mega.cu:717-737):
+ * with a DEVICE buffer of n_streams * cluster * lxb_profile_sections() uint64, every later
+ * lxb_decode adds, per stream and CTA, the clock64 cycles spent in each section (norms, GDN
+ * items, MLP, barrier, pull, write fix-ups, head, embedding) and two counts (fix-up steps,
+ * tokens). NULL turns it off (the default). */
+int lxb_plan_set_profile(lxb_plan* plan, unsigned long long* prof);
+int lxb_profile_sections(void);
+
 /* Bytes of the plan's device tables; the number of co-resident clusters for this plan. */
 size_t lxb_plan_bytes(const lxb_plan* plan);
 int lxb_plan_max_clusters(const lxb_plan* plan);

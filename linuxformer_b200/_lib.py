@@ -34,6 +34,8 @@ SIGNATURES = {
     "lxb_decode": (I, [P, P, P, I, P, P, I, P, I, I, P, P, P]),
     "lxb_scratch_bytes": (ctypes.c_size_t, [P, I]),
     "lxb_status": (I, [P, P]),
+    "lxb_plan_set_profile": (I, [P, P]),
+    "lxb_profile_sections": (I, []),
     "lxb_status_clear": (I, [P]),
     "lxb_plan_bytes": (ctypes.c_size_t, [P]),
     "lxb_plan_max_clusters": (I, [P]),

@@ -84,6 +84,22 @@ struct Run {
   int n_forced, n_tokens;
   int32_t* preds;
   int32_t* inputs;
+  unsigned long long* prof;  // optional: [stream][cta][LXB_PROF_N] cycle counters, accumulated
+};
+
+// profile sections (lxb_plan_set_profile): cycles spent per CTA
+enum {
+  PR_NORM,     // sum of squares, norms, ring write
+  PR_ITEMS,    // GDN items
+  PR_MLP,      // MLP owner (the paired step)
+  PR_SYNC,     // the paired step's cluster barrier
+  PR_PULL,     // pulling the residual after a step
+  PR_FIXUP,    // a write's out_proj step and MLP redo, barriers included
+  PR_HEAD,     // the head: norm, rows, barrier, reduce
+  PR_EMBED,    // the next token's embedding
+  PR_FIXUPS,   // count: fix-up steps
+  PR_TOKENS,   // count: tokens
+  PR_N
 };
 
 struct __align__(16) Smem {
@@ -701,6 +717,19 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
   __syncthreads();
   cluster.sync();  // every CTA's flags are initialised before anyone may push one
   int ph = 0;
+  unsigned long long pc[PR_N];
+#pragma unroll
+  for (int k = 0; k < PR_N; k++) pc[k] = 0;
+  long long c0 = clock64();
+  const bool prof = run.prof != nullptr;
+#define PROF(sec)                                \
+  do {                                           \
+    if (prof) {                                  \
+      const long long c1 = clock64();            \
+      pc[sec] += (unsigned long long)(c1 - c0);  \
+      c0 = c1;                                   \
+    }                                            \
+  } while (0)
   load_embed(run, P, sm, sm.tok);
   for (int i = 0; i < run.n_tokens; i++) {
     if (rank == 0 && t == 0 && run.inputs) run.inputs[(size_t)s * run.n_tokens + i] = sm.tok;
@@ -725,6 +754,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       }
       if (ly.has_mlp) norm_into(P, sm.xm, sm.x, ly.ln_post, r);
       __syncthreads();
+      PROF(PR_NORM);
       bool wrote = false;
       if (ly.has_gdn) {
         for (int k = 0; k < ly.n_items; k++) {
@@ -733,11 +763,15 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         }
       }
       if (wrote && t < C) *cluster.map_shared_rank(&sm.wflag[ph & 1], t) = 1;
+      PROF(PR_ITEMS);
       if (ly.has_mlp) mlp_owner(P, sm, ow, rank, sm.own[ph & 1]);
+      PROF(PR_MLP);
       cluster.sync();
+      PROF(PR_SYNC);
       const int fl = *reinterpret_cast<volatile int*>(&sm.wflag[ph & 1]);
       __syncthreads();
       if (fl) {
+        pc[PR_FIXUPS]++;
         if (t == 0) sm.wflag[ph & 1] = 0;
         ph++;
         out_owner(P, sm, ly, ow, rank, sm.own[ph & 1], cluster);
@@ -753,9 +787,11 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
           pull(P, sm, ph & 1, cluster);
           ph++;
         }
+        PROF(PR_FIXUP);
       } else {
         if (ly.has_mlp) pull(P, sm, ph & 1, cluster);
         ph++;
+        PROF(PR_PULL);
       }
     }
     // the output head: every CTA its rows, then the first maximum over the cluster
@@ -792,8 +828,17 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         }
       }
       __syncthreads();
+      PROF(PR_HEAD);
       if (i + 1 < run.n_tokens) load_embed(run, P, sm, sm.tok);
+      PROF(PR_EMBED);
+      pc[PR_TOKENS]++;
     }
+  }
+#undef PROF
+  if (prof && t == 0) {
+    unsigned long long* d = run.prof + ((size_t)s * C + rank) * PR_N;
+#pragma unroll
+    for (int k = 0; k < PR_N; k++) d[k] += pc[k];
   }
   cluster.sync();  // every ring write of the launch is visible cluster-wide
   materialize(P, run, sm, s, rank, run.n_tokens);
@@ -832,6 +877,7 @@ struct lxb_plan {
   Dev dev;
   uint32_t* status;
   int max_clusters;
+  unsigned long long* prof;
 };
 
 static_assert(offsetof(Smem, own) % 16 == 0 && offsetof(Smem, on) % 16 == 0 &&
@@ -1120,7 +1166,8 @@ extern "C" int lxb_decode(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bit
   uint16_t* ring = static_cast<uint16_t*>(scratch);
   float* ring_r = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) +
                                            ring_bytes(p, n_streams));
-  Run run{state_ptrs, bitmaps, ring, ring_r, embed, forced, n_forced, n_tokens, preds, inputs};
+  Run run{state_ptrs, bitmaps, ring, ring_r, embed, forced, n_forced, n_tokens, preds, inputs,
+          p->prof};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -1152,6 +1199,14 @@ extern "C" int lxb_status_clear(lxb_plan* p) {
   if (!p) return LXB_E_INVAL;
   return cuda_rc(cudaMemset(p->status, 0, 16));
 }
+
+extern "C" int lxb_plan_set_profile(lxb_plan* p, unsigned long long* prof) {
+  if (!p) return LXB_E_INVAL;
+  p->prof = prof;
+  return LXB_OK;
+}
+
+extern "C" int lxb_profile_sections(void) { return PR_N; }
 
 extern "C" size_t lxb_plan_bytes(const lxb_plan* p) { return p ? p->bytes : 0; }
 extern "C" int lxb_plan_max_clusters(const lxb_plan* p) { return p ? p->max_clusters : 0; }

@@ -125,6 +125,19 @@ class Decoder:
                                inputs.data_ptr() if inputs is not None else None, st),
               "lxb_decode")
 
+    PROFILE = ("norm", "items", "mlp", "sync", "pull", "fixup", "head", "embed", "fixups",
+               "tokens")
+
+    def set_profile(self, buf: torch.Tensor | None) -> None:
+        """Accumulate per-section cycle counters into buf (int64 [S, cluster, 10]) on every
+        later launch; None stops it."""
+        if buf is not None:
+            assert buf.dtype == torch.int64 and buf.is_contiguous()
+            assert buf.shape[-1] == lib().lxb_profile_sections() == len(self.PROFILE)
+        check(lib().lxb_plan_set_profile(self.plan, buf.data_ptr() if buf is not None else None),
+              "lxb_plan_set_profile")
+        self._prof = buf
+
     def status(self) -> Err:
         e = Err()
         check(lib().lxb_status(self.plan, ctypes.byref(e)), "lxb_status")
