@@ -33,6 +33,7 @@ extern "C" {
 
 /* device status bits (lxb_status) */
 #define LXB_S_TOKEN 1u       /* a token id outside the embedding: clamped, the stream is invalid */
+#define LXB_S_STAGE 2u       /* a staging copy did not land within 2 s: later steps skipped */
 
 typedef struct lxb_plan lxb_plan;
 

@@ -53,6 +53,7 @@ namespace cg = cooperative_groups;
 #define VD LXB_VD
 #define R LXB_R
 #define BLKMAX (LXB_H / LXB_MINC)
+#define LXB_MAXLAYERS 64
 
 struct Dev {
   const lxb_layer* layers;
@@ -72,6 +73,10 @@ struct Dev {
   float htab[4];
   int dense_cols[LXB_MAXDENSE];
   uint32_t* status;  // [0] bits, [1] first stream, [2] first step
+  const unsigned char* blobs;  // the step blobs
+  const lxb_blobref* blobidx;  // [(n_layers + 1) * C]
+  int nbuf;                    // staging buffers in shared memory (1 or 2)
+  int stage;                   // bytes per staging buffer
 };
 
 struct Run {
@@ -99,6 +104,7 @@ enum {
   PR_EMBED,    // the next token's embedding
   PR_FIXUPS,   // count: fix-up steps
   PR_TOKENS,   // count: tokens
+  PR_WAIT,     // waiting for a staged blob
   PR_N
 };
 
@@ -106,7 +112,6 @@ struct __align__(16) Smem {
   alignas(16) float x[H];          // the residual replica (bf16 values)
   float xn[H];                     // input_layernorm(x) (bf16 values)
   float xm[H];                     // post_attention_layernorm(x) or the final norm
-  float xr[H];                     // input_layernorm of an earlier step's residual (lazy windows)
   alignas(16) float own[2][BLKMAX];  // this CTA's rows after the step, by step parity
   float buf[LXB_NSLOT];            // an item's q | k | v
   float qval[KD], kval[KD];        // nonzero l2-normed query (x 1/16) and key values
@@ -121,13 +126,22 @@ struct __align__(16) Smem {
   alignas(16) uint16_t on[LXB_ITEMSLOTS][R * VD];  // the gated norm's output per item slot
   union {
     alignas(16) uint16_t onall[LXB_NK][R * VD];  // gathered for the out_proj step
-    uint16_t pw[4][LXB_NSLOT];     // lazy channels: their projections at 4 steps
+    struct {
+      float xr[H];                 // input_layernorm of an earlier step's residual
+      uint16_t pw[4][LXB_NSLOT];   // lazy channels: their projections at 4 steps
+    } lz;
   };
   float hbuf[LXB_MAXUNITS];        // MLP unit outputs
   float htg[LXB_MAXDENSE / 4][256];  // head: per group of 4 dense columns, each code's sum
   float bestv;
   int besti;
   int tok;
+  int broken;                      // a staging wait gave up: blobs are not used any more
+  alignas(8) unsigned long long mbar[2];  // staging buffers' transaction barriers
+  lxb_layer layers[LXB_MAXLAYERS];  // the layer descriptors
+  uint64_t sptr[LXB_MAXLAYERS][2];  // this stream's state pointers per layer
+  lxb_blobref bref[LXB_MAXLAYERS + 1];  // this CTA's step blobs (the head's last)
+  lxb_headcta hc;                   // this CTA's head rows
 };
 
 // --- block reductions in the canonical orders -------------------------------------------------
@@ -162,11 +176,66 @@ __device__ __forceinline__ float norm_factor(const Dev& P, float ss) {
   return lx_rsqrt(lx_add(lx_div(ss, (float)H), P.eps));
 }
 
-// Qwen3_5RMSNorm with the factor r: out[c] = bf16(x[c] * r * (1 + w[c]))
-__device__ void norm_into(const Dev& P, float* out, const float* x, int w_off, float r) {
-  const uint16_t* w = P.u16 + w_off;
+// Qwen3_5RMSNorm with the factor r: out[c] = bf16(x[c] * r * (1 + w[c])), w the bf16 weight
+// (a staged copy in shared memory)
+__device__ void norm_into(float* out, const float* x, const uint16_t* w, float r) {
   for (int c = threadIdx.x; c < H; c += NT)
-    out[c] = lx_rbf(lx_mul(lx_mul(x[c], r), lx_add(1.0f, lx_f(__ldg(w + c)))));
+    out[c] = lx_rbf(lx_mul(lx_mul(x[c], r), lx_add(1.0f, lx_f(w[c]))));
+}
+
+// --- staging: bulk copies (TMA) of the next step's blob into shared memory --------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void stage_issue(const Dev& P, Smem& sm, unsigned char* stage, int buf,
+                                            int L) {
+  const lxb_blobref br = sm.bref[L];
+  unsigned char* dst = stage + (size_t)buf * P.stage;
+  const unsigned char* src = P.blobs + br.off;
+  const uint32_t mb = smem_u32(&sm.mbar[buf]);
+  // the buffer was last read through the generic proxy; order that before the async writes
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mb),
+               "r"((uint32_t)br.bytes)
+               : "memory");
+  for (int o = 0; o < br.bytes; o += 32768) {
+    const uint32_t n = (uint32_t)min(32768, br.bytes - o);
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst + o)), "l"(src + o), "r"(n), "r"(mb)
+        : "memory");
+  }
+}
+
+// wait for a staging buffer (bounded by the global timer: a copy that never lands sets the
+// status and stops every later use of the staged blobs instead of spinning forever)
+__device__ __forceinline__ bool stage_wait(const Dev& P, Smem& sm, int buf, uint32_t phase,
+                                           int s, int step) {
+  const uint32_t mb = smem_u32(&sm.mbar[buf]);
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(mb), "r"(phase)
+        : "memory");
+    if (ok) return true;
+    unsigned long long t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (t1 - t0 > 2000000000ull) {  // 2 s
+      if (threadIdx.x == 0) {
+        if (atomicOr(P.status, LXB_S_STAGE) == 0) {
+          P.status[1] = (uint32_t)s;
+          P.status[2] = (uint32_t)step;
+        }
+      }
+      return false;
+    }
+  }
 }
 
 // sequential dot over entries [e0, e0 + n) (column | bf16 << 16), loads issued 8 at a time
@@ -215,34 +284,34 @@ __device__ __forceinline__ void set_status(const Dev& P, uint32_t bit, int strea
   }
 }
 
-// sm.xr = input_layernorm of step tau's residual at layer L, from the ring
+// sm.lz.xr = input_layernorm of step tau's residual at layer L, from the ring
 __device__ void build_xr(const Dev& P, const Run& run, Smem& sm, int s, int L, int tau,
-                         int w_off) {
+                         const uint16_t* w) {
   const size_t slot = ((size_t)s * P.n_layers + L) * 4 + (tau & 3);
   const uint4* xs = reinterpret_cast<const uint4*>(run.ring + slot * H);
   const float r = __ldcg(run.ring_r + slot);
   for (int k = threadIdx.x; k < H / 8; k += NT) {
     const uint4 v = __ldcg(xs + k);
     const uint32_t xw[4] = {v.x, v.y, v.z, v.w};
-    const uint16_t* wv = P.u16 + w_off + 8 * k;
+    const uint16_t* wv = w + 8 * k;
 #pragma unroll
     for (int q = 0; q < 8; q++) {
       const float xv = lx_f((uint16_t)(q & 1 ? xw[q >> 1] >> 16 : xw[q >> 1] & 0xffffu));
-      sm.xr[8 * k + q] = lx_rbf(lx_mul(lx_mul(xv, r), lx_add(1.0f, lx_f(__ldg(wv + q)))));
+      sm.lz.xr[8 * k + q] = lx_rbf(lx_mul(lx_mul(xv, r), lx_add(1.0f, lx_f(wv[q]))));
     }
   }
   __syncthreads();
 }
 
 // Lazily kept channels [c0, c1) of an item: their projections P at the steps tau = base + p
-// (p = 0..3) into sm.pw[p][c - c0]. P of a step before the launch comes from the channel's conv
+// (p = 0..3) into sm.lz.pw[p][c - c0]. P of a step before the launch comes from the channel's conv
 // window as the launch found it (a lazy channel's window is not written until the launch ends).
 // `cur` is the current step (its input norm is sm.xn already), or a value no step has.
 // taps_only: compute P only where the channel's tap p is nonzero (0 elsewhere: a zero tap's
 // product is a signed zero, which leaves the conv sum as it is).
 __device__ void lazy_proj(const Dev& P, const Run& run, Smem& sm, const lxb_item& it,
                           const uint16_t* conv, int s, int L, int base, int cur, bool taps_only,
-                          int c0, int c1, int w_off) {
+                          int c0, int c1, const uint16_t* w) {
   const int t = threadIdx.x;
   for (int p = 0; p < 4; p++) {
     const int tau = base + p;
@@ -250,8 +319,8 @@ __device__ void lazy_proj(const Dev& P, const Run& run, Smem& sm, const lxb_item
     if (tau == cur) {
       xsrc = sm.xn;
     } else if (tau >= 0) {
-      build_xr(P, run, sm, s, L, tau, w_off);
-      xsrc = sm.xr;
+      build_xr(P, run, sm, s, L, tau, w);
+      xsrc = sm.lz.xr;
     }
     for (int c = c0 + t; c < c1; c += NT) {
       const lxb_chan* cp = P.chans + it.ch0 + c;
@@ -267,7 +336,7 @@ __device__ void lazy_proj(const Dev& P, const Run& run, Smem& sm, const lxb_item
         const uint32_t wd = pos < 2 ? win.x : win.y;
         v = (uint16_t)((pos & 1) ? wd >> 16 : wd & 0xffffu);
       }
-      sm.pw[p][c - c0] = v;
+      sm.lz.pw[p][c - c0] = v;
     }
     __syncthreads();
   }
@@ -275,22 +344,29 @@ __device__ void lazy_proj(const Dev& P, const Run& run, Smem& sm, const lxb_item
 
 // --- a GDN item: one live key head of one layer --------------------------------------------------
 // Returns whether it wrote (some value head has output and the head has out_proj entries).
-__device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const lxb_item& it, float* rec,
-                         uint16_t* conv, uint32_t* bm, int s, int L, int step, int ln_in) {
+// B: the step blob (shared memory); bi: this item's record in it; w_in: the staged input norm
+__device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned char* B,
+                         const lxb_bitem& bi, float* rec, uint16_t* conv, uint32_t* bm, int s,
+                         int L, int step, const uint16_t* w_in) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  uint16_t* on = sm.on[it.slot];
+  uint16_t* on = sm.on[bi.slot];
   for (int k = t; k < LXB_NSLOT; k += NT) sm.buf[k] = 0.0f;
   for (int k = t; k < R * VD; k += NT) on[k] = 0;
-  if (t == 0) sm.vhmask[it.slot] = 0;
+  if (t == 0) sm.vhmask[bi.slot] = 0;
   __syncthreads();
-  // query / key channels: in_proj_qkv row, conv window shift, conv output with silu (bf16)
-  for (int c = t; c < it.n_eager; c += NT) {
-    const lxb_chan* cp = P.chans + it.ch0 + c;
-    const uint4 a = __ldg(reinterpret_cast<const uint4*>(cp));  // ent, n|slot, conv_ch, t01
-    const uint32_t t23 = __ldg(reinterpret_cast<const uint4*>(cp) + 1).x;
+  // query / key channels: in_proj_qkv row, conv window shift, conv output with silu (bf16);
+  // records and entries are in the staged blob
+  for (int c = t; c < bi.n_eager; c += NT) {
+    const uint4 a = reinterpret_cast<const uint4*>(B + bi.eager)[2 * c];  // ent, n|slot, conv_ch, t01
+    const uint32_t t23 = reinterpret_cast<const uint4*>(B + bi.eager)[2 * c + 1].x;
     uint2* wp = reinterpret_cast<uint2*>(conv + (size_t)a.z * 4);
     const uint2 win = *wp;
-    const uint16_t Pv = lx_rb(dotb(P.ent, a.x, (int)(a.y & 0xffffu), sm.xn));
+    const uint32_t* e = reinterpret_cast<const uint32_t*>(B + a.x);
+    const int ne = (int)(a.y & 0xffffu);
+    float ps = 0.0f;
+    for (int k = 0; k < ne; k++)
+      ps = lx_add(ps, lx_mul(sm.xn[e[k] & 0xffffu], lx_f((uint16_t)(e[k] >> 16))));
+    const uint16_t Pv = lx_rb(ps);
     const uint16_t n0 = (uint16_t)(win.x >> 16), n1 = (uint16_t)(win.y & 0xffffu),
                    n2 = (uint16_t)(win.y >> 16);
     *wp = make_uint2((uint32_t)n0 | ((uint32_t)n1 << 16), (uint32_t)n2 | ((uint32_t)Pv << 16));
@@ -301,16 +377,22 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const lxb_item&
     y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(Pv)));
     sm.buf[a.y >> 16] = lx_rbf(lx_silu(lx_rbf(y)));
   }
-  const int32_t* rows = P.i32 + it.rows;
-  const uint16_t* prm = P.u16 + it.params;
-  if (t < R) {  // g = -exp(A_log) * softplus(bf16(a . x) + dt_bias)
-    const float a = lx_rbf(dotb(P.ent, (uint32_t)rows[16 + 2 * t], rows[17 + 2 * t], sm.xn));
-    const float A = -lx_exp(lx_f(prm[t]));
-    sm.g[t] = lx_mul(A, lx_softplus(lx_add(a, lx_f(prm[R + t]))));
-  } else if (t < 2 * R) {  // beta = bf16(sigmoid(bf16(b . x)))
-    const int r = t - R;
-    const float b = lx_rbf(dotb(P.ent, (uint32_t)rows[2 * r], rows[2 * r + 1], sm.xn));
-    sm.beta[r] = lx_rbf(lx_sigmoid(b));
+  const int32_t* brows = reinterpret_cast<const int32_t*>(B + bi.rows);
+  const uint16_t* prm = reinterpret_cast<const uint16_t*>(B + bi.prm);
+  if (t < 2 * R) {  // g = -exp(A_log) * softplus(bf16(a . x) + dt_bias); beta = bf16(sigmoid(
+    const int r = t & (R - 1);  // bf16(b . x)))
+    const int q = t < R ? R + r : r;
+    const uint32_t* e = reinterpret_cast<const uint32_t*>(B + brows[2 * q]);
+    const int ne = brows[2 * q + 1];
+    float d = 0.0f;
+    for (int k = 0; k < ne; k++)
+      d = lx_add(d, lx_mul(sm.xn[e[k] & 0xffffu], lx_f((uint16_t)(e[k] >> 16))));
+    if (t < R) {
+      const float A = -lx_exp(lx_f(prm[r]));
+      sm.g[r] = lx_mul(A, lx_softplus(lx_add(lx_rbf(d), lx_f(prm[R + r]))));
+    } else {
+      sm.beta[r] = lx_rbf(lx_sigmoid(lx_rbf(d)));
+    }
   }
   __syncthreads();  // the predicates below read other threads' slots: evaluated before the barrier
   const int qa = __syncthreads_or(t < KD && sm.buf[t] != 0.0f);
@@ -321,19 +403,20 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const lxb_item&
   if (!qa && !ka && !anyg) return false;  // the state stays as it is and o = 0
   // a key fired: the value channels' conv outputs at this step, from their projections at
   // the last four steps (the window a stock step would hold)
+  const lxb_item it = ka ? P.items[bi.item] : lxb_item{};  // the lazy channels' table
   if (ka && it.n_vneed) {
     const int c0 = it.n_eager, c1 = it.n_eager + it.n_vneed;
-    lazy_proj(P, run, sm, it, conv, s, L, step - 3, step, true, c0, c1, ln_in);
+    lazy_proj(P, run, sm, it, conv, s, L, step - 3, step, true, c0, c1, w_in);
     for (int c = c0 + t; c < c1; c += NT) {
       const lxb_chan* cp = P.chans + it.ch0 + c;
       const uint4 a = __ldg(reinterpret_cast<const uint4*>(cp));
       const uint32_t t23 = __ldg(reinterpret_cast<const uint4*>(cp) + 1).x;
       const int i = c - c0;
       float y = 0.0f;
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(sm.pw[0][i])));
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(sm.pw[1][i])));
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 & 0xffffu)), lx_f(sm.pw[2][i])));
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(sm.pw[3][i])));
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(sm.lz.pw[0][i])));
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(sm.lz.pw[1][i])));
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 & 0xffffu)), lx_f(sm.lz.pw[2][i])));
+      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(sm.lz.pw[3][i])));
       sm.buf[a.y >> 16] = lx_rbf(lx_silu(lx_rbf(y)));
     }
   }
@@ -375,7 +458,7 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const lxb_item&
   {
     const int j = t & (VD - 1);
     for (int r = t >> 7; r < R; r += NT / VD) {
-      const int vh = it.kh * R + r;
+      const int vh = bi.kh * R + r;
       float* S = rec + (size_t)vh * KD * VD + j;
       const float g = sm.g[r];
       if (g != 0.0f) {  // decay the rows that may be nonzero (the others stay zero)
@@ -429,8 +512,8 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const lxb_item&
     }
   }
   __syncthreads();
-  if ((it.flags & LXB_IT_DECAYS) && t < R) {  // rows the key wrote may now be nonzero
-    uint32_t* b = bm + (it.kh * R + t) * 8;
+  if ((bi.flags & LXB_IT_DECAYS) && t < R) {  // rows the key wrote may now be nonzero
+    uint32_t* b = bm + (bi.kh * R + t) * 8;
     for (int a = 0; a < nk; a++) b[sm.kidx[a] >> 5] |= 1u << (sm.kidx[a] & 31);
   }
   // Qwen3_5RMSNormGated per value head with output (warp r): bf16(bf16(w * bf16(o * rsqrt(
@@ -442,6 +525,7 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const lxb_item&
                 o3 = o[4 * lane + 3];
     const bool nz = __any_sync(0xffffffffu, o0 != 0.0f || o1 != 0.0f || o2 != 0.0f || o3 != 0.0f);
     if (nz) {
+      const int32_t* rows = P.i32 + P.items[bi.item].rows;  // in_proj_z (global: rarely read)
       float sq = lx_mul(o0, o0);
       sq = lx_add(sq, lx_mul(o1, o1));
       sq = lx_add(sq, lx_mul(o2, o2));
@@ -462,53 +546,57 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const lxb_item&
         const float u = lx_rbf(lx_mul(lx_f(gw[j]), hn));
         on[r * VD + j] = lx_rb(lx_mul(u, lx_silu(z[q])));
       }
-      if (lane == 0) atomicOr(&sm.vhmask[it.slot], 1u << r);
+      if (lane == 0) atomicOr(&sm.vhmask[bi.slot], 1u << r);
     }
   }
   __syncthreads();
-  return sm.vhmask[it.slot] != 0 && (it.flags & LXB_IT_OUT);
+  return sm.vhmask[bi.slot] != 0 && (bi.flags & LXB_IT_OUT);
 }
 
 // --- the owned rows ---------------------------------------------------------------------------
-// The MLP over this CTA's rows: own[row] = bf16(x + bf16(sum_u h_u w_d)), h_u re-evaluated here.
-__device__ void mlp_owner(const Dev& P, Smem& sm, const lxb_owner& ow, int rank, float* own) {
+// The MLP over this CTA's rows: own[row] = bf16(x + bf16(sum_u h_u w_d)), h_u re-evaluated here;
+// the units and entries are in the staged blob (m: its MLP part)
+__device__ void mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, const lxb_bmlp& m,
+                          int rank, float* own) {
   const int t = threadIdx.x;
-  for (int u = t; u < ow.n_units; u += NT) {
-    const uint4 un = __ldg(reinterpret_cast<const uint4*>(P.units + ow.unit0 + u));
-    float gs, us;
-    dot2b(P.ent, un.x, (int)(un.z & 0xffffu), un.y, (int)(un.z >> 16), sm.xm, gs, us);
+  const lxb_bunit* units = reinterpret_cast<const lxb_bunit*>(B + m.units);
+  for (int u = t; u < m.n_units; u += NT) {
+    const lxb_bunit un = units[u];
+    const uint32_t* ge = reinterpret_cast<const uint32_t*>(B + un.g);
+    const uint32_t* ue = reinterpret_cast<const uint32_t*>(B + un.u);
+    float gs = 0.0f, us = 0.0f;
+    for (int k = 0; k < un.ng; k++)
+      gs = lx_add(gs, lx_mul(sm.xm[ge[k] & 0xffffu], lx_f((uint16_t)(ge[k] >> 16))));
+    for (int k = 0; k < un.nu; k++)
+      us = lx_add(us, lx_mul(sm.xm[ue[k] & 0xffffu], lx_f((uint16_t)(ue[k] >> 16))));
     const float gg = lx_rbf(gs), uu = lx_rbf(us);
     const float act = lx_rbf(lx_silu(gg));
     sm.hbuf[u] = lx_rbf(lx_mul(act, uu));
   }
   __syncthreads();
   const int r0 = rank * P.blk;
-  const int32_t* rp = ow.mrow >= 0 ? P.i32 + ow.mrow : nullptr;
+  const int32_t* rp = reinterpret_cast<const int32_t*>(B + m.down_ptr);
+  const uint32_t* de = reinterpret_cast<const uint32_t*>(B + m.down_ent);
   for (int k = t; k < P.blk; k += NT) {
     const float xv = sm.x[r0 + k];
     float res = xv;
-    if (rp) {
-      const int a = __ldg(rp + k), b = __ldg(rp + k + 1);
-      float s = 0.0f;
-      bool any = false;
-      for (int e = a; e < b; e += 8) {
-        uint32_t w[8];
-#pragma unroll
-        for (int q = 0; q < 8; q++) w[q] = e + q < b ? __ldg(P.ent + e + q) : 0u;
-#pragma unroll
-        for (int q = 0; q < 8; q++) {
-          if (e + q >= b) continue;
-          const float hv = sm.hbuf[w[q] & 0xffffu];
-          if (hv != 0.0f) {
-            s = lx_add(s, lx_mul(hv, lx_f((uint16_t)(w[q] >> 16))));
-            any = true;
-          }
-        }
+    float sd = 0.0f;
+    bool any = false;
+    for (int e = rp[k]; e < rp[k + 1]; e++) {
+      const float hv = sm.hbuf[de[e] & 0xffffu];
+      if (hv != 0.0f) {
+        sd = lx_add(sd, lx_mul(hv, lx_f((uint16_t)(de[e] >> 16))));
+        any = true;
       }
-      if (any) res = lx_rbf(lx_add(xv, lx_rbf(s)));
     }
+    if (any) res = lx_rbf(lx_add(xv, lx_rbf(sd)));
     own[k] = res;
   }
+}
+
+// every owned row unchanged (a step whose owners have no MLP work)
+__device__ void copy_owner(const Dev& P, Smem& sm, int rank, float* own) {
+  for (int k = threadIdx.x; k < P.blk; k += NT) own[k] = sm.x[rank * P.blk + k];
 }
 
 // out_proj over this CTA's rows, from the layer's items' outputs (gathered over DSMEM)
@@ -606,7 +694,7 @@ __device__ void head_part(const Dev& P, Smem& sm, int rank) {
     sm.htg[g][code] = s;
   }
   __syncthreads();
-  const lxb_headcta hc = P.headcta[rank];
+  const lxb_headcta hc = sm.hc;
   const int32_t* rp = P.i32 + hc.rowptr;
   float bv = -LXB_INF;
   int bi = 0x7fffffff;
@@ -683,13 +771,13 @@ __device__ void materialize(const Dev& P, const Run& run, Smem& sm, int s, int r
       if (it.cta != rank) continue;
       for (int c0 = it.n_eager; c0 < it.n_ch; c0 += LXB_NSLOT) {
         const int c1 = min(it.n_ch, c0 + LXB_NSLOT);
-        lazy_proj(P, run, sm, it, conv, s, L, n - 4, INT_MIN, false, c0, c1, ly.ln_in);
+        lazy_proj(P, run, sm, it, conv, s, L, n - 4, INT_MIN, false, c0, c1, P.u16 + ly.ln_in);
         for (int c = c0 + threadIdx.x; c < c1; c += NT) {
           const uint32_t cc = __ldg(reinterpret_cast<const uint32_t*>(P.chans + it.ch0 + c) + 2);
           const int i = c - c0;
           *reinterpret_cast<uint2*>(conv + (size_t)cc * 4) =
-              make_uint2((uint32_t)sm.pw[0][i] | ((uint32_t)sm.pw[1][i] << 16),
-                         (uint32_t)sm.pw[2][i] | ((uint32_t)sm.pw[3][i] << 16));
+              make_uint2((uint32_t)sm.lz.pw[0][i] | ((uint32_t)sm.lz.pw[1][i] << 16),
+                         (uint32_t)sm.lz.pw[2][i] | ((uint32_t)sm.lz.pw[3][i] << 16));
         }
         __syncthreads();
       }
@@ -698,13 +786,16 @@ __device__ void materialize(const Dev& P, const Run& run, Smem& sm, int s, int r
 }
 
 __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
-  extern __shared__ __align__(16) unsigned char dsm[];
+  extern __shared__ __align__(128) unsigned char dsm[];
   Smem& sm = *reinterpret_cast<Smem*>(dsm);
+  unsigned char* stage = dsm + ((sizeof(Smem) + 127) / 128) * 128;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int C = P.C;
   const int s = blockIdx.x / C;
   const int t = threadIdx.x;
+  const int nsteps_tok = P.n_layers + 1;  // the layers, then the head
+  const long long total = (long long)run.n_tokens * nsteps_tok;
   if (t < 2) sm.wflag[t] = 0;
   if (t == 0) {
     int tok = run.forced[(size_t)s * run.n_forced];
@@ -713,10 +804,24 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       tok = 0;
     }
     sm.tok = tok;
+    sm.broken = 0;
+    for (int b = 0; b < P.nbuf; b++)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&sm.mbar[b])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  for (int k = t; k <= P.n_layers; k += NT) sm.bref[k] = P.blobidx[k * C + rank];
+  if (t == 0) sm.hc = P.headcta[rank];
+  __syncthreads();
+  if (t == 0) stage_issue(P, sm, stage, 0, 0);  // step 0: layer 0
+  for (int k = t; k < P.n_layers * (int)(sizeof(lxb_layer) / 4); k += NT)
+    reinterpret_cast<int*>(sm.layers)[k] = reinterpret_cast<const int*>(P.layers)[k];
+  for (int k = t; k < 2 * P.n_layers; k += NT)
+    (&sm.sptr[0][0])[k] = run.state_ptrs[(size_t)s * P.n_layers * 2 + k];
   __syncthreads();
   cluster.sync();  // every CTA's flags are initialised before anyone may push one
   int ph = 0;
+  long long stp = 0;  // staged steps consumed
+  uint32_t phase[2] = {0u, 0u};
   unsigned long long pc[PR_N];
 #pragma unroll
   for (int k = 0; k < PR_N; k++) pc[k] = 0;
@@ -730,41 +835,75 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       c0 = c1;                                   \
     }                                            \
   } while (0)
+  // the next step's blob into the free staging buffer (thread 0; the caller has synchronised
+  // the block since the buffer's last use)
+  auto issue_next = [&](long long cur) {
+    const long long nx = cur + 1;
+    if (t == 0 && nx < total && !sm.broken) {
+      const int L = (int)(nx % nsteps_tok);
+      stage_issue(P, sm, stage, (int)(nx % P.nbuf), L);
+    }
+  };
+  // this step's blob: wait for it, and with two buffers start the next one's copy right away
+  auto take = [&](int i) -> const unsigned char* {
+    const int b = (int)(stp % P.nbuf);
+    bool ok = !sm.broken;
+    if (ok) ok = stage_wait(P, sm, b, phase[b], s, i);
+    phase[b] ^= 1u;
+    if (!ok && t == 0) sm.broken = 1;
+    __syncthreads();
+    if (sm.broken) return nullptr;
+    if (P.nbuf == 2) issue_next(stp);
+    return stage + (size_t)b * P.stage;
+  };
   load_embed(run, P, sm, sm.tok);
   for (int i = 0; i < run.n_tokens; i++) {
     if (rank == 0 && t == 0 && run.inputs) run.inputs[(size_t)s * run.n_tokens + i] = sm.tok;
     for (int L = 0; L < P.n_layers; L++) {
-      const lxb_layer ly = P.layers[L];
-      const uint64_t* sp = run.state_ptrs + ((size_t)s * P.n_layers + L) * 2;
-      float* rec = reinterpret_cast<float*>(sp[0]);
-      uint16_t* conv = reinterpret_cast<uint16_t*>(sp[1]);
+      const lxb_layer& ly = sm.layers[L];
+      const unsigned char* B = take(i);
+      PROF(PR_WAIT);
+      const lxb_bhdr bh = B ? *reinterpret_cast<const lxb_bhdr*>(B) : lxb_bhdr{};
+      float* rec = reinterpret_cast<float*>(sm.sptr[L][0]);
+      uint16_t* conv = reinterpret_cast<uint16_t*>(sm.sptr[L][1]);
       uint32_t* bm = run.bitmaps + ((size_t)s * P.n_layers + L) * LXB_NV * 8;
-      const lxb_owner ow = P.owners[ly.owner0 + rank];
       const float r = norm_factor(P, block_ssq(sm, sm.x));
+      const uint16_t* w_in = (B && bh.ln_in >= 0) ? reinterpret_cast<const uint16_t*>(B + bh.ln_in)
+                                                 : P.u16 + ly.ln_in;
+      const uint16_t* w_post = (B && bh.ln_post >= 0)
+                                   ? reinterpret_cast<const uint16_t*>(B + bh.ln_post)
+                                   : P.u16 + ly.ln_post;
+      const bool mlp = ly.has_mlp && B && bh.mlp >= 0;
+      lxb_bmlp mh{};
+      if (mlp) mh = *reinterpret_cast<const lxb_bmlp*>(B + bh.mlp);
       if (ly.has_gdn) {
-        norm_into(P, sm.xn, sm.x, ly.ln_in, r);
+        norm_into(sm.xn, sm.x, w_in, r);
         // this step's GDN input row into the ring (each CTA its block; rank 0 the factor)
         const size_t slot = ((size_t)s * P.n_layers + L) * 4 + (i & 3);
         uint16_t* rg = run.ring + slot * H + rank * P.blk;
         for (int k = t; k < P.blk / 2; k += NT) {
           const float* xv = sm.x + rank * P.blk + 2 * k;
-          reinterpret_cast<uint32_t*>(rg)[k] = (uint32_t)lx_rb(xv[0]) | ((uint32_t)lx_rb(xv[1]) << 16);
+          reinterpret_cast<uint32_t*>(rg)[k] =
+              (uint32_t)lx_rb(xv[0]) | ((uint32_t)lx_rb(xv[1]) << 16);
         }
         if (rank == 0 && t == 0) run.ring_r[slot] = r;
       }
-      if (ly.has_mlp) norm_into(P, sm.xm, sm.x, ly.ln_post, r);
+      if (ly.has_mlp) norm_into(sm.xm, sm.x, w_post, r);
       __syncthreads();
       PROF(PR_NORM);
       bool wrote = false;
-      if (ly.has_gdn) {
-        for (int k = 0; k < ly.n_items; k++) {
-          const lxb_item it = P.items[ly.item0 + k];
-          if (it.cta == rank) wrote |= gdn_item(P, run, sm, it, rec, conv, bm, s, L, i, ly.ln_in);
+      if (ly.has_gdn && B) {
+        for (int k = 0; k < bh.n_items; k++) {
+          const lxb_bitem bi = *reinterpret_cast<const lxb_bitem*>(B + bh.item[k]);
+          wrote |= gdn_item(P, run, sm, B, bi, rec, conv, bm, s, L, i, w_in);
         }
       }
       if (wrote && t < C) *cluster.map_shared_rank(&sm.wflag[ph & 1], t) = 1;
       PROF(PR_ITEMS);
-      if (ly.has_mlp) mlp_owner(P, sm, ow, rank, sm.own[ph & 1]);
+      if (ly.has_mlp) {
+        if (mlp) mlp_owner(P, sm, B, mh, rank, sm.own[ph & 1]);
+        else copy_owner(P, sm, rank, sm.own[ph & 1]);
+      }
       PROF(PR_MLP);
       cluster.sync();
       PROF(PR_SYNC);
@@ -773,32 +912,44 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       if (fl) {
         pc[PR_FIXUPS]++;
         if (t == 0) sm.wflag[ph & 1] = 0;
+        if (P.nbuf == 1 && !ly.has_mlp) issue_next(stp);  // the blob is no longer read
         ph++;
+        const lxb_owner ow = P.owners[ly.owner0 + rank];
         out_owner(P, sm, ly, ow, rank, sm.own[ph & 1], cluster);
         cluster.sync();
         pull(P, sm, ph & 1, cluster);
         ph++;
         if (ly.has_mlp) {
           const float r2 = norm_factor(P, block_ssq(sm, sm.x));
-          norm_into(P, sm.xm, sm.x, ly.ln_post, r2);
+          norm_into(sm.xm, sm.x, w_post, r2);
           __syncthreads();
-          mlp_owner(P, sm, ow, rank, sm.own[ph & 1]);
+          if (mlp) mlp_owner(P, sm, B, mh, rank, sm.own[ph & 1]);
+          else copy_owner(P, sm, rank, sm.own[ph & 1]);
           cluster.sync();
+          if (P.nbuf == 1) issue_next(stp);
           pull(P, sm, ph & 1, cluster);
           ph++;
         }
         PROF(PR_FIXUP);
       } else {
+        if (P.nbuf == 1) issue_next(stp);
         if (ly.has_mlp) pull(P, sm, ph & 1, cluster);
         ph++;
         PROF(PR_PULL);
       }
+      stp++;
     }
     // the output head: every CTA its rows, then the first maximum over the cluster
     {
+      const unsigned char* B = take(i);
+      PROF(PR_WAIT);
+      const lxb_bhdr bh = B ? *reinterpret_cast<const lxb_bhdr*>(B) : lxb_bhdr{};
       const float r = norm_factor(P, block_ssq(sm, sm.x));
-      norm_into(P, sm.xm, sm.x, P.final_norm, r);
+      norm_into(sm.xm, sm.x,
+                B ? reinterpret_cast<const uint16_t*>(B + bh.ln_in) : P.u16 + P.final_norm, r);
       __syncthreads();
+      if (P.nbuf == 1) issue_next(stp);
+      stp++;
       head_part(P, sm, rank);
       cluster.sync();
       if (t < 32) {
@@ -878,10 +1029,12 @@ struct lxb_plan {
   uint32_t* status;
   int max_clusters;
   unsigned long long* prof;
+  int smem;  // dynamic shared memory per CTA: Smem, then the staging buffers
 };
 
 static_assert(offsetof(Smem, own) % 16 == 0 && offsetof(Smem, on) % 16 == 0 &&
-                  offsetof(Smem, onall) % 16 == 0 && sizeof(Smem) < 200 * 1024,
+                  offsetof(Smem, onall) % 16 == 0 && offsetof(Smem, mbar) % 8 == 0 &&
+                  sizeof(Smem) < 160 * 1024,
               "shared memory layout");
 
 static int cuda_rc(cudaError_t e) { return e == cudaSuccess ? LXB_OK : (int)e; }
@@ -951,15 +1104,100 @@ bool rowptr_ok(const View& v, int32_t p, int n, uint32_t lim) {
   return ent_idx(v, rp[0], (int64_t)rp[n] - rp[0], lim);
 }
 
+// the step blobs: every offset, count and index the kernel follows inside one
+bool blob_rng(int64_t off, int64_t len, int64_t bytes, int align = 4) {
+  return off >= 0 && len >= 0 && off % align == 0 && off + len <= bytes;
+}
+bool blob_ent(const unsigned char* B, int64_t bytes, int64_t off, int64_t n, uint32_t lim) {
+  if (!blob_rng(off, 4 * n, bytes)) return false;
+  const uint32_t* e = reinterpret_cast<const uint32_t*>(B + off);
+  for (int64_t i = 0; i < n; i++)
+    if ((e[i] & 0xffffu) >= lim) return false;
+  return true;
+}
+
+int validate_blobs(const View& v, int C) {
+  const lxb_image_header* h = v.h;
+  const int nl = h->n_layers, blk = H / C;
+  if (v.n(LXB_SEC_BLOBIDX) != (int64_t)(nl + 1) * C || h->blob_max < (int)sizeof(lxb_bhdr) ||
+      h->blob_max % 16)
+    return LXB_E_IMAGE;
+  const lxb_blobref* refs = v.sec<lxb_blobref>(LXB_SEC_BLOBIDX);
+  const unsigned char* base = v.sec<unsigned char>(LXB_SEC_BLOBS);
+  const lxb_layer* layers = v.sec<lxb_layer>(LXB_SEC_LAYERS);
+  const lxb_item* items = v.sec<lxb_item>(LXB_SEC_ITEMS);
+  for (int L = 0; L <= nl; L++) {
+    for (int c = 0; c < C; c++) {
+      const lxb_blobref& br = refs[L * C + c];
+      if (br.off < 0 || br.off % 16 || br.bytes < (int)sizeof(lxb_bhdr) || br.bytes % 16 ||
+          br.bytes > h->blob_max || br.off + br.bytes > v.n(LXB_SEC_BLOBS))
+        return LXB_E_IMAGE;
+      const unsigned char* B = base + br.off;
+      const int64_t nb = br.bytes;
+      const lxb_bhdr* bh = reinterpret_cast<const lxb_bhdr*>(B);
+      if (bh->bytes != br.bytes) return LXB_E_IMAGE;
+      if (L == nl) {  // the head's blob: the final norm
+        if (!blob_rng(bh->ln_in, 2 * H, nb, 16)) return LXB_E_IMAGE;
+        continue;
+      }
+      const lxb_layer& ly = layers[L];
+      if (ly.has_gdn && !blob_rng(bh->ln_in, 2 * H, nb, 16)) return LXB_E_IMAGE;
+      if (ly.has_mlp && !blob_rng(bh->ln_post, 2 * H, nb, 16)) return LXB_E_IMAGE;
+      if (bh->n_items < 0 || bh->n_items > LXB_ITEMSLOTS || (bh->n_items && !ly.has_gdn))
+        return LXB_E_IMAGE;
+      for (int k = 0; k < bh->n_items; k++) {
+        if (!blob_rng(bh->item[k], sizeof(lxb_bitem), nb, 16)) return LXB_E_IMAGE;
+        const lxb_bitem& bi = *reinterpret_cast<const lxb_bitem*>(B + bh->item[k]);
+        if (bi.item < ly.item0 || bi.item >= ly.item0 + ly.n_items) return LXB_E_IMAGE;
+        const lxb_item& it = items[bi.item];
+        if (it.cta != c || it.kh != bi.kh || it.slot != bi.slot || it.flags != bi.flags ||
+            bi.n_eager != it.n_eager || bi.n_eager < 0 || bi.n_eager > 2 * LXB_KD)
+          return LXB_E_IMAGE;
+        if (!blob_rng(bi.eager, (int64_t)bi.n_eager * sizeof(lxb_bchan), nb, 16))
+          return LXB_E_IMAGE;
+        for (int e = 0; e < bi.n_eager; e++) {
+          const lxb_bchan& ch = reinterpret_cast<const lxb_bchan*>(B + bi.eager)[e];
+          if (ch.slot >= 2 * LXB_KD || ch.conv_ch >= LXB_CONV || !blob_ent(B, nb, ch.ent, ch.n, H))
+            return LXB_E_IMAGE;
+        }
+        if (!blob_rng(bi.rows, 16 * 8, nb, 16) || !blob_rng(bi.prm, 2 * (2 * R + VD), nb, 16))
+          return LXB_E_IMAGE;
+        const int32_t* rr = reinterpret_cast<const int32_t*>(B + bi.rows);
+        for (int q = 0; q < 2 * R; q++)
+          if (!blob_ent(B, nb, rr[2 * q], rr[2 * q + 1], H)) return LXB_E_IMAGE;
+      }
+      if (ly.has_mlp) {
+        if (!blob_rng(bh->mlp, sizeof(lxb_bmlp), nb, 16)) return LXB_E_IMAGE;
+        const lxb_bmlp& m = *reinterpret_cast<const lxb_bmlp*>(B + bh->mlp);
+        if (m.n_units < 0 || m.n_units > LXB_MAXUNITS ||
+            !blob_rng(m.units, (int64_t)m.n_units * sizeof(lxb_bunit), nb, 16) ||
+            !blob_rng(m.down_ptr, 4 * (int64_t)(blk + 1), nb, 16))
+          return LXB_E_IMAGE;
+        const lxb_bunit* un = reinterpret_cast<const lxb_bunit*>(B + m.units);
+        for (int u = 0; u < m.n_units; u++)
+          if (!blob_ent(B, nb, un[u].g, un[u].ng, H) || !blob_ent(B, nb, un[u].u, un[u].nu, H))
+            return LXB_E_IMAGE;
+        const int32_t* rp = reinterpret_cast<const int32_t*>(B + m.down_ptr);
+        if (rp[0] != 0) return LXB_E_IMAGE;
+        for (int k = 0; k < blk; k++)
+          if (rp[k + 1] < rp[k]) return LXB_E_IMAGE;
+        if (!blob_ent(B, nb, m.down_ent, rp[blk], (uint32_t)m.n_units)) return LXB_E_IMAGE;
+      }
+    }
+  }
+  return LXB_OK;
+}
+
 int validate(const View& v, int cluster) {
   const lxb_image_header* h = v.h;
   if (v.bytes < sizeof(lxb_image_header)) return LXB_E_IMAGE;
   if (h->magic != LXB_MAGIC || h->version != LXB_IMAGE_VERSION) return LXB_E_IMAGE;
-  if (h->hidden != H || h->cluster != cluster || h->n_layers < 1 || h->n_vocab < 1)
+  if (h->hidden != H || h->cluster != cluster || h->n_layers < 1 ||
+      h->n_layers > LXB_MAXLAYERS || h->n_vocab < 1)
     return LXB_E_IMAGE;
   const size_t esz[LXB_SEC_COUNT] = {sizeof(lxb_layer), sizeof(lxb_item), sizeof(lxb_chan), 4,
                                      sizeof(lxb_unit), sizeof(lxb_owner), 4, 2,
-                                     sizeof(lxb_headcta), 8};
+                                     sizeof(lxb_headcta), 8, 1, sizeof(lxb_blobref)};
   for (int k = 0; k < LXB_SEC_COUNT; k++) {
     const lxb_sec& s = h->sec[k];
     if (s.off < (int64_t)sizeof(lxb_image_header) || s.off % 16 || s.count < 0 ||
@@ -1029,7 +1267,6 @@ int validate(const View& v, int cluster) {
       }
       if (ow.mrow >= 0 && !rowptr_ok(v, ow.mrow, blk, (uint32_t)ow.n_units)) return LXB_E_IMAGE;
       if (ow.orow >= 0 && !rowptr_ok(v, ow.orow, blk, LXB_NV * LXB_VD)) return LXB_E_IMAGE;
-      if (ly.has_mlp && ow.mrow < 0 && ow.n_units) return LXB_E_IMAGE;
     }
   }
   const lxb_headcta* hc = v.sec<lxb_headcta>(LXB_SEC_HEADCTA);
@@ -1046,7 +1283,7 @@ int validate(const View& v, int cluster) {
     for (int64_t r = 0; r < h->n_vocab; r++)
       if (bits < 64 && (codes[r] >> bits)) return LXB_E_IMAGE;
   }
-  return LXB_OK;
+  return validate_blobs(v, cluster);
 }
 }  // namespace
 
@@ -1066,7 +1303,10 @@ extern "C" int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   cudaDeviceGetAttribute(&cl, cudaDevAttrClusterLaunch, dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  if (major < 10 || !cl || optin < (int)sizeof(Smem)) return LXB_E_DEVICE;
+  const int base = (int)((sizeof(Smem) + 127) / 128 * 128);
+  const int stage = (v.h->blob_max + 127) / 128 * 128;
+  const int nbuf = base + 2 * stage <= optin ? 2 : 1;
+  if (major < 10 || !cl || base + nbuf * stage > optin) return LXB_E_DEVICE;
   lxb_plan* p = new (std::nothrow) lxb_plan();
   if (!p) return LXB_E_INVAL;
   p->device = dev;
@@ -1109,8 +1349,13 @@ extern "C" int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb
   memcpy(d.htab, h->htab, sizeof(d.htab));
   memcpy(d.dense_cols, h->dense_cols, sizeof(d.dense_cols));
   d.status = p->status;
+  d.blobs = b + h->sec[LXB_SEC_BLOBS].off;
+  d.blobidx = reinterpret_cast<const lxb_blobref*>(b + h->sec[LXB_SEC_BLOBIDX].off);
+  d.nbuf = nbuf;
+  d.stage = stage;
+  p->smem = base + nbuf * stage;
   // launch attributes, and how many clusters fit at once
-  const int smem = (int)sizeof(Smem);
+  const int smem = p->smem;
   cudaFuncSetAttribute(lxb_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (cluster > 8)
     cudaFuncSetAttribute(lxb_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -1176,7 +1421,7 @@ extern "C" int lxb_decode(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bit
   at[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(p->cluster * n_streams);
   cfg.blockDim = dim3(NT);
-  cfg.dynamicSmemBytes = sizeof(Smem);
+  cfg.dynamicSmemBytes = p->smem;
   cfg.stream = st;
   cfg.attrs = at;
   cfg.numAttrs = 1;

@@ -15,7 +15,7 @@
 #include <stdint.h>
 
 #define LXB_MAGIC 0x50425a4cu  // "LZBP"
-#define LXB_IMAGE_VERSION 3
+#define LXB_IMAGE_VERSION 4
 
 #define LXB_H 2560
 #define LXB_KD 256
@@ -30,7 +30,7 @@
 #define LXB_MINC 4
 #define LXB_ITEMSLOTS 4 // items one CTA may run in one layer
 #define LXB_MAXDENSE 32
-#define LXB_MAXUNITS 4096  // MLP units one CTA evaluates in one layer
+#define LXB_MAXUNITS 2048  // MLP units one CTA evaluates in one layer
 
 // item flags
 #define LXB_IT_DECAYS 1  // some value head's g may be nonzero
@@ -47,6 +47,9 @@ enum {
   LXB_SEC_U16,         // uint16 pool: bf16 parameters (norm weights, A_log, dt_bias, gated norm)
   LXB_SEC_HEADCTA,     // lxb_headcta[cluster]
   LXB_SEC_HCODES,      // uint64 per vocabulary row: the dense columns' 2-bit codes
+  LXB_SEC_BLOBS,       // bytes: the step blobs (below)
+  LXB_SEC_BLOBIDX,     // lxb_blobref[(n_layers + 1) * cluster]: layer L (or the head, L =
+                       // n_layers) of CTA c at L * cluster + c
   LXB_SEC_COUNT
 };
 
@@ -67,6 +70,8 @@ typedef struct {
   int32_t pad0;
   float htab[4];         // the dense head columns' values, by code
   int32_t dense_cols[LXB_MAXDENSE];
+  int32_t blob_max;      // the largest step blob, bytes
+  int32_t pad1[3];
   lxb_sec sec[LXB_SEC_COUNT];
 } lxb_image_header;
 
@@ -123,8 +128,60 @@ typedef struct {
   int32_t pad;
 } lxb_headcta;  // 16 bytes
 
+// --- step blobs ---------------------------------------------------------------------------------
+// Everything one CTA reads on one step of the token loop, packed contiguously so that a single
+// stream of bulk copies (cp.async.bulk, TMA) brings it into shared memory one step ahead: the
+// layer's norm weights, the CTA's GDN items (their query/key channels with the in_proj
+// entries, the beta/a rows, the per-head parameters) and the MLP units its residual rows need
+// (gate/up entries, the rows' down_proj entries). Offsets are bytes from the blob's start, all
+// 16-aligned; entries are uint32 (index | bf16 << 16). The head's blob holds the final norm.
+typedef struct {
+  int64_t off;             // bytes from the BLOBS section start (16-aligned)
+  int32_t bytes;           // a multiple of 16
+  int32_t pad;
+} lxb_blobref;
+
+typedef struct {
+  int32_t bytes, n_items;
+  int32_t item[LXB_ITEMSLOTS];  // offsets of lxb_bitem
+  int32_t ln_in, ln_post;       // offsets of bf16[2560] norm weights, or -1
+  int32_t mlp;                  // offset of lxb_bmlp, or -1
+  int32_t pad[7];
+} lxb_bhdr;  // 64 bytes
+
+typedef struct {
+  int32_t item;            // the global item (lazy channels, z rows, output flags)
+  int32_t n_eager, eager;  // n_eager lxb_bchan at offset eager
+  int32_t rows;            // 16 int32 pairs (entry offset in bytes, count): 8 beta, 8 a rows
+  int32_t prm;             // bf16 A_log[8], dt_bias[8], gated-norm weight[128]
+  int32_t kh, slot, flags; // as the global item's
+} lxb_bitem;  // 32 bytes
+
+typedef struct {
+  int32_t ent;             // byte offset of its entries
+  uint16_t n, slot;
+  uint32_t conv_ch, t01, t23;
+  uint32_t pad[3];
+} lxb_bchan;  // 32 bytes
+
+typedef struct {
+  int32_t n_units, units;  // n_units lxb_bunit at offset units
+  int32_t down_ptr;        // int32[blk + 1]: the owned rows' entries (indices into down_ent)
+  int32_t down_ent;        // uint32 entries: local unit | bf16 << 16
+} lxb_bmlp;  // 16 bytes
+
+typedef struct {
+  int32_t g, u;            // byte offsets of the gate / up entries
+  uint16_t ng, nu;
+  int32_t pad;
+} lxb_bunit;  // 16 bytes
+
 #ifdef __cplusplus
-static_assert(sizeof(lxb_image_header) == 360, "lxb_image_header layout");
+static_assert(sizeof(lxb_bhdr) == 64 && sizeof(lxb_bitem) == 32 && sizeof(lxb_bchan) == 32,
+              "blob layout");
+static_assert(sizeof(lxb_bmlp) == 16 && sizeof(lxb_bunit) == 16 && sizeof(lxb_blobref) == 16,
+              "blob layout");
+static_assert(sizeof(lxb_image_header) == 408, "lxb_image_header layout");
 static_assert(sizeof(lxb_layer) == 48 && sizeof(lxb_item) == 48, "layer/item layout");
 static_assert(sizeof(lxb_chan) == 32 && sizeof(lxb_unit) == 16, "chan/unit layout");
 static_assert(sizeof(lxb_owner) == 16 && sizeof(lxb_headcta) == 16, "owner/headcta layout");

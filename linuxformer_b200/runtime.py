@@ -126,10 +126,10 @@ class Decoder:
               "lxb_decode")
 
     PROFILE = ("norm", "items", "mlp", "sync", "pull", "fixup", "head", "embed", "fixups",
-               "tokens")
+               "tokens", "wait")
 
     def set_profile(self, buf: torch.Tensor | None) -> None:
-        """Accumulate per-section cycle counters into buf (int64 [S, cluster, 10]) on every
+        """Accumulate per-section cycle counters into buf (int64 [S, cluster, 11]) on every
         later launch; None stops it."""
         if buf is not None:
             assert buf.dtype == torch.int64 and buf.is_contiguous()

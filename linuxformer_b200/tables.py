@@ -22,13 +22,15 @@ from __future__ import annotations
 import numpy as np
 
 from . import chip as C
+from .chip import _ranges
 
 MAGIC = 0x50425A4C
-VERSION = 3
+VERSION = 4
 NSLOT, NOSLOT = 1536, 0xFFFF
-ITEMSLOTS, MAXDENSE, MAXUNITS = 4, 32, 4096
+ITEMSLOTS, MAXDENSE, MAXUNITS = 4, 32, 2048
 IT_DECAYS, IT_OUT = 1, 2
-SEC = ("layers", "items", "chans", "ent", "units", "owners", "i32", "u16", "headcta", "hcodes")
+SEC = ("layers", "items", "chans", "ent", "units", "owners", "i32", "u16", "headcta", "hcodes",
+       "blobs", "blobidx")
 
 LAYER = np.dtype([(n, "<i4") for n in ("has_gdn", "has_mlp", "ln_in", "ln_post", "item0",
                                        "n_items", "owner0", "itemof", "decays", "p0", "p1",
@@ -45,10 +47,41 @@ HEADER = np.dtype([("magic", "<u4"), ("version", "<u4"), ("n_layers", "<i4"), ("
                    ("n_vocab", "<i4"), ("hidden", "<i4"), ("n_items", "<i4"), ("n_dense", "<i4"),
                    ("n_embed_rows", "<i8"), ("offset", "<i4"), ("eps", "<f4"),
                    ("final_norm", "<i4"), ("pad0", "<i4"), ("htab", "<f4", (4,)),
-                   ("dense_cols", "<i4", (MAXDENSE,)), ("sec", "<i8", (len(SEC), 2))])
+                   ("dense_cols", "<i4", (MAXDENSE,)), ("blob_max", "<i4"), ("pad1", "<i4", (3,)),
+                   ("sec", "<i8", (len(SEC), 2))])
+BLOBREF = np.dtype([("off", "<i8"), ("bytes", "<i4"), ("pad", "<i4")])
+BHDR = np.dtype([("bytes", "<i4"), ("n_items", "<i4"), ("item", "<i4", (ITEMSLOTS,)),
+                 ("ln_in", "<i4"), ("ln_post", "<i4"), ("mlp", "<i4"), ("pad", "<i4", (7,))])
+BITEM = np.dtype([(n, "<i4") for n in ("item", "n_eager", "eager", "rows", "prm", "kh", "slot",
+                                       "flags")])
+BCHAN = np.dtype([("ent", "<i4"), ("n", "<u2"), ("slot", "<u2"), ("conv_ch", "<u4"),
+                  ("t01", "<u4"), ("t23", "<u4"), ("p0", "<u4"), ("p1", "<u4"), ("p2", "<u4")])
+BMLP = np.dtype([(n, "<i4") for n in ("n_units", "units", "down_ptr", "down_ent")])
+BUNIT = np.dtype([("g", "<i4"), ("u", "<i4"), ("ng", "<u2"), ("nu", "<u2"), ("pad", "<i4")])
 assert LAYER.itemsize == 48 and ITEM.itemsize == 48 and CHAN.itemsize == 32
 assert UNIT.itemsize == 16 and OWNER.itemsize == 16 and HEADCTA.itemsize == 16
-assert HEADER.itemsize == 360
+assert HEADER.itemsize == 408 and BLOBREF.itemsize == 16 and BHDR.itemsize == 64
+assert BITEM.itemsize == 32 and BCHAN.itemsize == 32 and BMLP.itemsize == 16
+assert BUNIT.itemsize == 16
+
+
+class _Blob:
+    """One step blob: 16-aligned pieces appended to a bytearray."""
+
+    def __init__(self):
+        self.b = bytearray(BHDR.itemsize)
+
+    def add(self, a) -> int:
+        off = -(-len(self.b) // 16) * 16
+        self.b.extend(bytes(off - len(self.b)))
+        self.b.extend(np.ascontiguousarray(a).tobytes())
+        return off
+
+    def done(self, hdr) -> bytes:
+        self.b.extend(bytes(-len(self.b) % 16))
+        hdr["bytes"] = len(self.b)
+        self.b[:BHDR.itemsize] = np.array([hdr], BHDR).tobytes()
+        return bytes(self.b)
 
 
 class _Pool:
@@ -97,6 +130,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
     ent, i32, u16 = _Pool(np.uint32), _Pool(np.int32), _Pool(np.uint16)
     layers = np.zeros(chip.n_layers, LAYER)
     items, chans, units, owners = [], [], [], []
+    parts, blobs = {}, []
     stats = {"cluster": Cn, "items": 0, "chans": 0, "csr_nnz": 0, "units": 0, "unit_evals": 0,
              "down_nnz": 0, "out_nnz": 0}
     for L, ly in enumerate(chip.layers):
@@ -168,6 +202,17 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
             it["params"] = u16.add(np.concatenate([ly.A_log[vh], ly.dt_bias[vh], ly.gnorm]))
             it["flags"] = (IT_DECAYS if decays_vh[vh].any() else 0) | \
                 (IT_OUT if out_has[kh] else 0)
+            # the item's part of its CTA's step blob: query/key channels with their entries,
+            # the beta / a rows, the head's parameters
+            ne = int((cls == 0).sum())
+            e_ch = chs[:ne]
+            e_ent = [_pack(qkv.indices[qkv.indptr[c]:qkv.indptr[c + 1]],
+                           qkv.data[qkv.indptr[c]:qkv.indptr[c + 1]]) for c in e_ch]
+            ba = [(m.indices[m.indptr[v]:m.indptr[v + 1]], m.data[m.indptr[v]:m.indptr[v + 1]])
+                  for m in (ly.b, ly.a) for v in vh]
+            parts[len(items)] = dict(chan=ch[:ne].copy(), ent=e_ent,
+                                     ba=[_pack(i_, d_) for i_, d_ in ba],
+                                     prm=np.concatenate([ly.A_log[vh], ly.dt_bias[vh], ly.gnorm]))
             itemof[kh] = len(items)
             items.append(it)
             stats["chans"] += len(chs)
@@ -183,14 +228,37 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
         assert g_cnt.max(initial=0) < 1 << 16 and u_cnt.max(initial=0) < 1 << 16
         rec["has_mlp"] = int(unit_live.any())
         stats["units"] += int(unit_live.sum())
-        g_ent = ent.add(_pack(ly.gate.indices, ly.gate.data))
-        u_ent = ent.add(_pack(ly.up.indices, ly.up.data))
         item_heads = np.zeros(C.NK, bool)
         item_heads[heads] = True
         for c in range(Cn):
             ow = np.zeros(1, OWNER)[0]
-            ow["unit0"], ow["mrow"], ow["orow"] = sum(len(u) for u in units), -1, -1
+            ow["unit0"], ow["n_units"], ow["mrow"], ow["orow"] = 0, 0, -1, -1
             rows = np.arange(c * blk, (c + 1) * blk)
+            blob = _Blob()
+            bh = np.zeros(1, BHDR)[0]
+            bh["ln_in"] = blob.add(ly.ln_in) if rec["has_gdn"] else -1
+            bh["ln_post"] = blob.add(ly.ln_post) if rec["has_mlp"] else -1
+            bh["mlp"] = -1
+            mine = sorted((int(items[i]["slot"]), i) for i in range(rec["item0"], len(items))
+                          if items[i]["cta"] == c)
+            bh["n_items"] = len(mine)
+            for q, (_, i) in enumerate(mine):
+                pt = parts[i]
+                bi = np.zeros(1, BITEM)[0]
+                bi["item"], bi["n_eager"] = i, len(pt["chan"])
+                bi["kh"], bi["slot"], bi["flags"] = items[i]["kh"], items[i]["slot"], items[i]["flags"]
+                bc = np.zeros(len(pt["chan"]), BCHAN)
+                for f in ("n", "slot", "conv_ch", "t01", "t23"):
+                    bc[f] = pt["chan"][f]
+                e_off = blob.add(np.concatenate(pt["ent"]) if pt["ent"] else np.zeros(0, np.uint32))
+                bc["ent"] = e_off + 4 * np.concatenate([[0], np.cumsum([len(e) for e in pt["ent"]])[:-1]]).astype(np.int64) if len(bc) else 0
+                bi["eager"] = blob.add(bc)
+                pairs = np.zeros((2 * C.R, 2), np.int32)
+                for r_, e_ in enumerate(pt["ba"]):
+                    pairs[r_] = (blob.add(e_) if len(e_) else 0, len(e_))
+                bi["rows"] = blob.add(pairs)
+                bi["prm"] = blob.add(pt["prm"])
+                bh["item"][q] = blob.add(np.array([bi], BITEM))
             if rec["has_mlp"]:
                 sub = ly.down.rows_subset(rows)
                 keep = unit_live[sub.indices]
@@ -199,19 +267,25 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
                 need = np.unique(uidx)
                 assert len(need) <= MAXUNITS, "too many MLP units for one CTA: use a larger cluster"
                 loc = np.searchsorted(need, uidx)
-                un = np.zeros(len(need), UNIT)
-                un["g"] = g_ent + ly.gate.indptr[need]
-                un["u"] = u_ent + ly.up.indptr[need]
+                gi = _ranges(ly.gate.indptr[need], g_cnt[need])
+                ui = _ranges(ly.up.indptr[need], u_cnt[need])
+                g_off = blob.add(_pack(ly.gate.indices[gi], ly.gate.data[gi]))
+                u_off = blob.add(_pack(ly.up.indices[ui], ly.up.data[ui]))
+                un = np.zeros(len(need), BUNIT)
+                un["g"] = g_off + 4 * (np.cumsum(g_cnt[need]) - g_cnt[need])
+                un["u"] = u_off + 4 * (np.cumsum(u_cnt[need]) - u_cnt[need])
                 un["ng"], un["nu"] = g_cnt[need], u_cnt[need]
-                ow["unit0"] = sum(len(u) for u in units)
-                ow["n_units"] = len(need)
-                units.append(un)
                 ptr = np.zeros(blk + 1, np.int64)
                 np.cumsum(np.bincount(rowid, minlength=blk), out=ptr[1:])
-                base = ent.add(_pack(loc, w))
-                ow["mrow"] = i32.add((ptr + base).astype(np.int32))
+                bm = np.zeros(1, BMLP)[0]
+                bm["n_units"] = len(need)
+                bm["units"] = blob.add(un)
+                bm["down_ptr"] = blob.add(ptr.astype(np.int32))
+                bm["down_ent"] = blob.add(_pack(loc, w))
+                bh["mlp"] = blob.add(np.array([bm], BMLP))
                 stats["unit_evals"] += len(need)
                 stats["down_nnz"] += int(keep.sum())
+            blobs.append(blob.done(bh))
             if rec["has_gdn"] and out_has[item_heads].any():
                 sub = ly.out.rows_subset(rows)
                 keep = item_heads[sub.indices // (C.R * C.VD)]
@@ -256,13 +330,25 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
         headcta[c]["r0"], headcta[c]["r1"] = r0, r1
         headcta[c]["rowptr"] = i32.add((sp_ptr[r0:r1 + 1] + sp_base).astype(np.int32))
     final_norm = u16.add(chip.final_norm)
+    for c in range(Cn):  # the head's blobs: the final norm
+        blob = _Blob()
+        bh = np.zeros(1, BHDR)[0]
+        bh["ln_in"], bh["ln_post"], bh["mlp"] = blob.add(chip.final_norm), -1, -1
+        blobs.append(blob.done(bh))
+    bref = np.zeros(len(blobs), BLOBREF)
+    bref["bytes"] = [len(b) for b in blobs]
+    bref["off"] = np.concatenate([[0], np.cumsum(bref["bytes"])[:-1]])
+    blob_bytes = np.frombuffer(b"".join(blobs), np.uint8)
+    stats["blob_max"] = int(bref["bytes"].max())
+    stats["blob_bytes"] = int(bref["bytes"].sum())
     assert ent.n < 1 << 31 and i32.n < 1 << 31 and u16.n < 1 << 31
     stats.update(head_dense=len(dense), head_sparse_nnz=int(sp.sum()), ent=ent.n)
     # --- the image ---------------------------------------------------------------------------
     secs = [layers, np.array(items, ITEM) if items else np.zeros(0, ITEM),
             np.concatenate(chans) if chans else np.zeros(0, CHAN), ent.array(),
             np.concatenate(units) if units else np.zeros(0, UNIT),
-            np.array(owners, OWNER), i32.array(), u16.array(), headcta, hcodes]
+            np.array(owners, OWNER), i32.array(), u16.array(), headcta, hcodes, blob_bytes,
+            bref]
     hdr = np.zeros(1, HEADER)[0]
     hdr["magic"], hdr["version"] = MAGIC, VERSION
     hdr["n_layers"], hdr["cluster"], hdr["n_vocab"], hdr["hidden"] = chip.n_layers, Cn, V, C.H
@@ -271,6 +357,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
     hdr["final_norm"] = final_norm
     hdr["htab"] = htab
     hdr["dense_cols"][:len(dense)] = dense
+    hdr["blob_max"] = stats["blob_max"]
     blobs, pos = [], HEADER.itemsize
     for k, a in enumerate(secs):
         pos = -(-pos // 16) * 16
