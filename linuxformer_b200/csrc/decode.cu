@@ -75,6 +75,8 @@ struct Dev {
   uint32_t* status;  // [0] bits, [1] first stream, [2] first step
   const unsigned char* blobs;  // the step blobs
   const lxb_blobref* blobidx;  // [(n_layers + 1) * C]
+  const int32_t* winmap;       // (layer, conv channel) pairs
+  const int32_t* winidx;       // per CTA: (offset, count) into winmap
   int nbuf;                    // staging buffers in shared memory (1 or 2)
   int stage;                   // bytes per staging buffer
 };
@@ -141,6 +143,8 @@ struct __align__(16) Smem {
   lxb_layer layers[LXB_MAXLAYERS];  // the layer descriptors
   uint64_t sptr[LXB_MAXLAYERS][2];  // this stream's state pointers per layer
   lxb_blobref bref[LXB_MAXLAYERS + 1];  // this CTA's step blobs (the head's last)
+  alignas(8) uint2 win[LXB_MAXWIN];  // resident query/key conv windows
+  int nwin, win0;                   // their count and offset in the window map
   lxb_headcta hc;                   // this CTA's head rows
 };
 
@@ -160,15 +164,12 @@ __device__ float block_ssq(Smem& sm, const float* x) {
   s = warp_xor_sum(s);
   if (lane == 0) sm.red[warp] = s;
   __syncthreads();
-  if (warp == 0) {
-    float v = lane < 16 ? sm.red[lane] : 0.0f;
+  // every warp reduces the 16 warp sums itself (the same butterfly, so the same bits
+  // everywhere); every caller passes another block barrier before the next call writes red
+  float v = lane < 16 ? sm.red[lane] : 0.0f;
 #pragma unroll
-    for (int off = 8; off > 0; off >>= 1) v = lx_add(v, __shfl_xor_sync(0xffffffffu, v, off));
-    if (lane == 0) sm.red[32] = v;
-  }
-  __syncthreads();
-  const float r = sm.red[32];
-  __syncthreads();
+  for (int off = 8; off > 0; off >>= 1) v = lx_add(v, __shfl_xor_sync(0xffffffffu, v, off));
+  const float r = __shfl_sync(0xffffffffu, v, 0);
   return r;
 }
 
@@ -343,118 +344,167 @@ __device__ void lazy_proj(const Dev& P, const Run& run, Smem& sm, const lxb_item
 }
 
 // --- a GDN item: one live key head of one layer --------------------------------------------------
+// transformers' l2norm in bf16 over a compacted list (the nonzero entries in ascending order):
+// x * rsqrt(sum(x * x) + 1e-6), the bf16 squares summed sequentially from +0 by one lane
+__device__ __forceinline__ float l2_inv(const float* val, int n) {
+  float sq = 0.0f;
+  for (int i = 0; i < n; i++) sq = lx_add(sq, lx_rbf(lx_mul(val[i], val[i])));
+  return lx_rbf(lx_rsqrt(lx_rbf(lx_add(lx_rbf(sq), 1e-6f))));
+}
+
+// One eager (query/key) channel: in_proj_qkv row over the staged entries, conv window shift
+// (resident in shared memory, or in global), conv output with silu in bf16.
+__device__ __forceinline__ float eager_channel(Smem& sm, const unsigned char* B, const uint4 a,
+                                               const uint4 b, uint16_t* conv) {
+  const uint32_t* e = reinterpret_cast<const uint32_t*>(B + a.x);
+  const int ne = (int)(a.y & 0xffffu);
+  uint2* wp = b.y != LXB_NOWIN ? &sm.win[b.y] : reinterpret_cast<uint2*>(conv + (size_t)a.z * 4);
+  const uint2 win = *wp;
+  float ps = 0.0f;
+  for (int k = 0; k < ne; k++)
+    ps = lx_add(ps, lx_mul(sm.xn[e[k] & 0xffffu], lx_f((uint16_t)(e[k] >> 16))));
+  const uint16_t Pv = lx_rb(ps);
+  const uint16_t n0 = (uint16_t)(win.x >> 16), n1 = (uint16_t)(win.y & 0xffffu),
+                 n2 = (uint16_t)(win.y >> 16);
+  *wp = make_uint2((uint32_t)n0 | ((uint32_t)n1 << 16), (uint32_t)n2 | ((uint32_t)Pv << 16));
+  float y = 0.0f;
+  y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(n0)));
+  y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(n1)));
+  y = lx_add(y, lx_mul(lx_f((uint16_t)(b.x & 0xffffu)), lx_f(n2)));
+  y = lx_add(y, lx_mul(lx_f((uint16_t)(b.x >> 16)), lx_f(Pv)));
+  return lx_rbf(lx_silu(lx_rbf(y)));
+}
+
+// B: the step blob (shared memory); bi: this item's record in it; w_in: the staged input norm.
 // Returns whether it wrote (some value head has output and the head has out_proj entries).
-// B: the step blob (shared memory); bi: this item's record in it; w_in: the staged input norm
 __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned char* B,
                          const lxb_bitem& bi, float* rec, uint16_t* conv, uint32_t* bm, int s,
                          int L, int step, const uint16_t* w_in) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   uint16_t* on = sm.on[bi.slot];
-  for (int k = t; k < LXB_NSLOT; k += NT) sm.buf[k] = 0.0f;
-  for (int k = t; k < R * VD; k += NT) on[k] = 0;
-  if (t == 0) sm.vhmask[bi.slot] = 0;
-  __syncthreads();
-  // query / key channels: in_proj_qkv row, conv window shift, conv output with silu (bf16);
-  // records and entries are in the staged blob
-  for (int c = t; c < bi.n_eager; c += NT) {
-    const uint4 a = reinterpret_cast<const uint4*>(B + bi.eager)[2 * c];  // ent, n|slot, conv_ch, t01
-    const uint32_t t23 = reinterpret_cast<const uint4*>(B + bi.eager)[2 * c + 1].x;
-    uint2* wp = reinterpret_cast<uint2*>(conv + (size_t)a.z * 4);
-    const uint2 win = *wp;
-    const uint32_t* e = reinterpret_cast<const uint32_t*>(B + a.x);
-    const int ne = (int)(a.y & 0xffffu);
-    float ps = 0.0f;
-    for (int k = 0; k < ne; k++)
-      ps = lx_add(ps, lx_mul(sm.xn[e[k] & 0xffffu], lx_f((uint16_t)(e[k] >> 16))));
-    const uint16_t Pv = lx_rb(ps);
-    const uint16_t n0 = (uint16_t)(win.x >> 16), n1 = (uint16_t)(win.y & 0xffffu),
-                   n2 = (uint16_t)(win.y >> 16);
-    *wp = make_uint2((uint32_t)n0 | ((uint32_t)n1 << 16), (uint32_t)n2 | ((uint32_t)Pv << 16));
-    float y = 0.0f;
-    y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(n0)));
-    y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(n1)));
-    y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 & 0xffffu)), lx_f(n2)));
-    y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(Pv)));
-    sm.buf[a.y >> 16] = lx_rbf(lx_silu(lx_rbf(y)));
+  const uint4* ch = reinterpret_cast<const uint4*>(B + bi.eager);
+  if (bi.n_eager <= 32) {
+    // one warp: the channels in ascending order (queries, then keys), compacted by ballot
+    if (warp == 0) {
+      float v = 0.0f;
+      int slot = 0;
+      if (lane < bi.n_eager) {
+        const uint4 a = ch[2 * lane], b = ch[2 * lane + 1];
+        v = eager_channel(sm, B, a, b, conv);
+        slot = (int)(a.y >> 16);
+      }
+      const bool nz = lane < bi.n_eager && v != 0.0f;
+      const unsigned mq = __ballot_sync(0xffffffffu, nz && slot < KD);
+      const unsigned mk = __ballot_sync(0xffffffffu, nz && slot >= KD);
+      if (nz) {
+        const unsigned m = slot < KD ? mq : mk;
+        const int k = __popc(m & ((1u << lane) - 1u));
+        if (slot < KD) {
+          sm.qidx[k] = slot;
+          sm.qval[k] = v;
+        } else {
+          sm.kidx[k] = slot - KD;
+          sm.kval[k] = v;
+        }
+      }
+      __syncwarp();
+      const int nq = __popc(mq), nk = __popc(mk);
+      float inv = 0.0f;
+      if (lane == 0 && nq) inv = l2_inv(sm.qval, nq);
+      if (lane == 1 && nk) inv = l2_inv(sm.kval, nk);
+      const float iq = __shfl_sync(0xffffffffu, inv, 0), ik = __shfl_sync(0xffffffffu, inv, 1);
+      if (lane < nq) sm.qval[lane] = lx_mul(lx_rbf(lx_mul(sm.qval[lane], iq)), 0.0625f);
+      if (lane < nk) sm.kval[lane] = lx_rbf(lx_mul(sm.kval[lane], ik));
+      if (lane == 0) {
+        sm.nq = nq;
+        sm.nk = nk;
+        sm.vhmask[bi.slot] = 0;
+      }
+    }
+  } else {
+    // many query/key channels: a dense q | k buffer, then compaction by warps 0 and 1
+    for (int k = t; k < 2 * KD; k += NT) sm.buf[k] = 0.0f;
+    __syncthreads();
+    for (int c = t; c < bi.n_eager; c += NT) {
+      const uint4 a = ch[2 * c], b = ch[2 * c + 1];
+      sm.buf[a.y >> 16] = eager_channel(sm, B, a, b, conv);
+    }
+    __syncthreads();
+    if (warp < 2) {
+      const float* xv = sm.buf + warp * KD;
+      int* idx = warp ? sm.kidx : sm.qidx;
+      float* val = warp ? sm.kval : sm.qval;
+      int n = 0;
+      for (int base = 0; base < KD; base += 32) {
+        const float v = xv[base + lane];
+        const unsigned m = __ballot_sync(0xffffffffu, v != 0.0f);
+        if (v != 0.0f) {
+          const int k = n + __popc(m & ((1u << lane) - 1u));
+          idx[k] = base + lane;
+          val[k] = v;
+        }
+        n += __popc(m);
+      }
+      __syncwarp();
+      float inv = 0.0f;
+      if (lane == 0 && n) inv = l2_inv(val, n);
+      inv = __shfl_sync(0xffffffffu, inv, 0);
+      for (int i = lane; i < n; i += 32) {
+        const float vn = lx_rbf(lx_mul(val[i], inv));
+        val[i] = warp ? vn : lx_mul(vn, 0.0625f);  // the query times 256^-0.5
+      }
+      if (lane == 0) (warp ? sm.nk : sm.nq) = n;
+      if (t == 0) sm.vhmask[bi.slot] = 0;
+    }
   }
-  const int32_t* brows = reinterpret_cast<const int32_t*>(B + bi.rows);
+  // warp 1: g = -exp(A_log) * softplus(bf16(a . x) + dt_bias); beta = bf16(sigmoid(bf16(b . x)))
   const uint16_t* prm = reinterpret_cast<const uint16_t*>(B + bi.prm);
-  if (t < 2 * R) {  // g = -exp(A_log) * softplus(bf16(a . x) + dt_bias); beta = bf16(sigmoid(
-    const int r = t & (R - 1);  // bf16(b . x)))
-    const int q = t < R ? R + r : r;
+  if (warp == 1 && lane < 2 * R) {
+    const int32_t* brows = reinterpret_cast<const int32_t*>(B + bi.rows);
+    const int r = lane & (R - 1);
+    const int q = lane < R ? R + r : r;
     const uint32_t* e = reinterpret_cast<const uint32_t*>(B + brows[2 * q]);
     const int ne = brows[2 * q + 1];
     float d = 0.0f;
     for (int k = 0; k < ne; k++)
       d = lx_add(d, lx_mul(sm.xn[e[k] & 0xffffu], lx_f((uint16_t)(e[k] >> 16))));
-    if (t < R) {
+    if (lane < R) {
       const float A = -lx_exp(lx_f(prm[r]));
       sm.g[r] = lx_mul(A, lx_softplus(lx_add(lx_rbf(d), lx_f(prm[R + r]))));
     } else {
       sm.beta[r] = lx_rbf(lx_sigmoid(lx_rbf(d)));
     }
   }
-  __syncthreads();  // the predicates below read other threads' slots: evaluated before the barrier
-  const int qa = __syncthreads_or(t < KD && sm.buf[t] != 0.0f);
-  const int ka = __syncthreads_or(t >= KD && t < 2 * KD && sm.buf[t] != 0.0f);
+  __syncthreads();
+  const int nq = sm.nq, nk = sm.nk;
   int anyg = 0;
 #pragma unroll
   for (int r = 0; r < R; r++) anyg |= sm.g[r] != 0.0f;
-  if (!qa && !ka && !anyg) return false;  // the state stays as it is and o = 0
-  // a key fired: the value channels' conv outputs at this step, from their projections at
-  // the last four steps (the window a stock step would hold)
-  const lxb_item it = ka ? P.items[bi.item] : lxb_item{};  // the lazy channels' table
-  if (ka && it.n_vneed) {
-    const int c0 = it.n_eager, c1 = it.n_eager + it.n_vneed;
-    lazy_proj(P, run, sm, it, conv, s, L, step - 3, step, true, c0, c1, w_in);
-    for (int c = c0 + t; c < c1; c += NT) {
-      const lxb_chan* cp = P.chans + it.ch0 + c;
-      const uint4 a = __ldg(reinterpret_cast<const uint4*>(cp));
-      const uint32_t t23 = __ldg(reinterpret_cast<const uint4*>(cp) + 1).x;
-      const int i = c - c0;
-      float y = 0.0f;
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(sm.lz.pw[0][i])));
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(sm.lz.pw[1][i])));
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 & 0xffffu)), lx_f(sm.lz.pw[2][i])));
-      y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(sm.lz.pw[3][i])));
-      sm.buf[a.y >> 16] = lx_rbf(lx_silu(lx_rbf(y)));
-    }
-  }
-  // transformers' l2norm in bf16 on q (warp 0) and k (warp 1): the nonzero entries in
-  // ascending order, their bf16 squares summed sequentially from +0
-  __syncthreads();
-  if (warp < 2) {
-    const float* xv = sm.buf + warp * KD;
-    int* idx = warp ? sm.kidx : sm.qidx;
-    float* val = warp ? sm.kval : sm.qval;
-    int n = 0;
-    for (int base = 0; base < KD; base += 32) {
-      const float v = xv[base + lane];
-      const unsigned m = __ballot_sync(0xffffffffu, v != 0.0f);
-      if (v != 0.0f) {
-        const int k = n + __popc(m & ((1u << lane) - 1u));
-        idx[k] = base + lane;
-        val[k] = v;
+  if (!nq && !nk && !anyg) return false;  // the state stays as it is and o = 0
+  if (nk) {
+    // a key fired: the value channels' conv outputs at this step, from their projections at
+    // the last four steps (the window a stock step would hold); other value slots are zero
+    for (int k = t; k < R * VD; k += NT) sm.buf[2 * KD + k] = 0.0f;
+    const lxb_item it = P.items[bi.item];
+    if (it.n_vneed) {
+      const int c0 = it.n_eager, c1 = it.n_eager + it.n_vneed;
+      lazy_proj(P, run, sm, it, conv, s, L, step - 3, step, true, c0, c1, w_in);
+      for (int c = c0 + t; c < c1; c += NT) {
+        const lxb_chan* cp = P.chans + it.ch0 + c;
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(cp));
+        const uint32_t t23 = __ldg(reinterpret_cast<const uint4*>(cp) + 1).x;
+        const int i = c - c0;
+        float y = 0.0f;
+        y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(sm.lz.pw[0][i])));
+        y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(sm.lz.pw[1][i])));
+        y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 & 0xffffu)), lx_f(sm.lz.pw[2][i])));
+        y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(sm.lz.pw[3][i])));
+        sm.buf[a.y >> 16] = lx_rbf(lx_silu(lx_rbf(y)));
       }
-      n += __popc(m);
     }
-    __syncwarp();
-    float inv = 0.0f;
-    if (lane == 0) {
-      float sq = 0.0f;
-      for (int i = 0; i < n; i++) sq = lx_add(sq, lx_rbf(lx_mul(val[i], val[i])));
-      inv = lx_rbf(lx_rsqrt(lx_rbf(lx_add(lx_rbf(sq), 1e-6f))));
-    }
-    inv = __shfl_sync(0xffffffffu, inv, 0);
-    for (int i = lane; i < n; i += 32) {
-      const float vn = lx_rbf(lx_mul(val[i], inv));
-      val[i] = warp ? vn : lx_mul(vn, 0.0625f);  // the query times 256^-0.5
-    }
-    if (lane == 0) (warp ? sm.nk : sm.nq) = n;
+    __syncthreads();
   }
-  __syncthreads();
   // the delta rule, thread = (value head, state column)
-  const int nq = sm.nq, nk = sm.nk;
   {
     const int j = t & (VD - 1);
     for (int r = t >> 7; r < R; r += NT / VD) {
@@ -517,15 +567,17 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
     for (int a = 0; a < nk; a++) b[sm.kidx[a] >> 5] |= 1u << (sm.kidx[a] & 31);
   }
   // Qwen3_5RMSNormGated per value head with output (warp r): bf16(bf16(w * bf16(o * rsqrt(
-  // mean(o^2) + eps))) * silu(z)), z = bf16(in_proj_z . x)
-  if (warp < R) {
+  // mean(o^2) + eps))) * silu(z)), z = bf16(in_proj_z . x); a head without out_proj entries
+  // has no z rows staged and cannot write: it skips this
+  if (warp < R && bi.z >= 0) {
     const int r = warp;
     const float* o = sm.ob[r];
     const float o0 = o[4 * lane], o1 = o[4 * lane + 1], o2 = o[4 * lane + 2],
                 o3 = o[4 * lane + 3];
     const bool nz = __any_sync(0xffffffffu, o0 != 0.0f || o1 != 0.0f || o2 != 0.0f || o3 != 0.0f);
     if (nz) {
-      const int32_t* rows = P.i32 + P.items[bi.item].rows;  // in_proj_z (global: rarely read)
+      const int32_t* zp = reinterpret_cast<const int32_t*>(B + bi.z);
+      const uint32_t* ze = reinterpret_cast<const uint32_t*>(B + bi.z + ((4 * 1025 + 15) & ~15));
       float sq = lx_mul(o0, o0);
       sq = lx_add(sq, lx_mul(o1, o1));
       sq = lx_add(sq, lx_mul(o2, o2));
@@ -533,18 +585,16 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
       sq = warp_xor_sum(sq);
       const float rr = lx_rsqrt(lx_add(lx_div(sq, 128.0f), P.eps));
       const uint16_t* gw = prm + 2 * R;
-      float z[4];
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const int zr = 32 + 2 * (r * VD + lane + 32 * q);
-        z[q] = lx_rbf(dotb(P.ent, (uint32_t)rows[zr], rows[zr + 1], sm.xn));
-      }
 #pragma unroll
       for (int q = 0; q < 4; q++) {
         const int j = lane + 32 * q;
+        const int zr = r * VD + j;
+        float z = 0.0f;
+        for (int e = zp[zr]; e < zp[zr + 1]; e++)
+          z = lx_add(z, lx_mul(sm.xn[ze[e] & 0xffffu], lx_f((uint16_t)(ze[e] >> 16))));
         const float hn = lx_rbf(lx_mul(o[j], rr));
         const float u = lx_rbf(lx_mul(lx_f(gw[j]), hn));
-        on[r * VD + j] = lx_rb(lx_mul(u, lx_silu(z[q])));
+        on[r * VD + j] = lx_rb(lx_mul(u, lx_silu(lx_rbf(z))));
       }
       if (lane == 0) atomicOr(&sm.vhmask[bi.slot], 1u << r);
     }
@@ -809,14 +859,25 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&sm.mbar[b])));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  for (int k = t; k <= P.n_layers; k += NT) sm.bref[k] = P.blobidx[k * C + rank];
-  if (t == 0) sm.hc = P.headcta[rank];
-  __syncthreads();
-  if (t == 0) stage_issue(P, sm, stage, 0, 0);  // step 0: layer 0
+  // per-launch tables into shared memory: layer descriptors, this stream's state pointers, this
+  // CTA's blob index, head rows and resident windows (pointers first: the windows use them)
   for (int k = t; k < P.n_layers * (int)(sizeof(lxb_layer) / 4); k += NT)
     reinterpret_cast<int*>(sm.layers)[k] = reinterpret_cast<const int*>(P.layers)[k];
   for (int k = t; k < 2 * P.n_layers; k += NT)
     (&sm.sptr[0][0])[k] = run.state_ptrs[(size_t)s * P.n_layers * 2 + k];
+  for (int k = t; k <= P.n_layers; k += NT) sm.bref[k] = P.blobidx[k * C + rank];
+  if (t == 0) {
+    sm.hc = P.headcta[rank];
+    sm.win0 = P.winidx[2 * rank];
+    sm.nwin = P.winidx[2 * rank + 1];
+  }
+  __syncthreads();
+  for (int k = t; k < sm.nwin; k += NT) {  // the resident conv windows, from the state
+    const int L = P.winmap[2 * (sm.win0 + k)], ch = P.winmap[2 * (sm.win0 + k) + 1];
+    sm.win[k] = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(sm.sptr[L][1]) +
+                                                (size_t)ch * 4);
+  }
+  if (t == 0) stage_issue(P, sm, stage, 0, 0);  // step 0: layer 0
   __syncthreads();
   cluster.sync();  // every CTA's flags are initialised before anyone may push one
   int ph = 0;
@@ -991,6 +1052,11 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
 #pragma unroll
     for (int k = 0; k < PR_N; k++) d[k] += pc[k];
   }
+  for (int k = t; k < sm.nwin; k += NT) {  // the resident conv windows back into the state
+    const int L = P.winmap[2 * (sm.win0 + k)], ch = P.winmap[2 * (sm.win0 + k) + 1];
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(sm.sptr[L][1]) + (size_t)ch * 4) =
+        sm.win[k];
+  }
   cluster.sync();  // every ring write of the launch is visible cluster-wide
   materialize(P, run, sm, s, rank, run.n_tokens);
   cluster.sync();  // no CTA leaves while another may still read its shared memory
@@ -1126,6 +1192,17 @@ int validate_blobs(const View& v, int C) {
   const unsigned char* base = v.sec<unsigned char>(LXB_SEC_BLOBS);
   const lxb_layer* layers = v.sec<lxb_layer>(LXB_SEC_LAYERS);
   const lxb_item* items = v.sec<lxb_item>(LXB_SEC_ITEMS);
+  if (v.n(LXB_SEC_WINIDX) != C) return LXB_E_IMAGE;
+  const int32_t* widx = v.sec<int32_t>(LXB_SEC_WINIDX);
+  const int32_t* wmap = v.sec<int32_t>(LXB_SEC_WINMAP);
+  for (int c = 0; c < C; c++)
+    if (widx[2 * c] < 0 || widx[2 * c + 1] < 0 || widx[2 * c + 1] > LXB_MAXWIN ||
+        (int64_t)widx[2 * c] + widx[2 * c + 1] > v.n(LXB_SEC_WINMAP))
+      return LXB_E_IMAGE;
+  for (int64_t k = 0; k < v.n(LXB_SEC_WINMAP); k++)
+    if (wmap[2 * k] < 0 || wmap[2 * k] >= nl || wmap[2 * k + 1] < 0 ||
+        wmap[2 * k + 1] >= LXB_CONV)
+      return LXB_E_IMAGE;
   for (int L = 0; L <= nl; L++) {
     for (int c = 0; c < C; c++) {
       const lxb_blobref& br = refs[L * C + c];
@@ -1159,12 +1236,27 @@ int validate_blobs(const View& v, int C) {
           const lxb_bchan& ch = reinterpret_cast<const lxb_bchan*>(B + bi.eager)[e];
           if (ch.slot >= 2 * LXB_KD || ch.conv_ch >= LXB_CONV || !blob_ent(B, nb, ch.ent, ch.n, H))
             return LXB_E_IMAGE;
+          if (ch.win != LXB_NOWIN) {  // a resident window: the map must name this channel
+            if (ch.win >= (uint32_t)widx[2 * c + 1]) return LXB_E_IMAGE;
+            const int32_t* wp = wmap + 2 * ((int64_t)widx[2 * c] + ch.win);
+            if (wp[0] != L || wp[1] != (int32_t)ch.conv_ch) return LXB_E_IMAGE;
+          }
         }
         if (!blob_rng(bi.rows, 16 * 8, nb, 16) || !blob_rng(bi.prm, 2 * (2 * R + VD), nb, 16))
           return LXB_E_IMAGE;
         const int32_t* rr = reinterpret_cast<const int32_t*>(B + bi.rows);
         for (int q = 0; q < 2 * R; q++)
           if (!blob_ent(B, nb, rr[2 * q], rr[2 * q + 1], H)) return LXB_E_IMAGE;
+        if (bi.z >= 0) {  // the in_proj_z rows: 1025 pointers, then the entries
+          if (!blob_rng(bi.z, 4 * 1025, nb, 16)) return LXB_E_IMAGE;
+          const int32_t* zp = reinterpret_cast<const int32_t*>(B + bi.z);
+          if (zp[0] != 0) return LXB_E_IMAGE;
+          for (int k = 0; k < 1024; k++)
+            if (zp[k + 1] < zp[k]) return LXB_E_IMAGE;
+          if (!blob_ent(B, nb, bi.z + ((4 * 1025 + 15) & ~15), zp[1024], H)) return LXB_E_IMAGE;
+        } else if (bi.flags & LXB_IT_OUT) {
+          return LXB_E_IMAGE;  // a head that can write needs its z rows
+        }
       }
       if (ly.has_mlp) {
         if (!blob_rng(bh->mlp, sizeof(lxb_bmlp), nb, 16)) return LXB_E_IMAGE;
@@ -1197,7 +1289,7 @@ int validate(const View& v, int cluster) {
     return LXB_E_IMAGE;
   const size_t esz[LXB_SEC_COUNT] = {sizeof(lxb_layer), sizeof(lxb_item), sizeof(lxb_chan), 4,
                                      sizeof(lxb_unit), sizeof(lxb_owner), 4, 2,
-                                     sizeof(lxb_headcta), 8, 1, sizeof(lxb_blobref)};
+                                     sizeof(lxb_headcta), 8, 1, sizeof(lxb_blobref), 8, 8};
   for (int k = 0; k < LXB_SEC_COUNT; k++) {
     const lxb_sec& s = h->sec[k];
     if (s.off < (int64_t)sizeof(lxb_image_header) || s.off % 16 || s.count < 0 ||
@@ -1351,6 +1443,8 @@ extern "C" int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb
   d.status = p->status;
   d.blobs = b + h->sec[LXB_SEC_BLOBS].off;
   d.blobidx = reinterpret_cast<const lxb_blobref*>(b + h->sec[LXB_SEC_BLOBIDX].off);
+  d.winmap = reinterpret_cast<const int32_t*>(b + h->sec[LXB_SEC_WINMAP].off);
+  d.winidx = reinterpret_cast<const int32_t*>(b + h->sec[LXB_SEC_WINIDX].off);
   d.nbuf = nbuf;
   d.stage = stage;
   p->smem = base + nbuf * stage;

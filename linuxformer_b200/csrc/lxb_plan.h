@@ -15,7 +15,7 @@
 #include <stdint.h>
 
 #define LXB_MAGIC 0x50425a4cu  // "LZBP"
-#define LXB_IMAGE_VERSION 4
+#define LXB_IMAGE_VERSION 5
 
 #define LXB_H 2560
 #define LXB_KD 256
@@ -31,6 +31,8 @@
 #define LXB_ITEMSLOTS 4 // items one CTA may run in one layer
 #define LXB_MAXDENSE 32
 #define LXB_MAXUNITS 2048  // MLP units one CTA evaluates in one layer
+#define LXB_MAXWIN 1024    // query/key conv windows one CTA keeps in shared memory for a launch
+#define LXB_NOWIN 0xffffffffu
 
 // item flags
 #define LXB_IT_DECAYS 1  // some value head's g may be nonzero
@@ -50,6 +52,8 @@ enum {
   LXB_SEC_BLOBS,       // bytes: the step blobs (below)
   LXB_SEC_BLOBIDX,     // lxb_blobref[(n_layers + 1) * cluster]: layer L (or the head, L =
                        // n_layers) of CTA c at L * cluster + c
+  LXB_SEC_WINMAP,      // int32 (layer, conv channel) pairs: the windows each CTA keeps resident
+  LXB_SEC_WINIDX,      // int32 (offset in pairs, count) per CTA into WINMAP
   LXB_SEC_COUNT
 };
 
@@ -155,13 +159,17 @@ typedef struct {
   int32_t rows;            // 16 int32 pairs (entry offset in bytes, count): 8 beta, 8 a rows
   int32_t prm;             // bf16 A_log[8], dt_bias[8], gated-norm weight[128]
   int32_t kh, slot, flags; // as the global item's
-} lxb_bitem;  // 32 bytes
+  int32_t z;               // offset of int32 zptr[1025] (entry indices) then the in_proj_z
+                           // entries of the head's 1024 value dims; -1: no output possible
+  int32_t pad[7];
+} lxb_bitem;  // 64 bytes
 
 typedef struct {
   int32_t ent;             // byte offset of its entries
   uint16_t n, slot;
   uint32_t conv_ch, t01, t23;
-  uint32_t pad[3];
+  uint32_t win;            // its window's resident slot (LXB_NOWIN: read in global memory)
+  uint32_t pad[2];
 } lxb_bchan;  // 32 bytes
 
 typedef struct {
@@ -177,11 +185,11 @@ typedef struct {
 } lxb_bunit;  // 16 bytes
 
 #ifdef __cplusplus
-static_assert(sizeof(lxb_bhdr) == 64 && sizeof(lxb_bitem) == 32 && sizeof(lxb_bchan) == 32,
+static_assert(sizeof(lxb_bhdr) == 64 && sizeof(lxb_bitem) == 64 && sizeof(lxb_bchan) == 32,
               "blob layout");
 static_assert(sizeof(lxb_bmlp) == 16 && sizeof(lxb_bunit) == 16 && sizeof(lxb_blobref) == 16,
               "blob layout");
-static_assert(sizeof(lxb_image_header) == 408, "lxb_image_header layout");
+static_assert(sizeof(lxb_image_header) == 440, "lxb_image_header layout");
 static_assert(sizeof(lxb_layer) == 48 && sizeof(lxb_item) == 48, "layer/item layout");
 static_assert(sizeof(lxb_chan) == 32 && sizeof(lxb_unit) == 16, "chan/unit layout");
 static_assert(sizeof(lxb_owner) == 16 && sizeof(lxb_headcta) == 16, "owner/headcta layout");

@@ -25,12 +25,12 @@ from . import chip as C
 from .chip import _ranges
 
 MAGIC = 0x50425A4C
-VERSION = 4
+VERSION = 5
 NSLOT, NOSLOT = 1536, 0xFFFF
-ITEMSLOTS, MAXDENSE, MAXUNITS = 4, 32, 2048
+ITEMSLOTS, MAXDENSE, MAXUNITS, MAXWIN = 4, 32, 2048, 1024
 IT_DECAYS, IT_OUT = 1, 2
 SEC = ("layers", "items", "chans", "ent", "units", "owners", "i32", "u16", "headcta", "hcodes",
-       "blobs", "blobidx")
+       "blobs", "blobidx", "winmap", "winidx")
 
 LAYER = np.dtype([(n, "<i4") for n in ("has_gdn", "has_mlp", "ln_in", "ln_post", "item0",
                                        "n_items", "owner0", "itemof", "decays", "p0", "p1",
@@ -53,15 +53,15 @@ BLOBREF = np.dtype([("off", "<i8"), ("bytes", "<i4"), ("pad", "<i4")])
 BHDR = np.dtype([("bytes", "<i4"), ("n_items", "<i4"), ("item", "<i4", (ITEMSLOTS,)),
                  ("ln_in", "<i4"), ("ln_post", "<i4"), ("mlp", "<i4"), ("pad", "<i4", (7,))])
 BITEM = np.dtype([(n, "<i4") for n in ("item", "n_eager", "eager", "rows", "prm", "kh", "slot",
-                                       "flags")])
+                                       "flags", "z")] + [("pad", "<i4", (7,))])
 BCHAN = np.dtype([("ent", "<i4"), ("n", "<u2"), ("slot", "<u2"), ("conv_ch", "<u4"),
-                  ("t01", "<u4"), ("t23", "<u4"), ("p0", "<u4"), ("p1", "<u4"), ("p2", "<u4")])
+                  ("t01", "<u4"), ("t23", "<u4"), ("win", "<u4"), ("p1", "<u4"), ("p2", "<u4")])
 BMLP = np.dtype([(n, "<i4") for n in ("n_units", "units", "down_ptr", "down_ent")])
 BUNIT = np.dtype([("g", "<i4"), ("u", "<i4"), ("ng", "<u2"), ("nu", "<u2"), ("pad", "<i4")])
 assert LAYER.itemsize == 48 and ITEM.itemsize == 48 and CHAN.itemsize == 32
 assert UNIT.itemsize == 16 and OWNER.itemsize == 16 and HEADCTA.itemsize == 16
-assert HEADER.itemsize == 408 and BLOBREF.itemsize == 16 and BHDR.itemsize == 64
-assert BITEM.itemsize == 32 and BCHAN.itemsize == 32 and BMLP.itemsize == 16
+assert HEADER.itemsize == 440 and BLOBREF.itemsize == 16 and BHDR.itemsize == 64
+assert BITEM.itemsize == 64 and BCHAN.itemsize == 32 and BMLP.itemsize == 16
 assert BUNIT.itemsize == 16
 
 
@@ -131,6 +131,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
     layers = np.zeros(chip.n_layers, LAYER)
     items, chans, units, owners = [], [], [], []
     parts, blobs = {}, []
+    winmap = [[] for _ in range(Cn)]  # per CTA: its resident (layer, conv channel) windows
     stats = {"cluster": Cn, "items": 0, "chans": 0, "csr_nnz": 0, "units": 0, "unit_evals": 0,
              "down_nnz": 0, "out_nnz": 0}
     for L, ly in enumerate(chip.layers):
@@ -210,9 +211,11 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
                            qkv.data[qkv.indptr[c]:qkv.indptr[c + 1]]) for c in e_ch]
             ba = [(m.indices[m.indptr[v]:m.indptr[v + 1]], m.data[m.indptr[v]:m.indptr[v + 1]])
                   for m in (ly.b, ly.a) for v in vh]
+            zsub = ly.z.rows_subset(zrows) if out_has[kh] else None
             parts[len(items)] = dict(chan=ch[:ne].copy(), ent=e_ent,
                                      ba=[_pack(i_, d_) for i_, d_ in ba],
-                                     prm=np.concatenate([ly.A_log[vh], ly.dt_bias[vh], ly.gnorm]))
+                                     prm=np.concatenate([ly.A_log[vh], ly.dt_bias[vh], ly.gnorm]),
+                                     z=zsub)
             itemof[kh] = len(items)
             items.append(it)
             stats["chans"] += len(chs)
@@ -250,6 +253,16 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
                 bc = np.zeros(len(pt["chan"]), BCHAN)
                 for f in ("n", "slot", "conv_ch", "t01", "t23"):
                     bc[f] = pt["chan"][f]
+                if len(winmap[c]) + len(bc) <= MAXWIN:  # windows kept in shared memory
+                    bc["win"] = len(winmap[c]) + np.arange(len(bc))
+                    winmap[c] += [(L, int(x)) for x in bc["conv_ch"]]
+                else:
+                    bc["win"] = 0xFFFFFFFF
+                bi["z"] = -1
+                if pt["z"] is not None:
+                    zs = pt["z"]
+                    bi["z"] = blob.add(zs.indptr.astype(np.int32))
+                    blob.add(_pack(zs.indices, zs.data))  # follows zptr (16-aligned)
                 e_off = blob.add(np.concatenate(pt["ent"]) if pt["ent"] else np.zeros(0, np.uint32))
                 bc["ent"] = e_off + 4 * np.concatenate([[0], np.cumsum([len(e) for e in pt["ent"]])[:-1]]).astype(np.int64) if len(bc) else 0
                 bi["eager"] = blob.add(bc)
@@ -335,6 +348,10 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
         bh = np.zeros(1, BHDR)[0]
         bh["ln_in"], bh["ln_post"], bh["mlp"] = blob.add(chip.final_norm), -1, -1
         blobs.append(blob.done(bh))
+    widx = np.zeros((Cn, 2), np.int32)
+    widx[:, 1] = [len(w) for w in winmap]
+    widx[1:, 0] = np.cumsum(widx[:-1, 1])
+    wmap = np.array([p for w in winmap for p in w], np.int32).reshape(-1, 2)
     bref = np.zeros(len(blobs), BLOBREF)
     bref["bytes"] = [len(b) for b in blobs]
     bref["off"] = np.concatenate([[0], np.cumsum(bref["bytes"])[:-1]])
@@ -348,7 +365,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
             np.concatenate(chans) if chans else np.zeros(0, CHAN), ent.array(),
             np.concatenate(units) if units else np.zeros(0, UNIT),
             np.array(owners, OWNER), i32.array(), u16.array(), headcta, hcodes, blob_bytes,
-            bref]
+            bref, wmap, widx]
     hdr = np.zeros(1, HEADER)[0]
     hdr["magic"], hdr["version"] = MAGIC, VERSION
     hdr["n_layers"], hdr["cluster"], hdr["n_vocab"], hdr["hidden"] = chip.n_layers, Cn, V, C.H
