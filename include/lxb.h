@@ -96,6 +96,10 @@ int lxb_status_clear(lxb_plan* plan);
 int lxb_plan_set_profile(lxb_plan* plan, unsigned long long* prof);
 int lxb_profile_sections(void);
 
+/* How the plan stages its per-step tables: buffers (2 = the next step's copy overlaps the
+ * current step), bytes per buffer, and the shared memory each CTA uses. */
+int lxb_plan_staging(const lxb_plan* plan, int* nbuf, int* stage_bytes, int* smem_bytes);
+
 /* Bytes of the plan's device tables; the number of co-resident clusters for this plan. */
 size_t lxb_plan_bytes(const lxb_plan* plan);
 int lxb_plan_max_clusters(const lxb_plan* plan);

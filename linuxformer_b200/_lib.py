@@ -36,6 +36,7 @@ SIGNATURES = {
     "lxb_status": (I, [P, P]),
     "lxb_plan_set_profile": (I, [P, P]),
     "lxb_profile_sections": (I, []),
+    "lxb_plan_staging": (I, [P, P, P, P]),
     "lxb_status_clear": (I, [P]),
     "lxb_plan_bytes": (ctypes.c_size_t, [P]),
     "lxb_plan_max_clusters": (I, [P]),

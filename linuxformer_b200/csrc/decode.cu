@@ -54,6 +54,7 @@ namespace cg = cooperative_groups;
 #define R LXB_R
 #define BLKMAX (LXB_H / LXB_MINC)
 #define LXB_MAXLAYERS 64
+#define LXB_MAXPROD 4096
 
 struct Dev {
   const lxb_layer* layers;
@@ -107,6 +108,8 @@ enum {
   PR_FIXUPS,   // count: fix-up steps
   PR_TOKENS,   // count: tokens
   PR_WAIT,     // waiting for a staged blob
+  PR_POLLS,    // count: staging polls that found the copy still in flight
+  PR_TAKESYNC, // the block barrier after the staging wait
   PR_N
 };
 
@@ -134,6 +137,7 @@ struct __align__(16) Smem {
     } lz;
   };
   float hbuf[LXB_MAXUNITS];        // MLP unit outputs
+  float prod[LXB_MAXPROD];         // MLP gate/up products, in the units' entry order
   float htg[LXB_MAXDENSE / 4][256];  // head: per group of 4 dense columns, each code's sum
   float bestv;
   int besti;
@@ -212,11 +216,10 @@ __device__ __forceinline__ void stage_issue(const Dev& P, Smem& sm, unsigned cha
 // wait for a staging buffer (bounded by the global timer: a copy that never lands sets the
 // status and stops every later use of the staged blobs instead of spinning forever)
 __device__ __forceinline__ bool stage_wait(const Dev& P, Smem& sm, int buf, uint32_t phase,
-                                           int s, int step) {
+                                           int s, int step, unsigned long long& polls) {
   const uint32_t mb = smem_u32(&sm.mbar[buf]);
-  unsigned long long t0;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-  for (;;) {
+  long long t0 = 0;
+  for (int it = 0;; it++) {
     uint32_t ok;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
@@ -225,9 +228,9 @@ __device__ __forceinline__ bool stage_wait(const Dev& P, Smem& sm, int buf, uint
         : "r"(mb), "r"(phase)
         : "memory");
     if (ok) return true;
-    unsigned long long t1;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-    if (t1 - t0 > 2000000000ull) {  // 2 s
+    polls++;
+    if (it == 0) t0 = clock64();
+    if (clock64() - t0 > 4000000000ll) {  // ~2 s at the B200's clock
       if (threadIdx.x == 0) {
         if (atomicOr(P.status, LXB_S_STAGE) == 0) {
           P.status[1] = (uint32_t)s;
@@ -352,17 +355,24 @@ __device__ __forceinline__ float l2_inv(const float* val, int n) {
   return lx_rbf(lx_rsqrt(lx_rbf(lx_add(lx_rbf(sq), 1e-6f))));
 }
 
-// One eager (query/key) channel: in_proj_qkv row over the staged entries, conv window shift
-// (resident in shared memory, or in global), conv output with silu in bf16.
+// input_layernorm(x)[c] for one column: bf16(x[c] * r * (1 + w[c])), as norm_into computes it
+__device__ __forceinline__ float xn_at(const Smem& sm, const uint16_t* w, float r, uint32_t c) {
+  return lx_rbf(lx_mul(lx_mul(sm.x[c], r), lx_add(1.0f, lx_f(w[c]))));
+}
+
+// One eager (query/key) channel: in_proj_qkv row over the staged entries (the input norm taken
+// per column), conv window shift (resident in shared memory, or in global), conv output with
+// silu in bf16.
 __device__ __forceinline__ float eager_channel(Smem& sm, const unsigned char* B, const uint4 a,
-                                               const uint4 b, uint16_t* conv) {
+                                               const uint4 b, uint16_t* conv, const uint16_t* w,
+                                               float r) {
   const uint32_t* e = reinterpret_cast<const uint32_t*>(B + a.x);
   const int ne = (int)(a.y & 0xffffu);
   uint2* wp = b.y != LXB_NOWIN ? &sm.win[b.y] : reinterpret_cast<uint2*>(conv + (size_t)a.z * 4);
   const uint2 win = *wp;
   float ps = 0.0f;
   for (int k = 0; k < ne; k++)
-    ps = lx_add(ps, lx_mul(sm.xn[e[k] & 0xffffu], lx_f((uint16_t)(e[k] >> 16))));
+    ps = lx_add(ps, lx_mul(xn_at(sm, w, r, e[k] & 0xffffu), lx_f((uint16_t)(e[k] >> 16))));
   const uint16_t Pv = lx_rb(ps);
   const uint16_t n0 = (uint16_t)(win.x >> 16), n1 = (uint16_t)(win.y & 0xffffu),
                  n2 = (uint16_t)(win.y >> 16);
@@ -379,7 +389,7 @@ __device__ __forceinline__ float eager_channel(Smem& sm, const unsigned char* B,
 // Returns whether it wrote (some value head has output and the head has out_proj entries).
 __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned char* B,
                          const lxb_bitem& bi, float* rec, uint16_t* conv, uint32_t* bm, int s,
-                         int L, int step, const uint16_t* w_in) {
+                         int L, int step, const uint16_t* w_in, float r_in) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   uint16_t* on = sm.on[bi.slot];
   const uint4* ch = reinterpret_cast<const uint4*>(B + bi.eager);
@@ -390,7 +400,7 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
       int slot = 0;
       if (lane < bi.n_eager) {
         const uint4 a = ch[2 * lane], b = ch[2 * lane + 1];
-        v = eager_channel(sm, B, a, b, conv);
+        v = eager_channel(sm, B, a, b, conv, w_in, r_in);
         slot = (int)(a.y >> 16);
       }
       const bool nz = lane < bi.n_eager && v != 0.0f;
@@ -427,7 +437,7 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
     __syncthreads();
     for (int c = t; c < bi.n_eager; c += NT) {
       const uint4 a = ch[2 * c], b = ch[2 * c + 1];
-      sm.buf[a.y >> 16] = eager_channel(sm, B, a, b, conv);
+      sm.buf[a.y >> 16] = eager_channel(sm, B, a, b, conv, w_in, r_in);
     }
     __syncthreads();
     if (warp < 2) {
@@ -467,7 +477,7 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
     const int ne = brows[2 * q + 1];
     float d = 0.0f;
     for (int k = 0; k < ne; k++)
-      d = lx_add(d, lx_mul(sm.xn[e[k] & 0xffffu], lx_f((uint16_t)(e[k] >> 16))));
+      d = lx_add(d, lx_mul(xn_at(sm, w_in, r_in, e[k] & 0xffffu), lx_f((uint16_t)(e[k] >> 16))));
     if (lane < R) {
       const float A = -lx_exp(lx_f(prm[r]));
       sm.g[r] = lx_mul(A, lx_softplus(lx_add(lx_rbf(d), lx_f(prm[R + r]))));
@@ -487,6 +497,8 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
     for (int k = t; k < R * VD; k += NT) sm.buf[2 * KD + k] = 0.0f;
     const lxb_item it = P.items[bi.item];
     if (it.n_vneed) {
+      norm_into(sm.xn, sm.x, w_in, r_in);  // this step's input norm, for the lazy projections
+      __syncthreads();
       const int c0 = it.n_eager, c1 = it.n_eager + it.n_vneed;
       lazy_proj(P, run, sm, it, conv, s, L, step - 3, step, true, c0, c1, w_in);
       for (int c = c0 + t; c < c1; c += NT) {
@@ -591,7 +603,8 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
         const int zr = r * VD + j;
         float z = 0.0f;
         for (int e = zp[zr]; e < zp[zr + 1]; e++)
-          z = lx_add(z, lx_mul(sm.xn[ze[e] & 0xffffu], lx_f((uint16_t)(ze[e] >> 16))));
+          z = lx_add(z, lx_mul(xn_at(sm, w_in, r_in, ze[e] & 0xffffu),
+                               lx_f((uint16_t)(ze[e] >> 16))));
         const float hn = lx_rbf(lx_mul(o[j], rr));
         const float u = lx_rbf(lx_mul(lx_f(gw[j]), hn));
         on[r * VD + j] = lx_rb(lx_mul(u, lx_silu(lx_rbf(z))));
@@ -610,15 +623,34 @@ __device__ void mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, const 
                           int rank, float* own) {
   const int t = threadIdx.x;
   const lxb_bunit* units = reinterpret_cast<const lxb_bunit*>(B + m.units);
+  // the gate and up entries of all units are contiguous in the blob: their products first, all
+  // threads at once, into prod (the units' entries in order), then one thread per unit sums its
+  // own products in order, so the sums are the sequential ones
+  const int g0 = m.n_units ? units[0].g : 0;
+  const int ne = m.n_units ? (units[m.n_units - 1].u + 4 * units[m.n_units - 1].nu - g0) / 4 : 0;
+  const uint32_t* ent = reinterpret_cast<const uint32_t*>(B + g0);
+  float* prod = sm.prod;
+  if (ne <= LXB_MAXPROD) {
+    for (int e = t; e < ne; e += NT)
+      prod[e] = lx_mul(sm.xm[ent[e] & 0xffffu], lx_f((uint16_t)(ent[e] >> 16)));
+    __syncthreads();
+  }
   for (int u = t; u < m.n_units; u += NT) {
     const lxb_bunit un = units[u];
-    const uint32_t* ge = reinterpret_cast<const uint32_t*>(B + un.g);
-    const uint32_t* ue = reinterpret_cast<const uint32_t*>(B + un.u);
     float gs = 0.0f, us = 0.0f;
-    for (int k = 0; k < un.ng; k++)
-      gs = lx_add(gs, lx_mul(sm.xm[ge[k] & 0xffffu], lx_f((uint16_t)(ge[k] >> 16))));
-    for (int k = 0; k < un.nu; k++)
-      us = lx_add(us, lx_mul(sm.xm[ue[k] & 0xffffu], lx_f((uint16_t)(ue[k] >> 16))));
+    if (ne <= LXB_MAXPROD) {
+      const float* pg = prod + (un.g - g0) / 4;
+      const float* pu = prod + (un.u - g0) / 4;
+      for (int k = 0; k < un.ng; k++) gs = lx_add(gs, pg[k]);
+      for (int k = 0; k < un.nu; k++) us = lx_add(us, pu[k]);
+    } else {
+      const uint32_t* ge = reinterpret_cast<const uint32_t*>(B + un.g);
+      const uint32_t* ue = reinterpret_cast<const uint32_t*>(B + un.u);
+      for (int k = 0; k < un.ng; k++)
+        gs = lx_add(gs, lx_mul(sm.xm[ge[k] & 0xffffu], lx_f((uint16_t)(ge[k] >> 16))));
+      for (int k = 0; k < un.nu; k++)
+        us = lx_add(us, lx_mul(sm.xm[ue[k] & 0xffffu], lx_f((uint16_t)(ue[k] >> 16))));
+    }
     const float gg = lx_rbf(gs), uu = lx_rbf(us);
     const float act = lx_rbf(lx_silu(gg));
     sm.hbuf[u] = lx_rbf(lx_mul(act, uu));
@@ -746,6 +778,7 @@ __device__ void head_part(const Dev& P, Smem& sm, int rank) {
   __syncthreads();
   const lxb_headcta hc = sm.hc;
   const int32_t* rp = P.i32 + hc.rowptr;
+  const bool sparse = rp[0] != rp[hc.r1 - hc.r0];  // any sparse entry in these rows
   float bv = -LXB_INF;
   int bi = 0x7fffffff;
   constexpr int U = 8;  // rows in flight per thread
@@ -757,8 +790,8 @@ __device__ void head_part(const Dev& P, Smem& sm, int rank) {
       const int row = row0 + q * NT;
       const bool ok = row < hc.r1;
       code[q] = (ok && nd) ? __ldg(P.hcodes + row) : 0ull;
-      ea[q] = ok ? __ldg(rp + row - hc.r0) : 0;
-      eb[q] = ok ? __ldg(rp + row - hc.r0 + 1) : 0;
+      ea[q] = (ok && sparse) ? __ldg(rp + row - hc.r0) : 0;
+      eb[q] = (ok && sparse) ? __ldg(rp + row - hc.r0 + 1) : 0;
     }
 #pragma unroll
     for (int q = 0; q < U; q++) {
@@ -882,7 +915,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
   cluster.sync();  // every CTA's flags are initialised before anyone may push one
   int ph = 0;
   long long stp = 0;  // staged steps consumed
-  uint32_t phase[2] = {0u, 0u};
+  uint32_t phases = 0u;  // bit b: the parity staging buffer b waits for next
   unsigned long long pc[PR_N];
 #pragma unroll
   for (int k = 0; k < PR_N; k++) pc[k] = 0;
@@ -896,23 +929,27 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       c0 = c1;                                   \
     }                                            \
   } while (0)
+  // the layer (or head, = n_layers) of global step k: k runs over the layers then the head
+  auto nstep_layer = [&](long long k) -> int { return (int)(k % nsteps_tok); };
   // the next step's blob into the free staging buffer (thread 0; the caller has synchronised
   // the block since the buffer's last use)
   auto issue_next = [&](long long cur) {
     const long long nx = cur + 1;
-    if (t == 0 && nx < total && !sm.broken) {
-      const int L = (int)(nx % nsteps_tok);
-      stage_issue(P, sm, stage, (int)(nx % P.nbuf), L);
-    }
+    if (t == 0 && nx < total && !sm.broken)
+      stage_issue(P, sm, stage, P.nbuf == 2 ? (int)(nx & 1) : 0, nstep_layer(nx));
   };
   // this step's blob: wait for it, and with two buffers start the next one's copy right away
   auto take = [&](int i) -> const unsigned char* {
-    const int b = (int)(stp % P.nbuf);
+    const int b = P.nbuf == 2 ? (int)(stp & 1) : 0;
     bool ok = !sm.broken;
-    if (ok) ok = stage_wait(P, sm, b, phase[b], s, i);
-    phase[b] ^= 1u;
+    unsigned long long polls = 0;
+    if (ok) ok = stage_wait(P, sm, b, (phases >> b) & 1u, s, i, polls);
+    phases ^= 1u << b;
+    pc[PR_POLLS] += polls;
     if (!ok && t == 0) sm.broken = 1;
+    PROF(PR_WAIT);
     __syncthreads();
+    PROF(PR_TAKESYNC);
     if (sm.broken) return nullptr;
     if (P.nbuf == 2) issue_next(stp);
     return stage + (size_t)b * P.stage;
@@ -938,7 +975,6 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       lxb_bmlp mh{};
       if (mlp) mh = *reinterpret_cast<const lxb_bmlp*>(B + bh.mlp);
       if (ly.has_gdn) {
-        norm_into(sm.xn, sm.x, w_in, r);
         // this step's GDN input row into the ring (each CTA its block; rank 0 the factor)
         const size_t slot = ((size_t)s * P.n_layers + L) * 4 + (i & 3);
         uint16_t* rg = run.ring + slot * H + rank * P.blk;
@@ -954,9 +990,10 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       PROF(PR_NORM);
       bool wrote = false;
       if (ly.has_gdn && B) {
+        const lxb_bhdr* bhp = reinterpret_cast<const lxb_bhdr*>(B);  // (dynamic index: in smem)
         for (int k = 0; k < bh.n_items; k++) {
-          const lxb_bitem bi = *reinterpret_cast<const lxb_bitem*>(B + bh.item[k]);
-          wrote |= gdn_item(P, run, sm, B, bi, rec, conv, bm, s, L, i, w_in);
+          const lxb_bitem bi = *reinterpret_cast<const lxb_bitem*>(B + bhp->item[k]);
+          wrote |= gdn_item(P, run, sm, B, bi, rec, conv, bm, s, L, i, w_in, r);
         }
       }
       if (wrote && t < C) *cluster.map_shared_rank(&sm.wflag[ph & 1], t) = 1;
@@ -1269,6 +1306,13 @@ int validate_blobs(const View& v, int C) {
         for (int u = 0; u < m.n_units; u++)
           if (!blob_ent(B, nb, un[u].g, un[u].ng, H) || !blob_ent(B, nb, un[u].u, un[u].nu, H))
             return LXB_E_IMAGE;
+        if (m.n_units) {  // the kernel indexes the units' products from the first gate entry
+          const int64_t g0 = un[0].g, end = un[m.n_units - 1].u + 4 * (int64_t)un[m.n_units - 1].nu;
+          for (int u = 0; u < m.n_units; u++)
+            if (un[u].g < g0 || un[u].g + 4 * (int64_t)un[u].ng > end || un[u].u < g0 ||
+                un[u].u + 4 * (int64_t)un[u].nu > end)
+              return LXB_E_IMAGE;
+        }
         const int32_t* rp = reinterpret_cast<const int32_t*>(B + m.down_ptr);
         if (rp[0] != 0) return LXB_E_IMAGE;
         for (int k = 0; k < blk; k++)
@@ -1546,6 +1590,14 @@ extern "C" int lxb_plan_set_profile(lxb_plan* p, unsigned long long* prof) {
 }
 
 extern "C" int lxb_profile_sections(void) { return PR_N; }
+
+extern "C" int lxb_plan_staging(const lxb_plan* p, int* nbuf, int* stage_bytes, int* smem_bytes) {
+  if (!p || !nbuf || !stage_bytes || !smem_bytes) return LXB_E_INVAL;
+  *nbuf = p->dev.nbuf;
+  *stage_bytes = p->dev.stage;
+  *smem_bytes = p->smem;
+  return LXB_OK;
+}
 
 extern "C" size_t lxb_plan_bytes(const lxb_plan* p) { return p ? p->bytes : 0; }
 extern "C" int lxb_plan_max_clusters(const lxb_plan* p) { return p ? p->max_clusters : 0; }

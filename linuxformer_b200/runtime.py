@@ -126,10 +126,10 @@ class Decoder:
               "lxb_decode")
 
     PROFILE = ("norm", "items", "mlp", "sync", "pull", "fixup", "head", "embed", "fixups",
-               "tokens", "wait")
+               "tokens", "wait", "polls", "takesync")
 
     def set_profile(self, buf: torch.Tensor | None) -> None:
-        """Accumulate per-section cycle counters into buf (int64 [S, cluster, 11]) on every
+        """Accumulate per-section cycle counters into buf (int64 [S, cluster, 13]) on every
         later launch; None stops it."""
         if buf is not None:
             assert buf.dtype == torch.int64 and buf.is_contiguous()
@@ -137,6 +137,12 @@ class Decoder:
         check(lib().lxb_plan_set_profile(self.plan, buf.data_ptr() if buf is not None else None),
               "lxb_plan_set_profile")
         self._prof = buf
+
+    def staging(self) -> dict:
+        """The plan's staging: buffers, bytes per buffer, shared memory per CTA."""
+        v = [ctypes.c_int() for _ in range(3)]
+        check(lib().lxb_plan_staging(self.plan, *(ctypes.byref(x) for x in v)), "lxb_plan_staging")
+        return {"buffers": v[0].value, "stage_bytes": v[1].value, "smem_bytes": v[2].value}
 
     def status(self) -> Err:
         e = Err()
