@@ -30,6 +30,11 @@ extern "C" {
 #define LXB_E_IMAGE (-2)     /* a malformed plan image (an offset, count or index out of range) */
 #define LXB_E_DEVICE (-3)    /* the device cannot run the plan (arch, cluster size, shared memory) */
 #define LXB_E_STATUS (-4)    /* the kernel reported an error: read it with lxb_status */
+#define LXB_E_TOOBIG (-5)    /* more scratch than lxb_decode_noalloc's fixed array holds */
+
+/* lxb_decode_noalloc's scratch: a fixed device array of this many bytes per GPU */
+#define LXB_NOALLOC_MAX_SCRATCH (4u << 20)
+#define LXB_MAX_DEVICES 64
 
 /* device status bits (lxb_status) */
 #define LXB_S_TOKEN 1u       /* a token id outside the embedding: clamped, the stream is invalid */
@@ -82,6 +87,22 @@ int lxb_decode(lxb_plan* plan, const uint64_t* state_ptrs, uint32_t* bitmaps, in
  * rows per layer, from which the lazily kept conv windows are recomputed). The caller allocates
  * it (16-byte aligned); its contents need no initialisation and do not outlive a call. */
 size_t lxb_scratch_bytes(const lxb_plan* plan, int n_streams);
+
+/* lxb_decode for callers that cannot allocate device memory. No counterpart in the reference
+ * (its Python host allocates freely). Some hosts cannot hand this library device memory once
+ * they are running: a server that carves all device memory into one pool at start-up, or a
+ * host whose allocator is not CUDA-aware and only passes the buffers it owns (state, tokens,
+ * predictions). This call takes the same arguments as lxb_decode except the scratch, which it
+ * takes from a fixed array inside the library (LXB_NOALLOC_MAX_SCRATCH bytes, held by every GPU
+ * that loads the library until the process exits): it calls no cudaMalloc or cudaFree.
+ * Requests needing more (lxb_scratch_bytes(plan, n_streams) above the limit; for the 37-layer
+ * chip about 5 streams) return LXB_E_TOOBIG. The first call on a device looks up the array's
+ * device address there (the device must be current); make that first call before any stream
+ * capture. All calls on a device share the array: calls that overlap on the GPU race. */
+int lxb_decode_noalloc(lxb_plan* plan, const uint64_t* state_ptrs, uint32_t* bitmaps,
+                       int sync_bitmaps, const uint16_t* embed, int n_streams,
+                       const int32_t* forced, int n_forced, int n_tokens, int32_t* preds,
+                       int32_t* inputs, void* cuda_stream);
 
 /* The device status word (after the stream has synchronised). Replaces mk_last_error
  * (mega.cu:892) for kernel-side errors. */

@@ -33,6 +33,7 @@ SIGNATURES = {
     "lxb_plan_create": (I, [P, ctypes.c_size_t, I, P]),
     "lxb_decode": (I, [P, P, P, I, P, P, I, P, I, I, P, P, P]),
     "lxb_scratch_bytes": (ctypes.c_size_t, [P, I]),
+    "lxb_decode_noalloc": (I, [P, P, P, I, P, I, P, I, I, P, P, P]),
     "lxb_status": (I, [P, P]),
     "lxb_plan_set_profile": (I, [P, P]),
     "lxb_profile_sections": (I, []),

@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include <climits>
+#include <mutex>
 #include <new>
 #include <stddef.h>
 #include <stdint.h>
@@ -1165,6 +1166,8 @@ const char* lxb_error_string_c(int code) {
     case LXB_E_IMAGE: return "malformed plan image";
     case LXB_E_DEVICE: return "device cannot run this plan";
     case LXB_E_STATUS: return "kernel reported an error (lxb_status)";
+    case LXB_E_TOOBIG:
+      return "the request needs more scratch than lxb_decode_noalloc's fixed array holds";
     default: return code > 0 ? cudaGetErrorString((cudaError_t)code) : "unknown error";
   }
 }
@@ -1529,10 +1532,10 @@ extern "C" size_t lxb_scratch_bytes(const lxb_plan* p, int n_streams) {
   return ring_bytes(p, n_streams) + (size_t)n_streams * p->hdr.n_layers * 4 * sizeof(float);
 }
 
-extern "C" int lxb_decode(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitmaps,
-                          int sync_bitmaps, void* scratch, const uint16_t* embed, int n_streams,
-                          const int32_t* forced, int n_forced, int n_tokens, int32_t* preds,
-                          int32_t* inputs, void* cuda_stream) {
+static int decode_launch(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitmaps,
+                         int sync_bitmaps, void* scratch, const uint16_t* embed, int n_streams,
+                         const int32_t* forced, int n_forced, int n_tokens, int32_t* preds,
+                         int32_t* inputs, void* cuda_stream) {
   if (!p || !state_ptrs || !bitmaps || !scratch || !embed || !forced || !preds ||
       n_streams < 1 || n_forced < 1 || n_tokens < 1 || n_streams > 65535)
     return LXB_E_INVAL;
@@ -1565,6 +1568,54 @@ extern "C" int lxb_decode(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bit
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, lxb_decode_kernel, p->dev, run);
   return cuda_rc(e);
+}
+
+extern "C" int lxb_decode(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitmaps,
+                          int sync_bitmaps, void* scratch, const uint16_t* embed, int n_streams,
+                          const int32_t* forced, int n_forced, int n_tokens, int32_t* preds,
+                          int32_t* inputs, void* cuda_stream) {
+  return decode_launch(p, state_ptrs, bitmaps, sync_bitmaps, scratch, embed, n_streams, forced,
+                       n_forced, n_tokens, preds, inputs, cuda_stream);
+}
+
+// --- decoding without allocating -------------------------------------------------------------
+// Some hosts cannot give this library any device memory after start-up: a serving process whose
+// device memory is one pool carved up when it starts, or a host whose allocator is not
+// CUDA-aware and hands out only the buffers it manages (state, tokens, predictions). For them the
+// decode's scratch (the 4-step residual ring of the lazily kept conv windows) lives in this
+// file-scope device array instead of a caller buffer. Every GPU that loads the library holds it
+// until the process exits. All calls on a device share it and it keeps the last call's contents;
+// the kernel writes every ring slot before it reads it, so nothing needs clearing, but two calls
+// that overlap on the GPU (other streams, other threads) race on it.
+static __device__ __align__(256) unsigned char lxb_noalloc_scratch[LXB_NOALLOC_MAX_SCRATCH];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[LXB_MAX_DEVICES];  // the array's device address, per device
+
+extern "C" int lxb_decode_noalloc(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitmaps,
+                                  int sync_bitmaps, const uint16_t* embed, int n_streams,
+                                  const int32_t* forced, int n_forced, int n_tokens,
+                                  int32_t* preds, int32_t* inputs, void* cuda_stream) {
+  if (!p || n_streams < 1) return LXB_E_INVAL;
+  if (lxb_scratch_bytes(p, n_streams) > LXB_NOALLOC_MAX_SCRATCH) return LXB_E_TOOBIG;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e) return cuda_rc(e);
+  if (dev != p->device || dev < 0 || dev >= LXB_MAX_DEVICES) return LXB_E_INVAL;
+  void* ptr = nullptr;
+  {
+    // set-up, once per device, with that device current: the host-side name of the array is
+    // not its device address
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      e = cudaGetSymbolAddress(&ptr, lxb_noalloc_scratch);
+      if (e) return cuda_rc(e);
+      g_noalloc_ptr[dev] = ptr;
+    }
+    ptr = g_noalloc_ptr[dev];
+  }
+  return decode_launch(p, state_ptrs, bitmaps, sync_bitmaps, ptr, embed, n_streams, forced,
+                       n_forced, n_tokens, preds, inputs, cuda_stream);
 }
 
 extern "C" int lxb_status(lxb_plan* p, lxb_error* err) {
