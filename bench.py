@@ -151,11 +151,10 @@ def main():
 
     import numpy as np
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-
     from linuxformer_b200 import chip as C
+    from linuxformer_b200.streams import job_rate, rank_env, slowest, stream_seed
+
+    rank, world, local = rank_env()
 
     kw = {"vocab": a.vocab} if a.vocab else {}
     workload = (f"c2: 37-layer chip-shaped stack, greedy decode of {a.steps * a.tokens} tokens "
@@ -211,7 +210,7 @@ def main():
     from linuxformer_b200.runtime import Decoder
 
     chip = C.c2(1, **kw)
-    st0 = C.c2_state(chip, 1 + rank)
+    st0 = C.c2_state(chip, stream_seed(1, rank))
     dec = Decoder(chip, cluster=a.cluster, device=dev)
     states = dec.states([st0])
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -267,17 +266,13 @@ def main():
         e2e_t.append(time.perf_counter() - t0)
         last = int(out[0, -1])
     e2e_tot = sum(e2e_t)
-    if world > 1:
-        t = torch.tensor([tot, e2e_tot], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        tot, e2e_tot = float(t[0]), float(t[1])
+    tot, e2e_tot = slowest([tot, e2e_tot], dev)  # the slowest rank's times
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
         return
-    tokens = a.steps * T * world
-    value = tokens / tot
-    e2e_value = e2e_steps * T * world / e2e_tot
+    value = job_rate(a.steps * T, world, tot)
+    e2e_value = job_rate(e2e_steps * T, world, e2e_tot)
     peak, peak_kind = _peaks()
     cpu_v, counts, cores, same = cpu
     btok = bytes_per_token(counts)

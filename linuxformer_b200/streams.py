@@ -1,0 +1,43 @@
+"""Independent decode streams over several GPUs: one process per GPU, one machine per process.
+
+The chip decode does not shard inside a stream (every token depends on the previous one through
+the whole stack), so N GPUs run N independent machines: rank r decodes its own stream from its
+own state, with no collective on the decode path. The only exchange is the host-side timing
+reduction of a benchmark (the slowest rank's device time). Works with the ``nccl`` backend on
+GPUs and ``gloo`` on CPU (the multi-rank tests).
+"""
+
+from __future__ import annotations
+
+import os
+
+
+def rank_env() -> tuple[int, int, int]:
+    """(rank, world_size, local_rank) from the torchrun environment (1 process when unset)."""
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def stream_seed(base: int, rank: int) -> int:
+    """The state seed of rank ``rank``'s machine: every rank a different stream."""
+    return base + rank
+
+
+def slowest(values, device=None) -> list[float]:
+    """Element-wise maximum of ``values`` over all ranks (the identity with one process)."""
+    import torch
+    import torch.distributed as dist
+
+    vals = [float(v) for v in values]
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return vals
+    t = torch.tensor(vals, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.cpu()]
+
+
+def job_rate(units_per_rank: float, world: int, slowest_seconds: float) -> float:
+    """Whole-job throughput: the units every rank processed over the slowest rank's time."""
+    if slowest_seconds <= 0:
+        raise ValueError("a non-positive time")
+    return units_per_rank * world / slowest_seconds

@@ -1,0 +1,86 @@
+"""The multi-GPU path's host logic as two gloo ranks on CPU: every rank its own machine (a
+different stream, the same as a lone process decoding that seed), and the slowest rank's time
+as the whole job's. The decode itself is the CPU restatement here (no GPU)."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from linuxformer_b200 import chip as C  # noqa: E402
+from linuxformer_b200.streams import job_rate, rank_env, slowest, stream_seed  # noqa: E402
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _decode(seed: int, n: int):
+    from oracle.oracle import Oracle
+
+    chip = C.c1(0)
+    st = C.c1_state(chip, seed)
+    preds, _, _ = Oracle(chip).decode(st, [0], n)
+    return preds, st
+
+
+def _rank(rank: int, world: int, port: int, q) -> None:
+    import torch.distributed as dist
+
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    try:
+        import datetime
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+        r, w, _ = rank_env()
+        preds, st = _decode(stream_seed(1, r), 24)
+        times = slowest([0.5 + r, 2.0 - r])  # rank-dependent "device times"
+        got = [None] * w
+        dist.all_gather_object(got, preds.tolist())  # the test's own check, not the path's
+        dist.destroy_process_group()
+        q.put((r, w, (preds.tolist(), float(np.abs(st.recurrent).sum())), times, got))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, -1, repr(e), None, None))
+
+
+def test_two_ranks_decode_their_own_streams():
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in ps:
+        r, w, preds, times, got = q.get(timeout=240)
+        assert w == 2, preds
+        res[r] = (preds, times, got)
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # each rank's stream is what a lone process decodes from that rank's seed
+    for r in range(2):
+        alone, st = _decode(stream_seed(1, r), 24)
+        assert res[r][0] == (alone.tolist(), float(np.abs(st.recurrent).sum()))
+    assert res[0][0][1] != res[1][0][1]  # different machines (their final states differ)
+    # the reduction: element-wise max over ranks, the same on both
+    assert res[0][1] == res[1][1] == [1.5, 2.0]
+    assert res[0][2] == res[1][2] == [res[0][0][0], res[1][0][0]]
+
+
+def test_single_process_helpers():
+    assert slowest([1.0, 3.0]) == [1.0, 3.0]
+    assert job_rate(100, 4, 2.0) == 200.0
+    with pytest.raises(ValueError):
+        job_rate(1, 1, 0.0)
+    assert np.unique([stream_seed(1, r) for r in range(8)]).size == 8
