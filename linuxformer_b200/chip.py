@@ -284,6 +284,8 @@ def to_hf(chip: Chip):
     sd["lm_head.weight"] = t(chip.head.to_dense())
     missing, unexpected = model.load_state_dict(sd, strict=False, assign=True)
     assert not unexpected and not missing, (missing[:5], unexpected[:5])
+    # the rotary tables are buffers, not weights: build them on the host so the model can move
+    model.model.rotary_emb = type(model.model.rotary_emb)(config=cfg)
     return model.eval()
 
 
