@@ -136,6 +136,9 @@ struct __align__(16) Smem {
       float xr[H];                 // input_layernorm of an earlier step's residual
       uint16_t pw[4][LXB_NSLOT];   // lazy channels: their projections at 4 steps
     } lz;
+    struct {
+      alignas(16) uint16_t xb[3][H];  // a key's firing: the 3 earlier steps' input norms
+    } lf;
   };
   float hbuf[LXB_MAXUNITS];        // MLP unit outputs
   float prod[LXB_MAXPROD];         // MLP gate/up products, in the units' entry order
@@ -200,8 +203,9 @@ __device__ __forceinline__ void stage_issue(const Dev& P, Smem& sm, unsigned cha
   unsigned char* dst = stage + (size_t)buf * P.stage;
   const unsigned char* src = P.blobs + br.off;
   const uint32_t mb = smem_u32(&sm.mbar[buf]);
-  // the buffer was last read through the generic proxy; order that before the async writes
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  // the buffer was last read through the generic proxy, by threads that have passed a block
+  // barrier since: an async-proxy write after generic reads needs no proxy fence (the ordering
+  // of the usual bulk-copy producer/consumer pipelines)
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mb),
                "r"((uint32_t)br.bytes)
                : "memory");
@@ -347,6 +351,88 @@ __device__ void lazy_proj(const Dev& P, const Run& run, Smem& sm, const lxb_item
   }
 }
 
+__device__ __forceinline__ float d_silu(float x) { return lx_silu(x); }
+
+// A key fired: the conv outputs at this step of the item's value channels with a nonzero tap,
+// into sm.buf at their slots. The stock step's window would hold the channel's projections P at
+// the last four steps: P(step) from sm.xn (this step's input norm, built by the caller), P at the
+// three steps before from the residual ring (their input norms rebuilt once for all channels, as
+// bf16, only for the tap positions some channel has), or, for steps before the launch, from the
+// window as the launch found it. Every channel evaluates only its nonzero taps, all from one pass
+// over its entries (each tap's dot still sequential from +0 in entry order).
+__device__ void lazy_fire(const Dev& P, const Run& run, Smem& sm, const lxb_item& it,
+                          const uint16_t* conv, int s, int L, int step, const uint16_t* w) {
+  const int t = threadIdx.x;
+  int need = 0;
+  for (int p = 0; p < 3; p++)
+    if (((it.tapu >> p) & 1) && step - 3 + p >= 0) need |= 1 << p;
+  if (need) {
+    for (int k = t; k < 3 * (H / 8); k += NT) {
+      const int p = k / (H / 8), kk = k - p * (H / 8);
+      if (!((need >> p) & 1)) continue;
+      const size_t slot = ((size_t)s * P.n_layers + L) * 4 + ((step - 3 + p) & 3);
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(run.ring + slot * H) + kk);
+      const float r = __ldcg(run.ring_r + slot);
+      const uint32_t xw[4] = {v.x, v.y, v.z, v.w};
+      const uint16_t* wv = w + 8 * kk;
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const float x0 = lx_f((uint16_t)(xw[q] & 0xffffu)), x1 = lx_f((uint16_t)(xw[q] >> 16));
+        const uint16_t y0 = lx_rb(lx_mul(lx_mul(x0, r), lx_add(1.0f, lx_f(wv[2 * q]))));
+        const uint16_t y1 = lx_rb(lx_mul(lx_mul(x1, r), lx_add(1.0f, lx_f(wv[2 * q + 1]))));
+        o[q] = (uint32_t)y0 | ((uint32_t)y1 << 16);
+      }
+      reinterpret_cast<uint4*>(sm.lf.xb[p])[kk] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    __syncthreads();
+  }
+  for (int c = it.n_eager + t; c < it.n_eager + it.n_vneed; c += NT) {
+    const uint4* cp = reinterpret_cast<const uint4*>(P.chans + it.ch0 + c);
+    const uint4 a = __ldg(cp);      // entries, count | slot << 16, conv channel, taps 0-1
+    const uint4 b = __ldg(cp + 1);  // taps 2-3, tap mask
+    const uint32_t tm = b.y;
+    int dm = 0;  // the taps whose P is a dot product (a nonzero tap at a step of this launch)
+    for (int p = 0; p < 4; p++)
+      if (((tm >> p) & 1) && step - 3 + p >= 0) dm |= 1 << p;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int n = (int)(a.y & 0xffffu);
+    for (int e = 0; e < n; e += 8) {
+      uint32_t wv[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) wv[q] = e + q < n ? __ldg(P.ent + a.x + e + q) : 0u;
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        if (e + q >= n) continue;
+        const uint32_t col = wv[q] & 0xffffu;
+        const float wf = lx_f((uint16_t)(wv[q] >> 16));
+        if (dm & 1) acc[0] = lx_add(acc[0], lx_mul(lx_f(sm.lf.xb[0][col]), wf));
+        if (dm & 2) acc[1] = lx_add(acc[1], lx_mul(lx_f(sm.lf.xb[1][col]), wf));
+        if (dm & 4) acc[2] = lx_add(acc[2], lx_mul(lx_f(sm.lf.xb[2][col]), wf));
+        if (dm & 8) acc[3] = lx_add(acc[3], lx_mul(sm.xn[col], wf));
+      }
+    }
+    uint2 win = make_uint2(0u, 0u);
+    if (tm & ~dm & 15) win = *reinterpret_cast<const uint2*>(conv + (size_t)a.z * 4);
+    const uint16_t taps[4] = {(uint16_t)(a.w & 0xffffu), (uint16_t)(a.w >> 16),
+                              (uint16_t)(b.x & 0xffffu), (uint16_t)(b.x >> 16)};
+    float y = 0.0f;
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+      uint16_t pv = 0;
+      if ((dm >> p) & 1) {
+        pv = lx_rb(acc[p]);
+      } else if ((tm >> p) & 1) {  // a step before the launch: positions 0..3 hold steps -4..-1
+        const int pos = step + 1 + p;
+        const uint32_t wd = pos < 2 ? win.x : win.y;
+        pv = (uint16_t)((pos & 1) ? wd >> 16 : wd & 0xffffu);
+      }
+      y = lx_add(y, lx_mul(lx_f(taps[p]), lx_f(pv)));
+    }
+    sm.buf[a.y >> 16] = lx_rbf(d_silu(lx_rbf(y)));
+  }
+}
+
 // --- a GDN item: one live key head of one layer --------------------------------------------------
 // transformers' l2norm in bf16 over a compacted list (the nonzero entries in ascending order):
 // x * rsqrt(sum(x * x) + 1e-6), the bf16 squares summed sequentially from +0 by one lane
@@ -363,17 +449,30 @@ __device__ __forceinline__ float xn_at(const Smem& sm, const uint16_t* w, float 
 
 // One eager (query/key) channel: in_proj_qkv row over the staged entries (the input norm taken
 // per column), conv window shift (resident in shared memory, or in global), conv output with
-// silu in bf16.
+// silu in bf16. pr: the row's products, computed beforehand by the whole block (then only the
+// sequential sum is this thread's), or null (the products here).
 __device__ __forceinline__ float eager_channel(Smem& sm, const unsigned char* B, const uint4 a,
                                                const uint4 b, uint16_t* conv, const uint16_t* w,
-                                               float r) {
+                                               float r, const float* pr) {
   const uint32_t* e = reinterpret_cast<const uint32_t*>(B + a.x);
   const int ne = (int)(a.y & 0xffffu);
   uint2* wp = b.y != LXB_NOWIN ? &sm.win[b.y] : reinterpret_cast<uint2*>(conv + (size_t)a.z * 4);
   const uint2 win = *wp;
   float ps = 0.0f;
-  for (int k = 0; k < ne; k++)
-    ps = lx_add(ps, lx_mul(xn_at(sm, w, r, e[k] & 0xffffu), lx_f((uint16_t)(e[k] >> 16))));
+  if (pr) {
+    int k = 0;
+    for (; k + 8 <= ne; k += 8) {
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) v[q] = pr[k + q];
+#pragma unroll
+      for (int q = 0; q < 8; q++) ps = lx_add(ps, v[q]);
+    }
+    for (; k < ne; k++) ps = lx_add(ps, pr[k]);
+  } else {
+    for (int k = 0; k < ne; k++)
+      ps = lx_add(ps, lx_mul(xn_at(sm, w, r, e[k] & 0xffffu), lx_f((uint16_t)(e[k] >> 16))));
+  }
   const uint16_t Pv = lx_rb(ps);
   const uint16_t n0 = (uint16_t)(win.x >> 16), n1 = (uint16_t)(win.y & 0xffffu),
                  n2 = (uint16_t)(win.y >> 16);
@@ -383,7 +482,168 @@ __device__ __forceinline__ float eager_channel(Smem& sm, const unsigned char* B,
   y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(n1)));
   y = lx_add(y, lx_mul(lx_f((uint16_t)(b.x & 0xffffu)), lx_f(n2)));
   y = lx_add(y, lx_mul(lx_f((uint16_t)(b.x >> 16)), lx_f(Pv)));
-  return lx_rbf(lx_silu(lx_rbf(y)));
+  return lx_rbf(d_silu(lx_rbf(y)));
+}
+
+// Pieces of an item: the rare paths (many query/key channels, decay, a key firing, output).
+
+// a row dot over staged entries with the input norm taken per column (b / a rows, z rows)
+__device__ __forceinline__ float xrow_dot(const Smem& sm, const uint32_t* e, int ne,
+                                          const uint16_t* w_in, float r_in) {
+  float d = 0.0f;
+  for (int k = 0; k < ne; k++)
+    d = lx_add(d, lx_mul(xn_at(sm, w_in, r_in, e[k] & 0xffffu), lx_f((uint16_t)(e[k] >> 16))));
+  return d;
+}
+
+// many query/key channels: a dense q | k buffer, then compaction by warps 0 and 1
+__device__ __forceinline__ void eager_block(Smem& sm, const unsigned char* B, const lxb_bitem& bi,
+                                         uint16_t* conv, const uint16_t* w_in, float r_in,
+                                         const float* pre_base, uint32_t e_first) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const uint4* ch = reinterpret_cast<const uint4*>(B + bi.eager);
+  for (int k = t; k < 2 * KD; k += NT) sm.buf[k] = 0.0f;
+  __syncthreads();
+  for (int c = t; c < bi.n_eager; c += NT) {
+    const uint4 a = ch[2 * c], b = ch[2 * c + 1];
+    sm.buf[a.y >> 16] = eager_channel(sm, B, a, b, conv, w_in, r_in,
+                                      pre_base ? pre_base + (a.x - e_first) / 4u : nullptr);
+  }
+  __syncthreads();
+  if (warp < 2) {
+    const float* xv = sm.buf + warp * KD;
+    int* idx = warp ? sm.kidx : sm.qidx;
+    float* val = warp ? sm.kval : sm.qval;
+    int n = 0;
+    for (int base = 0; base < KD; base += 32) {
+      const float v = xv[base + lane];
+      const unsigned m = __ballot_sync(0xffffffffu, v != 0.0f);
+      if (v != 0.0f) {
+        const int k = n + __popc(m & ((1u << lane) - 1u));
+        idx[k] = base + lane;
+        val[k] = v;
+      }
+      n += __popc(m);
+    }
+    __syncwarp();
+    float inv = 0.0f;
+    if (lane == 0 && n) inv = l2_inv(val, n);
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    for (int i = lane; i < n; i += 32) {
+      const float vn = lx_rbf(lx_mul(val[i], inv));
+      val[i] = warp ? vn : lx_mul(vn, 0.0625f);  // the query times 256^-0.5
+    }
+    if (lane == 0) (warp ? sm.nk : sm.nq) = n;
+    if (t == 0) sm.vhmask[bi.slot] = 0;
+  }
+}
+
+// g = -exp(A_log) * softplus(bf16(a . x) + dt_bias) of value head r, for a head that can decay
+__device__ __forceinline__ float item_g(const Smem& sm, const unsigned char* B, const lxb_bitem& bi,
+                                     int r, const uint16_t* w_in, float r_in) {
+  const int32_t* brows = reinterpret_cast<const int32_t*>(B + bi.rows);
+  const uint16_t* prm = reinterpret_cast<const uint16_t*>(B + bi.prm);
+  const float d = xrow_dot(sm, reinterpret_cast<const uint32_t*>(B + brows[2 * (R + r)]),
+                           brows[2 * (R + r) + 1], w_in, r_in);
+  const float A = -lx_exp(lx_f(prm[r]));
+  return lx_mul(A, lx_softplus(lx_add(lx_rbf(d), lx_f(prm[R + r]))));
+}
+
+// A key fired: beta = bf16(sigmoid(bf16(b . x))) (warp 1), and the value channels' conv outputs
+// at this step into their q | k | v slots (the others zero). Ends with a block barrier.
+__device__ __forceinline__ void item_fire(const Dev& P, const Run& run, Smem& sm,
+                                       const unsigned char* B, const lxb_bitem& bi,
+                                       uint16_t* conv, int s, int L, int step,
+                                       const uint16_t* w_in, float r_in) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  if (warp == 1 && lane < R) {
+    const int32_t* brows = reinterpret_cast<const int32_t*>(B + bi.rows);
+    const float d = xrow_dot(sm, reinterpret_cast<const uint32_t*>(B + brows[2 * lane]),
+                             brows[2 * lane + 1], w_in, r_in);
+    sm.beta[lane] = lx_rbf(lx_sigmoid(lx_rbf(d)));
+  }
+  for (int k = t; k < R * VD; k += NT) sm.buf[2 * KD + k] = 0.0f;
+  const lxb_item it = P.items[bi.item];
+  if (it.n_vneed) {
+    norm_into(sm.xn, sm.x, w_in, r_in);  // this step's input norm, for the lazy projections
+    __syncthreads();
+    lazy_fire(P, run, sm, it, conv, s, L, step, w_in);
+  }
+  __syncthreads();
+}
+
+// The state's change for value head r, column j (S points at row 0, column j): the decay of the
+// rows that may be nonzero (the others stay zero), then the key's delta-rule write.
+__device__ __forceinline__ void item_write(Smem& sm, float* S, const uint32_t* bmv, int r, int j,
+                                        int nk) {
+  const float g = sm.g[r];
+  if (g != 0.0f) {
+    const float e = lx_exp(g);
+#pragma unroll 1
+    for (int w = 0; w < 8; w++) {
+      uint32_t m = bmv[w];
+      while (m) {
+        int ix[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          ix[q] = m ? (w * 32 + __ffs(m) - 1) : -1;
+          m &= m - 1;
+        }
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) v[q] = ix[q] >= 0 ? S[ix[q] * VD] : 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; q++)
+          if (ix[q] >= 0) S[ix[q] * VD] = lx_mul(v[q], e);
+      }
+    }
+  }
+  if (nk) {
+    float kv = 0.0f;
+    for (int a0 = 0; a0 < nk; a0 += 8) {
+      float hv[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) hv[q] = a0 + q < nk ? S[sm.kidx[a0 + q] * VD] : 0.0f;
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+        if (a0 + q < nk) kv = lx_add(kv, lx_mul(hv[q], sm.kval[a0 + q]));
+    }
+    const float delta = lx_mul(lx_sub(sm.buf[2 * KD + r * VD + j], kv), sm.beta[r]);
+    for (int a = 0; a < nk; a++) {
+      float* hp = S + sm.kidx[a] * VD;
+      *hp = lx_add(*hp, lx_mul(sm.kval[a], delta));
+    }
+  }
+}
+
+// Qwen3_5RMSNormGated of value head r (one warp, lane: columns lane + 32 q) whose o is not all
+// zero: bf16(bf16(w * bf16(o * rsqrt(mean(o^2) + eps))) * silu(z)), z = bf16(in_proj_z . x)
+__device__ __forceinline__ void item_out(const Dev& P, Smem& sm, const unsigned char* B,
+                                      const lxb_bitem& bi, int r, const uint16_t* w_in,
+                                      float r_in) {
+  const int lane = threadIdx.x & 31;
+  const float* o = sm.ob[r];
+  const float o0 = o[4 * lane], o1 = o[4 * lane + 1], o2 = o[4 * lane + 2], o3 = o[4 * lane + 3];
+  const int32_t* zp = reinterpret_cast<const int32_t*>(B + bi.z);
+  const uint32_t* ze = reinterpret_cast<const uint32_t*>(B + bi.z + ((4 * 1025 + 15) & ~15));
+  float sq = lx_mul(o0, o0);
+  sq = lx_add(sq, lx_mul(o1, o1));
+  sq = lx_add(sq, lx_mul(o2, o2));
+  sq = lx_add(sq, lx_mul(o3, o3));
+  sq = warp_xor_sum(sq);
+  const float rr = lx_rsqrt(lx_add(lx_div(sq, 128.0f), P.eps));
+  const uint16_t* gw = reinterpret_cast<const uint16_t*>(B + bi.prm) + 2 * R;
+  uint16_t* on = sm.on[bi.slot];
+#pragma unroll 1
+  for (int q = 0; q < 4; q++) {
+    const int j = lane + 32 * q;
+    const int zr = r * VD + j;
+    const float z = xrow_dot(sm, ze + zp[zr], zp[zr + 1] - zp[zr], w_in, r_in);
+    const float hn = lx_rbf(lx_mul(o[j], rr));
+    const float u = lx_rbf(lx_mul(lx_f(gw[j]), hn));
+    on[r * VD + j] = lx_rb(lx_mul(u, d_silu(lx_rbf(z))));
+  }
+  if (lane == 0) atomicOr(&sm.vhmask[bi.slot], 1u << r);
 }
 
 // B: the step blob (shared memory); bi: this item's record in it; w_in: the staged input norm.
@@ -392,8 +652,23 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
                          const lxb_bitem& bi, float* rec, uint16_t* conv, uint32_t* bm, int s,
                          int L, int step, const uint16_t* w_in, float r_in) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  uint16_t* on = sm.on[bi.slot];
   const uint4* ch = reinterpret_cast<const uint4*>(B + bi.eager);
+  // the eager rows' products, all entries at once over the block (the entries of the item's
+  // eager channels are contiguous in the blob, in channel order)
+  uint32_t e_first = 0;
+  bool pre = false;
+  if (bi.n_eager > 0) {
+    e_first = ch[0].x;
+    const uint4 al = ch[2 * (bi.n_eager - 1)];
+    const int ntot = (int)((al.x + 4u * (al.y & 0xffffu) - e_first) / 4u);
+    if (ntot <= LXB_MAXPROD) {
+      const uint32_t* E = reinterpret_cast<const uint32_t*>(B + e_first);
+      for (int k = t; k < ntot; k += NT)
+        sm.prod[k] = lx_mul(xn_at(sm, w_in, r_in, E[k] & 0xffffu), lx_f((uint16_t)(E[k] >> 16)));
+      __syncthreads();
+      pre = true;
+    }
+  }
   if (bi.n_eager <= 32) {
     // one warp: the channels in ascending order (queries, then keys), compacted by ballot
     if (warp == 0) {
@@ -401,7 +676,8 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
       int slot = 0;
       if (lane < bi.n_eager) {
         const uint4 a = ch[2 * lane], b = ch[2 * lane + 1];
-        v = eager_channel(sm, B, a, b, conv, w_in, r_in);
+        v = eager_channel(sm, B, a, b, conv, w_in, r_in,
+                          pre ? sm.prod + (a.x - e_first) / 4u : nullptr);
         slot = (int)(a.y >> 16);
       }
       const bool nz = lane < bi.n_eager && v != 0.0f;
@@ -420,12 +696,14 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
       }
       __syncwarp();
       const int nq = __popc(mq), nk = __popc(mk);
-      float inv = 0.0f;
-      if (lane == 0 && nq) inv = l2_inv(sm.qval, nq);
-      if (lane == 1 && nk) inv = l2_inv(sm.kval, nk);
-      const float iq = __shfl_sync(0xffffffffu, inv, 0), ik = __shfl_sync(0xffffffffu, inv, 1);
-      if (lane < nq) sm.qval[lane] = lx_mul(lx_rbf(lx_mul(sm.qval[lane], iq)), 0.0625f);
-      if (lane < nk) sm.kval[lane] = lx_rbf(lx_mul(sm.kval[lane], ik));
+      if (nq | nk) {
+        float inv = 0.0f;
+        if (lane == 0 && nq) inv = l2_inv(sm.qval, nq);
+        if (lane == 1 && nk) inv = l2_inv(sm.kval, nk);
+        const float iq = __shfl_sync(0xffffffffu, inv, 0), ik = __shfl_sync(0xffffffffu, inv, 1);
+        if (lane < nq) sm.qval[lane] = lx_mul(lx_rbf(lx_mul(sm.qval[lane], iq)), 0.0625f);
+        if (lane < nk) sm.kval[lane] = lx_rbf(lx_mul(sm.kval[lane], ik));
+      }
       if (lane == 0) {
         sm.nq = nq;
         sm.nk = nk;
@@ -433,185 +711,64 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
       }
     }
   } else {
-    // many query/key channels: a dense q | k buffer, then compaction by warps 0 and 1
-    for (int k = t; k < 2 * KD; k += NT) sm.buf[k] = 0.0f;
-    __syncthreads();
-    for (int c = t; c < bi.n_eager; c += NT) {
-      const uint4 a = ch[2 * c], b = ch[2 * c + 1];
-      sm.buf[a.y >> 16] = eager_channel(sm, B, a, b, conv, w_in, r_in);
-    }
-    __syncthreads();
-    if (warp < 2) {
-      const float* xv = sm.buf + warp * KD;
-      int* idx = warp ? sm.kidx : sm.qidx;
-      float* val = warp ? sm.kval : sm.qval;
-      int n = 0;
-      for (int base = 0; base < KD; base += 32) {
-        const float v = xv[base + lane];
-        const unsigned m = __ballot_sync(0xffffffffu, v != 0.0f);
-        if (v != 0.0f) {
-          const int k = n + __popc(m & ((1u << lane) - 1u));
-          idx[k] = base + lane;
-          val[k] = v;
-        }
-        n += __popc(m);
-      }
-      __syncwarp();
-      float inv = 0.0f;
-      if (lane == 0 && n) inv = l2_inv(val, n);
-      inv = __shfl_sync(0xffffffffu, inv, 0);
-      for (int i = lane; i < n; i += 32) {
-        const float vn = lx_rbf(lx_mul(val[i], inv));
-        val[i] = warp ? vn : lx_mul(vn, 0.0625f);  // the query times 256^-0.5
-      }
-      if (lane == 0) (warp ? sm.nk : sm.nq) = n;
-      if (t == 0) sm.vhmask[bi.slot] = 0;
-    }
+    eager_block(sm, B, bi, conv, w_in, r_in, pre ? sm.prod : nullptr, e_first);
   }
-  // warp 1: g = -exp(A_log) * softplus(bf16(a . x) + dt_bias); beta = bf16(sigmoid(bf16(b . x)))
-  const uint16_t* prm = reinterpret_cast<const uint16_t*>(B + bi.prm);
-  if (warp == 1 && lane < 2 * R) {
-    const int32_t* brows = reinterpret_cast<const int32_t*>(B + bi.rows);
-    const int r = lane & (R - 1);
-    const int q = lane < R ? R + r : r;
-    const uint32_t* e = reinterpret_cast<const uint32_t*>(B + brows[2 * q]);
-    const int ne = brows[2 * q + 1];
-    float d = 0.0f;
-    for (int k = 0; k < ne; k++)
-      d = lx_add(d, lx_mul(xn_at(sm, w_in, r_in, e[k] & 0xffffu), lx_f((uint16_t)(e[k] >> 16))));
-    if (lane < R) {
-      const float A = -lx_exp(lx_f(prm[r]));
-      sm.g[r] = lx_mul(A, lx_softplus(lx_add(lx_rbf(d), lx_f(prm[R + r]))));
-    } else {
-      sm.beta[r] = lx_rbf(lx_sigmoid(lx_rbf(d)));
-    }
-  }
+  // warp 1: g, only for a head that can decay (for the others softplus underflows to zero
+  // whatever the input: g is 0, as the table builder proved); beta only when a key fires
+  if (warp == 1 && lane < R)
+    sm.g[lane] = (bi.flags & LXB_IT_DECAYS) ? item_g(sm, B, bi, lane, w_in, r_in) : 0.0f;
   __syncthreads();
   const int nq = sm.nq, nk = sm.nk;
   int anyg = 0;
 #pragma unroll
   for (int r = 0; r < R; r++) anyg |= sm.g[r] != 0.0f;
   if (!nq && !nk && !anyg) return false;  // the state stays as it is and o = 0
-  if (nk) {
-    // a key fired: the value channels' conv outputs at this step, from their projections at
-    // the last four steps (the window a stock step would hold); other value slots are zero
-    for (int k = t; k < R * VD; k += NT) sm.buf[2 * KD + k] = 0.0f;
-    const lxb_item it = P.items[bi.item];
-    if (it.n_vneed) {
-      norm_into(sm.xn, sm.x, w_in, r_in);  // this step's input norm, for the lazy projections
-      __syncthreads();
-      const int c0 = it.n_eager, c1 = it.n_eager + it.n_vneed;
-      lazy_proj(P, run, sm, it, conv, s, L, step - 3, step, true, c0, c1, w_in);
-      for (int c = c0 + t; c < c1; c += NT) {
-        const lxb_chan* cp = P.chans + it.ch0 + c;
-        const uint4 a = __ldg(reinterpret_cast<const uint4*>(cp));
-        const uint32_t t23 = __ldg(reinterpret_cast<const uint4*>(cp) + 1).x;
-        const int i = c - c0;
-        float y = 0.0f;
-        y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(sm.lz.pw[0][i])));
-        y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(sm.lz.pw[1][i])));
-        y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 & 0xffffu)), lx_f(sm.lz.pw[2][i])));
-        y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(sm.lz.pw[3][i])));
-        sm.buf[a.y >> 16] = lx_rbf(lx_silu(lx_rbf(y)));
-      }
-    }
-    __syncthreads();
-  }
-  // the delta rule, thread = (value head, state column)
+  if (nk) item_fire(P, run, sm, B, bi, conv, s, L, step, w_in, r_in);
+  // the delta rule, thread = (state column j, value heads rA and rA + 4): the decay and the
+  // key's write per head (rare), then both heads' readouts with their loads in flight together
+  static_assert(NT / VD == 4 && R == 8, "two value heads per thread");
   {
     const int j = t & (VD - 1);
-    for (int r = t >> 7; r < R; r += NT / VD) {
-      const int vh = bi.kh * R + r;
-      float* S = rec + (size_t)vh * KD * VD + j;
-      const float g = sm.g[r];
-      if (g != 0.0f) {  // decay the rows that may be nonzero (the others stay zero)
-        const float e = lx_exp(g);
-        const uint32_t* b = bm + vh * 8;
-#pragma unroll 1
-        for (int w = 0; w < 8; w++) {
-          uint32_t m = b[w];
-          while (m) {
-            int ix[4];
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-              ix[q] = m ? (w * 32 + __ffs(m) - 1) : -1;
-              m &= m - 1;
-            }
-            float v[4];
-#pragma unroll
-            for (int q = 0; q < 4; q++) v[q] = ix[q] >= 0 ? S[ix[q] * VD] : 0.0f;
-#pragma unroll
-            for (int q = 0; q < 4; q++)
-              if (ix[q] >= 0) S[ix[q] * VD] = lx_mul(v[q], e);
-          }
-        }
-      }
-      if (nk) {
-        float kv = 0.0f;
-        for (int a0 = 0; a0 < nk; a0 += 8) {
-          float hv[8];
-#pragma unroll
-          for (int q = 0; q < 8; q++) hv[q] = a0 + q < nk ? S[sm.kidx[a0 + q] * VD] : 0.0f;
-#pragma unroll
-          for (int q = 0; q < 8; q++)
-            if (a0 + q < nk) kv = lx_add(kv, lx_mul(hv[q], sm.kval[a0 + q]));
-        }
-        const float delta = lx_mul(lx_sub(sm.buf[2 * KD + r * VD + j], kv), sm.beta[r]);
-        for (int a = 0; a < nk; a++) {
-          float* hp = S + sm.kidx[a] * VD;
-          *hp = lx_add(*hp, lx_mul(sm.kval[a], delta));
-        }
-      }
-      float o = 0.0f;
-      for (int a0 = 0; a0 < nq; a0 += 8) {
-        float hv[8];
-#pragma unroll
-        for (int q = 0; q < 8; q++) hv[q] = a0 + q < nq ? S[sm.qidx[a0 + q] * VD] : 0.0f;
-#pragma unroll
-        for (int q = 0; q < 8; q++)
-          if (a0 + q < nq) o = lx_add(o, lx_mul(hv[q], sm.qval[a0 + q]));
-      }
-      sm.ob[r][j] = lx_rbf(o);
+    const int rA = t >> 7;
+    float* SA = rec + (size_t)(bi.kh * R + rA) * KD * VD + j;
+    float* SB = SA + (size_t)4 * KD * VD;
+    if (anyg | nk) {
+      item_write(sm, SA, bm + (bi.kh * R + rA) * 8, rA, j, nk);
+      item_write(sm, SB, bm + (bi.kh * R + rA + 4) * 8, rA + 4, j, nk);
     }
+    float oA = 0.0f, oB = 0.0f;
+    for (int a0 = 0; a0 < nq; a0 += 8) {
+      float hA[8], hB[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        const bool ok = a0 + q < nq;
+        const int ix = ok ? sm.qidx[a0 + q] : 0;
+        hA[q] = ok ? SA[ix * VD] : 0.0f;
+        hB[q] = ok ? SB[ix * VD] : 0.0f;
+      }
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+        if (a0 + q < nq) {
+          const float qv = sm.qval[a0 + q];
+          oA = lx_add(oA, lx_mul(hA[q], qv));
+          oB = lx_add(oB, lx_mul(hB[q], qv));
+        }
+    }
+    sm.ob[rA][j] = lx_rbf(oA);
+    sm.ob[rA + 4][j] = lx_rbf(oB);
   }
   __syncthreads();
   if ((bi.flags & LXB_IT_DECAYS) && t < R) {  // rows the key wrote may now be nonzero
     uint32_t* b = bm + (bi.kh * R + t) * 8;
     for (int a = 0; a < nk; a++) b[sm.kidx[a] >> 5] |= 1u << (sm.kidx[a] & 31);
   }
-  // Qwen3_5RMSNormGated per value head with output (warp r): bf16(bf16(w * bf16(o * rsqrt(
-  // mean(o^2) + eps))) * silu(z)), z = bf16(in_proj_z . x); a head without out_proj entries
-  // has no z rows staged and cannot write: it skips this
+  // the gated norm per value head with output (warp r); a head without out_proj entries has no
+  // z rows staged and cannot write: it skips this
   if (warp < R && bi.z >= 0) {
-    const int r = warp;
-    const float* o = sm.ob[r];
-    const float o0 = o[4 * lane], o1 = o[4 * lane + 1], o2 = o[4 * lane + 2],
-                o3 = o[4 * lane + 3];
-    const bool nz = __any_sync(0xffffffffu, o0 != 0.0f || o1 != 0.0f || o2 != 0.0f || o3 != 0.0f);
-    if (nz) {
-      const int32_t* zp = reinterpret_cast<const int32_t*>(B + bi.z);
-      const uint32_t* ze = reinterpret_cast<const uint32_t*>(B + bi.z + ((4 * 1025 + 15) & ~15));
-      float sq = lx_mul(o0, o0);
-      sq = lx_add(sq, lx_mul(o1, o1));
-      sq = lx_add(sq, lx_mul(o2, o2));
-      sq = lx_add(sq, lx_mul(o3, o3));
-      sq = warp_xor_sum(sq);
-      const float rr = lx_rsqrt(lx_add(lx_div(sq, 128.0f), P.eps));
-      const uint16_t* gw = prm + 2 * R;
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const int j = lane + 32 * q;
-        const int zr = r * VD + j;
-        float z = 0.0f;
-        for (int e = zp[zr]; e < zp[zr + 1]; e++)
-          z = lx_add(z, lx_mul(xn_at(sm, w_in, r_in, ze[e] & 0xffffu),
-                               lx_f((uint16_t)(ze[e] >> 16))));
-        const float hn = lx_rbf(lx_mul(o[j], rr));
-        const float u = lx_rbf(lx_mul(lx_f(gw[j]), hn));
-        on[r * VD + j] = lx_rb(lx_mul(u, lx_silu(lx_rbf(z))));
-      }
-      if (lane == 0) atomicOr(&sm.vhmask[bi.slot], 1u << r);
-    }
+    const float* o = sm.ob[warp];
+    const bool nz = __any_sync(0xffffffffu, o[4 * lane] != 0.0f || o[4 * lane + 1] != 0.0f ||
+                                                o[4 * lane + 2] != 0.0f || o[4 * lane + 3] != 0.0f);
+    if (nz) item_out(P, sm, B, bi, warp, w_in, r_in);
   }
   __syncthreads();
   return sm.vhmask[bi.slot] != 0 && (bi.flags & LXB_IT_OUT);
@@ -653,7 +810,7 @@ __device__ void mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, const 
         us = lx_add(us, lx_mul(sm.xm[ue[k] & 0xffffu], lx_f((uint16_t)(ue[k] >> 16))));
     }
     const float gg = lx_rbf(gs), uu = lx_rbf(us);
-    const float act = lx_rbf(lx_silu(gg));
+    const float act = lx_rbf(d_silu(gg));
     sm.hbuf[u] = lx_rbf(lx_mul(act, uu));
   }
   __syncthreads();
@@ -782,31 +939,40 @@ __device__ void head_part(const Dev& P, Smem& sm, int rank) {
   const bool sparse = rp[0] != rp[hc.r1 - hc.r0];  // any sparse entry in these rows
   float bv = -LXB_INF;
   int bi = 0x7fffffff;
-  constexpr int U = 8;  // rows in flight per thread
+  constexpr int U = 4;  // rows in flight per thread
   for (int row0 = hc.r0 + t; row0 < hc.r1; row0 += NT * U) {
     uint64_t code[U];
-    int ea[U], eb[U];
 #pragma unroll
     for (int q = 0; q < U; q++) {
       const int row = row0 + q * NT;
-      const bool ok = row < hc.r1;
-      code[q] = (ok && nd) ? __ldg(P.hcodes + row) : 0ull;
-      ea[q] = (ok && sparse) ? __ldg(rp + row - hc.r0) : 0;
-      eb[q] = (ok && sparse) ? __ldg(rp + row - hc.r0 + 1) : 0;
+      code[q] = (row < hc.r1 && nd) ? __ldg(P.hcodes + row) : 0ull;
     }
+    // the dense part, groups in order per row; the table loads of all rows and groups are
+    // independent of the sums, so they are all in flight together
+    float tv[U][LXB_MAXDENSE / 4];
+#pragma unroll
+    for (int g = 0; g < LXB_MAXDENSE / 4; g++)
+#pragma unroll
+      for (int q = 0; q < U; q++)
+        tv[q][g] = g < ng ? sm.htg[g][(code[q] >> (8 * g)) & 255u] : 0.0f;
 #pragma unroll
     for (int q = 0; q < U; q++) {
       const int row = row0 + q * NT;
       if (row >= hc.r1) continue;
       float D = 0.0f;
-      for (int g = 0; g < ng; g++) D = lx_add(D, sm.htg[g][(code[q] >> (8 * g)) & 255u]);
+#pragma unroll
+      for (int g = 0; g < LXB_MAXDENSE / 4; g++)
+        if (g < ng) D = lx_add(D, tv[q][g]);
       float S = 0.0f;
-      for (int e = ea[q]; e < eb[q]; e++) {
-        const uint32_t w = __ldg(P.ent + e);
-        S = lx_add(S, lx_mul(lx_f((uint16_t)(w >> 16)), sm.xm[w & 0xffffu]));
+      if (sparse) {
+        const int ea = __ldg(rp + row - hc.r0), eb = __ldg(rp + row - hc.r0 + 1);
+        for (int e = ea; e < eb; e++) {
+          const uint32_t w = __ldg(P.ent + e);
+          S = lx_add(S, lx_mul(lx_f((uint16_t)(w >> 16)), sm.xm[w & 0xffffu]));
+        }
       }
       const float lg = lx_rbf(lx_add(D, S));
-      if (lg > bv) {
+      if (lg > bv) {  // a thread's rows ascend: the first maximum stays
         bv = lg;
         bi = row;
       }
@@ -931,13 +1097,14 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     }                                            \
   } while (0)
   // the layer (or head, = n_layers) of global step k: k runs over the layers then the head
-  auto nstep_layer = [&](long long k) -> int { return (int)(k % nsteps_tok); };
+  int cur_layer = 0;  // the current step's layer (n_layers: the head)
   // the next step's blob into the free staging buffer (thread 0; the caller has synchronised
   // the block since the buffer's last use)
   auto issue_next = [&](long long cur) {
     const long long nx = cur + 1;
     if (t == 0 && nx < total && !sm.broken)
-      stage_issue(P, sm, stage, P.nbuf == 2 ? (int)(nx & 1) : 0, nstep_layer(nx));
+      stage_issue(P, sm, stage, P.nbuf == 2 ? (int)(nx & 1) : 0,
+                  cur_layer + 1 == nsteps_tok ? 0 : cur_layer + 1);
   };
   // this step's blob: wait for it, and with two buffers start the next one's copy right away
   auto take = [&](int i) -> const unsigned char* {
@@ -960,6 +1127,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     if (rank == 0 && t == 0 && run.inputs) run.inputs[(size_t)s * run.n_tokens + i] = sm.tok;
     for (int L = 0; L < P.n_layers; L++) {
       const lxb_layer& ly = sm.layers[L];
+      cur_layer = L;
       const unsigned char* B = take(i);
       PROF(PR_WAIT);
       const lxb_bhdr bh = B ? *reinterpret_cast<const lxb_bhdr*>(B) : lxb_bhdr{};
@@ -1040,6 +1208,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     }
     // the output head: every CTA its rows, then the first maximum over the cluster
     {
+      cur_layer = P.n_layers;
       const unsigned char* B = take(i);
       PROF(PR_WAIT);
       const lxb_bhdr bh = B ? *reinterpret_cast<const lxb_bhdr*>(B) : lxb_bhdr{};

@@ -15,7 +15,7 @@
 #include <stdint.h>
 
 #define LXB_MAGIC 0x50425a4cu  // "LZBP"
-#define LXB_IMAGE_VERSION 5
+#define LXB_IMAGE_VERSION 6
 
 #define LXB_H 2560
 #define LXB_KD 256
@@ -100,7 +100,7 @@ typedef struct {
   int32_t n_vneed;         // then value channels with a nonzero tap: evaluated on the steps a key
                            // fires; every channel from n_eager on keeps its conv window lazily
                            // (recomputed from the residual ring at the launch's end)
-  int32_t pad;
+  int32_t tapu;            // the union of the value channels' tap masks (bit p: tap p nonzero)
 } lxb_item;  // 48 bytes
 
 typedef struct {

@@ -25,7 +25,7 @@ from . import chip as C
 from .chip import _ranges
 
 MAGIC = 0x50425A4C
-VERSION = 5
+VERSION = 6
 NSLOT, NOSLOT = 1536, 0xFFFF
 ITEMSLOTS, MAXDENSE, MAXUNITS, MAXWIN = 4, 32, 2048, 1024
 IT_DECAYS, IT_OUT = 1, 2
@@ -36,7 +36,7 @@ LAYER = np.dtype([(n, "<i4") for n in ("has_gdn", "has_mlp", "ln_in", "ln_post",
                                        "n_items", "owner0", "itemof", "decays", "p0", "p1",
                                        "p2")])
 ITEM = np.dtype([(n, "<i4") for n in ("layer", "kh", "cta", "slot", "ch0", "n_ch", "rows",
-                                      "params", "flags", "n_eager", "n_vneed", "p0")])
+                                      "params", "flags", "n_eager", "n_vneed", "tapu")])
 CHAN = np.dtype([("ent", "<u4"), ("n", "<u2"), ("slot", "<u2"), ("conv_ch", "<u4"),
                  ("t01", "<u4"), ("t23", "<u4"), ("tapmask", "<u4"), ("p1", "<u4"),
                  ("p2", "<u4")])
@@ -199,6 +199,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
             it["layer"], it["kh"], it["cta"], it["slot"] = L, kh, pos % Cn, pos // Cn
             it["ch0"], it["n_ch"] = ch0, len(chs)
             it["n_eager"], it["n_vneed"] = int((cls == 0).sum()), int((cls == 1).sum())
+            it["tapu"] = int(np.bitwise_or.reduce(ch["tapmask"][cls == 1], initial=0))
             it["rows"] = i32.add(refs)
             it["params"] = u16.add(np.concatenate([ly.A_log[vh], ly.dt_bias[vh], ly.gnorm]))
             it["flags"] = (IT_DECAYS if decays_vh[vh].any() else 0) | \
