@@ -1098,11 +1098,14 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
   } while (0)
   // the layer (or head, = n_layers) of global step k: k runs over the layers then the head
   int cur_layer = 0;  // the current step's layer (n_layers: the head)
+  bool x_new = true;  // the residual changed since r_x was computed
+  float r_x = 0.0f;   // the norm factor of the residual
   // the next step's blob into the free staging buffer (thread 0; the caller has synchronised
   // the block since the buffer's last use)
+  // (issued by the last warp's first lane: that warp has the least work at the start of a step)
   auto issue_next = [&](long long cur) {
     const long long nx = cur + 1;
-    if (t == 0 && nx < total && !sm.broken)
+    if (t == NT - 32 && nx < total && !sm.broken)
       stage_issue(P, sm, stage, P.nbuf == 2 ? (int)(nx & 1) : 0,
                   cur_layer + 1 == nsteps_tok ? 0 : cur_layer + 1);
   };
@@ -1119,7 +1122,6 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     __syncthreads();
     PROF(PR_TAKESYNC);
     if (sm.broken) return nullptr;
-    if (P.nbuf == 2) issue_next(stp);
     return stage + (size_t)b * P.stage;
   };
   load_embed(run, P, sm, sm.tok);
@@ -1134,7 +1136,11 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       float* rec = reinterpret_cast<float*>(sm.sptr[L][0]);
       uint16_t* conv = reinterpret_cast<uint16_t*>(sm.sptr[L][1]);
       uint32_t* bm = run.bitmaps + ((size_t)s * P.n_layers + L) * LXB_NV * 8;
-      const float r = norm_factor(P, block_ssq(sm, sm.x));
+      if (x_new) {  // the norm factor changes with the residual only
+        r_x = norm_factor(P, block_ssq(sm, sm.x));
+        x_new = false;
+      }
+      const float r = r_x;
       const uint16_t* w_in = (B && bh.ln_in >= 0) ? reinterpret_cast<const uint16_t*>(B + bh.ln_in)
                                                  : P.u16 + ly.ln_in;
       const uint16_t* w_post = (B && bh.ln_post >= 0)
@@ -1156,6 +1162,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       }
       if (ly.has_mlp) norm_into(sm.xm, sm.x, w_post, r);
       __syncthreads();
+      if (P.nbuf == 2) issue_next(stp);  // the next step's blob: its buffer was read a step ago
       PROF(PR_NORM);
       bool wrote = false;
       if (ly.has_gdn && B) {
@@ -1185,6 +1192,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         out_owner(P, sm, ly, ow, rank, sm.own[ph & 1], cluster);
         cluster.sync();
         pull(P, sm, ph & 1, cluster);
+        x_new = true;
         ph++;
         if (ly.has_mlp) {
           const float r2 = norm_factor(P, block_ssq(sm, sm.x));
@@ -1197,10 +1205,14 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
           pull(P, sm, ph & 1, cluster);
           ph++;
         }
+        x_new = true;
         PROF(PR_FIXUP);
       } else {
         if (P.nbuf == 1) issue_next(stp);
-        if (ly.has_mlp) pull(P, sm, ph & 1, cluster);
+        if (ly.has_mlp) {
+          pull(P, sm, ph & 1, cluster);
+          x_new = true;
+        }
         ph++;
         PROF(PR_PULL);
       }
@@ -1212,11 +1224,15 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       const unsigned char* B = take(i);
       PROF(PR_WAIT);
       const lxb_bhdr bh = B ? *reinterpret_cast<const lxb_bhdr*>(B) : lxb_bhdr{};
-      const float r = norm_factor(P, block_ssq(sm, sm.x));
+      if (x_new) {
+        r_x = norm_factor(P, block_ssq(sm, sm.x));
+        x_new = false;
+      }
+      const float r = r_x;
       norm_into(sm.xm, sm.x,
                 B ? reinterpret_cast<const uint16_t*>(B + bh.ln_in) : P.u16 + P.final_norm, r);
       __syncthreads();
-      if (P.nbuf == 1) issue_next(stp);
+      issue_next(stp);
       stp++;
       head_part(P, sm, rank);
       cluster.sync();
@@ -1249,6 +1265,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       __syncthreads();
       PROF(PR_HEAD);
       if (i + 1 < run.n_tokens) load_embed(run, P, sm, sm.tok);
+      x_new = true;
       PROF(PR_EMBED);
       pc[PR_TOKENS]++;
     }
