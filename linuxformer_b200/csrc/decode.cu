@@ -429,7 +429,8 @@ __device__ void lazy_fire(const Dev& P, const Run& run, Smem& sm, const lxb_item
       }
       y = lx_add(y, lx_mul(lx_f(taps[p]), lx_f(pv)));
     }
-    sm.buf[a.y >> 16] = lx_rbf(d_silu(lx_rbf(y)));
+    const float yb = lx_rbf(y);
+    sm.buf[a.y >> 16] = yb == 0.0f ? yb : lx_rbf(d_silu(yb));
   }
 }
 
@@ -482,7 +483,8 @@ __device__ __forceinline__ float eager_channel(Smem& sm, const unsigned char* B,
   y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(n1)));
   y = lx_add(y, lx_mul(lx_f((uint16_t)(b.x & 0xffffu)), lx_f(n2)));
   y = lx_add(y, lx_mul(lx_f((uint16_t)(b.x >> 16)), lx_f(Pv)));
-  return lx_rbf(d_silu(lx_rbf(y)));
+  const float yb = lx_rbf(y);
+  return yb == 0.0f ? yb : lx_rbf(d_silu(yb));
 }
 
 // Pieces of an item: the rare paths (many query/key channels, decay, a key firing, output).

@@ -18,7 +18,8 @@
 // roundings that follow almost always absorb that difference, and the parity tests state their
 // tolerance for the fp32 recurrent state.
 //
-// bf16 conversion is round-to-nearest-even on the bit pattern, as torch's float -> bfloat16.
+// bf16 conversion is round-to-nearest-even on the bit pattern, as torch's float -> bfloat16
+// (a NaN becomes the canonical bf16 NaN 0x7fff, where torch writes 0x7fc0).
 #pragma once
 #include <stdint.h>
 
@@ -70,11 +71,20 @@ LXB_FN float lx_sqrt(float a) { return sqrtf(a); }
 
 // --- bf16 ---------------------------------------------------------------------------------------
 LXB_FN float lx_f(lxb_bf16 b) { return lxb_bitsf(((uint32_t)b) << 16); }
+// On the device this is the hardware conversion (cvt.rn.bf16.f32): the same bits as the form
+// below for every non-NaN float (all 2^32 inputs checked on the B200), and 0x7fff for every NaN,
+// which the form below returns too (a NaN never arises from a valid machine state).
 LXB_FN lxb_bf16 lx_rb(float x) {
+#ifdef __CUDA_ARCH__
+  uint16_t r;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(x));
+  return r;
+#else
   uint32_t u = lxb_fbits(x);
-  if ((u & 0x7fffffffu) > 0x7f800000u) return (lxb_bf16)((u >> 16) | 0x40u);  // NaN stays NaN
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (lxb_bf16)0x7fffu;  // NaN: the canonical bf16 NaN
   u += 0x7fffu + ((u >> 16) & 1u);
   return (lxb_bf16)(u >> 16);
+#endif
 }
 LXB_FN float lx_rbf(float x) { return lx_f(lx_rb(x)); }
 
