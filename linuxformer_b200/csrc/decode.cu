@@ -119,6 +119,7 @@ struct __align__(16) Smem {
   float xn[H];                     // input_layernorm(x) (bf16 values)
   float xm[H];                     // post_attention_layernorm(x) or the final norm
   alignas(16) float own[2][BLKMAX];  // this CTA's rows after the step, by step parity
+  alignas(16) uint16_t xin[2][H];  // the residual as the owners push it (bf16), by step parity
   float buf[LXB_NSLOT];            // an item's q | k | v
   float qval[KD], kval[KD];        // nonzero l2-normed query (x 1/16) and key values
   int qidx[KD], kidx[KD];
@@ -899,13 +900,34 @@ __device__ void out_owner(const Dev& P, Smem& sm, const lxb_layer& ly, const lxb
   }
 }
 
-// every CTA's replica from the owners' blocks (16-byte DSMEM loads)
-__device__ void pull(const Dev& P, Smem& sm, int par, cg::cluster_group& cluster) {
-  const int per = P.blk / 4;  // uint4 per owner
-  for (int k = threadIdx.x; k < H / 4; k += NT) {
-    const int c = k / per, q = k % per;
-    const uint4* src = reinterpret_cast<const uint4*>(cluster.map_shared_rank(&sm.own[par][0], c));
-    reinterpret_cast<uint4*>(sm.x)[k] = src[q];
+// The owner's rows into every CTA's push buffer of this parity, as bf16 (the residual's values
+// are bf16; 16-byte DSMEM stores before the step's cluster barrier, which makes them visible);
+// own must be complete (a block barrier after it was written).
+__device__ void push_rows(const Dev& P, Smem& sm, const float* own, int par, int rank,
+                          cg::cluster_group& cluster) {
+  const int per = P.blk / 8;  // uint4 (8 rows) per owner
+  for (int k = threadIdx.x; k < per * P.C; k += NT) {
+    const int d = k / per, q = k % per;
+    const float* o = own + 8 * q;
+    const uint4 v = make_uint4((uint32_t)lx_rb(o[0]) | ((uint32_t)lx_rb(o[1]) << 16),
+                               (uint32_t)lx_rb(o[2]) | ((uint32_t)lx_rb(o[3]) << 16),
+                               (uint32_t)lx_rb(o[4]) | ((uint32_t)lx_rb(o[5]) << 16),
+                               (uint32_t)lx_rb(o[6]) | ((uint32_t)lx_rb(o[7]) << 16));
+    uint4* dst = reinterpret_cast<uint4*>(cluster.map_shared_rank(&sm.xin[par][rank * P.blk], d));
+    dst[q] = v;
+  }
+}
+
+// the replica from the push buffer (after the cluster barrier)
+__device__ void take_rows(Smem& sm, int par) {
+  for (int k = threadIdx.x; k < H / 8; k += NT) {
+    const uint4 v = reinterpret_cast<const uint4*>(sm.xin[par])[k];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      sm.x[8 * k + 2 * q] = lx_f((uint16_t)(w[q] & 0xffffu));
+      sm.x[8 * k + 2 * q + 1] = lx_f((uint16_t)(w[q] >> 16));
+    }
   }
   __syncthreads();
 }
@@ -1179,6 +1201,8 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       if (ly.has_mlp) {
         if (mlp) mlp_owner(P, sm, B, mh, rank, sm.own[ph & 1]);
         else copy_owner(P, sm, rank, sm.own[ph & 1]);
+        __syncthreads();
+        push_rows(P, sm, sm.own[ph & 1], ph & 1, rank, cluster);
       }
       PROF(PR_MLP);
       cluster.sync();
@@ -1192,8 +1216,10 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         ph++;
         const lxb_owner ow = P.owners[ly.owner0 + rank];
         out_owner(P, sm, ly, ow, rank, sm.own[ph & 1], cluster);
+        __syncthreads();
+        push_rows(P, sm, sm.own[ph & 1], ph & 1, rank, cluster);
         cluster.sync();
-        pull(P, sm, ph & 1, cluster);
+        take_rows(sm, ph & 1);
         x_new = true;
         ph++;
         if (ly.has_mlp) {
@@ -1202,9 +1228,11 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
           __syncthreads();
           if (mlp) mlp_owner(P, sm, B, mh, rank, sm.own[ph & 1]);
           else copy_owner(P, sm, rank, sm.own[ph & 1]);
+          __syncthreads();
+          push_rows(P, sm, sm.own[ph & 1], ph & 1, rank, cluster);
           cluster.sync();
           if (P.nbuf == 1) issue_next(stp);
-          pull(P, sm, ph & 1, cluster);
+          take_rows(sm, ph & 1);
           ph++;
         }
         x_new = true;
@@ -1212,7 +1240,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       } else {
         if (P.nbuf == 1) issue_next(stp);
         if (ly.has_mlp) {
-          pull(P, sm, ph & 1, cluster);
+          take_rows(sm, ph & 1);
           x_new = true;
         }
         ph++;
@@ -1324,7 +1352,7 @@ struct lxb_plan {
   int smem;  // dynamic shared memory per CTA: Smem, then the staging buffers
 };
 
-static_assert(offsetof(Smem, own) % 16 == 0 && offsetof(Smem, on) % 16 == 0 &&
+static_assert(offsetof(Smem, own) % 16 == 0 && offsetof(Smem, on) % 16 == 0 && offsetof(Smem, xin) % 16 == 0 &&
                   offsetof(Smem, onall) % 16 == 0 && offsetof(Smem, mbar) % 8 == 0 &&
                   sizeof(Smem) < 160 * 1024,
               "shared memory layout");
