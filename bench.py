@@ -207,6 +207,7 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=dev)
+    from linuxformer_b200._lib import S_ERRORS
     from linuxformer_b200.runtime import Decoder
 
     chip = C.c2(1, **kw)
@@ -251,7 +252,7 @@ def main():
             e1.synchronize()
             times.append(e0.elapsed_time(e1) / 1000.0)
     torch.cuda.synchronize(dev)
-    if dec.status().status:
+    if dec.status().status & S_ERRORS:
         raise RuntimeError(f"device status {dec.status().status:#x}")
     tot = sum(times)
     # e2e: the host-buffer call (pinned H2D of the forced token, D2H of the predictions)

@@ -39,6 +39,8 @@ extern "C" {
 /* device status bits (lxb_status) */
 #define LXB_S_TOKEN 1u       /* a token id outside the embedding: clamped, the stream is invalid */
 #define LXB_S_STAGE 2u       /* a staging copy did not land within 2 s: later steps skipped */
+#define LXB_S_HELPER 4u      /* a head helper cluster did not answer in time: the decoding cluster
+                                took its rows itself (informational: the stream is exact) */
 
 typedef struct lxb_plan lxb_plan;
 
@@ -116,6 +118,14 @@ int lxb_status_clear(lxb_plan* plan);
  * tokens). NULL turns it off (the default). */
 int lxb_plan_set_profile(lxb_plan* plan, unsigned long long* prof);
 int lxb_profile_sections(void);
+
+/* Head helpers: a single-stream launch also starts up to this many more clusters (default 7,
+ * at most what the device holds beside the decoding cluster), each of which takes a slice of the
+ * output head's rows per token and hands its maximum back through the scratch buffer, so the
+ * head's table lookups run on up to 8x the SMs. 0 turns them off. A helper that does not answer
+ * within a bounded wait is dropped for the rest of the launch (LXB_S_HELPER); the results do not
+ * depend on it. No counterpart in the reference (its head runs on its one 132-CTA grid). */
+int lxb_plan_set_head_helpers(lxb_plan* plan, int max_clusters);
 
 /* How the plan stages its per-step tables: buffers (2 = the next step's copy overlaps the
  * current step), bytes per buffer, and the shared memory each CTA uses. */

@@ -17,6 +17,11 @@ class LxbError(RuntimeError):
     pass
 
 
+# device status bits (include/lxb.h): the errors; LXB_S_HELPER (4) is informational
+S_TOKEN, S_STAGE, S_HELPER = 1, 2, 4
+S_ERRORS = S_TOKEN | S_STAGE
+
+
 class Caps(ctypes.Structure):
     _fields_ = [("device", I), ("cc_major", I), ("cc_minor", I), ("sm_count", I),
                 ("max_smem_optin", I), ("cluster_launch", I), ("max_clusters", I)]
@@ -36,6 +41,7 @@ SIGNATURES = {
     "lxb_decode_noalloc": (I, [P, P, P, I, P, I, P, I, I, P, P, P]),
     "lxb_status": (I, [P, P]),
     "lxb_plan_set_profile": (I, [P, P]),
+    "lxb_plan_set_head_helpers": (I, [P, I]),
     "lxb_profile_sections": (I, []),
     "lxb_plan_staging": (I, [P, P, P, P]),
     "lxb_status_clear": (I, [P]),

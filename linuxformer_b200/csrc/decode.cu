@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include <climits>
+#include <algorithm>
 #include <mutex>
 #include <new>
 #include <stddef.h>
@@ -94,6 +95,12 @@ struct Run {
   int32_t* preds;
   int32_t* inputs;
   unsigned long long* prof;  // optional: [stream][cta][LXB_PROF_N] cycle counters, accumulated
+  int n_streams;               // decoding clusters; the clusters after them are head helpers
+  int n_help;                  // head helper clusters (a single stream only), slices 1..n_help
+  float* hx;                   // [2560]: the head's input, published by the decoding cluster
+  unsigned long long* hseq;    // the token whose head input hx holds (epoch | token + 1)
+  uint4* hpart;                // [slice * cluster + rank]: a helper's maximum {v, row, seq lo, hi}
+  unsigned long long epoch;    // this launch's tag (launch count << 32): stale words never match
 };
 
 // profile sections (lxb_plan_set_profile): cycles spent per CTA
@@ -154,7 +161,9 @@ struct __align__(16) Smem {
   lxb_blobref bref[LXB_MAXLAYERS + 1];  // this CTA's step blobs (the head's last)
   alignas(8) uint2 win[LXB_MAXWIN];  // resident query/key conv windows
   int nwin, win0;                   // their count and offset in the window map
-  lxb_headcta hc;                   // this CTA's head rows
+  int help_dead;                    // the helpers stopped answering: the cluster does every slice
+  float cv, hv, gv;                 // the cluster's first maximum; with the helpers'; rank 0's
+  int ci, hi, gi, hok;              // gathering; their rows; whether every helper answered
 };
 
 // --- block reductions in the canonical orders -------------------------------------------------
@@ -946,11 +955,11 @@ __device__ void load_embed(const Run& run, const Dev& P, Smem& sm, int tok) {
   __syncthreads();
 }
 
-// the head over this CTA's rows: the first maximum of the bf16 logits
-__device__ void head_part(const Dev& P, Smem& sm, int rank) {
-  const int t = threadIdx.x;
+// The head's per-group tables from sm.xm: htg[g][code] = the sum, in column order from +0, of the
+// group's 4 dense columns' weights (by their 2-bit codes) times xm. Ends with a block barrier.
+__device__ void head_tables(const Dev& P, Smem& sm) {
   const int nd = P.n_dense, ng = (nd + 3) / 4;
-  for (int k = t; k < ng * 256; k += NT) {
+  for (int k = threadIdx.x; k < ng * 256; k += NT) {
     const int g = k >> 8, code = k & 255;
     float s = 0.0f;
     for (int j = 0; j < 4 && 4 * g + j < nd; j++)
@@ -958,11 +967,16 @@ __device__ void head_part(const Dev& P, Smem& sm, int rank) {
     sm.htg[g][code] = s;
   }
   __syncthreads();
-  const lxb_headcta hc = sm.hc;
+}
+
+// The head rows of one part, into this thread's running first maximum (bv, bi) of the bf16 logits
+// (a thread's rows ascend within a part, and parts are visited in ascending order).
+__device__ void head_rows(const Dev& P, const Smem& sm, const lxb_headcta hc, float& bv,
+                          int& bi) {
+  const int t = threadIdx.x;
+  const int nd = P.n_dense, ng = (nd + 3) / 4;
   const int32_t* rp = P.i32 + hc.rowptr;
   const bool sparse = rp[0] != rp[hc.r1 - hc.r0];  // any sparse entry in these rows
-  float bv = -LXB_INF;
-  int bi = 0x7fffffff;
   constexpr int U = 4;  // rows in flight per thread
   for (int row0 = hc.r0 + t; row0 < hc.r1; row0 += NT * U) {
     uint64_t code[U];
@@ -996,12 +1010,19 @@ __device__ void head_part(const Dev& P, Smem& sm, int rank) {
         }
       }
       const float lg = lx_rbf(lx_add(D, S));
-      if (lg > bv) {  // a thread's rows ascend: the first maximum stays
+      if (lg > bv) {
         bv = lg;
         bi = row;
       }
     }
   }
+}
+
+// the first maximum over the block (larger value, then smaller row) into *ov_out / *oi_out
+// (shared; by default sm.bestv / sm.besti, which other CTAs read after a cluster barrier)
+__device__ void head_reduce(Smem& sm, float bv, int bi, float* ov_out = nullptr,
+                            int* oi_out = nullptr) {
+  const int t = threadIdx.x;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
     const float ov = __shfl_down_sync(0xffffffffu, bv, off);
@@ -1027,8 +1048,98 @@ __device__ void head_part(const Dev& P, Smem& sm, int rank) {
         bi = oi;
       }
     }
-    sm.bestv = bv;
-    sm.besti = bi;
+    *(ov_out ? ov_out : &sm.bestv) = bv;
+    *(oi_out ? oi_out : &sm.besti) = bi;
+  }
+  __syncthreads();
+}
+
+// the first maximum of the cluster's CTAs' sm.bestv / sm.besti into sm.cv / sm.ci (every CTA the
+// same), after a cluster barrier that follows their head_reduce; ends with a block barrier
+__device__ void cluster_max(Smem& sm, cg::cluster_group& cluster, int C) {
+  const int t = threadIdx.x;
+  if (t < 32) {
+    float bv = -LXB_INF;
+    int bi = 0x7fffffff;
+    if (t < C) {
+      bv = *cluster.map_shared_rank(&sm.bestv, t);
+      bi = *cluster.map_shared_rank(&sm.besti, t);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_down_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_down_sync(0xffffffffu, bi, off);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (t == 0) {
+      sm.cv = bv;
+      sm.ci = bi;
+    }
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// A head helper CTA (helper cluster hk = 1..n_help, rank c): the slices LXB_HEADMAIN + j of
+// rank c's rows with j % n_help == hk - 1. Per token: wait for the decoding cluster's head input,
+// take the first maximum over its slices, publish it. Every wait is bounded; a helper that gives
+// up sets LXB_S_HELPER and leaves (the decoding cluster then takes its slices itself, so the
+// stream stays exact).
+__device__ void head_helper(const Dev& P, const Run& run, Smem& sm, int rank, int hk) {
+  const int t = threadIdx.x;
+  const int part = hk * P.C + rank;
+  const unsigned long long done = run.epoch | 0xffffffffull;
+  for (int i = 0; i < run.n_tokens; i++) {
+    const unsigned long long want = run.epoch | (unsigned long long)(i + 1);
+    if (t == 0) {
+      int go = 0;
+      const long long t0 = clock64();
+      for (;;) {
+        const unsigned long long v = ld_acquire_u64(run.hseq);
+        if (v == want) {
+          go = 1;
+          break;
+        }
+        if (v == done) break;
+        if (clock64() - t0 > (1ll << 32)) {  // ~2 s: the decoding cluster is gone
+          atomicOr(P.status, LXB_S_HELPER);
+          break;
+        }
+        __nanosleep(64);
+      }
+      sm.tok = go;
+    }
+    __syncthreads();
+    if (!sm.tok) return;
+    for (int k = t; k < H / 4; k += NT)
+      reinterpret_cast<float4*>(sm.xm)[k] = __ldcg(reinterpret_cast<const float4*>(run.hx) + k);
+    __syncthreads();
+    head_tables(P, sm);
+    float bv = -LXB_INF;
+    int bi = 0x7fffffff;
+    for (int k = LXB_HEADMAIN + hk - 1; k < LXB_HEADSLICES; k += run.n_help)
+      head_rows(P, sm, P.headcta[rank * LXB_HEADSLICES + k], bv, bi);
+    head_reduce(sm, bv, bi);
+    if (t == 0) {
+      uint4* hp = run.hpart + part;
+      hp->x = __float_as_uint(sm.bestv);
+      hp->y = (uint32_t)sm.besti;
+      hp->w = (uint32_t)(want >> 32);
+      __threadfence();
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(&hp->z), "r"((uint32_t)want)
+                   : "memory");
+    }
   }
 }
 
@@ -1068,9 +1179,14 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
   const int C = P.C;
   const int s = blockIdx.x / C;
   const int t = threadIdx.x;
+  if (s >= run.n_streams) {  // a head helper cluster
+    head_helper(P, run, sm, rank, s - run.n_streams + 1);
+    return;
+  }
   const int nsteps_tok = P.n_layers + 1;  // the layers, then the head
   const long long total = (long long)run.n_tokens * nsteps_tok;
   if (t < 2) sm.wflag[t] = 0;
+  if (t == 0) sm.help_dead = 0;
   if (t == 0) {
     int tok = run.forced[(size_t)s * run.n_forced];
     if (tok < 0 || (int64_t)tok + P.offset >= P.n_embed_rows) {
@@ -1091,7 +1207,6 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     (&sm.sptr[0][0])[k] = run.state_ptrs[(size_t)s * P.n_layers * 2 + k];
   for (int k = t; k <= P.n_layers; k += NT) sm.bref[k] = P.blobidx[k * C + rank];
   if (t == 0) {
-    sm.hc = P.headcta[rank];
     sm.win0 = P.winidx[2 * rank];
     sm.nwin = P.winidx[2 * rank + 1];
   }
@@ -1262,26 +1377,102 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       norm_into(sm.xm, sm.x,
                 B ? reinterpret_cast<const uint16_t*>(B + bh.ln_in) : P.u16 + P.final_norm, r);
       __syncthreads();
+      // with helper clusters, rank 0 publishes the head input for them first
+      const bool helped = run.n_help > 0 && !sm.help_dead;  // the same in every CTA
+      const unsigned long long want = run.epoch | (unsigned long long)(i + 1);
+      if (helped && rank == 0) {
+        for (int k = t; k < H / 4; k += NT)
+          reinterpret_cast<float4*>(run.hx)[k] = reinterpret_cast<const float4*>(sm.xm)[k];
+        __syncthreads();
+        if (t == 0) {
+          __threadfence();
+          st_release_u64(run.hseq, want);
+        }
+      }
       issue_next(stp);
       stp++;
-      head_part(P, sm, rank);
-      cluster.sync();
-      if (t < 32) {
+      head_tables(P, sm);
+      {  // this rank's first slices (helped), or its whole range
         float bv = -LXB_INF;
         int bi = 0x7fffffff;
-        if (t < C) {
-          bv = *cluster.map_shared_rank(&sm.bestv, t);
-          bi = *cluster.map_shared_rank(&sm.besti, t);
+        if (helped) {
+          for (int k = 0; k < LXB_HEADMAIN; k++)
+            head_rows(P, sm, P.headcta[rank * LXB_HEADSLICES + k], bv, bi);
+        } else {
+          head_rows(P, sm, P.headcta[C * LXB_HEADSLICES + rank], bv, bi);
         }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-          const float ov = __shfl_down_sync(0xffffffffu, bv, off);
-          const int oi = __shfl_down_sync(0xffffffffu, bi, off);
-          if (ov > bv || (ov == bv && oi < bi)) {
-            bv = ov;
-            bi = oi;
+        head_reduce(sm, bv, bi);
+      }
+      cluster.sync();
+      cluster_max(sm, cluster, C);  // sm.cv / sm.ci: the cluster's first maximum
+      if (helped) {
+        // rank 0 gathers the helpers' maxima (each wait bounded) and tells every CTA
+        if (rank == 0) {
+          float hv = -LXB_INF;
+          int hi = 0x7fffffff, ok = 1;
+          if (t < run.n_help * C) {
+            const uint4* hp = run.hpart + C + t;
+            const long long t0 = clock64();
+            for (;;) {
+              uint32_t z;
+              asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(z) : "l"(&hp->z) : "memory");
+              if (z == (uint32_t)want && __ldcg(&hp->w) == (uint32_t)(want >> 32)) break;
+              if (clock64() - t0 > (1ll << 26)) {  // ~34 ms: a helper is not there
+                ok = 0;
+                break;
+              }
+            }
+            if (ok) {
+              hv = __uint_as_float(__ldcg(&hp->x));
+              hi = (int)__ldcg(&hp->y);
+            }
+          }
+          if (t == 0 && (sm.cv > hv || (sm.cv == hv && sm.ci < hi))) {  // and the cluster's own
+            hv = sm.cv;
+            hi = sm.ci;
+          }
+          const int all = __syncthreads_and(ok);
+          head_reduce(sm, hv, hi, &sm.gv, &sm.gi);  // not bestv: other CTAs may still read it
+          if (t < C) {
+            *cluster.map_shared_rank(&sm.hv, t) = sm.gv;
+            *cluster.map_shared_rank(&sm.hi, t) = sm.gi;
+            *cluster.map_shared_rank(&sm.hok, t) = all;
           }
         }
+        cluster.sync();
+        if (sm.hok) {
+          if (t == 0) {
+            sm.cv = sm.hv;
+            sm.ci = sm.hi;
+          }
+        } else {  // a helper is missing: the helpers' slices here, now and from now on
+          float bv = sm.cv;
+          int bi = sm.ci;
+          __syncthreads();
+          if (t == 0) sm.help_dead = 1;
+          float v2 = -LXB_INF;
+          int i2 = 0x7fffffff;
+          for (int k = LXB_HEADMAIN; k < LXB_HEADSLICES; k++)
+            head_rows(P, sm, P.headcta[rank * LXB_HEADSLICES + k], v2, i2);
+          head_reduce(sm, v2, i2);
+          cluster.sync();
+          cluster_max(sm, cluster, C);
+          if (t == 0) {
+            if (bv > sm.cv || (bv == sm.cv && bi < sm.ci)) {
+              sm.cv = bv;
+              sm.ci = bi;
+            }
+            if (rank == 0) {
+              atomicOr(P.status, LXB_S_HELPER);
+              st_release_u64(run.hseq, run.epoch | 0xffffffffull);  // the helpers may leave
+            }
+          }
+        }
+        __syncthreads();
+      }
+      if (t < 32) {
+        const float bv = sm.cv;
+        const int bi = sm.ci;
         if (t == 0) {
           if (rank == 0) run.preds[(size_t)s * run.n_tokens + i] = bi;
           int nt = (i + 1 < run.n_forced) ? run.forced[(size_t)s * run.n_forced + i + 1] : bi;
@@ -1348,6 +1539,8 @@ struct lxb_plan {
   Dev dev;
   uint32_t* status;
   int max_clusters;
+  int head_helpers;              // the most head helper clusters a single-stream launch may use
+  unsigned long long launches;   // launches so far (the helpers' exchange tag)
   unsigned long long* prof;
   int smem;  // dynamic shared memory per CTA: Smem, then the staging buffers
 };
@@ -1561,7 +1754,7 @@ int validate(const View& v, int cluster) {
   }
   const int C = cluster, blk = H / C;
   if (v.n(LXB_SEC_LAYERS) != h->n_layers || v.n(LXB_SEC_OWNERS) != (int64_t)h->n_layers * C ||
-      v.n(LXB_SEC_HEADCTA) != C || v.n(LXB_SEC_ITEMS) != h->n_items)
+      v.n(LXB_SEC_HEADCTA) != (int64_t)C * (LXB_HEADSLICES + 1) || v.n(LXB_SEC_ITEMS) != h->n_items)
     return LXB_E_IMAGE;
   if (h->n_dense < 0 || h->n_dense > LXB_MAXDENSE) return LXB_E_IMAGE;
   if (h->n_dense && v.n(LXB_SEC_HCODES) != h->n_vocab) return LXB_E_IMAGE;
@@ -1626,12 +1819,18 @@ int validate(const View& v, int cluster) {
   }
   const lxb_headcta* hc = v.sec<lxb_headcta>(LXB_SEC_HEADCTA);
   int prev = 0;
-  for (int c = 0; c < C; c++) {
+  for (int c = 0; c < C * LXB_HEADSLICES; c++) {
     if (hc[c].r0 != prev || hc[c].r1 < hc[c].r0 || hc[c].r1 > h->n_vocab) return LXB_E_IMAGE;
     prev = hc[c].r1;
     if (!rowptr_ok(v, hc[c].rowptr, hc[c].r1 - hc[c].r0, H)) return LXB_E_IMAGE;
   }
   if (prev != h->n_vocab) return LXB_E_IMAGE;
+  for (int c = 0; c < C; c++) {  // each rank's whole range: its slices together
+    const lxb_headcta& w = hc[C * LXB_HEADSLICES + c];
+    if (w.r0 != hc[c * LXB_HEADSLICES].r0 || w.r1 != hc[c * LXB_HEADSLICES + LXB_HEADSLICES - 1].r1)
+      return LXB_E_IMAGE;
+    if (!rowptr_ok(v, w.rowptr, w.r1 - w.r0, H)) return LXB_E_IMAGE;
+  }
   if (h->n_dense) {
     const uint64_t* codes = v.sec<uint64_t>(LXB_SEC_HCODES);
     const int bits = 2 * h->n_dense;
@@ -1735,6 +1934,8 @@ extern "C" int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb
     return e ? cuda_rc(e) : LXB_E_DEVICE;
   }
   p->max_clusters = ncl;
+  p->head_helpers = LXB_HEADSLICES - 1;
+  p->launches = 0;
   *out = p;
   return LXB_OK;
 }
@@ -1743,9 +1944,16 @@ static size_t ring_bytes(const lxb_plan* p, int n_streams) {
   return (size_t)n_streams * p->hdr.n_layers * 4 * H * sizeof(uint16_t);
 }
 
+// the head helpers' exchange, after the ring and its factors: hx [2560] float, hseq, hpart
+static size_t head_xchg_bytes(const lxb_plan* p) {
+  return (size_t)H * 4 + 16 + (size_t)p->cluster * LXB_HEADSLICES * 16;
+}
+
 extern "C" size_t lxb_scratch_bytes(const lxb_plan* p, int n_streams) {
   if (!p || n_streams < 1) return 0;
-  return ring_bytes(p, n_streams) + (size_t)n_streams * p->hdr.n_layers * 4 * sizeof(float);
+  const size_t base =
+      ring_bytes(p, n_streams) + (size_t)n_streams * p->hdr.n_layers * 4 * sizeof(float);
+  return ((base + 15) & ~(size_t)15) + head_xchg_bytes(p);
 }
 
 static int decode_launch(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitmaps,
@@ -1768,15 +1976,27 @@ static int decode_launch(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitm
   uint16_t* ring = static_cast<uint16_t*>(scratch);
   float* ring_r = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) +
                                            ring_bytes(p, n_streams));
+  unsigned char* xg =
+      static_cast<unsigned char*>(scratch) +
+      ((ring_bytes(p, n_streams) + (size_t)n_streams * p->hdr.n_layers * 4 * sizeof(float) + 15) &
+       ~(size_t)15);
+  // head helpers: a single stream, clusters the device can hold beside it, tokens the tag counts
+  int n_help = 0;
+  if (n_streams == 1 && n_tokens < 0x7fffffff)
+    n_help = std::min(std::min(p->head_helpers, LXB_HEADSLICES - LXB_HEADMAIN), p->max_clusters - 1);
+  if (n_help < 0) n_help = 0;
+  p->launches++;
   Run run{state_ptrs, bitmaps, ring, ring_r, embed, forced, n_forced, n_tokens, preds, inputs,
-          p->prof};
+          p->prof, n_streams, n_help, reinterpret_cast<float*>(xg),
+          reinterpret_cast<unsigned long long*>(xg + (size_t)H * 4),
+          reinterpret_cast<uint4*>(xg + (size_t)H * 4 + 16), p->launches << 32};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = p->cluster;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(p->cluster * n_streams);
+  cfg.gridDim = dim3(p->cluster * (n_streams + n_help));
   cfg.blockDim = dim3(NT);
   cfg.dynamicSmemBytes = p->smem;
   cfg.stream = st;
@@ -1857,6 +2077,12 @@ extern "C" int lxb_plan_set_profile(lxb_plan* p, unsigned long long* prof) {
 }
 
 extern "C" int lxb_profile_sections(void) { return PR_N; }
+
+extern "C" int lxb_plan_set_head_helpers(lxb_plan* p, int max_clusters) {
+  if (!p || max_clusters < 0) return LXB_E_INVAL;
+  p->head_helpers = max_clusters;
+  return LXB_OK;
+}
 
 extern "C" int lxb_plan_staging(const lxb_plan* p, int* nbuf, int* stage_bytes, int* smem_bytes) {
   if (!p || !nbuf || !stage_bytes || !smem_bytes) return LXB_E_INVAL;

@@ -15,7 +15,7 @@
 #include <stdint.h>
 
 #define LXB_MAGIC 0x50425a4cu  // "LZBP"
-#define LXB_IMAGE_VERSION 6
+#define LXB_IMAGE_VERSION 7
 
 #define LXB_H 2560
 #define LXB_KD 256
@@ -29,6 +29,8 @@
 #define LXB_MAXC 16     // CTAs per cluster
 #define LXB_MINC 4
 #define LXB_ITEMSLOTS 4 // items one CTA may run in one layer
+#define LXB_HEADSLICES 32  // the head's rows in this many slices per CTA rank (helper clusters)
+#define LXB_HEADMAIN 2     // of which the decoding cluster takes the first (it also gathers)
 #define LXB_MAXDENSE 32
 #define LXB_MAXUNITS 2048  // MLP units one CTA evaluates in one layer
 #define LXB_MAXWIN 1024    // query/key conv windows one CTA keeps in shared memory for a launch
@@ -47,7 +49,8 @@ enum {
   LXB_SEC_OWNERS,      // lxb_owner[n_layers * cluster]
   LXB_SEC_I32,         // int32 pool: row pointers, row refs, item-of tables
   LXB_SEC_U16,         // uint16 pool: bf16 parameters (norm weights, A_log, dt_bias, gated norm)
-  LXB_SEC_HEADCTA,     // lxb_headcta[cluster]
+  LXB_SEC_HEADCTA,     // lxb_headcta[(LXB_HEADSLICES + 1) * cluster]: slice k of rank c at
+                       // c * LXB_HEADSLICES + k, then the ranks' whole ranges
   LXB_SEC_HCODES,      // uint64 per vocabulary row: the dense columns' 2-bit codes
   LXB_SEC_BLOBS,       // bytes: the step blobs (below)
   LXB_SEC_BLOBIDX,     // lxb_blobref[(n_layers + 1) * cluster]: layer L (or the head, L =

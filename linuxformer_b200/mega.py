@@ -21,6 +21,7 @@ import numpy as np
 import torch
 
 from . import chip as C
+from ._lib import S_ERRORS
 from .runtime import Decoder, state_pointers
 
 
@@ -123,6 +124,6 @@ class Mega:
             if prof is not None:
                 self.dec.set_profile(None)
         e = self.dec.status()
-        if e.status:
+        if e.status & S_ERRORS:
             raise RuntimeError(f"mega failed: device status {e.status:#x} at step {e.first_step}")
         return out

@@ -18,7 +18,7 @@ import torch
 
 from . import chip as C
 from . import tables
-from ._lib import Caps, Err, LxbError, check, lib
+from ._lib import S_ERRORS, Caps, Err, LxbError, check, lib
 
 
 def _u16(t: np.ndarray, dev) -> torch.Tensor:
@@ -174,7 +174,7 @@ class Decoder:
         ph.copy_(preds, non_blocking=True)
         torch.cuda.current_stream(self.dev).synchronize()
         e = self.status()
-        if e.status:
+        if e.status & S_ERRORS:
             check(lib().lxb_status_clear(self.plan), "lxb_status_clear")
             raise LxbError(f"device status {e.status:#x} (stream {e.first_stream}, "
                            f"step {e.first_step})")
@@ -190,7 +190,7 @@ class Decoder:
         self.launch(states.ptrs, states.bitmaps, f, n, preds, inputs, scratch=states.scratch)
         torch.cuda.synchronize(self.dev)
         e = self.status()
-        if e.status:
+        if e.status & S_ERRORS:
             check(lib().lxb_status_clear(self.plan), "lxb_status_clear")
             raise LxbError(f"device status {e.status:#x} (stream {e.first_stream}, "
                            f"step {e.first_step})")

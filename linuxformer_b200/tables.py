@@ -25,9 +25,10 @@ from . import chip as C
 from .chip import _ranges
 
 MAGIC = 0x50425A4C
-VERSION = 6
+VERSION = 7
 NSLOT, NOSLOT = 1536, 0xFFFF
 ITEMSLOTS, MAXDENSE, MAXUNITS, MAXWIN = 4, 32, 2048, 1024
+HEADSLICES = 32
 IT_DECAYS, IT_OUT = 1, 2
 SEC = ("layers", "items", "chans", "ent", "units", "owners", "i32", "u16", "headcta", "hcodes",
        "blobs", "blobidx", "winmap", "winidx")
@@ -338,11 +339,20 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
     sp_ptr = np.zeros(V + 1, np.int64)
     np.cumsum(np.bincount(sp_rows, minlength=V), out=sp_ptr[1:])
     sp_base = ent.add(_pack(sp_cols, sp_bits))
-    headcta = np.zeros(Cn, HEADCTA)
-    for c in range(Cn):
-        r0, r1 = V * c // Cn, V * (c + 1) // Cn
+    # the head rows: CTA rank c owns rows [V c / C, V (c + 1) / C) (entry C * HEADSLICES + c),
+    # cut in HEADSLICES slices (entry c * HEADSLICES + k) for a launch with helper clusters: the
+    # decoding cluster takes the first slices of its ranges, the helpers the others
+    n_parts = Cn * HEADSLICES
+    headcta = np.zeros(n_parts + Cn, HEADCTA)
+    for c in range(n_parts):
+        r0, r1 = V * c // n_parts, V * (c + 1) // n_parts
         headcta[c]["r0"], headcta[c]["r1"] = r0, r1
         headcta[c]["rowptr"] = i32.add((sp_ptr[r0:r1 + 1] + sp_base).astype(np.int32))
+    for c in range(Cn):
+        r0, r1 = V * c // Cn, V * (c + 1) // Cn
+        e = headcta[n_parts + c]
+        e["r0"], e["r1"] = r0, r1
+        e["rowptr"] = i32.add((sp_ptr[r0:r1 + 1] + sp_base).astype(np.int32))
     final_norm = u16.add(chip.final_norm)
     for c in range(Cn):  # the head's blobs: the final norm
         blob = _Blob()
