@@ -124,7 +124,9 @@ int lxb_profile_sections(void);
  * output head's rows per token and hands its maximum back through the scratch buffer, so the
  * head's table lookups run on up to 8x the SMs. 0 turns them off. A helper that does not answer
  * within a bounded wait is dropped for the rest of the launch (LXB_S_HELPER); the results do not
- * depend on it. No counterpart in the reference (its head runs on its one 132-CTA grid). */
+ * depend on it. A negative count -n is a drill: n helper clusters start but never answer, so the
+ * decoding cluster's wait runs out (about 34 ms) and it takes their rows itself (for tests of the
+ * fallback). No counterpart in the reference (its head runs on its one 132-CTA grid). */
 int lxb_plan_set_head_helpers(lxb_plan* plan, int max_clusters);
 
 /* How the plan stages its per-step tables: buffers (2 = the next step's copy overlaps the

@@ -101,6 +101,7 @@ struct Run {
   unsigned long long* hseq;    // the token whose head input hx holds (epoch | token + 1)
   uint4* hpart;                // [slice * cluster + rank]: a helper's maximum {v, row, seq lo, hi}
   unsigned long long epoch;    // this launch's tag (launch count << 32): stale words never match
+  int help_drill;              // the helpers start but never answer (the fallback's test)
 };
 
 // profile sections (lxb_plan_set_profile): cycles spent per CTA
@@ -1099,6 +1100,7 @@ __device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned l
 __device__ void head_helper(const Dev& P, const Run& run, Smem& sm, int rank, int hk) {
   const int t = threadIdx.x;
   const int part = hk * P.C + rank;
+  if (run.help_drill) return;
   const unsigned long long done = run.epoch | 0xffffffffull;
   for (int i = 0; i < run.n_tokens; i++) {
     const unsigned long long want = run.epoch | (unsigned long long)(i + 1);
@@ -1540,6 +1542,7 @@ struct lxb_plan {
   uint32_t* status;
   int max_clusters;
   int head_helpers;              // the most head helper clusters a single-stream launch may use
+  int help_drill;                // helpers that never answer (lxb_plan_set_head_helpers < 0)
   unsigned long long launches;   // launches so far (the helpers' exchange tag)
   unsigned long long* prof;
   int smem;  // dynamic shared memory per CTA: Smem, then the staging buffers
@@ -1935,6 +1938,7 @@ extern "C" int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb
   }
   p->max_clusters = ncl;
   p->head_helpers = LXB_HEADSLICES - 1;
+  p->help_drill = 0;
   p->launches = 0;
   *out = p;
   return LXB_OK;
@@ -1989,7 +1993,7 @@ static int decode_launch(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitm
   Run run{state_ptrs, bitmaps, ring, ring_r, embed, forced, n_forced, n_tokens, preds, inputs,
           p->prof, n_streams, n_help, reinterpret_cast<float*>(xg),
           reinterpret_cast<unsigned long long*>(xg + (size_t)H * 4),
-          reinterpret_cast<uint4*>(xg + (size_t)H * 4 + 16), p->launches << 32};
+          reinterpret_cast<uint4*>(xg + (size_t)H * 4 + 16), p->launches << 32, p->help_drill};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -2079,8 +2083,9 @@ extern "C" int lxb_plan_set_profile(lxb_plan* p, unsigned long long* prof) {
 extern "C" int lxb_profile_sections(void) { return PR_N; }
 
 extern "C" int lxb_plan_set_head_helpers(lxb_plan* p, int max_clusters) {
-  if (!p || max_clusters < 0) return LXB_E_INVAL;
-  p->head_helpers = max_clusters;
+  if (!p || max_clusters < -(LXB_HEADSLICES - LXB_HEADMAIN)) return LXB_E_INVAL;
+  p->head_helpers = max_clusters < 0 ? -max_clusters : max_clusters;
+  p->help_drill = max_clusters < 0;
   return LXB_OK;
 }
 

@@ -117,3 +117,23 @@ def test_chained_short_launches(c1_chip, which):
     want, _, _ = Oracle(chip).decode(host, [0], len(got))
     assert got == want.tolist()
     _same_state(ds, 0, host)
+
+
+def test_head_helpers_match_and_fall_back():
+    """The output head with helper clusters, without them, and with helpers that never answer
+    (a drill: the decoding cluster's bounded wait runs out, it takes their rows itself and flags
+    LXB_S_HELPER): the same stream as the oracle every time."""
+    from linuxformer_b200._lib import S_HELPER, lib
+
+    chip = C.c2(1, vocab=20000)
+    st0 = C.c2_state(chip, 1)
+    n = 12
+    p, _, _ = Oracle(chip).decode(st0.copy(), [0], n)
+    for helpers in (7, 0, -3):
+        dec = _decoder(chip, 16)
+        assert lib().lxb_plan_set_head_helpers(dec.plan, helpers) == 0
+        ds = dec.states([st0])
+        preds, _ = dec.run(ds, [[0]], n)
+        assert (preds[0].cpu().numpy() == p).all(), helpers
+        flagged = bool(dec.status().status & S_HELPER)
+        assert flagged == (helpers < 0 and dec.max_clusters > 1), (helpers, dec.status().status)
