@@ -133,6 +133,7 @@ struct __align__(16) Smem {
   int qidx[KD], kidx[KD];
   float ob[R][VD];                 // o per value head (bf16 values)
   float beta[R], g[R];
+  uint32_t dbm[R][8];              // a decaying item's nonzero-row bitmaps
   float red[40];
   int nq, nk;
   uint32_t vhmask[LXB_ITEMSLOTS];  // value heads with output, per item slot
@@ -587,30 +588,52 @@ __device__ __forceinline__ void item_fire(const Dev& P, const Run& run, Smem& sm
 
 // The state's change for value head r, column j (S points at row 0, column j): the decay of the
 // rows that may be nonzero (the others stay zero), then the key's delta-rule write.
-__device__ __forceinline__ void item_write(Smem& sm, float* S, const uint32_t* bmv, int r, int j,
-                                        int nk) {
-  const float g = sm.g[r];
-  if (g != 0.0f) {
-    const float e = lx_exp(g);
-#pragma unroll 1
-    for (int w = 0; w < 8; w++) {
-      uint32_t m = bmv[w];
-      while (m) {
-        int ix[8];
+// The decay of a thread's two value heads rA and rA + 4 (SA, SB at row 0, its column): every row
+// that may be nonzero (the bitmaps, staged in sm.dbm) times exp(g), each head's rows gathered
+// across the bitmap words, 12 loads in flight per round.
+__device__ __forceinline__ void item_decay(const Smem& sm, float* SA, float* SB, int rA) {
+  constexpr int HPT = 2, D = 6, HS = 4;
+  float* S[HPT] = {SA, SB};
+  float e[HPT];
+  int w[HPT];
+  uint32_t m[HPT];
+  bool on[HPT];
 #pragma unroll
-        for (int q = 0; q < 8; q++) {
-          ix[q] = m ? (w * 32 + __ffs(m) - 1) : -1;
-          m &= m - 1;
-        }
-        float v[8];
-#pragma unroll
-        for (int q = 0; q < 8; q++) v[q] = ix[q] >= 0 ? S[ix[q] * VD] : 0.0f;
-#pragma unroll
-        for (int q = 0; q < 8; q++)
-          if (ix[q] >= 0) S[ix[q] * VD] = lx_mul(v[q], e);
-      }
-    }
+  for (int k = 0; k < HPT; k++) {
+    const float g = sm.g[rA + k * HS];
+    on[k] = g != 0.0f;
+    e[k] = on[k] ? lx_exp(g) : 1.0f;
+    w[k] = 0;
+    m[k] = on[k] ? sm.dbm[rA + k * HS][0] : 0u;
   }
+  for (;;) {
+    int ix[HPT][D];
+    bool any = false;
+#pragma unroll
+    for (int k = 0; k < HPT; k++)
+#pragma unroll
+      for (int q = 0; q < D; q++) {
+        while (on[k] && !m[k] && w[k] < 7) m[k] = sm.dbm[rA + k * HS][++w[k]];
+        ix[k][q] = m[k] ? w[k] * 32 + __ffs(m[k]) - 1 : -1;
+        m[k] &= m[k] - 1;
+        any |= ix[k][q] >= 0;
+      }
+    if (!any) break;
+    float v[HPT][D];
+#pragma unroll
+    for (int k = 0; k < HPT; k++)
+#pragma unroll
+      for (int q = 0; q < D; q++) v[k][q] = ix[k][q] >= 0 ? S[k][ix[k][q] * VD] : 0.0f;
+#pragma unroll
+    for (int k = 0; k < HPT; k++)
+#pragma unroll
+      for (int q = 0; q < D; q++)
+        if (ix[k][q] >= 0) S[k][ix[k][q] * VD] = lx_mul(v[k][q], e[k]);
+  }
+}
+
+// the key's delta-rule write into value head r (S at row 0, column j), after the decay
+__device__ __forceinline__ void item_write(Smem& sm, float* S, int r, int j, int nk) {
   if (nk) {
     float kv = 0.0f;
     for (int a0 = 0; a0 < nk; a0 += 8) {
@@ -736,7 +759,10 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
 #pragma unroll
   for (int r = 0; r < R; r++) anyg |= sm.g[r] != 0.0f;
   if (!nq && !nk && !anyg) return false;  // the state stays as it is and o = 0
-  if (nk) item_fire(P, run, sm, B, bi, conv, s, L, step, w_in, r_in);
+  if (anyg && t < R * 8)  // the decaying heads' nonzero-row bitmaps, for item_decay
+    sm.dbm[t >> 3][t & 7] = bm[(bi.kh * R + (t >> 3)) * 8 + (t & 7)];
+  if (nk) item_fire(P, run, sm, B, bi, conv, s, L, step, w_in, r_in);  // (ends with a barrier)
+  else if (anyg) __syncthreads();
   // the delta rule, thread = (state column j, value heads rA and rA + 4): the decay and the
   // key's write per head (rare), then both heads' readouts with their loads in flight together
   static_assert(NT / VD == 4 && R == 8, "two value heads per thread");
@@ -745,9 +771,10 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
     const int rA = t >> 7;
     float* SA = rec + (size_t)(bi.kh * R + rA) * KD * VD + j;
     float* SB = SA + (size_t)4 * KD * VD;
-    if (anyg | nk) {
-      item_write(sm, SA, bm + (bi.kh * R + rA) * 8, rA, j, nk);
-      item_write(sm, SB, bm + (bi.kh * R + rA + 4) * 8, rA + 4, j, nk);
+    if (anyg) item_decay(sm, SA, SB, rA);
+    if (nk) {
+      item_write(sm, SA, rA, j, nk);
+      item_write(sm, SB, rA + 4, j, nk);
     }
     float oA = 0.0f, oB = 0.0f;
     for (int a0 = 0; a0 < nq; a0 += 8) {
