@@ -136,6 +136,7 @@ struct __align__(16) Smem {
   uint32_t dbm[R][8];              // a decaying item's nonzero-row bitmaps
   float red[40];
   int nq, nk;
+  int qkn;                         // the q / k lists are l2-normed already (eager_block)
   uint32_t vhmask[LXB_ITEMSLOTS];  // value heads with output, per item slot
   int wflag[2];                    // some item of the step wrote (pushed by the writer)
   int kmask[LXB_NK];               // out_proj step: active value heads per key head
@@ -548,7 +549,10 @@ __device__ __forceinline__ void eager_block(Smem& sm, const unsigned char* B, co
       val[i] = warp ? vn : lx_mul(vn, 0.0625f);  // the query times 256^-0.5
     }
     if (lane == 0) (warp ? sm.nk : sm.nq) = n;
-    if (t == 0) sm.vhmask[bi.slot] = 0;
+    if (t == 0) {
+      sm.vhmask[bi.slot] = 0;
+      sm.qkn = 1;
+    }
   }
 }
 
@@ -682,6 +686,39 @@ __device__ __forceinline__ void item_out(const Dev& P, Smem& sm, const unsigned 
   if (lane == 0) atomicOr(&sm.vhmask[bi.slot], 1u << r);
 }
 
+// the query's and key's l2 norms (warp 0; lane 0 the query's, lane 1 the key's), in place
+__device__ __forceinline__ void qk_norm(Smem& sm, int nq, int nk) {
+  const int lane = threadIdx.x & 31;
+  float inv = 0.0f;
+  if (lane == 0 && nq) inv = l2_inv(sm.qval, nq);
+  if (lane == 1 && nk) inv = l2_inv(sm.kval, nk);
+  const float iq = __shfl_sync(0xffffffffu, inv, 0), ik = __shfl_sync(0xffffffffu, inv, 1);
+  if (lane < nq) sm.qval[lane] = lx_mul(lx_rbf(lx_mul(sm.qval[lane], iq)), 0.0625f);
+  if (lane < nk) sm.kval[lane] = lx_rbf(lx_mul(sm.kval[lane], ik));
+}
+
+// An item's end, after o is in sm.ob: the bitmaps of the rows a key wrote, then the gated norm
+// per value head with output (warp r); a head without out_proj entries has no z rows staged and
+// cannot write: it skips this. Returns whether the item wrote.
+__device__ __forceinline__ bool item_tail(const Dev& P, Smem& sm, const unsigned char* B,
+                                          const lxb_bitem& bi, uint32_t* bm, int nk,
+                                          const uint16_t* w_in, float r_in) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  __syncthreads();
+  if ((bi.flags & LXB_IT_DECAYS) && t < R) {  // rows the key wrote may now be nonzero
+    uint32_t* b = bm + (bi.kh * R + t) * 8;
+    for (int a = 0; a < nk; a++) b[sm.kidx[a] >> 5] |= 1u << (sm.kidx[a] & 31);
+  }
+  if (warp < R && bi.z >= 0) {
+    const float* o = sm.ob[warp];
+    const bool nz = __any_sync(0xffffffffu, o[4 * lane] != 0.0f || o[4 * lane + 1] != 0.0f ||
+                                                o[4 * lane + 2] != 0.0f || o[4 * lane + 3] != 0.0f);
+    if (nz) item_out(P, sm, B, bi, warp, w_in, r_in);
+  }
+  __syncthreads();
+  return sm.vhmask[bi.slot] != 0 && (bi.flags & LXB_IT_OUT);
+}
+
 // B: the step blob (shared memory); bi: this item's record in it; w_in: the staged input norm.
 // Returns whether it wrote (some value head has output and the head has out_proj entries).
 __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned char* B,
@@ -732,17 +769,10 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
       }
       __syncwarp();
       const int nq = __popc(mq), nk = __popc(mk);
-      if (nq | nk) {
-        float inv = 0.0f;
-        if (lane == 0 && nq) inv = l2_inv(sm.qval, nq);
-        if (lane == 1 && nk) inv = l2_inv(sm.kval, nk);
-        const float iq = __shfl_sync(0xffffffffu, inv, 0), ik = __shfl_sync(0xffffffffu, inv, 1);
-        if (lane < nq) sm.qval[lane] = lx_mul(lx_rbf(lx_mul(sm.qval[lane], iq)), 0.0625f);
-        if (lane < nk) sm.kval[lane] = lx_rbf(lx_mul(sm.kval[lane], ik));
-      }
-      if (lane == 0) {
+      if (lane == 0) {  // the lists' l2 norms come after the block barrier (qk_norm)
         sm.nq = nq;
         sm.nk = nk;
+        sm.qkn = 0;
         sm.vhmask[bi.slot] = 0;
       }
     }
@@ -759,6 +789,56 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
 #pragma unroll
   for (int r = 0; r < R; r++) anyg |= sm.g[r] != 0.0f;
   if (!nq && !nk && !anyg) return false;  // the state stays as it is and o = 0
+  const bool normed = sm.qkn;
+  if (nq && !nk && !anyg) {
+    // a pure readout: its first rows' loads go out while warp 0 norms the query
+    static_assert(NT / VD == 4 && R == 8, "two value heads per thread");
+    const int j = t & (VD - 1);
+    const int rA = t >> 7;
+    const float* SA = rec + (size_t)(bi.kh * R + rA) * KD * VD + j;
+    const float* SB = SA + (size_t)4 * KD * VD;
+    float hA[8], hB[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const bool ok = q < nq;
+      const int ix = ok ? sm.qidx[q] : 0;
+      hA[q] = ok ? SA[ix * VD] : 0.0f;
+      hB[q] = ok ? SB[ix * VD] : 0.0f;
+    }
+    if (!normed && warp == 0) qk_norm(sm, nq, 0);
+    __syncthreads();
+    float oA = 0.0f, oB = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 8; q++)
+      if (q < nq) {
+        const float qv = sm.qval[q];
+        oA = lx_add(oA, lx_mul(hA[q], qv));
+        oB = lx_add(oB, lx_mul(hB[q], qv));
+      }
+    for (int a0 = 8; a0 < nq; a0 += 8) {
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        const bool ok = a0 + q < nq;
+        const int ix = ok ? sm.qidx[a0 + q] : 0;
+        hA[q] = ok ? SA[ix * VD] : 0.0f;
+        hB[q] = ok ? SB[ix * VD] : 0.0f;
+      }
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+        if (a0 + q < nq) {
+          const float qv = sm.qval[a0 + q];
+          oA = lx_add(oA, lx_mul(hA[q], qv));
+          oB = lx_add(oB, lx_mul(hB[q], qv));
+        }
+    }
+    sm.ob[rA][j] = lx_rbf(oA);
+    sm.ob[rA + 4][j] = lx_rbf(oB);
+    return item_tail(P, sm, B, bi, bm, 0, w_in, r_in);
+  }
+  if (!normed) {
+    if (warp == 0) qk_norm(sm, nq, nk);
+    __syncthreads();
+  }
   if (anyg && t < R * 8)  // the decaying heads' nonzero-row bitmaps, for item_decay
     sm.dbm[t >> 3][t & 7] = bm[(bi.kh * R + (t >> 3)) * 8 + (t & 7)];
   if (nk) item_fire(P, run, sm, B, bi, conv, s, L, step, w_in, r_in);  // (ends with a barrier)
@@ -797,21 +877,7 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
     sm.ob[rA][j] = lx_rbf(oA);
     sm.ob[rA + 4][j] = lx_rbf(oB);
   }
-  __syncthreads();
-  if ((bi.flags & LXB_IT_DECAYS) && t < R) {  // rows the key wrote may now be nonzero
-    uint32_t* b = bm + (bi.kh * R + t) * 8;
-    for (int a = 0; a < nk; a++) b[sm.kidx[a] >> 5] |= 1u << (sm.kidx[a] & 31);
-  }
-  // the gated norm per value head with output (warp r); a head without out_proj entries has no
-  // z rows staged and cannot write: it skips this
-  if (warp < R && bi.z >= 0) {
-    const float* o = sm.ob[warp];
-    const bool nz = __any_sync(0xffffffffu, o[4 * lane] != 0.0f || o[4 * lane + 1] != 0.0f ||
-                                                o[4 * lane + 2] != 0.0f || o[4 * lane + 3] != 0.0f);
-    if (nz) item_out(P, sm, B, bi, warp, w_in, r_in);
-  }
-  __syncthreads();
-  return sm.vhmask[bi.slot] != 0 && (bi.flags & LXB_IT_OUT);
+  return item_tail(P, sm, B, bi, bm, nk, w_in, r_in);
 }
 
 // --- the owned rows ---------------------------------------------------------------------------
