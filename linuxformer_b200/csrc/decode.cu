@@ -1035,6 +1035,27 @@ __device__ void take_rows(Smem& sm, int par) {
   __syncthreads();
 }
 
+// take_rows with the residual's sum of squares in the canonical order on the way (lane t: the
+// squares of x[t + 512 i], i = 0..4, in order, then the two butterflies): the norm factor
+__device__ float take_rows_norm(const Dev& P, Smem& sm, int par) {
+  static_assert(H == 5 * NT, "five residual rows per thread");
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 5; i++) {
+    const float v = lx_f(sm.xin[par][t + NT * i]);
+    sm.x[t + NT * i] = v;
+    s = i == 0 ? lx_mul(v, v) : lx_add(s, lx_mul(v, v));
+  }
+  s = warp_xor_sum(s);
+  if (lane == 0) sm.red[warp] = s;
+  __syncthreads();
+  float v = lane < 16 ? sm.red[lane] : 0.0f;
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) v = lx_add(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return norm_factor(P, __shfl_sync(0xffffffffu, v, 0));
+}
+
 __device__ void load_embed(const Run& run, const Dev& P, Smem& sm, int tok) {
   const uint4* e = reinterpret_cast<const uint4*>(run.embed + ((int64_t)tok + P.offset) * H);
   for (int k = threadIdx.x; k < H / 8; k += NT) {
@@ -1394,8 +1415,10 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         }
         if (rank == 0 && t == 0) run.ring_r[slot] = r;
       }
-      if (ly.has_mlp) norm_into(sm.xm, sm.x, w_post, r);
-      __syncthreads();
+      if (ly.has_mlp) {  // (a step without one needs no barrier here: nothing above is read
+        norm_into(sm.xm, sm.x, w_post, r);  // by another thread before the items' own barriers)
+        __syncthreads();
+      }
       if (P.nbuf == 2) issue_next(stp);  // the next step's blob: its buffer was read a step ago
       PROF(PR_NORM);
       bool wrote = false;
@@ -1429,12 +1452,11 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         __syncthreads();
         push_rows(P, sm, sm.own[ph & 1], ph & 1, rank, cluster);
         cluster.sync();
-        take_rows(sm, ph & 1);
-        x_new = true;
+        r_x = take_rows_norm(P, sm, ph & 1);
+        x_new = false;
         ph++;
         if (ly.has_mlp) {
-          const float r2 = norm_factor(P, block_ssq(sm, sm.x));
-          norm_into(sm.xm, sm.x, w_post, r2);
+          norm_into(sm.xm, sm.x, w_post, r_x);
           __syncthreads();
           if (mlp) mlp_owner(P, sm, B, mh, rank, sm.own[ph & 1]);
           else copy_owner(P, sm, rank, sm.own[ph & 1]);
@@ -1442,17 +1464,13 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
           push_rows(P, sm, sm.own[ph & 1], ph & 1, rank, cluster);
           cluster.sync();
           if (P.nbuf == 1) issue_next(stp);
-          take_rows(sm, ph & 1);
+          r_x = take_rows_norm(P, sm, ph & 1);
           ph++;
         }
-        x_new = true;
         PROF(PR_FIXUP);
       } else {
         if (P.nbuf == 1) issue_next(stp);
-        if (ly.has_mlp) {
-          take_rows(sm, ph & 1);
-          x_new = true;
-        }
+        if (ly.has_mlp) r_x = take_rows_norm(P, sm, ph & 1);
         ph++;
         PROF(PR_PULL);
       }
@@ -1565,9 +1583,8 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         }
         __syncthreads();
       }
-      if (t < 32) {
-        const float bv = sm.cv;
-        const int bi = sm.ci;
+      {
+        const int bi = sm.ci;  // the token: the first maximum of the logits
         if (t == 0) {
           if (rank == 0) run.preds[(size_t)s * run.n_tokens + i] = bi;
           int nt = (i + 1 < run.n_forced) ? run.forced[(size_t)s * run.n_forced + i + 1] : bi;
