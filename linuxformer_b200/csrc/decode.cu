@@ -473,16 +473,15 @@ __device__ __forceinline__ float eager_channel(Smem& sm, const unsigned char* B,
   uint2* wp = b.y != LXB_NOWIN ? &sm.win[b.y] : reinterpret_cast<uint2*>(conv + (size_t)a.z * 4);
   const uint2 win = *wp;
   float ps = 0.0f;
-  if (pr) {
-    int k = 0;
-    for (; k + 8 <= ne; k += 8) {
+  if (pr) {  // in batches of 8, the last one partial: every batch's loads in flight together
+    for (int k = 0; k < ne; k += 8) {
       float v[8];
 #pragma unroll
-      for (int q = 0; q < 8; q++) v[q] = pr[k + q];
+      for (int q = 0; q < 8; q++) v[q] = k + q < ne ? pr[k + q] : 0.0f;
 #pragma unroll
-      for (int q = 0; q < 8; q++) ps = lx_add(ps, v[q]);
+      for (int q = 0; q < 8; q++)
+        if (k + q < ne) ps = lx_add(ps, v[q]);
     }
-    for (; k < ne; k++) ps = lx_add(ps, pr[k]);
   } else {
     for (int k = 0; k < ne; k++)
       ps = lx_add(ps, lx_mul(xn_at(sm, w, r, e[k] & 0xffffu), lx_f((uint16_t)(e[k] >> 16))));

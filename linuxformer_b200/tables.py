@@ -123,6 +123,23 @@ def _may_decay(layer: C.Layer, vh: np.ndarray) -> np.ndarray:
         (_f32(layer.A_log[vh]) >= -103.98)
 
 
+def _mlp_order(layer: C.Layer, Cn: int, blk: int, L: int) -> np.ndarray:
+    """CTA ranks by ascending MLP work in this layer (ties, and layers without an MLP, rotated
+    by the layer index)."""
+    rot = (np.arange(Cn) - 3 * L) % Cn
+    g_cnt, u_cnt = layer.gate.row_nnz(), layer.up.row_nnz()
+    live = (g_cnt > 0) & (u_cnt > 0) & (layer.down.transpose().row_nnz() > 0)
+    if not live.any():
+        return np.argsort(rot, kind="stable")
+    cost = np.zeros(Cn, np.int64)
+    for c in range(Cn):
+        sub = layer.down.rows_subset(np.arange(c * blk, (c + 1) * blk))
+        keep = live[sub.indices]
+        need = np.unique(sub.indices[keep])
+        cost[c] = int(g_cnt[need].sum() + u_cnt[need].sum() + keep.sum())
+    return np.lexsort((rot, cost))
+
+
 def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
     """The plan image for `chip` on clusters of `cluster` CTAs, and build statistics."""
     Cn = cluster
@@ -164,9 +181,12 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
         # the row entries of the whole in_proj_qkv, packed once
         qkv_ent0 = ent.add(_pack(qkv.indices, qkv.data))
         stats["csr_nnz"] += qkv.nnz
-        rot = (3 * L) % Cn
+        # the CTAs in order of their MLP work in this layer (gate/up entries of the units their
+        # rows need, down entries): the items go to the lightest first, as a paired step waits
+        # for the CTA that has both; without an MLP, a rotation spreads them over the layers
+        cta_order = _mlp_order(ly, Cn, blk, L)
         for k, kh in enumerate(heads):
-            pos = k + rot
+            cta_k, slot_k = int(cta_order[k % Cn]), k // Cn
             sel = np.nonzero(kh_of == kh)[0]
             # order: eager (query/key with a tap) | value with a tap | the rest (window only)
             tapped = (ly.conv[live[sel]] & 0x7FFF).any(1)
@@ -197,7 +217,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
                 refs[q0:q0 + len(rr), 0] = np.where(n > 0, base + sub.indptr[:-1], 0)
                 refs[q0:q0 + len(rr), 1] = n
             it = np.zeros(1, ITEM)[0]
-            it["layer"], it["kh"], it["cta"], it["slot"] = L, kh, pos % Cn, pos // Cn
+            it["layer"], it["kh"], it["cta"], it["slot"] = L, kh, cta_k, slot_k
             it["ch0"], it["n_ch"] = ch0, len(chs)
             it["n_eager"], it["n_vneed"] = int((cls == 0).sum()), int((cls == 1).sum())
             it["tapu"] = int(np.bitwise_or.reduce(ch["tapmask"][cls == 1], initial=0))
