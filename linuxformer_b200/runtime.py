@@ -73,7 +73,10 @@ class Decoder:
     def __del__(self):
         p = getattr(self, "plan", None)
         if p is not None and p.value:
-            lib().lxb_plan_destroy(p)
+            try:
+                lib().lxb_plan_destroy(p)
+            except TypeError:  # interpreter shutdown: the module's globals are gone already
+                pass
             self.plan = None
 
     def caps(self) -> Caps:
