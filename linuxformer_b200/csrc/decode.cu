@@ -57,6 +57,10 @@ namespace cg = cooperative_groups;
 #define BLKMAX (LXB_H / LXB_MINC)
 #define LXB_MAXLAYERS 64
 #define LXB_MAXPROD 4096
+#define LXB_LOGMAX 320  // group steps: window shifts a CTA may undo (entries of 12 bytes)
+#ifndef LXB_GROUPS
+#define LXB_GROUPS 1    // runs of GDN-only layers as optimistic group steps
+#endif
 
 struct Dev {
   const lxb_layer* layers;
@@ -138,6 +142,10 @@ struct __align__(16) Smem {
   int nq, nk;
   int qkn;                         // the q / k lists are l2-normed already (eager_block)
   uint32_t vhmask[LXB_ITEMSLOTS];  // value heads with output, per item slot
+  int vhlay[LXB_ITEMSLOTS];        // the layer whose item last set the slot's vhmask
+  int gkey[2];                     // group steps, by parity: 2 layer + (0 pending | 1 wrote)
+  uint32_t lmeta[LXB_LOGMAX];      // undo log: window index | item << 10 | (layer - lo) << 12
+  uint2 lold[LXB_LOGMAX];          // the window before the shift
   int wflag[2];                    // some item of the step wrote (pushed by the writer)
   int kmask[LXB_NK];               // out_proj step: active value heads per key head
   alignas(16) uint16_t on[LXB_ITEMSLOTS][R * VD];  // the gated norm's output per item slot
@@ -719,11 +727,19 @@ __device__ __forceinline__ bool item_tail(const Dev& P, Smem& sm, const unsigned
 }
 
 // B: the step blob (shared memory); bi: this item's record in it; w_in: the staged input norm.
-// Returns whether it wrote (some value head has output and the head has out_proj entries).
-__device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned char* B,
-                         const lxb_bitem& bi, float* rec, uint16_t* conv, uint32_t* bm, int s,
-                         int L, int step, const uint16_t* w_in, float r_in) {
+// lmeta / lold (a group step's layer after its first, "speculative"): where to log the item's
+// window shifts (meta: window index | item << 10 | lrel << 12), and a key firing or a decay is
+// not done but reported. Returns ITEM_DONE, ITEM_WROTE (some value head has output and the head
+// has out_proj entries), ITEM_PENDING (speculative and heavy: its windows shifted and logged,
+// nothing else done) or ITEM_UNTOUCHED (speculative and not loggable: nothing done).
+enum { ITEM_DONE = 0, ITEM_WROTE = 1, ITEM_PENDING = 2, ITEM_UNTOUCHED = 3 };
+__device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned char* B,
+                        const lxb_bitem& bi, float* rec, uint16_t* conv, uint32_t* bm, int s,
+                        int L, int step, const uint16_t* w_in, float r_in, uint32_t* lmeta,
+                        uint2* lold, uint32_t lmark) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const bool spec = lmeta != nullptr;
+  if (spec && (bi.n_eager > 32 || (bi.flags & LXB_IT_NONRES))) return ITEM_UNTOUCHED;
   const uint4* ch = reinterpret_cast<const uint4*>(B + bi.eager);
   // the eager rows' products, all entries at once over the block (the entries of the item's
   // eager channels are contiguous in the blob, in channel order)
@@ -748,6 +764,10 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
       int slot = 0;
       if (lane < bi.n_eager) {
         const uint4 a = ch[2 * lane], b = ch[2 * lane + 1];
+        if (spec) {  // the window before the shift (resident: LXB_IT_NONRES is clear)
+          lmeta[lane] = b.y | lmark;
+          lold[lane] = sm.win[b.y];
+        }
         v = eager_channel(sm, B, a, b, conv, w_in, r_in,
                           pre ? sm.prod + (a.x - e_first) / 4u : nullptr);
         slot = (int)(a.y >> 16);
@@ -773,10 +793,12 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
         sm.nk = nk;
         sm.qkn = 0;
         sm.vhmask[bi.slot] = 0;
+        sm.vhlay[bi.slot] = L;
       }
     }
   } else {
     eager_block(sm, B, bi, conv, w_in, r_in, pre ? sm.prod : nullptr, e_first);
+    if (t == 0) sm.vhlay[bi.slot] = L;
   }
   // warp 1: g, only for a head that can decay (for the others softplus underflows to zero
   // whatever the input: g is 0, as the table builder proved); beta only when a key fires
@@ -787,7 +809,8 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
   int anyg = 0;
 #pragma unroll
   for (int r = 0; r < R; r++) anyg |= sm.g[r] != 0.0f;
-  if (!nq && !nk && !anyg) return false;  // the state stays as it is and o = 0
+  if (!nq && !nk && !anyg) return ITEM_DONE;  // the state stays as it is and o = 0
+  if (spec && (nk || anyg)) return ITEM_PENDING;  // a state write waits for its input to be final
   const bool normed = sm.qkn;
   if (nq && !nk && !anyg) {
     // a pure readout: its first rows' loads go out while warp 0 norms the query
@@ -832,7 +855,7 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
     }
     sm.ob[rA][j] = lx_rbf(oA);
     sm.ob[rA + 4][j] = lx_rbf(oB);
-    return item_tail(P, sm, B, bi, bm, 0, w_in, r_in);
+    return item_tail(P, sm, B, bi, bm, 0, w_in, r_in) ? ITEM_WROTE : ITEM_DONE;
   }
   if (!normed) {
     if (warp == 0) qk_norm(sm, nq, nk);
@@ -876,7 +899,7 @@ __device__ bool gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned 
     sm.ob[rA][j] = lx_rbf(oA);
     sm.ob[rA + 4][j] = lx_rbf(oB);
   }
-  return item_tail(P, sm, B, bi, bm, nk, w_in, r_in);
+  return item_tail(P, sm, B, bi, bm, nk, w_in, r_in) ? ITEM_WROTE : ITEM_DONE;
 }
 
 // --- the owned rows ---------------------------------------------------------------------------
@@ -952,10 +975,10 @@ __device__ void out_owner(const Dev& P, Smem& sm, const lxb_layer& ly, const lxb
   if (t < LXB_NK) {
     const int ii = itemof[t];
     uint32_t m = 0;
-    if (ii >= 0) {
+    if (ii >= 0) {  // (a slot a later layer's item has used since holds no output of this one)
       const lxb_item it = P.items[ii];
-      const uint32_t* rm = cluster.map_shared_rank(&sm.vhmask[it.slot], it.cta);
-      m = *rm;
+      m = *cluster.map_shared_rank(&sm.vhmask[it.slot], it.cta);
+      if (*cluster.map_shared_rank(&sm.vhlay[it.slot], it.cta) != it.layer) m = 0;
     }
     sm.kmask[t] = (int)m;
   }
@@ -1299,8 +1322,10 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     return;
   }
   const int nsteps_tok = P.n_layers + 1;  // the layers, then the head
-  const long long total = (long long)run.n_tokens * nsteps_tok;
-  if (t < 2) sm.wflag[t] = 0;
+  if (t < 2) {
+    sm.wflag[t] = 0;
+    sm.gkey[t] = 0x7fffffff;
+  }
   if (t == 0) sm.help_dead = 0;
   if (t == 0) {
     int tok = run.forced[(size_t)s * run.n_forced];
@@ -1352,16 +1377,36 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
   } while (0)
   // the layer (or head, = n_layers) of global step k: k runs over the layers then the head
   int cur_layer = 0;  // the current step's layer (n_layers: the head)
+  int cur_tok = 0;    // the current token
+  int inflight = 0;   // the layer whose blob was issued last (-1: none), staged for the next take
   bool x_new = true;  // the residual changed since r_x was computed
   float r_x = 0.0f;   // the norm factor of the residual
   // the next step's blob into the free staging buffer (thread 0; the caller has synchronised
   // the block since the buffer's last use)
   // (issued by the last warp's first lane: that warp has the least work at the start of a step)
   auto issue_next = [&](long long cur) {
-    const long long nx = cur + 1;
-    if (t == NT - 32 && nx < total && !sm.broken)
-      stage_issue(P, sm, stage, P.nbuf == 2 ? (int)(nx & 1) : 0,
-                  cur_layer + 1 == nsteps_tok ? 0 : cur_layer + 1);
+    if (cur_layer == P.n_layers && cur_tok == run.n_tokens - 1) {  // the launch's last step
+      inflight = -1;
+      return;
+    }
+    inflight = cur_layer + 1 == nsteps_tok ? 0 : cur_layer + 1;
+    if (t == NT - 32 && !sm.broken)
+      stage_issue(P, sm, stage, P.nbuf == 2 ? (int)((cur + 1) & 1) : 0, inflight);
+  };
+  // two buffers: make the copy staged for the next take layer Lnext's (a group step that starts
+  // again at another layer): the copy in flight lands first, then Lnext's is issued in its place
+  auto restage = [&](int Lnext) {
+    if (inflight == Lnext) return;
+    const int b = (int)(stp & 1);
+    if (inflight >= 0) {
+      unsigned long long polls = 0;
+      const bool ok = !sm.broken && stage_wait(P, sm, b, (phases >> b) & 1u, s, cur_tok, polls);
+      phases ^= 1u << b;
+      if (!ok && t == 0) sm.broken = 1;
+    }
+    __syncthreads();  // every thread has seen that phase complete before the next one begins
+    if (t == NT - 32 && !sm.broken) stage_issue(P, sm, stage, b, Lnext);
+    inflight = Lnext;
   };
   // this step's blob: wait for it, and with two buffers start the next one's copy right away
   auto take = [&](int i) -> const unsigned char* {
@@ -1378,11 +1423,144 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     if (sm.broken) return nullptr;
     return stage + (size_t)b * P.stage;
   };
+  // A run of GDN-only layers [lo0, hi) as group steps: each CTA takes its items layer after
+  // layer with no cluster barrier between them, all on the residual as it was at the step's
+  // start. That is exact as long as no layer before changes it: an item that writes (output)
+  // or one after the step's first layer that would change its state (a key firing, a decay)
+  // ends the CTA's walk after that layer and posts key 2 layer + (0 pending | 1 wrote) to every
+  // CTA's shared minimum; the others stop before any later layer. After the barrier, with J
+  // the minimum's layer: the window shifts of the layers after J (and of J's pending items) are
+  // undone from the log; then either J again with only its pending items (as the first layer
+  // of the next group step) or J's out_proj rows (the fix-up) and on from J + 1.
+  int gp = 0;  // group steps so far (the key's parity)
+  auto group_run = [&](const int lo0, const int hi, const int i) {
+    int lo = lo0, rs_mask = 0, held_out = 0;
+    bool resume = false;
+    if (x_new) {
+      r_x = norm_factor(P, block_ssq(sm, sm.x));
+      x_new = false;
+    }
+    while (lo < hi) {
+      const int gpar = gp & 1;
+      if (t == 0) sm.gkey[gpar ^ 1] = 0x7fffffff;  // the next step's (nobody posts it before
+      restage(lo);                                 // this step's barrier)
+      int nlog = 0, sL = -1, pend = 0, outL = 0;
+      for (int L = lo; L < hi; L++) {
+        if (L > lo &&
+            __syncthreads_or(t == 0 && *reinterpret_cast<volatile int*>(&sm.gkey[gpar]) < 2 * L))
+          break;
+        const lxb_layer& ly = sm.layers[L];
+        cur_layer = L;
+        const unsigned char* B = take(i);
+        PROF(PR_WAIT);
+        const lxb_bhdr bh = B ? *reinterpret_cast<const lxb_bhdr*>(B) : lxb_bhdr{};
+        float* rec = reinterpret_cast<float*>(sm.sptr[L][0]);
+        uint16_t* conv = reinterpret_cast<uint16_t*>(sm.sptr[L][1]);
+        uint32_t* bm = run.bitmaps + ((size_t)s * P.n_layers + L) * LXB_NV * 8;
+        const float r = r_x;
+        const uint16_t* w_in = (B && bh.ln_in >= 0)
+                                   ? reinterpret_cast<const uint16_t*>(B + bh.ln_in)
+                                   : P.u16 + ly.ln_in;
+        {  // this step's GDN input row into the ring (each CTA its block; rank 0 the factor)
+          const size_t slot = ((size_t)s * P.n_layers + L) * 4 + (i & 3);
+          uint16_t* rg = run.ring + slot * H + rank * P.blk;
+          for (int k = t; k < P.blk / 2; k += NT) {
+            const float* xv = sm.x + rank * P.blk + 2 * k;
+            reinterpret_cast<uint32_t*>(rg)[k] =
+                (uint32_t)lx_rb(xv[0]) | ((uint32_t)lx_rb(xv[1]) << 16);
+          }
+          if (rank == 0 && t == 0) run.ring_r[slot] = r;
+        }
+        issue_next(stp);
+        PROF(PR_NORM);
+        int st_any = 0;
+        if (B) {
+          const lxb_bhdr* bhp = reinterpret_cast<const lxb_bhdr*>(B);  // (dynamic index: smem)
+          for (int k = 0; k < bh.n_items; k++) {
+            if (resume && L == lo && !((rs_mask >> k) & 1)) continue;  // done already
+            const lxb_bitem bi = *reinterpret_cast<const lxb_bitem*>(B + bhp->item[k]);
+            const bool spec = L > lo;
+            if (spec && nlog + bi.n_eager > LXB_LOGMAX) {  // no room to undo: k.. wait for J = L
+              for (int kk = k; kk < bh.n_items; kk++) pend |= 1 << kk;
+              st_any |= 2;
+              break;
+            }
+            const int stt = gdn_item(P, run, sm, B, bi, rec, conv, bm, s, L, i, w_in, r,
+                                     spec ? sm.lmeta + nlog : nullptr,
+                                     spec ? sm.lold + nlog : nullptr,
+                                     (uint32_t)k << 10 | (uint32_t)(L - lo) << 12);
+            if (spec && stt != ITEM_UNTOUCHED) nlog += bi.n_eager;
+            if (stt == ITEM_WROTE) st_any |= 1;
+            if (stt >= ITEM_PENDING) {
+              st_any |= 2;
+              pend |= 1 << k;
+            }
+          }
+        }
+        if (resume && L == lo && held_out) st_any |= 1;  // J's outputs from the last step
+        PROF(PR_ITEMS);
+        stp++;
+        if (st_any) {
+          sL = L;
+          outL = st_any & 1;
+          if (t < C)
+            atomicMin(cluster.map_shared_rank(&sm.gkey[gpar], t), 2 * L + ((st_any & 2) ? 0 : 1));
+          break;
+        }
+      }
+      cluster.sync();
+      PROF(PR_SYNC);
+      const int key = *reinterpret_cast<volatile int*>(&sm.gkey[gpar]);
+      gp++;
+      if (key == 0x7fffffff) break;  // every layer of the run done, none wrote
+      const int J = key >> 1;
+      for (int e = t; e < nlog; e += NT) {  // undo: the layers after J, J's pending items
+        const uint32_t m = sm.lmeta[e];
+        const int lay = lo + (int)(m >> 12), kk = (int)(m >> 10) & 3;
+        if (lay > J || (lay == J && sL == J && ((pend >> kk) & 1))) sm.win[m & 1023u] = sm.lold[e];
+      }
+      __syncthreads();
+      if (!(key & 1)) {  // J has pending items: J again first, with only those
+        resume = true;
+        rs_mask = sL == J ? pend : 0;
+        held_out = sL == J && outL;
+        lo = J;
+      } else {  // J wrote: its out_proj rows into the residual, then on from J + 1
+        pc[PR_FIXUPS]++;
+        ph++;
+        const lxb_layer& lyJ = sm.layers[J];
+        const lxb_owner ow = P.owners[lyJ.owner0 + rank];
+        out_owner(P, sm, lyJ, ow, rank, sm.own[ph & 1], cluster);
+        __syncthreads();
+        push_rows(P, sm, sm.own[ph & 1], ph & 1, rank, cluster);
+        cluster.sync();
+        r_x = take_rows_norm(P, sm, ph & 1);
+        x_new = false;
+        ph++;
+        PROF(PR_FIXUP);
+        resume = false;
+        rs_mask = 0;
+        held_out = 0;
+        lo = J + 1;
+      }
+    }
+  };
   load_embed(run, P, sm, sm.tok);
   for (int i = 0; i < run.n_tokens; i++) {
+    cur_tok = i;
     if (rank == 0 && t == 0 && run.inputs) run.inputs[(size_t)s * run.n_tokens + i] = sm.tok;
-    for (int L = 0; L < P.n_layers; L++) {
+    for (int L = 0; L < P.n_layers;) {
       const lxb_layer& ly = sm.layers[L];
+#if LXB_GROUPS
+      if (P.nbuf == 2 && ly.has_gdn && !ly.has_mlp && L + 1 < P.n_layers &&
+          sm.layers[L + 1].has_gdn && !sm.layers[L + 1].has_mlp) {
+        int hi = L + 1;
+        while (hi < P.n_layers && sm.layers[hi].has_gdn && !sm.layers[hi].has_mlp) hi++;
+        group_run(L, hi, i);
+        L = hi;
+        continue;
+      }
+#endif
       cur_layer = L;
       const unsigned char* B = take(i);
       PROF(PR_WAIT);
@@ -1425,7 +1603,8 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         const lxb_bhdr* bhp = reinterpret_cast<const lxb_bhdr*>(B);  // (dynamic index: in smem)
         for (int k = 0; k < bh.n_items; k++) {
           const lxb_bitem bi = *reinterpret_cast<const lxb_bitem*>(B + bhp->item[k]);
-          wrote |= gdn_item(P, run, sm, B, bi, rec, conv, bm, s, L, i, w_in, r);
+          wrote |= gdn_item(P, run, sm, B, bi, rec, conv, bm, s, L, i, w_in, r, nullptr, nullptr,
+                            0) == ITEM_WROTE;
         }
       }
       if (wrote && t < C) *cluster.map_shared_rank(&sm.wflag[ph & 1], t) = 1;
@@ -1474,6 +1653,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         PROF(PR_PULL);
       }
       stp++;
+      L++;
     }
     // the output head: every CTA its rows, then the first maximum over the cluster
     {
@@ -1797,6 +1977,7 @@ int validate_blobs(const View& v, int C) {
           const lxb_bchan& ch = reinterpret_cast<const lxb_bchan*>(B + bi.eager)[e];
           if (ch.slot >= 2 * LXB_KD || ch.conv_ch >= LXB_CONV || !blob_ent(B, nb, ch.ent, ch.n, H))
             return LXB_E_IMAGE;
+          if (ch.win == LXB_NOWIN && !(bi.flags & LXB_IT_NONRES)) return LXB_E_IMAGE;
           if (ch.win != LXB_NOWIN) {  // a resident window: the map must name this channel
             if (ch.win >= (uint32_t)widx[2 * c + 1]) return LXB_E_IMAGE;
             const int32_t* wp = wmap + 2 * ((int64_t)widx[2 * c] + ch.win);

@@ -39,6 +39,8 @@
 // item flags
 #define LXB_IT_DECAYS 1  // some value head's g may be nonzero
 #define LXB_IT_OUT 2     // the key head's value dims have out_proj entries
+#define LXB_IT_NONRES 4  // some query/key window is not resident in shared memory (its CTA's
+                         // window table was full): the item never runs speculatively
 
 enum {
   LXB_SEC_LAYERS = 0,  // lxb_layer[n_layers]

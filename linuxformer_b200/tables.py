@@ -29,7 +29,7 @@ VERSION = 7
 NSLOT, NOSLOT = 1536, 0xFFFF
 ITEMSLOTS, MAXDENSE, MAXUNITS, MAXWIN = 4, 32, 2048, 1024
 HEADSLICES = 32
-IT_DECAYS, IT_OUT = 1, 2
+IT_DECAYS, IT_OUT, IT_NONRES = 1, 2, 4
 SEC = ("layers", "items", "chans", "ent", "units", "owners", "i32", "u16", "headcta", "hcodes",
        "blobs", "blobidx", "winmap", "winidx")
 
@@ -280,6 +280,9 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
                     winmap[c] += [(L, int(x)) for x in bc["conv_ch"]]
                 else:
                     bc["win"] = 0xFFFFFFFF
+                    if len(bc):
+                        items[i]["flags"] |= IT_NONRES
+                        bi["flags"] |= IT_NONRES
                 bi["z"] = -1
                 if pt["z"] is not None:
                     zs = pt["z"]
