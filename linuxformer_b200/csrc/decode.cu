@@ -158,10 +158,10 @@ struct __align__(16) Smem {
     struct {
       alignas(16) uint16_t xb[3][H];  // a key's firing: the 3 earlier steps' input norms
     } lf;
-  };
+    float htg[LXB_MAXDENSE / 4][256];  // head: per group of 4 dense columns, each code's sum
+  };  // (each member lives within one step: an item, an out_proj step or the head)
   float hbuf[LXB_MAXUNITS];        // MLP unit outputs
   float prod[LXB_MAXPROD];         // MLP gate/up products, in the units' entry order
-  float htg[LXB_MAXDENSE / 4][256];  // head: per group of 4 dense columns, each code's sum
   float bestv;
   int besti;
   int tok;
@@ -472,16 +472,18 @@ __device__ __forceinline__ float xn_at(const Smem& sm, const uint16_t* w, float 
 // One eager (query/key) channel: in_proj_qkv row over the staged entries (the input norm taken
 // per column), conv window shift (resident in shared memory, or in global), conv output with
 // silu in bf16. pr: the row's products, computed beforehand by the whole block (then only the
-// sequential sum is this thread's), or null (the products here).
+// sequential sum is this thread's), or null (the products here). zin: every product of the item
+// is +0 or -0 (most steps: the residual is sparse), so the sequential sum from +0 is +0.
 __device__ __forceinline__ float eager_channel(Smem& sm, const unsigned char* B, const uint4 a,
                                                const uint4 b, uint16_t* conv, const uint16_t* w,
-                                               float r, const float* pr) {
+                                               float r, const float* pr, bool zin) {
   const uint32_t* e = reinterpret_cast<const uint32_t*>(B + a.x);
   const int ne = (int)(a.y & 0xffffu);
   uint2* wp = b.y != LXB_NOWIN ? &sm.win[b.y] : reinterpret_cast<uint2*>(conv + (size_t)a.z * 4);
   const uint2 win = *wp;
   float ps = 0.0f;
-  if (pr) {  // in batches of 8, the last one partial: every batch's loads in flight together
+  if (zin) {
+  } else if (pr) {  // in batches of 8, the last one partial: every batch's loads in flight together
     for (int k = 0; k < ne; k += 8) {
       float v[8];
 #pragma unroll
@@ -521,7 +523,7 @@ __device__ __forceinline__ float xrow_dot(const Smem& sm, const uint32_t* e, int
 // many query/key channels: a dense q | k buffer, then compaction by warps 0 and 1
 __device__ __forceinline__ void eager_block(Smem& sm, const unsigned char* B, const lxb_bitem& bi,
                                          uint16_t* conv, const uint16_t* w_in, float r_in,
-                                         const float* pre_base, uint32_t e_first) {
+                                         const float* pre_base, uint32_t e_first, bool zin) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const uint4* ch = reinterpret_cast<const uint4*>(B + bi.eager);
   for (int k = t; k < 2 * KD; k += NT) sm.buf[k] = 0.0f;
@@ -529,7 +531,7 @@ __device__ __forceinline__ void eager_block(Smem& sm, const unsigned char* B, co
   for (int c = t; c < bi.n_eager; c += NT) {
     const uint4 a = ch[2 * c], b = ch[2 * c + 1];
     sm.buf[a.y >> 16] = eager_channel(sm, B, a, b, conv, w_in, r_in,
-                                      pre_base ? pre_base + (a.x - e_first) / 4u : nullptr);
+                                      pre_base ? pre_base + (a.x - e_first) / 4u : nullptr, zin);
   }
   __syncthreads();
   if (warp < 2) {
@@ -742,18 +744,23 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
   if (spec && (bi.n_eager > 32 || (bi.flags & LXB_IT_NONRES))) return ITEM_UNTOUCHED;
   const uint4* ch = reinterpret_cast<const uint4*>(B + bi.eager);
   // the eager rows' products, all entries at once over the block (the entries of the item's
-  // eager channels are contiguous in the blob, in channel order)
+  // eager channels are contiguous in the blob, in channel order); whether any is nonzero comes
+  // with the barrier after them
   uint32_t e_first = 0;
-  bool pre = false;
+  bool pre = false, zin = false;
   if (bi.n_eager > 0) {
     e_first = ch[0].x;
     const uint4 al = ch[2 * (bi.n_eager - 1)];
     const int ntot = (int)((al.x + 4u * (al.y & 0xffffu) - e_first) / 4u);
     if (ntot <= LXB_MAXPROD) {
       const uint32_t* E = reinterpret_cast<const uint32_t*>(B + e_first);
-      for (int k = t; k < ntot; k += NT)
-        sm.prod[k] = lx_mul(xn_at(sm, w_in, r_in, E[k] & 0xffffu), lx_f((uint16_t)(E[k] >> 16)));
-      __syncthreads();
+      bool nz = false;
+      for (int k = t; k < ntot; k += NT) {
+        const float p = lx_mul(xn_at(sm, w_in, r_in, E[k] & 0xffffu), lx_f((uint16_t)(E[k] >> 16)));
+        sm.prod[k] = p;
+        nz |= p != 0.0f;
+      }
+      zin = !__syncthreads_or(nz);
       pre = true;
     }
   }
@@ -769,7 +776,7 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
           lold[lane] = sm.win[b.y];
         }
         v = eager_channel(sm, B, a, b, conv, w_in, r_in,
-                          pre ? sm.prod + (a.x - e_first) / 4u : nullptr);
+                          pre ? sm.prod + (a.x - e_first) / 4u : nullptr, zin);
         slot = (int)(a.y >> 16);
       }
       const bool nz = lane < bi.n_eager && v != 0.0f;
@@ -797,7 +804,7 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
       }
     }
   } else {
-    eager_block(sm, B, bi, conv, w_in, r_in, pre ? sm.prod : nullptr, e_first);
+    eager_block(sm, B, bi, conv, w_in, r_in, pre ? sm.prod : nullptr, e_first, zin);
     if (t == 0) sm.vhlay[bi.slot] = L;
   }
   // warp 1: g, only for a head that can decay (for the others softplus underflows to zero
