@@ -913,7 +913,7 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
 // The MLP over this CTA's rows: own[row] = bf16(x + bf16(sum_u h_u w_d)), h_u re-evaluated here;
 // the units and entries are in the staged blob (m: its MLP part)
 __device__ void mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, const lxb_bmlp& m,
-                          int rank, float* own) {
+                          float* own) {
   const int t = threadIdx.x;
   const lxb_bunit* units = reinterpret_cast<const lxb_bunit*>(B + m.units);
   // the gate and up entries of all units are contiguous in the blob: their products first, all
@@ -924,6 +924,7 @@ __device__ void mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, const 
   const uint32_t* ent = reinterpret_cast<const uint32_t*>(B + g0);
   float* prod = sm.prod;
   if (ne <= LXB_MAXPROD) {
+#pragma unroll 4
     for (int e = t; e < ne; e += NT)
       prod[e] = lx_mul(sm.xm[ent[e] & 0xffffu], lx_f((uint16_t)(ent[e] >> 16)));
     __syncthreads();
@@ -932,10 +933,23 @@ __device__ void mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, const 
     const lxb_bunit un = units[u];
     float gs = 0.0f, us = 0.0f;
     if (ne <= LXB_MAXPROD) {
+      // both sums in order, 8 products of each loaded at a time (the two chains interleave)
       const float* pg = prod + (un.g - g0) / 4;
       const float* pu = prod + (un.u - g0) / 4;
-      for (int k = 0; k < un.ng; k++) gs = lx_add(gs, pg[k]);
-      for (int k = 0; k < un.nu; k++) us = lx_add(us, pu[k]);
+      const int nmax = max((int)un.ng, (int)un.nu);
+      for (int k = 0; k < nmax; k += 8) {
+        float vg[8], vu[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          vg[q] = k + q < un.ng ? pg[k + q] : 0.0f;
+          vu[q] = k + q < un.nu ? pu[k + q] : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          if (k + q < un.ng) gs = lx_add(gs, vg[q]);
+          if (k + q < un.nu) us = lx_add(us, vu[q]);
+        }
+      }
     } else {
       const uint32_t* ge = reinterpret_cast<const uint32_t*>(B + un.g);
       const uint32_t* ue = reinterpret_cast<const uint32_t*>(B + un.u);
@@ -949,29 +963,37 @@ __device__ void mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, const 
     sm.hbuf[u] = lx_rbf(lx_mul(act, uu));
   }
   __syncthreads();
-  const int r0 = rank * P.blk;
+  const int r0 = m.r0;
   const int32_t* rp = reinterpret_cast<const int32_t*>(B + m.down_ptr);
   const uint32_t* de = reinterpret_cast<const uint32_t*>(B + m.down_ent);
-  for (int k = t; k < P.blk; k += NT) {
+  for (int k = t; k < m.nr; k += NT) {
     const float xv = sm.x[r0 + k];
     float res = xv;
     float sd = 0.0f;
     bool any = false;
-    for (int e = rp[k]; e < rp[k + 1]; e++) {
-      const float hv = sm.hbuf[de[e] & 0xffffu];
-      if (hv != 0.0f) {
-        sd = lx_add(sd, lx_mul(hv, lx_f((uint16_t)(de[e] >> 16))));
-        any = true;
-      }
+    const int e1 = rp[k + 1];
+    for (int e = rp[k]; e < e1; e += 8) {  // 8 entries' loads in flight, then the sum in order
+      uint32_t w[8];
+      float hv[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) w[q] = e + q < e1 ? de[e + q] : 0u;
+#pragma unroll
+      for (int q = 0; q < 8; q++) hv[q] = e + q < e1 ? sm.hbuf[w[q] & 0xffffu] : 0.0f;
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+        if (hv[q] != 0.0f) {  // (0 past the row's end)
+          sd = lx_add(sd, lx_mul(hv[q], lx_f((uint16_t)(w[q] >> 16))));
+          any = true;
+        }
     }
     if (any) res = lx_rbf(lx_add(xv, lx_rbf(sd)));
     own[k] = res;
   }
 }
 
-// every owned row unchanged (a step whose owners have no MLP work)
-__device__ void copy_owner(const Dev& P, Smem& sm, int rank, float* own) {
-  for (int k = threadIdx.x; k < P.blk; k += NT) own[k] = sm.x[rank * P.blk + k];
+// every owned MLP row [r0, r0 + nr) unchanged (no staged MLP tables)
+__device__ void copy_owner(Smem& sm, int r0, int nr, float* own) {
+  for (int k = threadIdx.x; k < nr; k += NT) own[k] = sm.x[r0 + k];
 }
 
 // out_proj over this CTA's rows, from the layer's items' outputs (gathered over DSMEM)
@@ -1035,9 +1057,9 @@ __device__ void out_owner(const Dev& P, Smem& sm, const lxb_layer& ly, const lxb
 // The owner's rows into every CTA's push buffer of this parity, as bf16 (the residual's values
 // are bf16; 16-byte DSMEM stores before the step's cluster barrier, which makes them visible);
 // own must be complete (a block barrier after it was written).
-__device__ void push_rows(const Dev& P, Smem& sm, const float* own, int par, int rank,
+__device__ void push_rows(const Dev& P, Smem& sm, const float* own, int par, int r0, int nr,
                           cg::cluster_group& cluster) {
-  const int per = P.blk / 8;  // uint4 (8 rows) per owner
+  const int per = nr / 8;  // uint4 (8 rows) per destination
   for (int k = threadIdx.x; k < per * P.C; k += NT) {
     const int d = k / per, q = k % per;
     const float* o = own + 8 * q;
@@ -1045,35 +1067,28 @@ __device__ void push_rows(const Dev& P, Smem& sm, const float* own, int par, int
                                (uint32_t)lx_rb(o[2]) | ((uint32_t)lx_rb(o[3]) << 16),
                                (uint32_t)lx_rb(o[4]) | ((uint32_t)lx_rb(o[5]) << 16),
                                (uint32_t)lx_rb(o[6]) | ((uint32_t)lx_rb(o[7]) << 16));
-    uint4* dst = reinterpret_cast<uint4*>(cluster.map_shared_rank(&sm.xin[par][rank * P.blk], d));
+    uint4* dst = reinterpret_cast<uint4*>(cluster.map_shared_rank(&sm.xin[par][r0], d));
     dst[q] = v;
   }
 }
 
-// the replica from the push buffer (after the cluster barrier)
-__device__ void take_rows(Smem& sm, int par) {
-  for (int k = threadIdx.x; k < H / 8; k += NT) {
-    const uint4 v = reinterpret_cast<const uint4*>(sm.xin[par])[k];
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      sm.x[8 * k + 2 * q] = lx_f((uint16_t)(w[q] & 0xffffu));
-      sm.x[8 * k + 2 * q + 1] = lx_f((uint16_t)(w[q] >> 16));
-    }
-  }
-  __syncthreads();
-}
-
-// take_rows with the residual's sum of squares in the canonical order on the way (lane t: the
+// The replica's rows [lo, hi) from the push buffer (after the cluster barrier; the others did not
+// change), with the residual's sum of squares in the canonical order on the way (lane t: the
 // squares of x[t + 512 i], i = 0..4, in order, then the two butterflies): the norm factor
-__device__ float take_rows_norm(const Dev& P, Smem& sm, int par) {
+__device__ float take_rows_norm(const Dev& P, Smem& sm, int par, int lo = 0, int hi = H) {
   static_assert(H == 5 * NT, "five residual rows per thread");
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   float s = 0.0f;
 #pragma unroll
   for (int i = 0; i < 5; i++) {
-    const float v = lx_f(sm.xin[par][t + NT * i]);
-    sm.x[t + NT * i] = v;
+    const int c = t + NT * i;
+    float v;
+    if (c >= lo && c < hi) {
+      v = lx_f(sm.xin[par][c]);
+      sm.x[c] = v;
+    } else {
+      v = sm.x[c];
+    }
     s = i == 0 ? lx_mul(v, v) : lx_add(s, lx_mul(v, v));
   }
   s = warp_xor_sum(s);
@@ -1539,7 +1554,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         const lxb_owner ow = P.owners[lyJ.owner0 + rank];
         out_owner(P, sm, lyJ, ow, rank, sm.own[ph & 1], cluster);
         __syncthreads();
-        push_rows(P, sm, sm.own[ph & 1], ph & 1, rank, cluster);
+        push_rows(P, sm, sm.own[ph & 1], ph & 1, rank * P.blk, P.blk, cluster);
         cluster.sync();
         r_x = take_rows_norm(P, sm, ph & 1);
         x_new = false;
@@ -1588,6 +1603,12 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       const bool mlp = ly.has_mlp && B && bh.mlp >= 0;
       lxb_bmlp mh{};
       if (mlp) mh = *reinterpret_cast<const lxb_bmlp*>(B + bh.mlp);
+      int mr0 = mh.r0, mnr = mh.nr;  // this CTA's MLP rows
+      if (ly.has_mlp && !mlp) {      // (no staged tables: the rows stay as they are)
+        const lxb_owner o = P.owners[ly.owner0 + rank];
+        mr0 = o.mr0;
+        mnr = o.mr1 - o.mr0;
+      }
       if (ly.has_gdn) {
         // this step's GDN input row into the ring (each CTA its block; rank 0 the factor)
         const size_t slot = ((size_t)s * P.n_layers + L) * 4 + (i & 3);
@@ -1617,10 +1638,10 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       if (wrote && t < C) *cluster.map_shared_rank(&sm.wflag[ph & 1], t) = 1;
       PROF(PR_ITEMS);
       if (ly.has_mlp) {
-        if (mlp) mlp_owner(P, sm, B, mh, rank, sm.own[ph & 1]);
-        else copy_owner(P, sm, rank, sm.own[ph & 1]);
+        if (mlp) mlp_owner(P, sm, B, mh, sm.own[ph & 1]);
+        else copy_owner(sm, mr0, mnr, sm.own[ph & 1]);
         __syncthreads();
-        push_rows(P, sm, sm.own[ph & 1], ph & 1, rank, cluster);
+        push_rows(P, sm, sm.own[ph & 1], ph & 1, mr0, mnr, cluster);
       }
       PROF(PR_MLP);
       cluster.sync();
@@ -1635,7 +1656,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         const lxb_owner ow = P.owners[ly.owner0 + rank];
         out_owner(P, sm, ly, ow, rank, sm.own[ph & 1], cluster);
         __syncthreads();
-        push_rows(P, sm, sm.own[ph & 1], ph & 1, rank, cluster);
+        push_rows(P, sm, sm.own[ph & 1], ph & 1, rank * P.blk, P.blk, cluster);
         cluster.sync();
         r_x = take_rows_norm(P, sm, ph & 1);
         x_new = false;
@@ -1643,19 +1664,19 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         if (ly.has_mlp) {
           norm_into(sm.xm, sm.x, w_post, r_x);
           __syncthreads();
-          if (mlp) mlp_owner(P, sm, B, mh, rank, sm.own[ph & 1]);
-          else copy_owner(P, sm, rank, sm.own[ph & 1]);
+          if (mlp) mlp_owner(P, sm, B, mh, sm.own[ph & 1]);
+          else copy_owner(sm, mr0, mnr, sm.own[ph & 1]);
           __syncthreads();
-          push_rows(P, sm, sm.own[ph & 1], ph & 1, rank, cluster);
+          push_rows(P, sm, sm.own[ph & 1], ph & 1, mr0, mnr, cluster);
           cluster.sync();
           if (P.nbuf == 1) issue_next(stp);
-          r_x = take_rows_norm(P, sm, ph & 1);
+          r_x = take_rows_norm(P, sm, ph & 1, ly.mrow0, ly.mrow1);
           ph++;
         }
         PROF(PR_FIXUP);
       } else {
         if (P.nbuf == 1) issue_next(stp);
-        if (ly.has_mlp) r_x = take_rows_norm(P, sm, ph & 1);
+        if (ly.has_mlp) r_x = take_rows_norm(P, sm, ph & 1, ly.mrow0, ly.mrow1);
         ph++;
         PROF(PR_PULL);
       }
@@ -1932,7 +1953,7 @@ bool blob_ent(const unsigned char* B, int64_t bytes, int64_t off, int64_t n, uin
 
 int validate_blobs(const View& v, int C) {
   const lxb_image_header* h = v.h;
-  const int nl = h->n_layers, blk = H / C;
+  const int nl = h->n_layers;
   if (v.n(LXB_SEC_BLOBIDX) != (int64_t)(nl + 1) * C || h->blob_max < (int)sizeof(lxb_bhdr) ||
       h->blob_max % 16)
     return LXB_E_IMAGE;
@@ -2010,9 +2031,11 @@ int validate_blobs(const View& v, int C) {
       if (ly.has_mlp) {
         if (!blob_rng(bh->mlp, sizeof(lxb_bmlp), nb, 16)) return LXB_E_IMAGE;
         const lxb_bmlp& m = *reinterpret_cast<const lxb_bmlp*>(B + bh->mlp);
-        if (m.n_units < 0 || m.n_units > LXB_MAXUNITS ||
+        const lxb_owner& ow = v.sec<lxb_owner>(LXB_SEC_OWNERS)[L * C + c];  // (checked)
+        if (m.n_units < 0 || m.n_units > LXB_MAXUNITS || m.r0 != ow.mr0 ||
+            m.nr != ow.mr1 - ow.mr0 ||
             !blob_rng(m.units, (int64_t)m.n_units * sizeof(lxb_bunit), nb, 16) ||
-            !blob_rng(m.down_ptr, 4 * (int64_t)(blk + 1), nb, 16))
+            !blob_rng(m.down_ptr, 4 * (int64_t)(m.nr + 1), nb, 16))
           return LXB_E_IMAGE;
         const lxb_bunit* un = reinterpret_cast<const lxb_bunit*>(B + m.units);
         for (int u = 0; u < m.n_units; u++)
@@ -2027,9 +2050,9 @@ int validate_blobs(const View& v, int C) {
         }
         const int32_t* rp = reinterpret_cast<const int32_t*>(B + m.down_ptr);
         if (rp[0] != 0) return LXB_E_IMAGE;
-        for (int k = 0; k < blk; k++)
+        for (int k = 0; k < m.nr; k++)
           if (rp[k + 1] < rp[k]) return LXB_E_IMAGE;
-        if (!blob_ent(B, nb, m.down_ent, rp[blk], (uint32_t)m.n_units)) return LXB_E_IMAGE;
+        if (!blob_ent(B, nb, m.down_ent, rp[m.nr], (uint32_t)m.n_units)) return LXB_E_IMAGE;
       }
     }
   }
@@ -2065,7 +2088,6 @@ int validate(const View& v, int cluster) {
   const lxb_item* items = v.sec<lxb_item>(LXB_SEC_ITEMS);
   const lxb_chan* chans = v.sec<lxb_chan>(LXB_SEC_CHANS);
   const lxb_owner* owners = v.sec<lxb_owner>(LXB_SEC_OWNERS);
-  const lxb_unit* units = v.sec<lxb_unit>(LXB_SEC_UNITS);
   for (int L = 0; L < h->n_layers; L++) {
     const lxb_layer& ly = layers[L];
     if (!u16_range(v, ly.ln_in, H) || !u16_range(v, ly.ln_post, H)) return LXB_E_IMAGE;
@@ -2106,14 +2128,11 @@ int validate(const View& v, int cluster) {
     }
     for (int c = 0; c < C; c++) {
       const lxb_owner& ow = owners[L * C + c];
-      if (ow.unit0 < 0 || ow.n_units < 0 || ow.n_units > LXB_MAXUNITS ||
-          (int64_t)ow.unit0 + ow.n_units > v.n(LXB_SEC_UNITS))
+      // the MLP row ranges: 8-row aligned, at most BLKMAX rows, tiling [mrow0, mrow1) in order
+      if (ow.mr0 < 0 || ow.mr1 < ow.mr0 || ow.mr1 > H || (ow.mr0 & 7) || (ow.mr1 & 7) ||
+          ow.mr1 - ow.mr0 > BLKMAX || ow.mr0 != (c ? owners[L * C + c - 1].mr1 : ly.mrow0) ||
+          (c == C - 1 && ow.mr1 != ly.mrow1) || (!ly.has_mlp && ow.mr1 != ow.mr0))
         return LXB_E_IMAGE;
-      for (int u = 0; u < ow.n_units; u++) {
-        const lxb_unit& un = units[ow.unit0 + u];
-        if (!ent_idx(v, un.g, un.ng, H) || !ent_idx(v, un.u, un.nu, H)) return LXB_E_IMAGE;
-      }
-      if (ow.mrow >= 0 && !rowptr_ok(v, ow.mrow, blk, (uint32_t)ow.n_units)) return LXB_E_IMAGE;
       if (ow.orow >= 0 && !rowptr_ok(v, ow.orow, blk, LXB_NV * LXB_VD)) return LXB_E_IMAGE;
     }
   }

@@ -15,7 +15,7 @@
 #include <stdint.h>
 
 #define LXB_MAGIC 0x50425a4cu  // "LZBP"
-#define LXB_IMAGE_VERSION 7
+#define LXB_IMAGE_VERSION 8
 
 #define LXB_H 2560
 #define LXB_KD 256
@@ -91,7 +91,9 @@ typedef struct {
   int32_t owner0;          // owners[owner0 + rank]
   int32_t itemof;          // i32 pool offset: item index of key head kh (16 entries, -1 none)
   int32_t decays;          // some item of the layer decays (its bitmaps are kept)
-  int32_t pad[3];
+  int32_t mrow0, mrow1;    // the rows the MLP can change, [mrow0, mrow1): the owners' MLP row
+                           // ranges tile it in rank order (both 0 without an MLP)
+  int32_t pad;
 } lxb_layer;  // 48 bytes
 
 typedef struct {
@@ -124,9 +126,9 @@ typedef struct {
 } lxb_unit;  // 16 bytes
 
 typedef struct {
-  int32_t unit0, n_units;  // units[unit0, unit0 + n_units): every unit with a down weight here
-  int32_t mrow;            // i32 pool: blk + 1 entry pointers of the owned rows' down_proj
-                           // entries (local unit index | bf16 << 16), or -1
+  int32_t mr0, mr1;        // the MLP rows this CTA owns, [mr0, mr1): multiples of 8, at most
+                           // H / LXB_MINC rows (the out_proj rows are rank * blk .. + blk)
+  int32_t pad;
   int32_t orow;            // i32 pool: blk + 1 entry pointers of the owned rows' out_proj
                            // entries (value dim | bf16 << 16), or -1
 } lxb_owner;  // 16 bytes
@@ -179,9 +181,11 @@ typedef struct {
 
 typedef struct {
   int32_t n_units, units;  // n_units lxb_bunit at offset units
-  int32_t down_ptr;        // int32[blk + 1]: the owned rows' entries (indices into down_ent)
+  int32_t down_ptr;        // int32[nr + 1]: the owned rows' entries (indices into down_ent)
   int32_t down_ent;        // uint32 entries: local unit | bf16 << 16
-} lxb_bmlp;  // 16 bytes
+  int32_t r0, nr;          // the owned MLP rows [r0, r0 + nr): the owner's mr0, mr1 - mr0
+  int32_t pad[2];
+} lxb_bmlp;  // 32 bytes
 
 typedef struct {
   int32_t g, u;            // byte offsets of the gate / up entries
@@ -192,7 +196,7 @@ typedef struct {
 #ifdef __cplusplus
 static_assert(sizeof(lxb_bhdr) == 64 && sizeof(lxb_bitem) == 64 && sizeof(lxb_bchan) == 32,
               "blob layout");
-static_assert(sizeof(lxb_bmlp) == 16 && sizeof(lxb_bunit) == 16 && sizeof(lxb_blobref) == 16,
+static_assert(sizeof(lxb_bmlp) == 32 && sizeof(lxb_bunit) == 16 && sizeof(lxb_blobref) == 16,
               "blob layout");
 static_assert(sizeof(lxb_image_header) == 440, "lxb_image_header layout");
 static_assert(sizeof(lxb_layer) == 48 && sizeof(lxb_item) == 48, "layer/item layout");

@@ -11,10 +11,12 @@ tables, per-CTA blobs and a phase schedule, lx/lx/mega.py:199-504). What is kept
 - the head: the columns nonzero in every row (at most 32, at most 4 distinct values) as 2-bit
   codes, the rest as sparse rows (mega.py:354-395).
 
-What differs: the layout is for a cluster of C CTAs per stream. Residual rows are owned in
-blocks of 2560 / C; each owner gets the down_proj and out_proj entries of its rows in CSR order
-(so every sum is taken by one thread, in column order) and the list of MLP units those rows
-need. Items are spread over the CTAs, at most LXB_ITEMSLOTS per CTA per layer.
+What differs: the layout is for a cluster of C CTAs per stream. Each owner gets the down_proj and
+out_proj entries of its residual rows in CSR order (so every sum is taken by one thread, in
+column order) and the list of MLP units those rows need. The out_proj rows are owned in blocks
+of 2560 / C; an MLP layer's rows are split per layer in contiguous ranges balanced by their work
+(only the rows the MLP can change, around the CTAs' items). Items are spread over the CTAs, at
+most LXB_ITEMSLOTS per CTA per layer.
 """
 
 from __future__ import annotations
@@ -25,24 +27,28 @@ from . import chip as C
 from .chip import _ranges
 
 MAGIC = 0x50425A4C
-VERSION = 7
+VERSION = 8
 NSLOT, NOSLOT = 1536, 0xFFFF
 ITEMSLOTS, MAXDENSE, MAXUNITS, MAXWIN = 4, 32, 2048, 1024
+MINC = 4  # the smallest cluster: an owner holds at most H / MINC rows
+# the MLP row split's cost model, in gate/up products: an item on the CTA (the step's average),
+# and each owned row (its down sum and its push)
+ITEM_COST, ROW_COST = 1000, 2
 HEADSLICES = 32
 IT_DECAYS, IT_OUT, IT_NONRES = 1, 2, 4
 SEC = ("layers", "items", "chans", "ent", "units", "owners", "i32", "u16", "headcta", "hcodes",
        "blobs", "blobidx", "winmap", "winidx")
 
 LAYER = np.dtype([(n, "<i4") for n in ("has_gdn", "has_mlp", "ln_in", "ln_post", "item0",
-                                       "n_items", "owner0", "itemof", "decays", "p0", "p1",
-                                       "p2")])
+                                       "n_items", "owner0", "itemof", "decays", "mrow0",
+                                       "mrow1", "p2")])
 ITEM = np.dtype([(n, "<i4") for n in ("layer", "kh", "cta", "slot", "ch0", "n_ch", "rows",
                                       "params", "flags", "n_eager", "n_vneed", "tapu")])
 CHAN = np.dtype([("ent", "<u4"), ("n", "<u2"), ("slot", "<u2"), ("conv_ch", "<u4"),
                  ("t01", "<u4"), ("t23", "<u4"), ("tapmask", "<u4"), ("p1", "<u4"),
                  ("p2", "<u4")])
 UNIT = np.dtype([("g", "<u4"), ("u", "<u4"), ("ng", "<u2"), ("nu", "<u2"), ("pad", "<u4")])
-OWNER = np.dtype([("unit0", "<i4"), ("n_units", "<i4"), ("mrow", "<i4"), ("orow", "<i4")])
+OWNER = np.dtype([("mr0", "<i4"), ("mr1", "<i4"), ("pad", "<i4"), ("orow", "<i4")])
 HEADCTA = np.dtype([("r0", "<i4"), ("r1", "<i4"), ("rowptr", "<i4"), ("pad", "<i4")])
 HEADER = np.dtype([("magic", "<u4"), ("version", "<u4"), ("n_layers", "<i4"), ("cluster", "<i4"),
                    ("n_vocab", "<i4"), ("hidden", "<i4"), ("n_items", "<i4"), ("n_dense", "<i4"),
@@ -57,12 +63,13 @@ BITEM = np.dtype([(n, "<i4") for n in ("item", "n_eager", "eager", "rows", "prm"
                                        "flags", "z")] + [("pad", "<i4", (7,))])
 BCHAN = np.dtype([("ent", "<i4"), ("n", "<u2"), ("slot", "<u2"), ("conv_ch", "<u4"),
                   ("t01", "<u4"), ("t23", "<u4"), ("win", "<u4"), ("p1", "<u4"), ("p2", "<u4")])
-BMLP = np.dtype([(n, "<i4") for n in ("n_units", "units", "down_ptr", "down_ent")])
+BMLP = np.dtype([(n, "<i4") for n in ("n_units", "units", "down_ptr", "down_ent", "r0", "nr",
+                                      "p0", "p1")])
 BUNIT = np.dtype([("g", "<i4"), ("u", "<i4"), ("ng", "<u2"), ("nu", "<u2"), ("pad", "<i4")])
 assert LAYER.itemsize == 48 and ITEM.itemsize == 48 and CHAN.itemsize == 32
 assert UNIT.itemsize == 16 and OWNER.itemsize == 16 and HEADCTA.itemsize == 16
 assert HEADER.itemsize == 440 and BLOBREF.itemsize == 16 and BHDR.itemsize == 64
-assert BITEM.itemsize == 64 and BCHAN.itemsize == 32 and BMLP.itemsize == 16
+assert BITEM.itemsize == 64 and BCHAN.itemsize == 32 and BMLP.itemsize == 32
 assert BUNIT.itemsize == 16
 
 
@@ -123,21 +130,57 @@ def _may_decay(layer: C.Layer, vh: np.ndarray) -> np.ndarray:
         (_f32(layer.A_log[vh]) >= -103.98)
 
 
-def _mlp_order(layer: C.Layer, Cn: int, blk: int, L: int) -> np.ndarray:
-    """CTA ranks by ascending MLP work in this layer (ties, and layers without an MLP, rotated
-    by the layer index)."""
-    rot = (np.arange(Cn) - 3 * L) % Cn
+def _cta_order(Cn: int, L: int) -> np.ndarray:
+    """The CTAs a layer's items go to, in order: a rotation by the layer index, so that the
+    ranks without an item change from layer to layer."""
+    return np.argsort((np.arange(Cn) - 3 * L) % Cn, kind="stable")
+
+
+def _mlp_split(layer: C.Layer, live: np.ndarray, base: np.ndarray) -> np.ndarray:
+    """The owners' MLP rows: bounds R[0..Cn] (multiples of 8) with owner c holding [R[c], R[c+1]),
+    the ranges tiling the rows the MLP can change (those with a live unit's down weight, rounded
+    out to 8) in rank order, and the largest of base[c] + the range's cost as small as it can be
+    (cost: the gate/up entries of the rows' units and ROW_COST a row; base: the owner's items).
+    Without an MLP every range is empty."""
+    Cn = len(base)
+    d = layer.down
+    rowid = np.repeat(np.arange(C.H), d.row_nnz())
+    keep = live[d.indices]
+    R = np.zeros(Cn + 1, np.int64)
+    if not keep.any():
+        return R
     g_cnt, u_cnt = layer.gate.row_nnz(), layer.up.row_nnz()
-    live = (g_cnt > 0) & (u_cnt > 0) & (layer.down.transpose().row_nnz() > 0)
-    if not live.any():
-        return np.argsort(rot, kind="stable")
-    cost = np.zeros(Cn, np.int64)
-    for c in range(Cn):
-        sub = layer.down.rows_subset(np.arange(c * blk, (c + 1) * blk))
-        keep = live[sub.indices]
-        need = np.unique(sub.indices[keep])
-        cost[c] = int(g_cnt[need].sum() + u_cnt[need].sum() + keep.sum())
-    return np.lexsort((rot, cost))
+    u = d.indices[keep]
+    rc = np.bincount(rowid[keep], weights=(g_cnt[u] + u_cnt[u]).astype(np.float64),
+                     minlength=C.H).astype(np.int64) + ROW_COST
+    act = np.nonzero(np.bincount(rowid[keep], minlength=C.H))[0]
+    a, b = int(act[0]) & ~7, (int(act[-1]) + 8) & ~7
+    ck = rc[a:b].reshape(-1, 8).sum(1)
+    cap = C.H // MINC // 8  # chunks of 8 rows an owner may hold
+
+    def fit(T):
+        out = np.full(Cn + 1, b, np.int64)
+        out[0], c, cur, n = a, 0, int(base[0]), 0
+        for j, w in enumerate(ck.tolist()):
+            while cur + w > T or n == cap:
+                c += 1
+                if c == Cn:
+                    return None
+                out[c], cur, n = a + 8 * j, int(base[c]), 0
+            cur += w
+            n += 1
+        return out
+
+    lo, hi = 0, int(ck.sum() + base.max())
+    while fit(hi) is None:  # (the row cap alone can leave no split: only if Cn * cap < chunks)
+        hi *= 2
+    while lo < hi:
+        mid = (lo + hi) // 2
+        if fit(mid) is None:
+            lo = mid + 1
+        else:
+            hi = mid
+    return fit(lo)
 
 
 def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
@@ -181,10 +224,8 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
         # the row entries of the whole in_proj_qkv, packed once
         qkv_ent0 = ent.add(_pack(qkv.indices, qkv.data))
         stats["csr_nnz"] += qkv.nnz
-        # the CTAs in order of their MLP work in this layer (gate/up entries of the units their
-        # rows need, down entries): the items go to the lightest first, as a paired step waits
-        # for the CTA that has both; without an MLP, a rotation spreads them over the layers
-        cta_order = _mlp_order(ly, Cn, blk, L)
+        # the items over the CTAs (the MLP rows are split around them below)
+        cta_order = _cta_order(Cn, L)
         for k, kh in enumerate(heads):
             cta_k, slot_k = int(cta_order[k % Cn]), k // Cn
             sel = np.nonzero(kh_of == kh)[0]
@@ -255,10 +296,16 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
         stats["units"] += int(unit_live.sum())
         item_heads = np.zeros(C.NK, bool)
         item_heads[heads] = True
+        n_it = np.bincount([int(items[i]["cta"]) for i in range(rec["item0"], len(items))],
+                           minlength=Cn)
+        R = _mlp_split(ly, unit_live, ITEM_COST * n_it)
+        rec["mrow0"], rec["mrow1"] = R[0], R[Cn]
         for c in range(Cn):
             ow = np.zeros(1, OWNER)[0]
-            ow["unit0"], ow["n_units"], ow["mrow"], ow["orow"] = 0, 0, -1, -1
-            rows = np.arange(c * blk, (c + 1) * blk)
+            ow["mr0"], ow["mr1"], ow["orow"] = R[c], R[c + 1], -1
+            rows = np.arange(c * blk, (c + 1) * blk)  # out_proj rows
+            mrows = np.arange(R[c], R[c + 1])
+            nr = len(mrows)
             blob = _Blob()
             bh = np.zeros(1, BHDR)[0]
             bh["ln_in"] = blob.add(ly.ln_in) if rec["has_gdn"] else -1
@@ -298,9 +345,9 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
                 bi["prm"] = blob.add(pt["prm"])
                 bh["item"][q] = blob.add(np.array([bi], BITEM))
             if rec["has_mlp"]:
-                sub = ly.down.rows_subset(rows)
+                sub = ly.down.rows_subset(mrows)
                 keep = unit_live[sub.indices]
-                rowid = np.repeat(np.arange(blk), sub.row_nnz())[keep]
+                rowid = np.repeat(np.arange(nr), sub.row_nnz())[keep]
                 uidx, w = sub.indices[keep], sub.data[keep]
                 need = np.unique(uidx)
                 assert len(need) <= MAXUNITS, "too many MLP units for one CTA: use a larger cluster"
@@ -313,10 +360,11 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
                 un["g"] = g_off + 4 * (np.cumsum(g_cnt[need]) - g_cnt[need])
                 un["u"] = u_off + 4 * (np.cumsum(u_cnt[need]) - u_cnt[need])
                 un["ng"], un["nu"] = g_cnt[need], u_cnt[need]
-                ptr = np.zeros(blk + 1, np.int64)
-                np.cumsum(np.bincount(rowid, minlength=blk), out=ptr[1:])
+                ptr = np.zeros(nr + 1, np.int64)
+                np.cumsum(np.bincount(rowid, minlength=nr), out=ptr[1:])
                 bm = np.zeros(1, BMLP)[0]
                 bm["n_units"] = len(need)
+                bm["r0"], bm["nr"] = R[c], nr
                 bm["units"] = blob.add(un)
                 bm["down_ptr"] = blob.add(ptr.astype(np.int32))
                 bm["down_ent"] = blob.add(_pack(loc, w))
