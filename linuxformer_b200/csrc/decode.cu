@@ -57,7 +57,10 @@ namespace cg = cooperative_groups;
 #define BLKMAX (LXB_H / LXB_MINC)
 #define LXB_MAXLAYERS 64
 #define LXB_MAXPROD 4096
-#define LXB_LOGMAX 320  // group steps: window shifts a CTA may undo (entries of 12 bytes)
+#define LXB_LOGMAX 512  // group steps: window shifts a CTA may undo (entries of 12 bytes)
+#define LXB_NOLOG 0xffffffffu  // an undo log entry that undoes nothing
+#define LXB_QLAYERS 32  // layers one quiet pass covers
+#define LXB_QTASKS (LXB_QLAYERS * LXB_ITEMSLOTS)
 #ifndef LXB_GROUPS
 #define LXB_GROUPS 1    // runs of GDN-only layers as optimistic group steps
 #endif
@@ -142,10 +145,15 @@ struct __align__(16) Smem {
   int nq, nk;
   int qkn;                         // the q / k lists are l2-normed already (eager_block)
   uint32_t vhmask[LXB_ITEMSLOTS];  // value heads with output, per item slot
-  int vhlay[LXB_ITEMSLOTS];        // the layer whose item last set the slot's vhmask
+  int vhlay[LXB_ITEMSLOTS];        // the layer and token whose item last set the slot's vhmask
+  int vhtok[LXB_ITEMSLOTS];
   int gkey[2];                     // group steps, by parity: 2 layer + (0 pending | 1 wrote)
   uint32_t lmeta[LXB_LOGMAX];      // undo log: window index | item << 10 | (layer - lo) << 12
   uint2 lold[LXB_LOGMAX];          // the window before the shift
+  int16_t litem[LXB_MAXLAYERS][LXB_ITEMSLOTS];  // this CTA's items per layer (blob order), or -1
+  uint4 qtask[LXB_QTASKS];         // a quiet pass's items: item | k << 24, layer | log << 8, ch0, n
+  int qfull[LXB_QLAYERS];          // per layer of the pass: the items that need a full run
+  int qn, qlog;                    // the pass's item count, its undo log entries
   int wflag[2];                    // some item of the step wrote (pushed by the writer)
   int kmask[LXB_NK];               // out_proj step: active value heads per key head
   alignas(16) uint16_t on[LXB_ITEMSLOTS][R * VD];  // the gated norm's output per item slot
@@ -469,6 +477,23 @@ __device__ __forceinline__ float xn_at(const Smem& sm, const uint16_t* w, float 
   return lx_rbf(lx_mul(lx_mul(sm.x[c], r), lx_add(1.0f, lx_f(w[c]))));
 }
 
+// A channel's conv step: the window (taps 0..2 of the last three projections) shifted with this
+// step's projection Pv (nw), the conv output over it (taps t01, t23: bf16 pairs, low half first)
+// in order from +0, and its silu in bf16 (0 stays 0)
+__device__ __forceinline__ float conv_step(const uint2 win, uint16_t Pv, uint32_t t01, uint32_t t23,
+                                           uint2& nw) {
+  const uint16_t n0 = (uint16_t)(win.x >> 16), n1 = (uint16_t)(win.y & 0xffffu),
+                 n2 = (uint16_t)(win.y >> 16);
+  nw = make_uint2((uint32_t)n0 | ((uint32_t)n1 << 16), (uint32_t)n2 | ((uint32_t)Pv << 16));
+  float y = 0.0f;
+  y = lx_add(y, lx_mul(lx_f((uint16_t)(t01 & 0xffffu)), lx_f(n0)));
+  y = lx_add(y, lx_mul(lx_f((uint16_t)(t01 >> 16)), lx_f(n1)));
+  y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 & 0xffffu)), lx_f(n2)));
+  y = lx_add(y, lx_mul(lx_f((uint16_t)(t23 >> 16)), lx_f(Pv)));
+  const float yb = lx_rbf(y);
+  return yb == 0.0f ? yb : lx_rbf(d_silu(yb));
+}
+
 // One eager (query/key) channel: in_proj_qkv row over the staged entries (the input norm taken
 // per column), conv window shift (resident in shared memory, or in global), conv output with
 // silu in bf16. pr: the row's products, computed beforehand by the whole block (then only the
@@ -496,17 +521,10 @@ __device__ __forceinline__ float eager_channel(Smem& sm, const unsigned char* B,
     for (int k = 0; k < ne; k++)
       ps = lx_add(ps, lx_mul(xn_at(sm, w, r, e[k] & 0xffffu), lx_f((uint16_t)(e[k] >> 16))));
   }
-  const uint16_t Pv = lx_rb(ps);
-  const uint16_t n0 = (uint16_t)(win.x >> 16), n1 = (uint16_t)(win.y & 0xffffu),
-                 n2 = (uint16_t)(win.y >> 16);
-  *wp = make_uint2((uint32_t)n0 | ((uint32_t)n1 << 16), (uint32_t)n2 | ((uint32_t)Pv << 16));
-  float y = 0.0f;
-  y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w & 0xffffu)), lx_f(n0)));
-  y = lx_add(y, lx_mul(lx_f((uint16_t)(a.w >> 16)), lx_f(n1)));
-  y = lx_add(y, lx_mul(lx_f((uint16_t)(b.x & 0xffffu)), lx_f(n2)));
-  y = lx_add(y, lx_mul(lx_f((uint16_t)(b.x >> 16)), lx_f(Pv)));
-  const float yb = lx_rbf(y);
-  return yb == 0.0f ? yb : lx_rbf(d_silu(yb));
+  uint2 nw;
+  const float v = conv_step(win, lx_rb(ps), a.w, b.x, nw);
+  *wp = nw;
+  return v;
 }
 
 // Pieces of an item: the rare paths (many query/key channels, decay, a key firing, output).
@@ -801,11 +819,15 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
         sm.qkn = 0;
         sm.vhmask[bi.slot] = 0;
         sm.vhlay[bi.slot] = L;
+        sm.vhtok[bi.slot] = step;
       }
     }
   } else {
     eager_block(sm, B, bi, conv, w_in, r_in, pre ? sm.prod : nullptr, e_first, zin);
-    if (t == 0) sm.vhlay[bi.slot] = L;
+    if (t == 0) {
+      sm.vhlay[bi.slot] = L;
+      sm.vhtok[bi.slot] = step;
+    }
   }
   // warp 1: g, only for a head that can decay (for the others softplus underflows to zero
   // whatever the input: g is 0, as the table builder proved); beta only when a key fires
@@ -909,6 +931,139 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
   return item_tail(P, sm, B, bi, bm, nk, w_in, r_in) ? ITEM_WROTE : ITEM_DONE;
 }
 
+// A query/key channel evaluated from the global tables (its entries in the entry pool, the input
+// norm's weights w in the u16 pool): the same sums in the same order as eager_channel, the
+// window left as it is (nw: the shifted one)
+__device__ __forceinline__ float quiet_chan(const Dev& P, const Smem& sm, const lxb_chan& c,
+                                            const uint16_t* w, float r, const uint2 win, uint2& nw) {
+  const uint32_t* e = P.ent + c.ent;
+  const int ne = c.n;
+  float ps = 0.0f;
+  for (int k = 0; k < ne; k += 8) {  // 8 entries' loads in flight, then the sum in order
+    uint32_t en[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) en[q] = k + q < ne ? __ldg(e + k + q) : 0u;
+    float pv[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++)
+      pv[q] = k + q < ne ? lx_mul(xn_at(sm, w, r, en[q] & 0xffffu), lx_f((uint16_t)(en[q] >> 16)))
+                         : 0.0f;
+#pragma unroll
+    for (int q = 0; q < 8; q++)
+      if (k + q < ne) ps = lx_add(ps, pv[q]);
+  }
+  return conv_step(win, lx_rb(ps), c.t01, c.t23, nw);
+}
+
+// A group step's quiet pass over layers [l0, qhi), qhi = min(hi, l0 + LXB_QLAYERS) (returned):
+// every item of this CTA in those layers at once, one warp each (a lane per query/key channel).
+// An item that cannot decay and whose query/key outputs are all zero changes nothing but its
+// windows (gdn_item would return at its first check): they are shifted here, logged for the undo
+// when the layer is after lo (the step's first), and the item is done. Every other item (one
+// that is not resident, has more than 32 such channels, may decay, has a nonzero output, or
+// finds no room in the log) is left as it was, for the walk: sm.qfull. Also the layers' ring
+// rows of this step. Ends with a block barrier.
+__device__ int quiet_pass(const Dev& P, const Run& run, Smem& sm, int s, int rank, int lo, int l0,
+                          int hi, int step, float r) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int nl = max(0, min(hi, l0 + LXB_QLAYERS) - l0);
+  if (warp == 0) {
+    // lane: layer l0 + lane. Its eligible items, and the log entries they need, in (layer, item)
+    // order: the first ones that fit the log are this pass's (a contiguous log prefix)
+    const int L = l0 + lane;
+    int cnt = 0, need = 0;
+    if (lane < nl)
+      for (int k = 0; k < LXB_ITEMSLOTS && sm.litem[L][k] >= 0; k++) {
+        const lxb_item it = P.items[sm.litem[L][k]];
+        if (it.n_eager <= 32 && !(it.flags & (LXB_IT_NONRES | LXB_IT_DECAYS))) {
+          cnt++;
+          need += L > lo ? it.n_eager : 0;
+        }
+      }
+    int cb = cnt, nb = need;  // inclusive scans over the lanes
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int c2 = __shfl_up_sync(0xffffffffu, cb, o), n2 = __shfl_up_sync(0xffffffffu, nb, o);
+      if (lane >= o) {
+        cb += c2;
+        nb += n2;
+      }
+    }
+    int pos = cb - cnt, off = nb - need, full = 0, end = 0;
+    if (lane < nl)
+      for (int k = 0; k < LXB_ITEMSLOTS && sm.litem[L][k] >= 0; k++) {
+        const int g = sm.litem[L][k];
+        const lxb_item it = P.items[g];
+        if (!(it.n_eager <= 32 && !(it.flags & (LXB_IT_NONRES | LXB_IT_DECAYS)))) {
+          full |= 1 << k;
+          continue;
+        }
+        const int nd = L > lo ? it.n_eager : 0;
+        if (off + nd <= LXB_LOGMAX) {
+          sm.qtask[pos] = make_uint4((uint32_t)g | (uint32_t)k << 24, (uint32_t)L | (uint32_t)off << 8,
+                                     (uint32_t)it.ch0, (uint32_t)it.n_eager);
+          end = off + nd;
+        } else {
+          sm.qtask[pos] = make_uint4(0u, 0xffffffffu, 0u, 0u);  // no room: the walk's
+          full |= 1 << k;
+        }
+        pos++;
+        off += nd;
+      }
+    if (lane < nl) sm.qfull[lane] = full;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) end = max(end, __shfl_xor_sync(0xffffffffu, end, o));
+    const int total = __shfl_sync(0xffffffffu, cb, 31);
+    if (lane == 0) {
+      sm.qn = total;
+      sm.qlog = end;
+    }
+  } else {
+    // meanwhile the other warps: the layers' ring rows (each CTA its block; rank 0 the factor)
+    const int per = P.blk / 2;
+    for (int idx = t - 32; idx < nl * per; idx += NT - 32) {
+      const int q = idx / per, k = idx - q * per;
+      const size_t slot = ((size_t)s * P.n_layers + l0 + q) * 4 + (step & 3);
+      const float* xv = sm.x + rank * P.blk + 2 * k;
+      reinterpret_cast<uint32_t*>(run.ring + slot * H + rank * P.blk)[k] =
+          (uint32_t)lx_rb(xv[0]) | ((uint32_t)lx_rb(xv[1]) << 16);
+    }
+    if (rank == 0 && t - 32 < nl)
+      run.ring_r[((size_t)s * P.n_layers + l0 + (t - 32)) * 4 + (step & 3)] = r;
+  }
+  __syncthreads();
+  const int nt = sm.qn;
+  for (int j = warp; j < nt; j += NT / 32) {
+    const uint4 q = sm.qtask[j];
+    if (q.y == 0xffffffffu) continue;
+    const int k = (int)(q.x >> 24), L = (int)(q.y & 255u), off = (int)(q.y >> 8), n = (int)q.w;
+    float v = 0.0f;
+    uint32_t wi = 0;
+    uint2 old = make_uint2(0u, 0u), nw = make_uint2(0u, 0u);
+    if (lane < n) {
+      const lxb_chan c = P.chans[q.z + lane];
+      wi = c.win;
+      old = sm.win[wi];
+      v = quiet_chan(P, sm, c, P.u16 + sm.layers[L].ln_in, r, old, nw);
+    }
+    const bool quiet = !__any_sync(0xffffffffu, lane < n && v != 0.0f);
+    if (lane < n) {
+      if (quiet) {
+        if (L > lo) {
+          sm.lmeta[off + lane] = wi | (uint32_t)k << 10 | (uint32_t)(L - lo) << 12;
+          sm.lold[off + lane] = old;
+        }
+        sm.win[wi] = nw;
+      } else if (L > lo) {
+        sm.lmeta[off + lane] = LXB_NOLOG;
+      }
+    }
+    if (!quiet && lane == 0) atomicOr(&sm.qfull[L - l0], 1 << k);
+  }
+  __syncthreads();
+  return l0 + nl;
+}
+
 // --- the owned rows ---------------------------------------------------------------------------
 // The MLP over this CTA's rows: own[row] = bf16(x + bf16(sum_u h_u w_d)), h_u re-evaluated here;
 // the units and entries are in the staged blob (m: its MLP part)
@@ -998,16 +1153,18 @@ __device__ void copy_owner(Smem& sm, int r0, int nr, float* own) {
 
 // out_proj over this CTA's rows, from the layer's items' outputs (gathered over DSMEM)
 __device__ void out_owner(const Dev& P, Smem& sm, const lxb_layer& ly, const lxb_owner& ow,
-                          int rank, float* own, cg::cluster_group& cluster) {
+                          int rank, int tok, float* own, cg::cluster_group& cluster) {
   const int t = threadIdx.x;
   const int32_t* itemof = P.i32 + ly.itemof;
   if (t < LXB_NK) {
     const int ii = itemof[t];
     uint32_t m = 0;
-    if (ii >= 0) {  // (a slot a later layer's item has used since holds no output of this one)
+    if (ii >= 0) {  // (a slot another layer's or token's item has set since holds none of this)
       const lxb_item it = P.items[ii];
       m = *cluster.map_shared_rank(&sm.vhmask[it.slot], it.cta);
-      if (*cluster.map_shared_rank(&sm.vhlay[it.slot], it.cta) != it.layer) m = 0;
+      if (*cluster.map_shared_rank(&sm.vhlay[it.slot], it.cta) != it.layer ||
+          *cluster.map_shared_rank(&sm.vhtok[it.slot], it.cta) != tok)
+        m = 0;
     }
     sm.kmask[t] = (int)m;
   }
@@ -1378,6 +1535,18 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     sm.win[k] = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(sm.sptr[L][1]) +
                                                 (size_t)ch * 4);
   }
+  for (int k = t; k < P.n_layers * LXB_ITEMSLOTS; k += NT) {  // this CTA's items per layer
+    const int L = k / LXB_ITEMSLOTS, q = k % LXB_ITEMSLOTS;
+    const unsigned char* Bg = P.blobs + sm.bref[L].off;
+    const lxb_bhdr* bh = reinterpret_cast<const lxb_bhdr*>(Bg);
+    sm.litem[L][q] =
+        q < bh->n_items ? (int16_t)reinterpret_cast<const lxb_bitem*>(Bg + bh->item[q])->item : -1;
+  }
+  if (t < LXB_ITEMSLOTS) {  // no slot holds an output yet
+    sm.vhmask[t] = 0;
+    sm.vhlay[t] = -1;
+    sm.vhtok[t] = -1;
+  }
   if (t == 0) stage_issue(P, sm, stage, 0, 0);  // step 0: layer 0
   __syncthreads();
   cluster.sync();  // every CTA's flags are initialised before anyone may push one
@@ -1445,15 +1614,17 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     if (sm.broken) return nullptr;
     return stage + (size_t)b * P.stage;
   };
-  // A run of GDN-only layers [lo0, hi) as group steps: each CTA takes its items layer after
-  // layer with no cluster barrier between them, all on the residual as it was at the step's
-  // start. That is exact as long as no layer before changes it: an item that writes (output)
-  // or one after the step's first layer that would change its state (a key firing, a decay)
-  // ends the CTA's walk after that layer and posts key 2 layer + (0 pending | 1 wrote) to every
-  // CTA's shared minimum; the others stop before any later layer. After the barrier, with J
-  // the minimum's layer: the window shifts of the layers after J (and of J's pending items) are
-  // undone from the log; then either J again with only its pending items (as the first layer
-  // of the next group step) or J's out_proj rows (the fix-up) and on from J + 1.
+  // A run of GDN-only layers [lo0, hi) as group steps, all on the residual as it was at the
+  // step's start. That is exact as long as no layer before changes it. Each step first takes a
+  // quiet pass over its layers (every item of this CTA at once: the ones whose query/key outputs
+  // are all zero are done there), then walks the layers that still have items here, with no
+  // cluster barrier between them: an item that writes (output) or one after the step's first
+  // layer that would change its state (a key firing, a decay) ends the CTA's walk after that
+  // layer and posts key 2 layer + (0 pending | 1 wrote) to every CTA's shared minimum; the
+  // others stop before any later layer. After the barrier, with J the minimum's layer: the
+  // window shifts of the layers after J (and of J's pending items) are undone from the log;
+  // then either J again with only its pending items (as the first layer of the next group step)
+  // or J's out_proj rows (the fix-up) and on from J + 1.
   int gp = 0;  // group steps so far (the key's parity)
   auto group_run = [&](const int lo0, const int hi, const int i) {
     int lo = lo0, rs_mask = 0, held_out = 0;
@@ -1465,63 +1636,78 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     while (lo < hi) {
       const int gpar = gp & 1;
       if (t == 0) sm.gkey[gpar ^ 1] = 0x7fffffff;  // the next step's (nobody posts it before
-      restage(lo);                                 // this step's barrier)
-      int nlog = 0, sL = -1, pend = 0, outL = 0;
-      for (int L = lo; L < hi; L++) {
+                                                   // this step's barrier)
+      const int l0 = resume ? lo + 1 : lo;  // (J's other items are done)
+      const int qhi = quiet_pass(P, run, sm, s, rank, lo, l0, hi, i, r_x);
+      PROF(PR_ITEMS);
+      // the items each layer still has here (the same in every thread)
+      auto want_of = [&](int L) -> int {
+        return (resume && L == lo) ? rs_mask : sm.qfull[L - l0];
+      };
+      auto next_visit = [&](int L) -> int {
+        for (; L < qhi; L++)
+          if (want_of(L)) return L;
+        return -1;
+      };
+      {
+        const int f = next_visit(lo);
+        if (f >= 0) restage(f);
+      }
+      int nlog = sm.qlog, sL = -1, pend = 0, outL = 0;
+      for (int L = lo; L < qhi; L++) {
+        const int want = want_of(L);
+        const bool held = resume && L == lo && held_out;  // J's outputs from the last step
+        if (!want && !held) continue;
         if (L > lo &&
             __syncthreads_or(t == 0 && *reinterpret_cast<volatile int*>(&sm.gkey[gpar]) < 2 * L))
           break;
-        const lxb_layer& ly = sm.layers[L];
-        cur_layer = L;
-        const unsigned char* B = take(i);
-        PROF(PR_WAIT);
-        const lxb_bhdr bh = B ? *reinterpret_cast<const lxb_bhdr*>(B) : lxb_bhdr{};
-        float* rec = reinterpret_cast<float*>(sm.sptr[L][0]);
-        uint16_t* conv = reinterpret_cast<uint16_t*>(sm.sptr[L][1]);
-        uint32_t* bm = run.bitmaps + ((size_t)s * P.n_layers + L) * LXB_NV * 8;
-        const float r = r_x;
-        const uint16_t* w_in = (B && bh.ln_in >= 0)
-                                   ? reinterpret_cast<const uint16_t*>(B + bh.ln_in)
-                                   : P.u16 + ly.ln_in;
-        {  // this step's GDN input row into the ring (each CTA its block; rank 0 the factor)
-          const size_t slot = ((size_t)s * P.n_layers + L) * 4 + (i & 3);
-          uint16_t* rg = run.ring + slot * H + rank * P.blk;
-          for (int k = t; k < P.blk / 2; k += NT) {
-            const float* xv = sm.x + rank * P.blk + 2 * k;
-            reinterpret_cast<uint32_t*>(rg)[k] =
-                (uint32_t)lx_rb(xv[0]) | ((uint32_t)lx_rb(xv[1]) << 16);
+        int st_any = held ? 1 : 0;
+        if (want) {
+          const lxb_layer& ly = sm.layers[L];
+          cur_layer = L;
+          restage(L);  // (in flight already, normally)
+          const unsigned char* B = take(i);
+          {  // the next layer with items here: its blob into the other buffer
+            const int nx = next_visit(L + 1);
+            inflight = nx;
+            if (nx >= 0 && t == NT - 32 && !sm.broken)
+              stage_issue(P, sm, stage, (int)((stp + 1) & 1), nx);
           }
-          if (rank == 0 && t == 0) run.ring_r[slot] = r;
-        }
-        issue_next(stp);
-        PROF(PR_NORM);
-        int st_any = 0;
-        if (B) {
-          const lxb_bhdr* bhp = reinterpret_cast<const lxb_bhdr*>(B);  // (dynamic index: smem)
-          for (int k = 0; k < bh.n_items; k++) {
-            if (resume && L == lo && !((rs_mask >> k) & 1)) continue;  // done already
-            const lxb_bitem bi = *reinterpret_cast<const lxb_bitem*>(B + bhp->item[k]);
-            const bool spec = L > lo;
-            if (spec && nlog + bi.n_eager > LXB_LOGMAX) {  // no room to undo: k.. wait for J = L
-              for (int kk = k; kk < bh.n_items; kk++) pend |= 1 << kk;
-              st_any |= 2;
-              break;
-            }
-            const int stt = gdn_item(P, run, sm, B, bi, rec, conv, bm, s, L, i, w_in, r,
-                                     spec ? sm.lmeta + nlog : nullptr,
-                                     spec ? sm.lold + nlog : nullptr,
-                                     (uint32_t)k << 10 | (uint32_t)(L - lo) << 12);
-            if (spec && stt != ITEM_UNTOUCHED) nlog += bi.n_eager;
-            if (stt == ITEM_WROTE) st_any |= 1;
-            if (stt >= ITEM_PENDING) {
-              st_any |= 2;
-              pend |= 1 << k;
+          PROF(PR_WAIT);
+          const lxb_bhdr bh = B ? *reinterpret_cast<const lxb_bhdr*>(B) : lxb_bhdr{};
+          float* rec = reinterpret_cast<float*>(sm.sptr[L][0]);
+          uint16_t* conv = reinterpret_cast<uint16_t*>(sm.sptr[L][1]);
+          uint32_t* bm = run.bitmaps + ((size_t)s * P.n_layers + L) * LXB_NV * 8;
+          const float r = r_x;
+          const uint16_t* w_in = (B && bh.ln_in >= 0)
+                                     ? reinterpret_cast<const uint16_t*>(B + bh.ln_in)
+                                     : P.u16 + ly.ln_in;
+          if (B) {
+            const lxb_bhdr* bhp = reinterpret_cast<const lxb_bhdr*>(B);  // (dynamic index: smem)
+            for (int k = 0; k < bh.n_items; k++) {
+              if (!((want >> k) & 1)) continue;  // done already
+              const lxb_bitem bi = *reinterpret_cast<const lxb_bitem*>(B + bhp->item[k]);
+              const bool spec = L > lo;
+              if (spec && nlog + bi.n_eager > LXB_LOGMAX) {  // no room to undo: wait for J = L
+                pend |= want & ~((1 << k) - 1);
+                st_any |= 2;
+                break;
+              }
+              const int stt = gdn_item(P, run, sm, B, bi, rec, conv, bm, s, L, i, w_in, r,
+                                       spec ? sm.lmeta + nlog : nullptr,
+                                       spec ? sm.lold + nlog : nullptr,
+                                       (uint32_t)k << 10 | (uint32_t)(L - lo) << 12);
+              if (spec && stt != ITEM_UNTOUCHED) nlog += bi.n_eager;
+              if (stt == ITEM_WROTE) st_any |= 1;
+              if (stt >= ITEM_PENDING) {
+                st_any |= 2;
+                pend |= 1 << k;
+              }
             }
           }
+          stp++;
         }
-        if (resume && L == lo && held_out) st_any |= 1;  // J's outputs from the last step
         PROF(PR_ITEMS);
-        stp++;
         if (st_any) {
           sL = L;
           outL = st_any & 1;
@@ -1534,10 +1720,17 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       PROF(PR_SYNC);
       const int key = *reinterpret_cast<volatile int*>(&sm.gkey[gpar]);
       gp++;
-      if (key == 0x7fffffff) break;  // every layer of the run done, none wrote
+      if (key == 0x7fffffff) {  // every layer of the step done, none wrote
+        lo = qhi;
+        resume = false;
+        rs_mask = 0;
+        held_out = 0;
+        continue;
+      }
       const int J = key >> 1;
       for (int e = t; e < nlog; e += NT) {  // undo: the layers after J, J's pending items
         const uint32_t m = sm.lmeta[e];
+        if (m == LXB_NOLOG) continue;
         const int lay = lo + (int)(m >> 12), kk = (int)(m >> 10) & 3;
         if (lay > J || (lay == J && sL == J && ((pend >> kk) & 1))) sm.win[m & 1023u] = sm.lold[e];
       }
@@ -1552,7 +1745,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         ph++;
         const lxb_layer& lyJ = sm.layers[J];
         const lxb_owner ow = P.owners[lyJ.owner0 + rank];
-        out_owner(P, sm, lyJ, ow, rank, sm.own[ph & 1], cluster);
+        out_owner(P, sm, lyJ, ow, rank, i, sm.own[ph & 1], cluster);
         __syncthreads();
         push_rows(P, sm, sm.own[ph & 1], ph & 1, rank * P.blk, P.blk, cluster);
         cluster.sync();
@@ -1566,6 +1759,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         lo = J + 1;
       }
     }
+    restage(hi);  // the step after the run: the next layer's blob (or the head's)
   };
   load_embed(run, P, sm, sm.tok);
   for (int i = 0; i < run.n_tokens; i++) {
@@ -1654,7 +1848,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         if (P.nbuf == 1 && !ly.has_mlp) issue_next(stp);  // the blob is no longer read
         ph++;
         const lxb_owner ow = P.owners[ly.owner0 + rank];
-        out_owner(P, sm, ly, ow, rank, sm.own[ph & 1], cluster);
+        out_owner(P, sm, ly, ow, rank, i, sm.own[ph & 1], cluster);
         __syncthreads();
         push_rows(P, sm, sm.own[ph & 1], ph & 1, rank * P.blk, P.blk, cluster);
         cluster.sync();
@@ -1961,6 +2155,8 @@ int validate_blobs(const View& v, int C) {
   const unsigned char* base = v.sec<unsigned char>(LXB_SEC_BLOBS);
   const lxb_layer* layers = v.sec<lxb_layer>(LXB_SEC_LAYERS);
   const lxb_item* items = v.sec<lxb_item>(LXB_SEC_ITEMS);
+  const lxb_chan* gchans = v.sec<lxb_chan>(LXB_SEC_CHANS);
+  const uint32_t* gent = v.sec<uint32_t>(LXB_SEC_ENT);
   if (v.n(LXB_SEC_WINIDX) != C) return LXB_E_IMAGE;
   const int32_t* widx = v.sec<int32_t>(LXB_SEC_WINIDX);
   const int32_t* wmap = v.sec<int32_t>(LXB_SEC_WINMAP);
@@ -1997,7 +2193,8 @@ int validate_blobs(const View& v, int C) {
         if (bi.item < ly.item0 || bi.item >= ly.item0 + ly.n_items) return LXB_E_IMAGE;
         const lxb_item& it = items[bi.item];
         if (it.cta != c || it.kh != bi.kh || it.slot != bi.slot || it.flags != bi.flags ||
-            bi.n_eager != it.n_eager || bi.n_eager < 0 || bi.n_eager > 2 * LXB_KD)
+            bi.n_eager != it.n_eager || bi.n_eager < 0 || bi.n_eager > 2 * LXB_KD ||
+            bi.n_eager > it.n_ch)
           return LXB_E_IMAGE;
         if (!blob_rng(bi.eager, (int64_t)bi.n_eager * sizeof(lxb_bchan), nb, 16))
           return LXB_E_IMAGE;
@@ -2006,6 +2203,15 @@ int validate_blobs(const View& v, int C) {
           if (ch.slot >= 2 * LXB_KD || ch.conv_ch >= LXB_CONV || !blob_ent(B, nb, ch.ent, ch.n, H))
             return LXB_E_IMAGE;
           if (ch.win == LXB_NOWIN && !(bi.flags & LXB_IT_NONRES)) return LXB_E_IMAGE;
+          // the global table's record of the channel (the quiet pass reads that one): the same
+          // window, taps and entries
+          const lxb_chan& gc = gchans[it.ch0 + e];
+          if (gc.win != ch.win || gc.n != ch.n || gc.conv_ch != ch.conv_ch || gc.t01 != ch.t01 ||
+              gc.t23 != ch.t23)
+            return LXB_E_IMAGE;
+          for (int q = 0; q < ch.n; q++)
+            if (gent[gc.ent + q] != reinterpret_cast<const uint32_t*>(B + ch.ent)[q])
+              return LXB_E_IMAGE;
           if (ch.win != LXB_NOWIN) {  // a resident window: the map must name this channel
             if (ch.win >= (uint32_t)widx[2 * c + 1]) return LXB_E_IMAGE;
             const int32_t* wp = wmap + 2 * ((int64_t)widx[2 * c] + ch.win);

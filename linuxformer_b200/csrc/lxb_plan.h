@@ -15,7 +15,7 @@
 #include <stdint.h>
 
 #define LXB_MAGIC 0x50425a4cu  // "LZBP"
-#define LXB_IMAGE_VERSION 8
+#define LXB_IMAGE_VERSION 9
 
 #define LXB_H 2560
 #define LXB_KD 256
@@ -116,7 +116,9 @@ typedef struct {
   uint32_t conv_ch;        // the channel's index in the layer's conv state
   uint32_t t01, t23;       // conv taps 0..3, bf16 pairs (low half first)
   uint32_t tapmask;        // bit j: tap j is nonzero
-  uint32_t pad[2];
+  uint32_t win;            // a query/key channel's resident window slot in its CTA's shared
+                           // memory (as its blob entry's), else LXB_NOWIN
+  uint32_t pad;
 } lxb_chan;  // 32 bytes: two aligned 16-byte loads
 
 typedef struct {

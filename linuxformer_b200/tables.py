@@ -27,7 +27,7 @@ from . import chip as C
 from .chip import _ranges
 
 MAGIC = 0x50425A4C
-VERSION = 8
+VERSION = 9
 NSLOT, NOSLOT = 1536, 0xFFFF
 ITEMSLOTS, MAXDENSE, MAXUNITS, MAXWIN = 4, 32, 2048, 1024
 MINC = 4  # the smallest cluster: an owner holds at most H / MINC rows
@@ -45,7 +45,7 @@ LAYER = np.dtype([(n, "<i4") for n in ("has_gdn", "has_mlp", "ln_in", "ln_post",
 ITEM = np.dtype([(n, "<i4") for n in ("layer", "kh", "cta", "slot", "ch0", "n_ch", "rows",
                                       "params", "flags", "n_eager", "n_vneed", "tapu")])
 CHAN = np.dtype([("ent", "<u4"), ("n", "<u2"), ("slot", "<u2"), ("conv_ch", "<u4"),
-                 ("t01", "<u4"), ("t23", "<u4"), ("tapmask", "<u4"), ("p1", "<u4"),
+                 ("t01", "<u4"), ("t23", "<u4"), ("tapmask", "<u4"), ("win", "<u4"),
                  ("p2", "<u4")])
 UNIT = np.dtype([("g", "<u4"), ("u", "<u4"), ("ng", "<u2"), ("nu", "<u2"), ("pad", "<u4")])
 OWNER = np.dtype([("mr0", "<i4"), ("mr1", "<i4"), ("pad", "<i4"), ("orow", "<i4")])
@@ -245,6 +245,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
             ch["t01"] = taps[:, 0] | (taps[:, 1] << 16)
             ch["t23"] = taps[:, 2] | (taps[:, 3] << 16)
             ch["tapmask"] = ((taps & 0x7FFF) != 0).astype(np.uint32) @ (1 << np.arange(4))
+            ch["win"] = 0xFFFFFFFF
             assert len(chs) <= 2 * NSLOT
             ch0 = sum(len(c) for c in chans)
             chans.append(ch)
@@ -325,6 +326,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
                 if len(winmap[c]) + len(bc) <= MAXWIN:  # windows kept in shared memory
                     bc["win"] = len(winmap[c]) + np.arange(len(bc))
                     winmap[c] += [(L, int(x)) for x in bc["conv_ch"]]
+                    chans[i]["win"][:len(bc)] = bc["win"]  # (the item's first channels)
                 else:
                     bc["win"] = 0xFFFFFFFF
                     if len(bc):
