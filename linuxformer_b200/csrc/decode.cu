@@ -61,6 +61,8 @@ namespace cg = cooperative_groups;
 #define LXB_NOLOG 0xffffffffu  // an undo log entry that undoes nothing
 #define LXB_QLAYERS 32  // layers one quiet pass covers
 #define LXB_QTASKS (LXB_QLAYERS * LXB_ITEMSLOTS)
+#define LXB_QNONE 0xffffffffu
+#define LXB_QFULL 0x40000000u
 #ifndef LXB_GROUPS
 #define LXB_GROUPS 1    // runs of GDN-only layers as optimistic group steps
 #endif
@@ -150,10 +152,12 @@ struct __align__(16) Smem {
   int gkey[2];                     // group steps, by parity: 2 layer + (0 pending | 1 wrote)
   uint32_t lmeta[LXB_LOGMAX];      // undo log: window index | item << 10 | (layer - lo) << 12
   uint2 lold[LXB_LOGMAX];          // the window before the shift
-  int16_t litem[LXB_MAXLAYERS][LXB_ITEMSLOTS];  // this CTA's items per layer (blob order), or -1
-  uint4 qtask[LXB_QTASKS];         // a quiet pass's items: item | k << 24, layer | log << 8, ch0, n
+  uint32_t qinfo[LXB_MAXLAYERS][LXB_ITEMSLOTS];  // this CTA's items per layer (blob order):
+                                   // first channel | n_eager << 24 if a quiet pass may take it,
+                                   // LXB_QFULL if not, LXB_QNONE past the last
+  uint4 qtask[LXB_QTASKS];         // a quiet pass's items: k | layer << 8, log, channel, qinfo
   int qfull[LXB_QLAYERS];          // per layer of the pass: the items that need a full run
-  int qn, qlog;                    // the pass's item count, its undo log entries
+  int qn, qlog, qnch;              // the pass's item count, undo log entries, channels
   int wflag[2];                    // some item of the step wrote (pushed by the writer)
   int kmask[LXB_NK];               // out_proj step: active value heads per key head
   alignas(16) uint16_t on[LXB_ITEMSLOTS][R * VD];  // the gated norm's output per item slot
@@ -956,67 +960,74 @@ __device__ __forceinline__ float quiet_chan(const Dev& P, const Smem& sm, const 
 }
 
 // A group step's quiet pass over layers [l0, qhi), qhi = min(hi, l0 + LXB_QLAYERS) (returned):
-// every item of this CTA in those layers at once, one warp each (a lane per query/key channel).
-// An item that cannot decay and whose query/key outputs are all zero changes nothing but its
-// windows (gdn_item would return at its first check): they are shifted here, logged for the undo
-// when the layer is after lo (the step's first), and the item is done. Every other item (one
-// that is not resident, has more than 32 such channels, may decay, has a nonzero output, or
-// finds no room in the log) is left as it was, for the walk: sm.qfull. Also the layers' ring
-// rows of this step. Ends with a block barrier.
+// every item of this CTA in those layers at once, a thread per query/key channel. An item that
+// cannot decay and whose query/key outputs are all zero changes nothing but its windows
+// (gdn_item would return at its first check): they are shifted here, logged for the undo when the
+// layer is after lo (the step's first), and the item is done. Every other item (one that is not
+// resident, has more than 32 such channels, may decay, has a nonzero output, or finds no room in
+// the log or the block) is left as it was, for the walk: sm.qfull, and vis (bit b: layer l0 + b
+// has such items). Also the layers' ring rows of this step. Ends with a block barrier.
 __device__ int quiet_pass(const Dev& P, const Run& run, Smem& sm, int s, int rank, int lo, int l0,
-                          int hi, int step, float r) {
+                          int hi, int step, float r, uint32_t& vis) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int nl = max(0, min(hi, l0 + LXB_QLAYERS) - l0);
   if (warp == 0) {
-    // lane: layer l0 + lane. Its eligible items, and the log entries they need, in (layer, item)
-    // order: the first ones that fit the log are this pass's (a contiguous log prefix)
+    // lane: layer l0 + lane. Its items with channels, in (layer, item) order: the first ones that
+    // fit the log and the block are this pass's (their log entries and threads contiguous)
     const int L = l0 + lane;
-    int cnt = 0, need = 0;
+    int cnt = 0, need = 0, chn = 0;
     if (lane < nl)
-      for (int k = 0; k < LXB_ITEMSLOTS && sm.litem[L][k] >= 0; k++) {
-        const lxb_item it = P.items[sm.litem[L][k]];
-        if (it.n_eager <= 32 && !(it.flags & (LXB_IT_NONRES | LXB_IT_DECAYS))) {
-          cnt++;
-          need += L > lo ? it.n_eager : 0;
-        }
+      for (int k = 0; k < LXB_ITEMSLOTS && sm.qinfo[L][k] != LXB_QNONE; k++) {
+        const uint32_t qi = sm.qinfo[L][k];
+        if (qi == LXB_QFULL || !(qi >> 24)) continue;  // (no channel: nothing to do)
+        cnt++;
+        need += L > lo ? (int)(qi >> 24) : 0;
+        chn += (int)(qi >> 24);
       }
-    int cb = cnt, nb = need;  // inclusive scans over the lanes
+    int cb = cnt, nb = need, hb = chn;  // inclusive scans over the lanes
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int c2 = __shfl_up_sync(0xffffffffu, cb, o), n2 = __shfl_up_sync(0xffffffffu, nb, o);
+      const int c2 = __shfl_up_sync(0xffffffffu, cb, o), n2 = __shfl_up_sync(0xffffffffu, nb, o),
+                h2 = __shfl_up_sync(0xffffffffu, hb, o);
       if (lane >= o) {
         cb += c2;
         nb += n2;
+        hb += h2;
       }
     }
-    int pos = cb - cnt, off = nb - need, full = 0, end = 0;
+    int pos = cb - cnt, off = nb - need, coff = hb - chn, full = 0, acc = 0, end = 0, cend = 0;
     if (lane < nl)
-      for (int k = 0; k < LXB_ITEMSLOTS && sm.litem[L][k] >= 0; k++) {
-        const int g = sm.litem[L][k];
-        const lxb_item it = P.items[g];
-        if (!(it.n_eager <= 32 && !(it.flags & (LXB_IT_NONRES | LXB_IT_DECAYS)))) {
+      for (int k = 0; k < LXB_ITEMSLOTS && sm.qinfo[L][k] != LXB_QNONE; k++) {
+        const uint32_t qi = sm.qinfo[L][k];
+        if (qi == LXB_QFULL) {
           full |= 1 << k;
           continue;
         }
-        const int nd = L > lo ? it.n_eager : 0;
-        if (off + nd <= LXB_LOGMAX) {
-          sm.qtask[pos] = make_uint4((uint32_t)g | (uint32_t)k << 24, (uint32_t)L | (uint32_t)off << 8,
-                                     (uint32_t)it.ch0, (uint32_t)it.n_eager);
+        const int n = (int)(qi >> 24), nd = L > lo ? n : 0;
+        if (!n) continue;
+        if (off + nd <= LXB_LOGMAX && coff + n <= NT) {
+          sm.qtask[pos] = make_uint4((uint32_t)k | (uint32_t)L << 8, (uint32_t)off, (uint32_t)coff, qi);
+          acc++;
           end = off + nd;
+          cend = coff + n;
         } else {
-          sm.qtask[pos] = make_uint4(0u, 0xffffffffu, 0u, 0u);  // no room: the walk's
-          full |= 1 << k;
+          full |= 1 << k;  // no room: the walk's
         }
         pos++;
         off += nd;
+        coff += n;
       }
     if (lane < nl) sm.qfull[lane] = full;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) end = max(end, __shfl_xor_sync(0xffffffffu, end, o));
-    const int total = __shfl_sync(0xffffffffu, cb, 31);
+    for (int o = 16; o > 0; o >>= 1) {
+      acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      end = max(end, __shfl_xor_sync(0xffffffffu, end, o));
+      cend = max(cend, __shfl_xor_sync(0xffffffffu, cend, o));
+    }
     if (lane == 0) {
-      sm.qn = total;
+      sm.qn = acc;  // (the accepted items are a prefix of the order)
       sm.qlog = end;
+      sm.qnch = cend;
     }
   } else {
     // meanwhile the other warps: the layers' ring rows (each CTA its block; rank 0 the factor)
@@ -1032,33 +1043,39 @@ __device__ int quiet_pass(const Dev& P, const Run& run, Smem& sm, int s, int ran
       run.ring_r[((size_t)s * P.n_layers + l0 + (t - 32)) * 4 + (step & 3)] = r;
   }
   __syncthreads();
-  const int nt = sm.qn;
-  for (int j = warp; j < nt; j += NT / 32) {
-    const uint4 q = sm.qtask[j];
-    if (q.y == 0xffffffffu) continue;
-    const int k = (int)(q.x >> 24), L = (int)(q.y & 255u), off = (int)(q.y >> 8), n = (int)q.w;
-    float v = 0.0f;
-    uint32_t wi = 0;
-    uint2 old = make_uint2(0u, 0u), nw = make_uint2(0u, 0u);
-    if (lane < n) {
-      const lxb_chan c = P.chans[q.z + lane];
-      wi = c.win;
-      old = sm.win[wi];
-      v = quiet_chan(P, sm, c, P.u16 + sm.layers[L].ln_in, r, old, nw);
+  // thread t: channel t of the pass (its item: the last whose first thread is <= t)
+  const int nch = sm.qnch;
+  uint4 q = make_uint4(0u, 0u, 0u, 0u);
+  uint32_t wi = 0;
+  uint2 old = make_uint2(0u, 0u), nw = make_uint2(0u, 0u);
+  if (t < nch) {
+    int a = 0, b = sm.qn - 1;
+    while (a < b) {
+      const int m = (a + b + 1) >> 1;
+      if ((int)sm.qtask[m].z <= t) a = m;
+      else b = m - 1;
     }
-    const bool quiet = !__any_sync(0xffffffffu, lane < n && v != 0.0f);
-    if (lane < n) {
-      if (quiet) {
-        if (L > lo) {
-          sm.lmeta[off + lane] = wi | (uint32_t)k << 10 | (uint32_t)(L - lo) << 12;
-          sm.lold[off + lane] = old;
-        }
-        sm.win[wi] = nw;
-      } else if (L > lo) {
-        sm.lmeta[off + lane] = LXB_NOLOG;
+    q = sm.qtask[a];
+    const int L = (int)((q.x >> 8) & 255u);
+    const lxb_chan c = P.chans[(q.w & 0xffffffu) + (t - q.z)];
+    wi = c.win;
+    old = sm.win[wi];
+    const float v = quiet_chan(P, sm, c, P.u16 + sm.layers[L].ln_in, r, old, nw);
+    if (v != 0.0f) atomicOr(&sm.qfull[L - l0], 1 << (q.x & 255u));
+  }
+  __syncthreads();
+  vis = __ballot_sync(0xffffffffu, lane < nl && sm.qfull[lane] != 0);
+  if (t < nch) {
+    const int k = (int)(q.x & 255u), L = (int)((q.x >> 8) & 255u), e = (int)q.y + (t - (int)q.z);
+    if (!((sm.qfull[L - l0] >> k) & 1)) {  // quiet: the shift stands (undone if L > J)
+      if (L > lo) {
+        sm.lmeta[e] = wi | (uint32_t)k << 10 | (uint32_t)(L - lo) << 12;
+        sm.lold[e] = old;
       }
+      sm.win[wi] = nw;
+    } else if (L > lo) {
+      sm.lmeta[e] = LXB_NOLOG;
     }
-    if (!quiet && lane == 0) atomicOr(&sm.qfull[L - l0], 1 << k);
   }
   __syncthreads();
   return l0 + nl;
@@ -1539,8 +1556,15 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     const int L = k / LXB_ITEMSLOTS, q = k % LXB_ITEMSLOTS;
     const unsigned char* Bg = P.blobs + sm.bref[L].off;
     const lxb_bhdr* bh = reinterpret_cast<const lxb_bhdr*>(Bg);
-    sm.litem[L][q] =
-        q < bh->n_items ? (int16_t)reinterpret_cast<const lxb_bitem*>(Bg + bh->item[q])->item : -1;
+    uint32_t v = LXB_QNONE;
+    if (q < bh->n_items) {
+      const lxb_item it = P.items[reinterpret_cast<const lxb_bitem*>(Bg + bh->item[q])->item];
+      v = (it.n_eager <= 32 && it.ch0 < (1 << 24) &&
+           !(it.flags & (LXB_IT_NONRES | LXB_IT_DECAYS)))
+              ? (uint32_t)it.ch0 | (uint32_t)it.n_eager << 24
+              : LXB_QFULL;
+    }
+    sm.qinfo[L][q] = v;
   }
   if (t < LXB_ITEMSLOTS) {  // no slot holds an output yet
     sm.vhmask[t] = 0;
@@ -1638,26 +1662,23 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       if (t == 0) sm.gkey[gpar ^ 1] = 0x7fffffff;  // the next step's (nobody posts it before
                                                    // this step's barrier)
       const int l0 = resume ? lo + 1 : lo;  // (J's other items are done)
-      const int qhi = quiet_pass(P, run, sm, s, rank, lo, l0, hi, i, r_x);
+      uint32_t vis;  // the layers l0 + b that still have items here (the same in every thread)
+      const int qhi = quiet_pass(P, run, sm, s, rank, lo, l0, hi, i, r_x, vis);
       PROF(PR_ITEMS);
-      // the items each layer still has here (the same in every thread)
-      auto want_of = [&](int L) -> int {
-        return (resume && L == lo) ? rs_mask : sm.qfull[L - l0];
-      };
-      auto next_visit = [&](int L) -> int {
-        for (; L < qhi; L++)
-          if (want_of(L)) return L;
-        return -1;
-      };
+      bool at_lo = resume && (rs_mask || held_out);  // J first: its pending items, its outputs
+      auto peek = [&]() -> int { return at_lo ? lo : (vis ? l0 + __ffs(vis) - 1 : -1); };
       {
-        const int f = next_visit(lo);
+        const int f = peek();
         if (f >= 0) restage(f);
       }
       int nlog = sm.qlog, sL = -1, pend = 0, outL = 0;
-      for (int L = lo; L < qhi; L++) {
-        const int want = want_of(L);
+      for (;;) {
+        const int L = peek();
+        if (L < 0) break;
+        if (at_lo) at_lo = false;
+        else vis &= vis - 1;
+        const int want = (resume && L == lo) ? rs_mask : sm.qfull[L - l0];
         const bool held = resume && L == lo && held_out;  // J's outputs from the last step
-        if (!want && !held) continue;
         if (L > lo &&
             __syncthreads_or(t == 0 && *reinterpret_cast<volatile int*>(&sm.gkey[gpar]) < 2 * L))
           break;
@@ -1668,7 +1689,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
           restage(L);  // (in flight already, normally)
           const unsigned char* B = take(i);
           {  // the next layer with items here: its blob into the other buffer
-            const int nx = next_visit(L + 1);
+            const int nx = peek();
             inflight = nx;
             if (nx >= 0 && t == NT - 32 && !sm.broken)
               stage_issue(P, sm, stage, (int)((stp + 1) & 1), nx);
