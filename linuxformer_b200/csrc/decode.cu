@@ -63,6 +63,7 @@ namespace cg = cooperative_groups;
 #define LXB_QTASKS (LXB_QLAYERS * LXB_ITEMSLOTS)
 #define LXB_QNONE 0xffffffffu
 #define LXB_QFULL 0x40000000u
+#define LXB_QOUT 0x80000000u   // (qinfo) the item's head has out_proj entries
 #ifndef LXB_GROUPS
 #define LXB_GROUPS 1    // runs of GDN-only layers as optimistic group steps
 #endif
@@ -838,7 +839,9 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
   if (warp == 1 && lane < R)
     sm.g[lane] = (bi.flags & LXB_IT_DECAYS) ? item_g(sm, B, bi, lane, w_in, r_in) : 0.0f;
   __syncthreads();
-  const int nq = sm.nq, nk = sm.nk;
+  // a head without out_proj entries: its readout has no use (nothing of it reaches the
+  // residual), only a key's write and a decay change its state
+  const int nq = (bi.flags & LXB_IT_OUT) ? sm.nq : 0, nk = sm.nk;
   int anyg = 0;
 #pragma unroll
   for (int r = 0; r < R; r++) anyg |= sm.g[r] != 0.0f;
@@ -961,12 +964,13 @@ __device__ __forceinline__ float quiet_chan(const Dev& P, const Smem& sm, const 
 
 // A group step's quiet pass over layers [l0, qhi), qhi = min(hi, l0 + LXB_QLAYERS) (returned):
 // every item of this CTA in those layers at once, a thread per query/key channel. An item that
-// cannot decay and whose query/key outputs are all zero changes nothing but its windows
-// (gdn_item would return at its first check): they are shifted here, logged for the undo when the
-// layer is after lo (the step's first), and the item is done. Every other item (one that is not
-// resident, has more than 32 such channels, may decay, has a nonzero output, or finds no room in
-// the log or the block) is left as it was, for the walk: sm.qfull, and vis (bit b: layer l0 + b
-// has such items). Also the layers' ring rows of this step. Ends with a block barrier.
+// cannot decay and whose key outputs are all zero (and query outputs too, if its head has
+// out_proj entries) changes nothing but its windows (gdn_item would return at its first check):
+// they are shifted here, logged for the undo when the layer is after lo (the step's first), and
+// the item is done. Every other item (one that is not resident, has more than 32 such channels,
+// may decay, has a nonzero output, or finds no room in the log or the block) is left as it was,
+// for the walk: sm.qfull, and vis (bit b: layer l0 + b has such items). Also the layers' ring
+// rows of this step. Ends with a block barrier.
 __device__ int quiet_pass(const Dev& P, const Run& run, Smem& sm, int s, int rank, int lo, int l0,
                           int hi, int step, float r, uint32_t& vis) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -979,10 +983,11 @@ __device__ int quiet_pass(const Dev& P, const Run& run, Smem& sm, int s, int ran
     if (lane < nl)
       for (int k = 0; k < LXB_ITEMSLOTS && sm.qinfo[L][k] != LXB_QNONE; k++) {
         const uint32_t qi = sm.qinfo[L][k];
-        if (qi == LXB_QFULL || !(qi >> 24)) continue;  // (no channel: nothing to do)
+        const int n = (int)((qi >> 24) & 63u);
+        if (qi == LXB_QFULL || !n) continue;  // (no channel: nothing to do)
         cnt++;
-        need += L > lo ? (int)(qi >> 24) : 0;
-        chn += (int)(qi >> 24);
+        need += L > lo ? n : 0;
+        chn += n;
       }
     int cb = cnt, nb = need, hb = chn;  // inclusive scans over the lanes
 #pragma unroll
@@ -1003,7 +1008,7 @@ __device__ int quiet_pass(const Dev& P, const Run& run, Smem& sm, int s, int ran
           full |= 1 << k;
           continue;
         }
-        const int n = (int)(qi >> 24), nd = L > lo ? n : 0;
+        const int n = (int)((qi >> 24) & 63u), nd = L > lo ? n : 0;
         if (!n) continue;
         if (off + nd <= LXB_LOGMAX && coff + n <= NT) {
           sm.qtask[pos] = make_uint4((uint32_t)k | (uint32_t)L << 8, (uint32_t)off, (uint32_t)coff, qi);
@@ -1061,7 +1066,8 @@ __device__ int quiet_pass(const Dev& P, const Run& run, Smem& sm, int s, int ran
     wi = c.win;
     old = sm.win[wi];
     const float v = quiet_chan(P, sm, c, P.u16 + sm.layers[L].ln_in, r, old, nw);
-    if (v != 0.0f) atomicOr(&sm.qfull[L - l0], 1 << (q.x & 255u));
+    // (a query matters only to a head with out_proj entries)
+    if (v != 0.0f && ((q.w & LXB_QOUT) || c.slot >= KD)) atomicOr(&sm.qfull[L - l0], 1 << (q.x & 255u));
   }
   __syncthreads();
   vis = __ballot_sync(0xffffffffu, lane < nl && sm.qfull[lane] != 0);
@@ -1561,7 +1567,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       const lxb_item it = P.items[reinterpret_cast<const lxb_bitem*>(Bg + bh->item[q])->item];
       v = (it.n_eager <= 32 && it.ch0 < (1 << 24) &&
            !(it.flags & (LXB_IT_NONRES | LXB_IT_DECAYS)))
-              ? (uint32_t)it.ch0 | (uint32_t)it.n_eager << 24
+              ? (uint32_t)it.ch0 | (uint32_t)it.n_eager << 24 | ((it.flags & LXB_IT_OUT) ? LXB_QOUT : 0u)
               : LXB_QFULL;
     }
     sm.qinfo[L][q] = v;
