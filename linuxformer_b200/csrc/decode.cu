@@ -159,6 +159,7 @@ struct __align__(16) Smem {
   uint4 qtask[LXB_QTASKS];         // a quiet pass's items: k | layer << 8, log, channel, qinfo
   int qfull[LXB_QLAYERS];          // per layer of the pass: the items that need a full run
   int qn, qlog, qnch;              // the pass's item count, undo log entries, channels
+  uint32_t qbad;                   // an MLP step's items with a nonzero key (or query) output
   int wflag[2];                    // some item of the step wrote (pushed by the writer)
   int kmask[LXB_NK];               // out_proj step: active value heads per key head
   alignas(16) uint16_t on[LXB_ITEMSLOTS][R * VD];  // the gated norm's output per item slot
@@ -938,18 +939,16 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
   return item_tail(P, sm, B, bi, bm, nk, w_in, r_in) ? ITEM_WROTE : ITEM_DONE;
 }
 
-// A query/key channel evaluated from the global tables (its entries in the entry pool, the input
-// norm's weights w in the u16 pool): the same sums in the same order as eager_channel, the
-// window left as it is (nw: the shifted one)
-__device__ __forceinline__ float quiet_chan(const Dev& P, const Smem& sm, const lxb_chan& c,
-                                            const uint16_t* w, float r, const uint2 win, uint2& nw) {
-  const uint32_t* e = P.ent + c.ent;
-  const int ne = c.n;
+// A query/key channel's projection by one thread: its in_proj_qkv row's products (the input
+// norm taken per column, weights w) summed in entry order from +0, the same sum as
+// eager_channel's; the entries e (column | bf16 << 16) staged or in global memory
+__device__ __forceinline__ float chan_sum(const Smem& sm, const uint32_t* e, int ne,
+                                          const uint16_t* w, float r) {
   float ps = 0.0f;
   for (int k = 0; k < ne; k += 8) {  // 8 entries' loads in flight, then the sum in order
     uint32_t en[8];
 #pragma unroll
-    for (int q = 0; q < 8; q++) en[q] = k + q < ne ? __ldg(e + k + q) : 0u;
+    for (int q = 0; q < 8; q++) en[q] = k + q < ne ? e[k + q] : 0u;
     float pv[8];
 #pragma unroll
     for (int q = 0; q < 8; q++)
@@ -959,7 +958,14 @@ __device__ __forceinline__ float quiet_chan(const Dev& P, const Smem& sm, const 
     for (int q = 0; q < 8; q++)
       if (k + q < ne) ps = lx_add(ps, pv[q]);
   }
-  return conv_step(win, lx_rb(ps), c.t01, c.t23, nw);
+  return ps;
+}
+
+// A query/key channel evaluated from the global tables (its entries in the entry pool, the input
+// norm's weights w in the u16 pool), the window left as it is (nw: the shifted one)
+__device__ __forceinline__ float quiet_chan(const Dev& P, const Smem& sm, const lxb_chan& c,
+                                            const uint16_t* w, float r, const uint2 win, uint2& nw) {
+  return conv_step(win, lx_rb(chan_sum(sm, P.ent + c.ent, c.n, w, r)), c.t01, c.t23, nw);
 }
 
 // A group step's quiet pass over layers [l0, qhi), qhi = min(hi, l0 + LXB_QLAYERS) (returned):
@@ -1089,11 +1095,44 @@ __device__ int quiet_pass(const Dev& P, const Run& run, Smem& sm, int s, int ran
 
 // --- the owned rows ---------------------------------------------------------------------------
 // The MLP over this CTA's rows: own[row] = bf16(x + bf16(sum_u h_u w_d)), h_u re-evaluated here;
-// the units and entries are in the staged blob (m: its MLP part)
-__device__ void mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, const lxb_bmlp& m,
-                          float* own) {
+// the units and entries are in the staged blob (m: its MLP part).
+// With w_in (the staged input norm, r_in its factor), the blob's GDN items are checked on the way,
+// a thread per query/key channel on the top threads while the units are summed: an item that
+// cannot decay and whose key outputs (and query outputs, if its head has out_proj entries) are
+// all zero is done here (its windows shifted). Returns the items that need gdn_item: the others
+// (the same in every thread; sm.qbad cleared by the caller before a block barrier).
+__device__ uint32_t mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, const lxb_bmlp& m,
+                              float* own, const uint16_t* w_in = nullptr, float r_in = 0.0f) {
   const int t = threadIdx.x;
   const lxb_bunit* units = reinterpret_cast<const lxb_bunit*>(B + m.units);
+  uint32_t full = 0;  // items not taken here
+  int qk = -1;        // this thread's item, and channel (qa, qb)
+  uint4 qa = make_uint4(0u, 0u, 0u, 0u), qb = qa;
+  bool qout = false;
+  if (w_in) {
+    const lxb_bhdr* bh = reinterpret_cast<const lxb_bhdr*>(B);
+    int qn = 0;
+    for (int k = 0; k < bh->n_items; k++) {
+      const lxb_bitem* bi = reinterpret_cast<const lxb_bitem*>(B + bh->item[k]);
+      if (bi->n_eager > 32 || (bi->flags & (LXB_IT_NONRES | LXB_IT_DECAYS))) full |= 1u << k;
+      else qn += bi->n_eager;
+    }
+    int idx = t - (NT - qn);
+    if (idx >= 0)
+      for (int k = 0; k < bh->n_items; k++) {
+        const lxb_bitem* bi = reinterpret_cast<const lxb_bitem*>(B + bh->item[k]);
+        if ((full >> k) & 1) continue;
+        if (idx < bi->n_eager) {
+          const uint4* ch = reinterpret_cast<const uint4*>(B + bi->eager);
+          qa = ch[2 * idx];
+          qb = ch[2 * idx + 1];
+          qout = (bi->flags & LXB_IT_OUT) != 0;
+          qk = k;
+          break;
+        }
+        idx -= bi->n_eager;
+      }
+  }
   // the gate and up entries of all units are contiguous in the blob: their products first, all
   // threads at once, into prod (the units' entries in order), then one thread per unit sums its
   // own products in order, so the sums are the sequential ones
@@ -1140,6 +1179,14 @@ __device__ void mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, const 
     const float act = lx_rbf(d_silu(gg));
     sm.hbuf[u] = lx_rbf(lx_mul(act, uu));
   }
+  uint2 qnw = make_uint2(0u, 0u);
+  if (qk >= 0) {  // an item's channel (a query matters only to a head with out_proj entries)
+    const float v = conv_step(sm.win[qb.y],
+                              lx_rb(chan_sum(sm, reinterpret_cast<const uint32_t*>(B + qa.x),
+                                             (int)(qa.y & 0xffffu), w_in, r_in)),
+                              qa.w, qb.x, qnw);
+    if (v != 0.0f && (qout || (qa.y >> 16) >= KD)) atomicOr(&sm.qbad, 1u << qk);
+  }
   __syncthreads();
   const int r0 = m.r0;
   const int32_t* rp = reinterpret_cast<const int32_t*>(B + m.down_ptr);
@@ -1167,6 +1214,9 @@ __device__ void mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, const 
     if (any) res = lx_rbf(lx_add(xv, lx_rbf(sd)));
     own[k] = res;
   }
+  const uint32_t bad = w_in ? sm.qbad : 0u;
+  if (qk >= 0 && !((bad >> qk) & 1)) sm.win[qb.y] = qnw;  // a quiet item: its windows shift
+  return full | bad;
 }
 
 // every owned MLP row [r0, r0 + nr) unchanged (no staged MLP tables)
@@ -1843,14 +1893,27 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       }
       if (ly.has_mlp) {  // (a step without one needs no barrier here: nothing above is read
         norm_into(sm.xm, sm.x, w_post, r);  // by another thread before the items' own barriers)
+        if (t == 0) sm.qbad = 0u;
         __syncthreads();
       }
       if (P.nbuf == 2) issue_next(stp);  // the next step's blob: its buffer was read a step ago
       PROF(PR_NORM);
+      // with an MLP the items are checked on its way and only the others run after it (they are
+      // independent: the items read x, the MLP xm, and neither changes x before the barrier)
+      const bool merged = ly.has_gdn && B && mlp;
+      uint32_t todo = ly.has_gdn && B && !merged ? 0xffffffffu : 0u;  // items for gdn_item
+      if (ly.has_mlp) {
+        if (mlp) todo |= mlp_owner(P, sm, B, mh, sm.own[ph & 1], merged ? w_in : nullptr, r);
+        else copy_owner(sm, mr0, mnr, sm.own[ph & 1]);
+        __syncthreads();
+        push_rows(P, sm, sm.own[ph & 1], ph & 1, mr0, mnr, cluster);
+      }
+      PROF(PR_MLP);
       bool wrote = false;
-      if (ly.has_gdn && B) {
+      if (ly.has_gdn && B && todo) {
         const lxb_bhdr* bhp = reinterpret_cast<const lxb_bhdr*>(B);  // (dynamic index: in smem)
         for (int k = 0; k < bh.n_items; k++) {
+          if (!((todo >> k) & 1)) continue;
           const lxb_bitem bi = *reinterpret_cast<const lxb_bitem*>(B + bhp->item[k]);
           wrote |= gdn_item(P, run, sm, B, bi, rec, conv, bm, s, L, i, w_in, r, nullptr, nullptr,
                             0) == ITEM_WROTE;
@@ -1858,13 +1921,6 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       }
       if (wrote && t < C) *cluster.map_shared_rank(&sm.wflag[ph & 1], t) = 1;
       PROF(PR_ITEMS);
-      if (ly.has_mlp) {
-        if (mlp) mlp_owner(P, sm, B, mh, sm.own[ph & 1]);
-        else copy_owner(sm, mr0, mnr, sm.own[ph & 1]);
-        __syncthreads();
-        push_rows(P, sm, sm.own[ph & 1], ph & 1, mr0, mnr, cluster);
-      }
-      PROF(PR_MLP);
       cluster.sync();
       PROF(PR_SYNC);
       const int fl = *reinterpret_cast<volatile int*>(&sm.wflag[ph & 1]);
