@@ -1881,15 +1881,18 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         mnr = o.mr1 - o.mr0;
       }
       if (ly.has_gdn) {
-        // this step's GDN input row into the ring (each CTA its block; rank 0 the factor)
+        // this step's GDN input row into the ring (each CTA its block, 8 rows a thread of the
+        // last two warps, which have the least to do at a step's start; rank 0 the factor)
         const size_t slot = ((size_t)s * P.n_layers + L) * 4 + (i & 3);
-        uint16_t* rg = run.ring + slot * H + rank * P.blk;
-        for (int k = t; k < P.blk / 2; k += NT) {
-          const float* xv = sm.x + rank * P.blk + 2 * k;
-          reinterpret_cast<uint32_t*>(rg)[k] =
-              (uint32_t)lx_rb(xv[0]) | ((uint32_t)lx_rb(xv[1]) << 16);
+        uint4* rg = reinterpret_cast<uint4*>(run.ring + slot * H + rank * P.blk);
+        for (int k = t - (NT - 64); k >= 0 && k < P.blk / 8; k += 64) {
+          const float* xv = sm.x + rank * P.blk + 8 * k;
+          rg[k] = make_uint4((uint32_t)lx_rb(xv[0]) | ((uint32_t)lx_rb(xv[1]) << 16),
+                             (uint32_t)lx_rb(xv[2]) | ((uint32_t)lx_rb(xv[3]) << 16),
+                             (uint32_t)lx_rb(xv[4]) | ((uint32_t)lx_rb(xv[5]) << 16),
+                             (uint32_t)lx_rb(xv[6]) | ((uint32_t)lx_rb(xv[7]) << 16));
         }
-        if (rank == 0 && t == 0) run.ring_r[slot] = r;
+        if (rank == 0 && t == NT - 1) run.ring_r[slot] = r;
       }
       if (ly.has_mlp) {  // (a step without one needs no barrier here: nothing above is read
         norm_into(sm.xm, sm.x, w_post, r);  // by another thread before the items' own barriers)
