@@ -33,6 +33,11 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+# The CPU baseline (the OpenMP restatement) runs on every host thread this process may use, also
+# under torchrun, which sets OMP_NUM_THREADS=1 for its ranks (set before anything loads OpenMP).
+HOST_THREADS = len(os.sched_getaffinity(0))
+os.environ["OMP_NUM_THREADS"] = str(HOST_THREADS)
+
 BASELINE_TOKS = 6017.4  # the reference's megakernel, single-stream, H100
 FALLBACK_HBM = 6650.0
 
@@ -133,7 +138,7 @@ def cpu_sample(chip, state, n_tokens: int):
     t0 = time.perf_counter()
     preds, _, _, counts = o.decode(st, [0], n_tokens, counts=True)
     dt = time.perf_counter() - t0
-    return n_tokens / dt, preds, counts, os.cpu_count()
+    return n_tokens / dt, preds, counts, HOST_THREADS
 
 
 def main():
@@ -190,7 +195,7 @@ def main():
             "warmup": a.warmup, "ms_per_step": round(1000 * dt / a.steps, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic", "config": dict(config, tokens_per_step=per),
-            "cpu_baseline": {"value": round(v, 2), "unit": "tok/s", "cores": os.cpu_count(),
+            "cpu_baseline": {"value": round(v, 2), "unit": "tok/s", "cores": HOST_THREADS,
                              "kind": "port", "sample": f"{a.steps} x {per} tokens of the c2 stream"},
             "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}))
