@@ -57,6 +57,22 @@ def test_corrupt_images_are_rejected(image):
     b = bytearray(image); b[ch_off + 8:ch_off + 12] = np.uint32(1 << 20).tobytes(); bad.append(b)
     # a truncated image
     bad.append(bytearray(image[:len(image) // 2]))
+    # an owner's MLP row range not 8-aligned; a layer's MLP rows not the owners' ranges
+    ow_off = int(hdr["sec"][tables.SEC.index("owners")][0])
+    mr1 = np.frombuffer(image[ow_off + 4:ow_off + 8], np.int32)[0]
+    b = bytearray(image); b[ow_off + 4:ow_off + 8] = np.int32(mr1 + 1).tobytes(); bad.append(b)
+    ly_off = int(hdr["sec"][tables.SEC.index("layers")][0])
+    f = tables.LAYER.fields["mrow1"][1]
+    v = np.frombuffer(image[ly_off + f:ly_off + f + 4], np.int32)[0]
+    b = bytearray(image); b[ly_off + f:ly_off + f + 4] = np.int32(v + 8).tobytes(); bad.append(b)
+    # the channel table naming another resident window than the blob (first item's first channel)
+    it_off = int(hdr["sec"][tables.SEC.index("items")][0])
+    it0 = np.frombuffer(image[it_off:it_off + tables.ITEM.itemsize], tables.ITEM)[0]
+    assert it0["n_eager"] > 0 and not (it0["flags"] & tables.IT_NONRES)
+    ch0 = int(it0["ch0"])
+    w = ch_off + ch0 * tables.CHAN.itemsize + tables.CHAN.fields["win"][1]
+    win = np.frombuffer(image[w:w + 4], np.uint32)[0]
+    b = bytearray(image); b[w:w + 4] = np.uint32(win ^ 1).tobytes(); bad.append(b)
     for k, img in enumerate(bad):
         assert _create(img) == -2, k
     assert _create(image, cluster=8) == -2  # built for 16
