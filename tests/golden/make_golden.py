@@ -15,7 +15,8 @@ its checkout, builds the seeded config-1 stack as a stock model, seeds fp32 recu
 - ``c1_prefill.npz``: two 256-token chunks of seeded random ids run as chunked prefill (the
   verified mode), the argmax at every position, the same state summaries after each chunk.
 
-Run here (needs /root/reference); the GPU box only reads the .npz files:
+Run where the reference's checkout is (its directory in LXB_REFERENCE); the GPU tests only read
+the .npz files:
 
     python tests/golden/make_golden.py
 """

@@ -7,11 +7,13 @@ from the reference's checkout and saves a small two-layer state (the layout does
 the tensor shapes, so small tensors keep the fixture at a few KB) with host fields of every kind.
 tests/test_snapshot.py rebuilds the same values with ``fixture()`` below and reads the file.
 
-Run here (needs /root/reference); the GPU box only reads the .safetensors file:
+Run where the reference's checkout is (its directory in LXB_REFERENCE); the tests only read
+the .safetensors file:
 
     python tests/golden/make_snapshot.py
 """
 
+import os
 import sys
 from pathlib import Path
 from types import SimpleNamespace
@@ -37,7 +39,7 @@ def fixture():
 
 
 def main():
-    sys.path.insert(0, "/root/reference/lx")
+    sys.path.insert(0, os.environ.get("LXB_REFERENCE", "/root/reference") + "/lx")
     from lx.session import save_safe
 
     state, host, ref = fixture()

@@ -5,6 +5,7 @@ reference's checkout is present, load with the reference's own reader; the bitwi
 every changed element; on a GPU a decoded stream's state goes through a file and back."""
 
 import importlib.util
+import os
 import sys
 from pathlib import Path
 
@@ -16,7 +17,7 @@ from linuxformer_b200 import chip as C
 from linuxformer_b200 import snapshot
 
 GOLD = Path(__file__).parent / "golden"
-REF = Path("/root/reference/lx")
+REF = Path(os.environ.get("LXB_REFERENCE", "/root/reference")) / "lx"
 
 
 def _fixture():
