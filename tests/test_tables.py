@@ -26,10 +26,12 @@ class Image:
         return self.b[off:off + int(ref["bytes"])]
 
 
-@pytest.fixture(scope="module")
-def built(c1_chip):
-    img, _ = tables.build_image(c1_chip, 16)
-    return c1_chip, 16, Image(img)
+@pytest.fixture(scope="module", params=["c1", "c2"])
+def built(request, c1_chip):
+    """Config 1 (two dense-ish layers) and config 2 (the bench's 37 layers, GDN-only runs)."""
+    chip = c1_chip if request.param == "c1" else C.c2(1)
+    img, _ = tables.build_image(chip, 16)
+    return chip, 16, Image(img)
 
 
 def test_mlp_row_ranges_tile_the_changing_rows(built):
