@@ -86,8 +86,10 @@ int lxb_decode(lxb_plan* plan, const uint64_t* state_ptrs, uint32_t* bitmaps, in
                int n_forced, int n_tokens, int32_t* preds, int32_t* inputs, void* cuda_stream);
 
 /* Device scratch lxb_decode needs for n_streams streams (a ring of the last 4 steps' residual
- * rows per layer, from which the lazily kept conv windows are recomputed). The caller allocates
- * it (16-byte aligned); its contents need no initialisation and do not outlive a call. */
+ * rows per layer, from which the lazily kept conv windows are recomputed, and the head helpers'
+ * exchange area). The caller allocates it (16-byte aligned) and need not initialise it: the
+ * launch clears, on its stream, the words that must start cleared. Its contents do not outlive a
+ * call, so one buffer may serve several plans in turn, but not two launches at once. */
 size_t lxb_scratch_bytes(const lxb_plan* plan, int n_streams);
 
 /* lxb_decode for callers that cannot allocate device memory. No counterpart in the reference

@@ -36,6 +36,7 @@
 
 #include <climits>
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <new>
 #include <stddef.h>
@@ -2101,6 +2102,8 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(sm.sptr[L][1]) + (size_t)ch * 4) =
         sm.win[k];
   }
+  if (run.n_help > 0 && rank == 0 && t == 0)  // a helper still waiting for a token may leave
+    st_release_u64(run.hseq, run.epoch | 0xffffffffull);
   cluster.sync();  // every ring write of the launch is visible cluster-wide
   materialize(P, run, sm, s, rank, run.n_tokens);
   cluster.sync();  // no CTA leaves while another may still read its shared memory
@@ -2140,7 +2143,6 @@ struct lxb_plan {
   int max_clusters;
   int head_helpers;              // the most head helper clusters a single-stream launch may use
   int help_drill;                // helpers that never answer (lxb_plan_set_head_helpers < 0)
-  unsigned long long launches;   // launches so far (the helpers' exchange tag)
   unsigned long long* prof;
   int smem;  // dynamic shared memory per CTA: Smem, then the staging buffers
 };
@@ -2547,7 +2549,6 @@ extern "C" int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb
   p->max_clusters = ncl;
   p->head_helpers = LXB_HEADSLICES - 1;
   p->help_drill = 0;
-  p->launches = 0;
   *out = p;
   return LXB_OK;
 }
@@ -2567,6 +2568,9 @@ extern "C" size_t lxb_scratch_bytes(const lxb_plan* p, int n_streams) {
       ring_bytes(p, n_streams) + (size_t)n_streams * p->hdr.n_layers * 4 * sizeof(float);
   return ((base + 15) & ~(size_t)15) + head_xchg_bytes(p);
 }
+
+// the head helpers' launch epochs (see decode_launch)
+static std::atomic<unsigned long long> g_launch_epoch{0};
 
 static int decode_launch(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitmaps,
                          int sync_bitmaps, void* scratch, const uint16_t* embed, int n_streams,
@@ -2597,11 +2601,19 @@ static int decode_launch(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitm
   if (n_streams == 1 && n_tokens < 0x7fffffff)
     n_help = std::min(std::min(p->head_helpers, LXB_HEADSLICES - LXB_HEADMAIN), p->max_clusters - 1);
   if (n_help < 0) n_help = 0;
-  p->launches++;
+  // The helpers' exchange words are tagged (launch epoch | token + 1). The epoch comes from one
+  // counter for the whole process, so no two launches share it, whichever plans they belong to;
+  // and the words are cleared on the stream before the launch, so nothing another launch (or
+  // another process) left in this scratch memory can match a tag: 0 is never a valid tag.
+  const unsigned long long epoch = (g_launch_epoch.fetch_add(1) + 1) << 32;
+  if (n_help > 0) {
+    e = cudaMemsetAsync(xg + (size_t)H * 4, 0, head_xchg_bytes(p) - (size_t)H * 4, st);
+    if (e) return cuda_rc(e);
+  }
   Run run{state_ptrs, bitmaps, ring, ring_r, embed, forced, n_forced, n_tokens, preds, inputs,
           p->prof, n_streams, n_help, reinterpret_cast<float*>(xg),
           reinterpret_cast<unsigned long long*>(xg + (size_t)H * 4),
-          reinterpret_cast<uint4*>(xg + (size_t)H * 4 + 16), p->launches << 32, p->help_drill};
+          reinterpret_cast<uint4*>(xg + (size_t)H * 4 + 16), epoch, p->help_drill};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -2632,9 +2644,11 @@ extern "C" int lxb_decode(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bit
 // CUDA-aware and hands out only the buffers it manages (state, tokens, predictions). For them the
 // decode's scratch (the 4-step residual ring of the lazily kept conv windows) lives in this
 // file-scope device array instead of a caller buffer. Every GPU that loads the library holds it
-// until the process exits. All calls on a device share it and it keeps the last call's contents;
-// the kernel writes every ring slot before it reads it, so nothing needs clearing, but two calls
-// that overlap on the GPU (other streams, other threads) race on it.
+// until the process exits. All calls on a device share it and it keeps the last call's contents.
+// The kernel writes every ring slot before it reads it; the head helpers' exchange words, which
+// must not match a tag from an earlier call, are cleared on the stream before every launch that
+// uses helpers (decode_launch). Two calls that overlap on the GPU (other streams, other threads)
+// race on the array.
 static __device__ __align__(256) unsigned char lxb_noalloc_scratch[LXB_NOALLOC_MAX_SCRATCH];
 
 static std::mutex g_noalloc_mu;

@@ -137,3 +137,32 @@ def test_head_helpers_match_and_fall_back():
         assert (preds[0].cpu().numpy() == p).all(), helpers
         flagged = bool(dec.status().status & S_HELPER)
         assert flagged == (helpers < 0 and dec.max_clusters > 1), (helpers, dec.status().status)
+
+
+def test_two_plans_share_one_scratch(c1_chip):
+    """Two plans (the same chip, different machine states) take turns on ONE scratch buffer,
+    with launches of equal lengths: 1 token each, then 9 tokens each. The head helpers' exchange
+    words in that buffer are tagged per launch, so neither plan may take the other's stale head
+    input or maximum; both streams equal their own oracle runs bit for bit."""
+    import torch
+
+    sts = [C.c1_state(c1_chip, 0), C.c1_state(c1_chip, 5)]
+    decs = [_decoder(c1_chip, 16), _decoder(c1_chip, 16)]
+    dss = [d.states([st]) for d, st in zip(decs, sts)]
+    shared = decs[0].scratch(1)
+    got = [[], []]
+    last = [0, 7]
+    for n in (1, 1, 9, 9):
+        for k in (0, 1):
+            f = torch.tensor([[last[k]]], dtype=torch.int32, device=decs[k].dev)
+            preds = torch.empty((1, n), dtype=torch.int32, device=decs[k].dev)
+            decs[k].launch(dss[k].ptrs, dss[k].bitmaps, f, n, preds, None, scratch=shared)
+            p = preds[0].cpu().numpy().tolist()
+            got[k] += p
+            last[k] = p[-1]
+    o = Oracle(c1_chip)
+    for k, first in ((0, 0), (1, 7)):
+        host = sts[k].copy()
+        want, _, _ = o.decode(host, [first], len(got[k]))
+        assert got[k] == want.tolist(), k
+        _same_state(dss[k], 0, host)
