@@ -141,6 +141,59 @@ int lxb_plan_max_clusters(const lxb_plan* plan);
 
 void lxb_plan_destroy(lxb_plan* plan);
 
+/* --- The chunked prefill (verified mode) -----------------------------------------------------
+ *
+ * The reference checks a proposed trace by running it as chunked prefill: Session.verify
+ * (lx/lx/session.py:86-116) embeds each chunk and calls Fast.forward (lx/lx/fast.py:252-257) and
+ * Fast.head_argmax (fast.py:544-550), then compares every position's argmax with the next token.
+ * A prefill plan holds the chip's tables in a token-parallel layout (format in
+ * linuxformer_b200/csrc/lxb_prefill.h, built by linuxformer_b200.prefill_tables); one call runs one
+ * chunk of T tokens through every chip layer, updating the caller's state in place (the HF cache
+ * layout, as lxb_decode), with the same results as T single-token decode steps with every input
+ * forced: predictions, conv windows and recurrent states bit for bit. Calls are asynchronous on the
+ * given stream (the plan also runs work on a stream of its own, joined back before the call's last
+ * operation); the plan's device must be current; one call at a time per plan. */
+typedef struct lxb_prefill_plan lxb_prefill_plan;
+
+/* Validate a prefill image on the host (every offset, count and index); 0 or LXB_E_IMAGE. */
+int lxb_prefill_check_image(const void* image, size_t bytes);
+
+/* Validate and upload a prefill image to the current device. Replaces Fast.__init__'s packing of
+ * the live rows and columns (lx/lx/fast.py:172-248). LXB_E_IMAGE for a malformed image,
+ * LXB_E_DEVICE below compute capability 10. */
+int lxb_prefill_plan_create(const void* image, size_t bytes, lxb_prefill_plan** out);
+
+/* Device scratch one call of T tokens needs (the caller allocates it, 256-byte aligned, no
+ * initialisation; a call for fewer tokens fits in it). */
+size_t lxb_prefill_scratch_bytes(const lxb_prefill_plan* plan, int T);
+
+/* Verify one chunk: embed tokens[0..T) (DEVICE int32; row offset + id of the DEVICE bf16 embedding
+ * [rows][2560]), run the chip layers on the state (state_ptrs: a DEVICE array of n_layers * 2
+ * uint64, recurrent and conv pointers per layer), write preds[i] (DEVICE int32 [T]) = the head's
+ * first argmax at position i, and, if first_wrong (DEVICE int32) is not NULL, the first i < T - 1
+ * with preds[i] != tokens[i + 1], or -1. A token id outside the embedding is clamped and reported
+ * by lxb_prefill_status (LXB_S_TOKEN). Replaces one chunk of Session.verify
+ * (lx/lx/session.py:94-100) with Fast.forward and Fast.head_argmax. */
+int lxb_prefill(lxb_prefill_plan* plan, const uint64_t* state_ptrs, const uint16_t* embed,
+                const int32_t* tokens, int T, int32_t* preds, int32_t* first_wrong, void* scratch,
+                void* cuda_stream);
+
+/* The chip layers alone: h_in (DEVICE bf16 [T][2560], the embedded rows) -> h_out (DEVICE bf16
+ * [T][2560], may be NULL or h_in), updating the state. Replaces Fast.forward(h, cache)
+ * (lx/lx/fast.py:252-257). */
+int lxb_prefill_layers(lxb_prefill_plan* plan, const uint64_t* state_ptrs, const uint16_t* h_in,
+                       uint16_t* h_out, int T, void* scratch, void* cuda_stream);
+
+/* The head alone: preds[i] = the first argmax of the head over the final norm of h[i] (DEVICE bf16
+ * [T][2560]). Replaces Fast.head_argmax(h) (lx/lx/fast.py:544-550). */
+int lxb_prefill_head(lxb_prefill_plan* plan, const uint16_t* h, int T, int32_t* preds,
+                     void* scratch, void* cuda_stream);
+
+/* The prefill plan's status word (LXB_S_TOKEN), after the stream has synchronised. */
+int lxb_prefill_status(lxb_prefill_plan* plan, lxb_error* err);
+int lxb_prefill_status_clear(lxb_prefill_plan* plan);
+void lxb_prefill_plan_destroy(lxb_prefill_plan* plan);
+
 /* A short text for an error code. */
 const char* lxb_error_string(int code);
 

@@ -49,6 +49,15 @@ SIGNATURES = {
     "lxb_plan_max_clusters": (I, [P]),
     "lxb_plan_destroy": (None, [P]),
     "lxb_error_string": (ctypes.c_char_p, [I]),
+    "lxb_prefill_check_image": (I, [P, ctypes.c_size_t]),
+    "lxb_prefill_plan_create": (I, [P, ctypes.c_size_t, P]),
+    "lxb_prefill_scratch_bytes": (ctypes.c_size_t, [P, I]),
+    "lxb_prefill": (I, [P, P, P, P, I, P, P, P, P]),
+    "lxb_prefill_layers": (I, [P, P, P, P, I, P, P]),
+    "lxb_prefill_head": (I, [P, P, I, P, P, P]),
+    "lxb_prefill_status": (I, [P, P]),
+    "lxb_prefill_status_clear": (I, [P]),
+    "lxb_prefill_plan_destroy": (None, [P]),
 }
 
 

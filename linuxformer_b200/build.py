@@ -18,8 +18,9 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 OUT = PKG / "_build"
 LIB = OUT / "liblxb.so"
-SOURCES = [PKG / "csrc" / "decode.cu"]
-HEADERS = [PKG / "csrc" / "lxb_math.h", PKG / "csrc" / "lxb_plan.h", ROOT / "include" / "lxb.h"]
+SOURCES = [PKG / "csrc" / "decode.cu", PKG / "csrc" / "prefill.cu"]
+HEADERS = [PKG / "csrc" / "lxb_math.h", PKG / "csrc" / "lxb_plan.h", PKG / "csrc" / "lxb_prefill.h",
+           ROOT / "include" / "lxb.h"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-lineinfo",
               "-fmad=false", "-Xcompiler", "-fPIC", "-shared", f"-I{ROOT / 'include'}"]
 

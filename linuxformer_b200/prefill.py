@@ -1,0 +1,212 @@
+"""The chunked prefill (verified mode) on the B200 kernels, and the reference's ``Fast`` interface
+on it.
+
+    pf = Prefill(chip)                              # tables built and uploaded once
+    preds, first_wrong = pf.run(ptrs, tokens)       # one chunk; state updated in place
+
+``Fast`` is a drop-in for ``lx.fast.Fast`` (lx/lx/fast.py:172-550) where the reference's verified
+mode uses it: ``Session(c, model, machine, fast=Fast(model, n_chip, rows))`` calls
+``fast.forward(e, cache)`` and ``fast.head_argmax(h)`` per chunk (lx/lx/session.py:94-98), and
+``Linux.__init__`` builds it (lx/lx/linux.py:109). Both run on liblxb.so (include/lxb.h); the
+cache's conv and recurrent tensors are updated in place, as the reference's are. There is no CPU
+fallback: without a CUDA device or the built library the constructors raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import chip as C
+from . import prefill_tables
+from ._lib import S_ERRORS, Err, LxbError, check, lib
+
+
+class Prefill:
+    """A chip's prefill plan on one device."""
+
+    def __init__(self, chip: C.Chip, device=None, embed: torch.Tensor | None = None) -> None:
+        self.dev = torch.device(device or "cuda")
+        if self.dev.type != "cuda":
+            raise LxbError("the chip prefill runs on a CUDA device only")
+        if self.dev.index is None:
+            self.dev = torch.device("cuda", torch.cuda.current_device())
+        torch.cuda.set_device(self.dev)
+        self.chip = chip
+        self.image, self.stats = prefill_tables.build_image(chip)
+        self._img = np.frombuffer(self.image, np.uint8)
+        p = ctypes.c_void_p()
+        check(lib().lxb_prefill_plan_create(self._img.ctypes.data, len(self.image),
+                                            ctypes.byref(p)), "lxb_prefill_plan_create")
+        self.plan = p
+        if embed is None:
+            embed = torch.from_numpy(np.ascontiguousarray(chip.embed).view(np.int16)).to(self.dev)
+        self.embed = embed
+        self._scratch = None
+
+    def __del__(self):
+        p = getattr(self, "plan", None)
+        if p is not None and p.value:
+            try:
+                lib().lxb_prefill_plan_destroy(p)
+            except TypeError:  # interpreter shutdown
+                pass
+            self.plan = None
+
+    def scratch(self, T: int) -> torch.Tensor:
+        """Scratch for chunks of up to T tokens (kept and grown as needed)."""
+        nb = lib().lxb_prefill_scratch_bytes(self.plan, T)
+        if self._scratch is None or self._scratch.numel() < nb:
+            self._scratch = None
+            self._scratch = torch.empty(nb, dtype=torch.uint8, device=self.dev)
+        return self._scratch
+
+    def _stream(self, stream):
+        return (stream or torch.cuda.current_stream(self.dev)).cuda_stream
+
+    def launch(self, ptrs: torch.Tensor, tokens: torch.Tensor, preds: torch.Tensor,
+               first_wrong: torch.Tensor | None = None, stream=None,
+               scratch: torch.Tensor | None = None) -> None:
+        """Raw launch on device tensors (no host sync): ptrs int64 [n_layers, 2] (or [1, L, 2]),
+        tokens int32 [T], preds int32 [T], first_wrong int32 [1] or None."""
+        T = tokens.numel()
+        assert tokens.dtype == torch.int32 and tokens.is_contiguous()
+        assert preds.dtype == torch.int32 and preds.numel() >= T and preds.is_contiguous()
+        assert ptrs.dtype == torch.int64 and ptrs.numel() == 2 * self.chip.n_layers
+        sc = scratch if scratch is not None else self.scratch(T)
+        check(lib().lxb_prefill(self.plan, ptrs.data_ptr(), self.embed.data_ptr(),
+                                tokens.data_ptr(), T, preds.data_ptr(),
+                                first_wrong.data_ptr() if first_wrong is not None else None,
+                                sc.data_ptr(), self._stream(stream)), "lxb_prefill")
+
+    def status(self) -> Err:
+        e = Err()
+        check(lib().lxb_prefill_status(self.plan, ctypes.byref(e)), "lxb_prefill_status")
+        return e
+
+    def _raise_status(self) -> None:
+        e = self.status()
+        if e.status & S_ERRORS:
+            check(lib().lxb_prefill_status_clear(self.plan), "lxb_prefill_status_clear")
+            raise LxbError(f"device status {e.status:#x} (token {e.first_step})")
+
+    def run(self, ptrs: torch.Tensor, tokens, chunk: int | None = None):
+        """Verify tokens in chunks of `chunk` (default: all at once): returns (preds int32
+        device tensor [T], the first position i whose prediction is not tokens[i + 1], or -1).
+        Raises on a device error (a token id outside the embedding)."""
+        tok = torch.as_tensor(np.asarray(tokens, np.int32), device=self.dev)
+        T = tok.numel()
+        chunk = chunk or T
+        preds = torch.empty(T, dtype=torch.int32, device=self.dev)
+        first = -1
+        fws = []
+        for a in range(0, T, chunk):
+            part = tok[a:a + chunk]
+            f = torch.empty(1, dtype=torch.int32, device=self.dev)
+            self.launch(ptrs, part, preds[a:a + chunk], f)
+            fws.append((a, f))
+        torch.cuda.synchronize(self.dev)
+        self._raise_status()
+        for a, f in fws:  # within chunks, then across each chunk boundary
+            v = int(f.item())
+            if v >= 0:
+                first = a + v
+                break
+            b = a + chunk
+            if b < T and int(preds[b - 1]) != int(tok[b]):
+                first = b - 1
+                break
+        return preds, first
+
+    def layers(self, ptrs: torch.Tensor, h: torch.Tensor, out: torch.Tensor | None = None,
+               stream=None) -> torch.Tensor:
+        """The chip layers on rows h (bf16 [T, 2560] on the device), state updated in place."""
+        assert h.dtype == torch.bfloat16 and h.is_contiguous() and h.shape[-1] == C.H
+        T = h.numel() // C.H
+        out = torch.empty_like(h) if out is None else out
+        check(lib().lxb_prefill_layers(self.plan, ptrs.data_ptr(), h.data_ptr(), out.data_ptr(),
+                                       T, self.scratch(T).data_ptr(), self._stream(stream)),
+              "lxb_prefill_layers")
+        return out
+
+    def head(self, h: torch.Tensor, stream=None) -> torch.Tensor:
+        """The head's first argmax for rows h (bf16 [T, 2560]): int32 [T]."""
+        assert h.dtype == torch.bfloat16 and h.is_contiguous() and h.shape[-1] == C.H
+        T = h.numel() // C.H
+        preds = torch.empty(T, dtype=torch.int32, device=self.dev)
+        check(lib().lxb_prefill_head(self.plan, h.data_ptr(), T, preds.data_ptr(),
+                                     self.scratch(T).data_ptr(), self._stream(stream)),
+              "lxb_prefill_head")
+        return preds
+
+
+def cache_pointers(cache, n_chip: int, dev) -> torch.Tensor:
+    """[n_chip, 2] device pointers (recurrent, conv) of an HF DynamicCache's chip layers."""
+    rows = []
+    for L in range(n_chip):
+        cl = cache.layers[L]
+        r, c = cl.recurrent_states[0], cl.conv_states[0]
+        assert r.is_contiguous() and c.is_contiguous() and r.dtype == torch.float32
+        assert c.dtype == torch.bfloat16 and c.shape[-1] == C.TAPS
+        rows.append((r.data_ptr(), c.data_ptr()))
+    return torch.tensor(rows, dtype=torch.int64, device=dev)
+
+
+class Fast:
+    """lx.fast.Fast's interface (lx/lx/fast.py:172-550) on liblxb.so: the chip layers' forward
+    over a chunk (``forward``), the head's argmax (``head_argmax``) and the single-token step
+    (``decode``, a chunk of one token)."""
+
+    compile = False     # the reference's flags, kept for its callers; nothing to compile here
+    lean = False
+    head_block = 8192
+    stats = None
+    idle_skip = False
+
+    def __init__(self, model, n_chip: int, rows: slice | None = None) -> None:
+        from .mega import chip_from_model
+
+        self.model, self.n_chip, self.rows = model, n_chip, rows
+        self.dev = next(model.parameters()).device
+        offset = rows.start if rows is not None else 0
+        chip = chip_from_model(model, n_chip, rows, offset)
+        emb = model.model.embed_tokens.weight
+        chip.embed = chip.embed[:, :0]  # the kernels read the model's own embedding
+        self.pf = Prefill(chip, device=self.dev, embed=emb.view(torch.int16))
+        w = model.lm_head.weight if rows is None else model.lm_head.weight[rows]
+        self.head_cols = (w != 0).any(0).nonzero()[:, 0]
+        self.w_head = w[:, self.head_cols]
+
+    @torch.no_grad()
+    def forward(self, h: torch.Tensor, cache) -> torch.Tensor:
+        """h (1, T, hidden) -> (1, T, hidden), updating the cache's conv and recurrent states."""
+        x = h[0].contiguous()
+        out = self.pf.layers(cache_pointers(cache, self.n_chip, self.dev), x)
+        return out[None]
+
+    @torch.no_grad()
+    def decode(self, h: torch.Tensor, cache) -> torch.Tensor:
+        """One token: h (1, hidden) -> (1, hidden)."""
+        return self.pf.layers(cache_pointers(cache, self.n_chip, self.dev), h.contiguous())
+
+    @torch.no_grad()
+    def head_argmax(self, h: torch.Tensor, block: int | None = None) -> torch.Tensor:
+        """The output head's argmax over the rows given at construction, for h (T, hidden)."""
+        return self.pf.head(h.contiguous()).long()
+
+    def to(self, dev) -> "Fast":
+        if torch.device(dev) != self.dev:
+            raise LxbError("a Fast plan lives on the device it was built on")
+        return self
+
+    def init_cache(self, cache, dev) -> None:
+        """The chip layers' states as the stock forward of one zero token leaves them: all zero
+        (conv windows bf16, recurrent states fp32), as the reference's (lx/lx/fast.py:420-430)."""
+        conv = 2 * C.NK * C.KD + C.NV * C.VD
+        for L in range(self.n_chip):
+            cache.update_conv_state(torch.zeros(1, conv, 1, dtype=torch.bfloat16, device=dev), L,
+                                    conv_kernel_size=C.TAPS)
+            cache.layers[L].update_recurrent_state(
+                torch.zeros(1, C.NV, C.KD, C.VD, dtype=torch.float32, device=dev))

@@ -13,12 +13,15 @@ its checkout, builds the seeded config-1 stack as a stock model, seeds fp32 recu
   windows, per-value-head checksums of the final recurrent states plus two full value heads, and
   the residual after the chip layers for the first 8 steps;
 - ``c1_prefill.npz``: two 256-token chunks of seeded random ids run as chunked prefill (the
-  verified mode), the argmax at every position, the same state summaries after each chunk.
+  verified mode), the argmax at every position, the same state summaries after each chunk;
+- ``c1_prefill8k.npz``: one 8,192-token chunk of config 3's ids (uniform over the vocabulary,
+  seed 2) run as chunked prefill from the seeded state: the argmax and its top-2 margin at every
+  position, the final conv windows and state summaries.
 
-Run where the reference's checkout is (its directory in LXB_REFERENCE); the GPU tests only read
-the .npz files:
+Run where the reference's checkout is (its directory in LXB_REFERENCE); the tests only read the
+.npz files:
 
-    python tests/golden/make_golden.py
+    LXB_REFERENCE=<checkout> python tests/golden/make_golden.py [decode] [prefill] [prefill8k]
 """
 
 import os
@@ -31,12 +34,13 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
-REF = os.environ.get("LXB_REFERENCE", "/root/reference") + "/lx"
+REF = os.environ.get("LXB_REFERENCE")
 
 from linuxformer_b200 import chip as C  # noqa: E402
 
 N_DEC = 512
 PRE_T = 256
+PRE_8K = 8192
 
 
 def new_cache(model, st: C.State):
@@ -69,8 +73,10 @@ def margins(logits: torch.Tensor) -> np.ndarray:
 
 
 @torch.no_grad()
-def main():
-    sys.path.insert(0, REF)
+def main(parts):
+    if not REF:
+        sys.exit("set LXB_REFERENCE to the reference checkout's directory")
+    sys.path.insert(0, REF + "/lx")
     from lx import hf as ref_hf  # the reference's stock forward
 
     torch.manual_seed(0)
@@ -80,7 +86,15 @@ def main():
     st0 = C.c1_state(chip, 0)
     n = chip.n_layers
     emb = model.model.embed_tokens
+    if "decode" in parts:
+        decode(ref_hf, chip, model, st0, n, emb)
+    if "prefill" in parts:
+        prefill(ref_hf, chip, model, st0, n, emb)
+    if "prefill8k" in parts:
+        prefill8k(ref_hf, chip, model, st0, n, emb)
 
+
+def decode(ref_hf, chip, model, st0, n, emb):
     # --- model-alone decode --------------------------------------------------------------
     cache = new_cache(model, st0)
     tok, toks, preds, marg, resid = 0, [], [], [], []
@@ -104,6 +118,8 @@ def main():
                         rec_heads=heads, cpu_s=dt)
     print(f"decode: {N_DEC} tokens in {dt:.1f}s, min margin {min(marg):.3g}")
 
+
+def prefill(ref_hf, chip, model, st0, n, emb):
     # --- verified-mode prefill (chunked) -------------------------------------------------
     cache = new_cache(model, st0)
     rng = np.random.default_rng(2)
@@ -123,5 +139,23 @@ def main():
     np.savez_compressed(HERE / "c1_prefill.npz", digest=chip.digest(), **out)
 
 
+def prefill8k(ref_hf, chip, model, st0, n, emb):
+    # --- one config-3 chunk: 8,192 ids uniform over the vocabulary (seed 2) --------------
+    ids = np.random.default_rng(2).integers(0, chip.n_vocab, PRE_8K)
+    cache = new_cache(model, st0)
+    t0 = time.time()
+    h = ref_hf.chip_forward(model, emb(torch.from_numpy(ids)[None]), cache, n)[0]
+    p = ref_hf.head_argmax(model, h).numpy()
+    logits = torch.cat([torch.nn.functional.linear(model.model.norm(h[a:a + 1024]),
+                                                   model.lm_head.weight)
+                        for a in range(0, PRE_8K, 1024)])
+    dt = time.time() - t0
+    conv, sums, abss, heads = summarize(cache, n)
+    np.savez_compressed(HERE / "c1_prefill8k.npz", digest=chip.digest(), ids=ids, preds=p,
+                        margin=margins(logits), conv=conv, rec_sum=sums, rec_abs=abss,
+                        rec_heads=heads, cpu_s=dt)
+    print(f"prefill 8k: {PRE_8K} tokens in {dt:.1f}s")
+
+
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:] or ["decode", "prefill", "prefill8k"])

@@ -39,7 +39,10 @@ def fixture():
 
 
 def main():
-    sys.path.insert(0, os.environ.get("LXB_REFERENCE", "/root/reference") + "/lx")
+    ref = os.environ.get("LXB_REFERENCE")
+    if not ref:
+        sys.exit("set LXB_REFERENCE to the reference checkout's directory")
+    sys.path.insert(0, ref + "/lx")
     from lx.session import save_safe
 
     state, host, ref = fixture()

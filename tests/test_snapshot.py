@@ -17,7 +17,7 @@ from linuxformer_b200 import chip as C
 from linuxformer_b200 import snapshot
 
 GOLD = Path(__file__).parent / "golden"
-REF = Path(os.environ.get("LXB_REFERENCE", "/root/reference")) / "lx"
+REF = Path(os.environ["LXB_REFERENCE"]) / "lx" if os.environ.get("LXB_REFERENCE") else None
 
 
 def _fixture():
@@ -56,7 +56,8 @@ def test_round_trip(tmp_path, suffix, c1_chip):
     assert np.array_equal(back.recurrent.view(np.uint32), st.recurrent.view(np.uint32))
 
 
-@pytest.mark.skipif(not REF.exists(), reason="the reference's checkout is not here")
+@pytest.mark.skipif(REF is None or not REF.exists(),
+                    reason="LXB_REFERENCE (the reference checkout) is not set")
 def test_the_references_reader_loads_our_file(tmp_path):
     state, host, ref = _fixture()
     p = tmp_path / "ours.safetensors"

@@ -91,3 +91,16 @@ def test_verify_on_the_kernel_matches_stock_prefill(c1_chip):
         rec = np.stack([cache.layers[L].recurrent_states[0].cpu().numpy()
                         for L in range(c1_chip.n_layers)])
         assert np.abs(rec[:, [5, 77]] - g[f"rec_heads{k}"]).max() <= 1e-9
+
+
+def test_oracle_matches_stock_chunked_prefill_8192(c1_chip):
+    """Config 3's first chunk (8,192 ids, seed 2) through the reference's own chunked forward
+    (tests/golden/c1_prefill8k.npz): the forced per-token oracle gives the same predictions for
+    the first 2,048 positions (a prefix keeps the CPU suite quick; the GPU test runs all 8,192)."""
+    from oracle.oracle import Oracle
+
+    g = np.load(GOLD / "c1_prefill8k.npz")
+    assert str(g["digest"]) == c1_chip.digest()
+    n = 2048
+    p, _, _ = Oracle(c1_chip).decode(C.c1_state(c1_chip, 0), g["ids"][:n].astype(np.int32), n)
+    assert (p == g["preds"][:n]).all()
