@@ -45,8 +45,7 @@ namespace {
 constexpr int H = 2560, KD = 256, VD = 128, NK = 16, NV = 128, R = 8, CONV = 24576;
 constexpr int TPAD = 256;    // the token dimension of every buffer is padded to this
 constexpr int ROWT = 256;    // tokens per block in the row kernels (128 threads, 2 tokens each)
-constexpr int TILE = 64;     // tokens per shared-memory tile in the recurrence
-constexpr int HEAD_ROWS = 1024;  // head rows per slice (lpf_head)
+constexpr int HEAD_ROWS = 16384;  // head rows per slice (lpf_head_tile)
 
 __device__ __forceinline__ float bf(uint16_t b) { return lx_f(b); }
 __device__ __forceinline__ float bflo(uint32_t u) { return lx_f((uint16_t)(u & 0xffffu)); }
@@ -172,25 +171,80 @@ __global__ void __launch_bounds__(128) lpf_norm(const uint16_t* __restrict__ x, 
 #pragma unroll
     for (int l = 0; l < off; l++) ws[l] = lx_add(ws[l], ws[l + off]);
   const float r = lx_rsqrt(lx_add(lx_div(ws[0], (float)H), eps));
+#pragma unroll 16
   for (int c = 0; c < H; c++) {
-    const float w1 = lx_add(1.0f, bf(w[c]));
+    const float w1 = lx_add(1.0f, bf(__ldg(w + c)));
     xn[(size_t)c * Tp + t] = lx_rb(lx_mul(lx_mul(bf(xc[(size_t)c * Tp]), r), w1));
   }
 }
 
-// sequential dot over a row's entries (column | bf16 << 16) for two consecutive tokens, from +0
+// Sequential sums over a row's entries (index | bf16 << 16) for two consecutive tokens, from +0:
+// up to 8 entries at a time, their 8 input columns read at once (the loads first, then the adds
+// in order), so a row costs one or two memory round trips instead of one per entry.
+constexpr int DW = 8;
+struct Acc2 {
+  float a0 = 0.0f, a1 = 0.0f;
+};
+template <bool SKIP_ZERO>
+__device__ __forceinline__ void acc2(Acc2& a, bool& any0, bool& any1, uint32_t e, uint32_t xx) {
+  const float w = bfhi(e);
+  const float v0 = bflo(xx), v1 = bfhi(xx);
+  if (!SKIP_ZERO || v0 != 0.0f) {
+    a.a0 = lx_add(a.a0, lx_mul(v0, w));
+    any0 = true;
+  }
+  if (!SKIP_ZERO || v1 != 0.0f) {
+    a.a1 = lx_add(a.a1, lx_mul(v1, w));
+    any1 = true;
+  }
+}
+// NR rows (row r: entries ep[r][0..n[r])), their sums advancing together
+template <int NR, bool SKIP_ZERO>
+__device__ __forceinline__ void dotsn(const uint32_t* const* __restrict__ ep, const uint32_t* n,
+                                      const uint16_t* __restrict__ x, int Tp, int t, Acc2* acc,
+                                      bool* any) {
+  const uint16_t* xt = x + t;
+  uint32_t nmax = n[0];
+#pragma unroll
+  for (int r = 1; r < NR; r++) nmax = max(nmax, n[r]);
+  for (uint32_t k = 0; k < nmax; k += DW) {
+    uint32_t e[NR][DW], xx[NR][DW];
+#pragma unroll
+    for (int r = 0; r < NR; r++)
+#pragma unroll
+      for (int q = 0; q < DW; q++) e[r][q] = k + q < n[r] ? __ldg(ep[r] + k + q) : 0u;
+#pragma unroll
+    for (int r = 0; r < NR; r++)
+#pragma unroll
+      for (int q = 0; q < DW; q++)
+        xx[r][q] = k + q < n[r] ? *reinterpret_cast<const uint32_t*>(
+                                      xt + (size_t)(e[r][q] & 0xffffu) * Tp)
+                                : 0u;
+#pragma unroll
+    for (int r = 0; r < NR; r++)
+#pragma unroll
+      for (int q = 0; q < DW; q++)
+        if (k + q < n[r]) acc2<SKIP_ZERO>(acc[r], any[2 * r], any[2 * r + 1], e[r][q], xx[r][q]);
+  }
+}
+template <int NR, bool SKIP_ZERO>
+__device__ __forceinline__ void dots(const uint32_t* __restrict__ e0p, uint32_t n0,
+                                     const uint32_t* __restrict__ e1p, uint32_t n1,
+                                     const uint16_t* __restrict__ x, int Tp, int t, Acc2* acc,
+                                     bool* any) {
+  const uint32_t* ep[2] = {e0p, e1p};
+  const uint32_t n[2] = {n0, n1};
+  dotsn<NR, SKIP_ZERO>(ep, n, x, Tp, t, acc, any);
+}
+
 __device__ __forceinline__ void dot2(const uint32_t* __restrict__ ent, uint32_t n,
                                      const uint16_t* __restrict__ xn, int Tp, int t, float& a0,
                                      float& a1) {
-  a0 = 0.0f;
-  a1 = 0.0f;
-  for (uint32_t k = 0; k < n; k++) {
-    const uint32_t e = __ldg(ent + k);
-    const float w = bfhi(e);
-    const uint32_t xx = *reinterpret_cast<const uint32_t*>(xn + (size_t)(e & 0xffffu) * Tp + t);
-    a0 = lx_add(a0, lx_mul(bflo(xx), w));
-    a1 = lx_add(a1, lx_mul(bfhi(xx), w));
-  }
+  Acc2 acc[1];
+  bool any[2] = {false, false};
+  dots<1, false>(ent, n, nullptr, 0, xn, Tp, t, acc, any);
+  a0 = acc[0].a0;
+  a1 = acc[0].a1;
 }
 
 // tap channels' in_proj_qkv projections: P = bf16(row . xn)
@@ -209,9 +263,10 @@ __global__ void __launch_bounds__(128) lpf_gates(PV pv, int L, Buf b) {
   const int vh = blockIdx.y;
   const int t = blockIdx.x * ROWT + 2 * threadIdx.x;
   const lxb_pf_vh p = pv.vhs[(size_t)L * NV + vh];
-  float a[2], bb[2];
-  dot2(pv.ent + p.a_ent, p.a_n, b.xn, b.Tp, t, a[0], a[1]);
-  dot2(pv.ent + p.b_ent, p.b_n, b.xn, b.Tp, t, bb[0], bb[1]);
+  Acc2 ab[2];
+  bool any[4] = {false, false, false, false};
+  dots<2, false>(pv.ent + p.a_ent, p.a_n, pv.ent + p.b_ent, p.b_n, b.xn, b.Tp, t, ab, any);
+  const float a[2] = {ab[0].a0, ab[0].a1}, bb[2] = {ab[1].a0, ab[1].a1};
   const float A = -lx_exp(bf(p.A_log));
   const float dt = bf(p.dt_bias);
   float ev[2], be[2];
@@ -337,17 +392,76 @@ __global__ void __launch_bounds__(128) lpf_qk(PV pv, const lxb_pf_layer* lyp, Bu
   }
 }
 
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // The recurrence over the live rows of one value head (a CTA per live value head, a thread per
 // column j; NL register slots, the key head's live rows in ascending order). Per token, as the
 // per-token decode: S *= exp(g); if a key: kv = sum over the key's nonzero rows S k, delta =
 // (v - kv) beta, S += k delta; if a query: o = bf16(sum over the query's nonzero rows S q/16).
+// The body has no branch: a slot whose key or query value is zero (a zero row, a token without
+// a key or query, a slot past the head's live rows) adds S * 0 = +-0 to a sum that started at +0,
+// which leaves the sum's bits as they are (+0 + -0 = +0; x + +-0 = x for x != 0); the state
+// itself takes k delta only where the key's mask bit is set (a select: a -0 state value keeps its
+// sign). So the tokens of a tile form one basic block and the compiler overlaps a token's loads
+// with the previous token's chain.
+// The per-token inputs shared by the CTA (exp(g), beta, the key mask, the live rows' query and
+// key values) come through shared memory in double-buffered tiles of RT tokens (cp.async, the
+// next tile in flight while this one runs); each thread's value column for the tile sits in
+// registers (prefetched a tile ahead).
+constexpr int RT = 32;  // tokens per recurrence tile
+template <int NL>
+__device__ __forceinline__ void recur_token(float (&S)[NL], const float4 tk, const float* kp,
+                                            const float* qp, float v, uint16_t* out) {
+  constexpr int NP = (NL + 3) / 4 * 4;
+  float kk[NP], qq[NP];
+#pragma unroll
+  for (int s = 0; s < NP; s += 4) {
+    const float4 a = *reinterpret_cast<const float4*>(kp + s);
+    const float4 c = *reinterpret_cast<const float4*>(qp + s);
+    kk[s] = a.x, kk[s + 1] = a.y, kk[s + 2] = a.z, kk[s + 3] = a.w;
+    qq[s] = c.x, qq[s + 1] = c.y, qq[s + 2] = c.z, qq[s + 3] = c.w;
+  }
+  const uint32_t km = __float_as_uint(tk.z);
+#pragma unroll
+  for (int s = 0; s < NL; s++) S[s] = lx_mul(S[s], tk.x);
+  float kv = 0.0f;
+#pragma unroll
+  for (int s = 0; s < NL; s++) kv = lx_add(kv, lx_mul(S[s], kk[s]));
+  const float delta = lx_mul(lx_sub(v, kv), tk.y);
+#pragma unroll
+  for (int s = 0; s < NL; s++) {
+    const float nv = lx_add(S[s], lx_mul(kk[s], delta));
+    S[s] = ((km >> s) & 1u) ? nv : S[s];
+  }
+  float o = 0.0f;
+#pragma unroll
+  for (int s = 0; s < NL; s++) o = lx_add(o, lx_mul(S[s], qq[s]));
+  *out = lx_rb(o);
+}
+
 template <int NL>
 __global__ void __launch_bounds__(128) lpf_recur(PV pv, const lxb_pf_layer* lyp, int L,
                                                  const uint64_t* __restrict__ sp, Buf b) {
-  __shared__ float s_e[TILE], s_b[TILE];
-  __shared__ uint32_t s_qm[TILE], s_km[TILE];
-  __shared__ float s_qs[NL][TILE], s_ks[NL][TILE];
-  __shared__ uint16_t s_v[TILE][VD];
+  constexpr int NP = (NL + 3) / 4 * 4;
+  __shared__ __align__(16) float4 s_tok[2][RT];      // exp(g), beta, key mask, query mask
+  __shared__ __align__(16) float s_k[2][RT][NP];
+  __shared__ __align__(16) float s_q[2][RT][NP];
   const lxb_pf_layer ly = *lyp;
   const int lvh = blockIdx.x, i = lvh / R, r = lvh % R;
   const int j = threadIdx.x;
@@ -365,62 +479,73 @@ __global__ void __launch_bounds__(128) lpf_recur(PV pv, const lxb_pf_layer* lyp,
   const float* bv = b.beta + (size_t)vh * b.Tp;
   const uint32_t* qmv = b.qm + (size_t)i * b.Tp;
   const uint32_t* kmv = b.km + (size_t)i * b.Tp;
+  const float* ksv = b.ks + (size_t)s0 * b.Tp;
+  const float* qsv = b.qs + (size_t)s0 * b.Tp;
+  const uint4* vsrc = vt >= 0 ? reinterpret_cast<const uint4*>(b.Y + (size_t)vt * b.Tp) : nullptr;
   const int ostride = ly.n_kh * R * VD;
   uint16_t* op = b.o + lvh * VD + j;
-  for (int t0 = 0; t0 < b.T; t0 += TILE) {
-    const int n = min(TILE, b.T - t0);
-    if (j < TILE) {
-      s_e[j] = ev[t0 + j];
-      s_b[j] = bv[t0 + j];
+  // the slots past the head's live rows stay zero in both buffers (nothing copies into them)
+  for (int k = j; k < 2 * RT * NP; k += 128) {
+    const int s = k % NP;
+    if (s >= nl) {
+      (&s_k[0][0][0])[k] = 0.0f;
+      (&s_q[0][0][0])[k] = 0.0f;
+    }
+  }
+  auto issue = [&](int buf, int t0) {
+    for (int k = j; k < RT * 4; k += 128) {
+      const int tt = k >> 2, f = k & 3;
+      const void* src = f == 0 ? (const void*)(ev + t0 + tt) : f == 1 ? (const void*)(bv + t0 + tt)
+                        : f == 2 ? (const void*)(kmv + t0 + tt) : (const void*)(qmv + t0 + tt);
+      cp_async4(reinterpret_cast<float*>(&s_tok[buf][tt]) + f, src);
+    }
+    for (int k = j; k < RT * nl; k += 128) {
+      const int s = k / RT, tt = k % RT;
+      cp_async4(&s_k[buf][tt][s], ksv + (size_t)s * b.Tp + t0 + tt);
+      cp_async4(&s_q[buf][tt][s], qsv + (size_t)s * b.Tp + t0 + tt);
+    }
+    cp_commit();
+  };
+  uint4 vc[RT / 8], vn[RT / 8];  // this tile's and the next tile's value column (bf16 pairs)
+#pragma unroll
+  for (int q = 0; q < RT / 8; q++) vc[q] = vsrc ? vsrc[q] : make_uint4(0, 0, 0, 0);
+  issue(0, 0);
+  int buf = 0;
+  for (int t0 = 0; t0 < b.T; t0 += RT) {
+    const bool more = t0 + RT < b.T;
+    if (more) {
+      issue(buf ^ 1, t0 + RT);
+#pragma unroll
+      for (int q = 0; q < RT / 8; q++)
+        vn[q] = vsrc ? vsrc[(t0 + RT) / 8 + q] : make_uint4(0, 0, 0, 0);
+      cp_wait<1>();
     } else {
-      s_qm[j - TILE] = qmv[t0 + j - TILE];
-      s_km[j - TILE] = kmv[t0 + j - TILE];
+      cp_wait<0>();
     }
-    for (int k = j; k < nl * TILE; k += 128) {
-      const int s = k / TILE, tt = k % TILE;
-      s_qs[s][tt] = b.qs[(size_t)(s0 + s) * b.Tp + t0 + tt];
-      s_ks[s][tt] = b.ks[(size_t)(s0 + s) * b.Tp + t0 + tt];
-    }
-    if (vt >= 0) {
-      const uint4* src = reinterpret_cast<const uint4*>(b.Y + (size_t)vt * b.Tp + t0);
+    __syncthreads();
+    uint16_t* ot = op + (size_t)t0 * ostride;
+    if (b.T - t0 >= RT) {  // a whole tile: one basic block
 #pragma unroll
-      for (int q = 0; q < TILE / 8; q++) {
-        const uint4 u = src[q];
-        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+      for (int tt = 0; tt < RT; tt++) {
+        const uint32_t vw = (&vc[tt / 8].x)[(tt % 8) / 2];
+        recur_token<NL>(S, s_tok[buf][tt], s_k[buf][tt], s_q[buf][tt],
+                        (tt & 1) ? bfhi(vw) : bflo(vw), ot + (size_t)tt * ostride);
+      }
+    } else {
+      const int n = b.T - t0;
 #pragma unroll
-        for (int h = 0; h < 4; h++) {
-          s_v[q * 8 + 2 * h][j] = (uint16_t)(w4[h] & 0xffffu);
-          s_v[q * 8 + 2 * h + 1][j] = (uint16_t)(w4[h] >> 16);
+      for (int tt = 0; tt < RT; tt++) {
+        if (tt < n) {
+          const uint32_t vw = (&vc[tt / 8].x)[(tt % 8) / 2];
+          recur_token<NL>(S, s_tok[buf][tt], s_k[buf][tt], s_q[buf][tt],
+                          (tt & 1) ? bfhi(vw) : bflo(vw), ot + (size_t)tt * ostride);
         }
       }
     }
-    __syncthreads();
-    for (int tt = 0; tt < n; tt++) {
-      const float e = s_e[tt];
+    __syncthreads();  // the buffer is reused by the issue two tiles on
 #pragma unroll
-      for (int s = 0; s < NL; s++) S[s] = lx_mul(S[s], e);
-      const uint32_t km = s_km[tt];
-      if (km >> 31) {
-        float kv = 0.0f;
-#pragma unroll
-        for (int s = 0; s < NL; s++)
-          if ((km >> s) & 1u) kv = lx_add(kv, lx_mul(S[s], s_ks[s][tt]));
-        const float v = vt >= 0 ? bf(s_v[tt][j]) : 0.0f;
-        const float delta = lx_mul(lx_sub(v, kv), s_b[tt]);
-#pragma unroll
-        for (int s = 0; s < NL; s++)
-          if ((km >> s) & 1u) S[s] = lx_add(S[s], lx_mul(s_ks[s][tt], delta));
-      }
-      const uint32_t qm = s_qm[tt];
-      float o = 0.0f;
-      if (qm >> 31) {
-#pragma unroll
-        for (int s = 0; s < NL; s++)
-          if ((qm >> s) & 1u) o = lx_add(o, lx_mul(S[s], s_qs[s][tt]));
-      }
-      op[(size_t)(t0 + tt) * ostride] = lx_rb(o);
-    }
-    __syncthreads();
+    for (int q = 0; q < RT / 8; q++) vc[q] = vn[q];
+    buf ^= 1;
   }
 #pragma unroll
   for (int s = 0; s < NL; s++)
@@ -428,57 +553,79 @@ __global__ void __launch_bounds__(128) lpf_recur(PV pv, const lxb_pf_layer* lyp,
 }
 
 // The decay of every other state row: S <- S * exp(g_t), token by token (the per-token decode's
-// rounding), a float4 per thread; a thread stops once its four values are zero (they stay zero).
+// rounding), a float4 per thread (a block: 8 rows of one value head); the factors come through
+// shared memory in double-buffered tiles. A thread is done once its four values are zero (they
+// stay zero); the block stops when all its threads are.
+constexpr int ST = 1024;  // tokens per scan tile
 __global__ void __launch_bounds__(256) lpf_scan(PV pv, const lxb_pf_layer* lyp, int L,
                                                 const uint64_t* __restrict__ sp, Buf b) {
+  __shared__ __align__(16) float s_e[2][ST];
   const int vh = blockIdx.x;
   const int row = blockIdx.y * 8 + (threadIdx.x >> 5);
   const int c4 = threadIdx.x & 31;
   if (!b.flags[(size_t)L * NV + vh]) return;
   const lxb_pf_layer ly = *lyp;
   const uint32_t live = (uint32_t)pv.i32[ly.livemask + (vh / R) * 8 + row / 32];
-  if ((live >> (row % 32)) & 1u) return;
   float* rec = reinterpret_cast<float*>(sp[2 * L]);
   float4* p = reinterpret_cast<float4*>(rec + ((size_t)vh * KD + row) * VD) + c4;
-  float4 v = *p;
-  if (v.x == 0.0f && v.y == 0.0f && v.z == 0.0f && v.w == 0.0f) return;
+  float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  bool act = !((live >> (row % 32)) & 1u);
+  if (act) {
+    v = *p;
+    act = v.x != 0.0f || v.y != 0.0f || v.z != 0.0f || v.w != 0.0f;
+  }
+  const bool wrote = act;
+  if (!__syncthreads_or(act)) return;
   const float* ev = b.e + ((size_t)L * NV + vh) * b.Tp;
-  const int T4 = b.T & ~3;
-  int t = 0;
-  for (; t < T4; t += 4) {
-    const float4 e = *reinterpret_cast<const float4*>(ev + t);
-    v.x = lx_mul(lx_mul(lx_mul(lx_mul(v.x, e.x), e.y), e.z), e.w);
-    v.y = lx_mul(lx_mul(lx_mul(lx_mul(v.y, e.x), e.y), e.z), e.w);
-    v.z = lx_mul(lx_mul(lx_mul(lx_mul(v.z, e.x), e.y), e.z), e.w);
-    v.w = lx_mul(lx_mul(lx_mul(lx_mul(v.w, e.x), e.y), e.z), e.w);
-    if ((t & 63) == 60 && v.x == 0.0f && v.y == 0.0f && v.z == 0.0f && v.w == 0.0f) {
-      t = b.T;
-      break;
+  auto issue = [&](int buf, int t0) {  // b.Tp is a multiple of 256: reads stay inside the row
+    for (int k = threadIdx.x; k < ST / 4 && t0 + 4 * k < b.Tp; k += 256)
+      cp_async16(&s_e[buf][4 * k], ev + t0 + 4 * k);
+    cp_commit();
+  };
+  issue(0, 0);
+  int buf = 0;
+  for (int t0 = 0; t0 < b.T; t0 += ST) {
+    if (t0 + ST < b.T) {
+      issue(buf ^ 1, t0 + ST);
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
     }
+    __syncthreads();
+    if (act) {
+      const int n = min(ST, b.T - t0);
+      const float4* e4 = reinterpret_cast<const float4*>(s_e[buf]);
+      int tt = 0;
+      for (; tt + 4 <= n; tt += 4) {
+        const float4 e = e4[tt / 4];
+        v.x = lx_mul(lx_mul(lx_mul(lx_mul(v.x, e.x), e.y), e.z), e.w);
+        v.y = lx_mul(lx_mul(lx_mul(lx_mul(v.y, e.x), e.y), e.z), e.w);
+        v.z = lx_mul(lx_mul(lx_mul(lx_mul(v.z, e.x), e.y), e.z), e.w);
+        v.w = lx_mul(lx_mul(lx_mul(lx_mul(v.w, e.x), e.y), e.z), e.w);
+      }
+      for (; tt < n; tt++) {
+        const float e = s_e[buf][tt];
+        v.x = lx_mul(v.x, e);
+        v.y = lx_mul(v.y, e);
+        v.z = lx_mul(v.z, e);
+        v.w = lx_mul(v.w, e);
+      }
+      act = v.x != 0.0f || v.y != 0.0f || v.z != 0.0f || v.w != 0.0f;
+    }
+    if (!__syncthreads_or(act)) break;  // also: no thread still reads buf when it is refilled
+    buf ^= 1;
   }
-  for (; t < b.T; t++) {
-    const float e = ev[t];
-    v.x = lx_mul(v.x, e);
-    v.y = lx_mul(v.y, e);
-    v.z = lx_mul(v.z, e);
-    v.w = lx_mul(v.w, e);
-  }
-  *p = v;
+  cp_wait<0>();
+  if (wrote) *p = v;
 }
 
 // Qwen3_5RMSNormGated per (token, live value head): bf16(bf16(w bf16(o rsqrt(mean(o^2) + eps)))
 // silu(bf16(z . xn))), the sum of squares as lane l of 32 summing o[4l..4l+3]^2 then an xor
-// butterfly; a head whose 128 outputs are all zero gives zeros (the decode skips it).
-__global__ void __launch_bounds__(128) lpf_gnorm(PV pv, const lxb_pf_layer* lyp, float eps,
-                                                 Buf b) {
-  const int t = blockIdx.x * 128 + threadIdx.x;
-  if (t >= b.T) return;
-  const lxb_pf_layer ly = *lyp;
-  const int lvh = blockIdx.y;
-  const uint16_t* orow = b.o + (size_t)t * (ly.n_kh * R * VD) + lvh * VD;
-  uint16_t* on = b.on + (size_t)lvh * VD * b.Tp + t;
+// butterfly; a head whose 128 outputs are all zero gives zeros (the decode skips it). Two tokens
+// per thread; the in_proj_z rows four at a time.
+__device__ __forceinline__ float o_rr(const uint16_t* orow, float eps, bool& nz) {
   float v[32];
-  bool nz = false;
+  nz = false;
 #pragma unroll
   for (int l = 0; l < 32; l++) {
     const uint2 u = *reinterpret_cast<const uint2*>(orow + 4 * l);
@@ -490,28 +637,59 @@ __global__ void __launch_bounds__(128) lpf_gnorm(PV pv, const lxb_pf_layer* lyp,
     s = lx_add(s, lx_mul(f, f));
     v[l] = s;
   }
-  if (!nz) {
-    for (int k = 0; k < VD; k++) on[(size_t)k * b.Tp] = 0;
-    return;
-  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
     for (int l = 0; l < off; l++) v[l] = lx_add(v[l], v[l + off]);
-  const float rr = lx_rsqrt(lx_add(lx_div(v[0], 128.0f), eps));
+  return lx_rsqrt(lx_add(lx_div(v[0], 128.0f), eps));
+}
+
+__global__ void __launch_bounds__(128) lpf_gnorm(PV pv, const lxb_pf_layer* lyp, float eps,
+                                                 Buf b) {
+  const int t = blockIdx.x * ROWT + 2 * threadIdx.x;
+  if (t >= b.T) return;
+  const lxb_pf_layer ly = *lyp;
+  const int lvh = blockIdx.y;
+  const int ostride = ly.n_kh * R * VD;
+  const uint16_t* o0 = b.o + (size_t)t * ostride + lvh * VD;
+  const uint16_t* o1 = o0 + ostride;  // token t + 1 (inside the padded buffer)
+  uint32_t* on = reinterpret_cast<uint32_t*>(b.on + (size_t)lvh * VD * b.Tp + t);
+  bool nz0, nz1;
+  const float r0 = o_rr(o0, eps, nz0);
+  const float r1 = o_rr(o1, eps, nz1);
+  nz1 = nz1 && t + 1 < b.T;
+  if (!nz0 && !nz1) {
+    for (int k = 0; k < VD; k++) on[(size_t)k * b.Tp / 2] = 0u;
+    return;
+  }
   const uint16_t* gw = pv.u16 + ly.gnorm;
   const int32_t* zr = pv.i32 + ly.zrow + 2 * lvh * VD;
-  for (int k = 0; k < VD; k++) {
-    const float hn = lx_rbf(lx_mul(bf(orow[k]), rr));
-    const float u = lx_rbf(lx_mul(bf(gw[k]), hn));
-    float z = 0.0f;
-    const uint32_t* ze = pv.ent + zr[2 * k];
-    const int zn = zr[2 * k + 1];
-    for (int q = 0; q < zn; q++) {
-      const uint32_t e = __ldg(ze + q);
-      z = lx_add(z, lx_mul(bf(b.xn[(size_t)(e & 0xffffu) * b.Tp + t]), bfhi(e)));
+  for (int k0 = 0; k0 < VD; k0 += 4) {
+    const uint32_t* ep[4];
+    uint32_t n[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      ep[q] = pv.ent + __ldg(zr + 2 * (k0 + q));
+      n[q] = (uint32_t)__ldg(zr + 2 * (k0 + q) + 1);
     }
-    on[(size_t)k * b.Tp] = lx_rb(lx_mul(u, lx_silu(lx_rbf(z))));
+    Acc2 z[4];
+    bool any[8];
+    dotsn<4, false>(ep, n, b.xn, b.Tp, t, z, any);
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int k = k0 + q;
+      const float w = bf(__ldg(gw + k));
+      uint16_t h0 = 0, h1 = 0;
+      if (nz0) {
+        const float u = lx_rbf(lx_mul(w, lx_rbf(lx_mul(bf(o0[k]), r0))));
+        h0 = lx_rb(lx_mul(u, lx_silu(lx_rbf(z[q].a0))));
+      }
+      if (nz1) {
+        const float u = lx_rbf(lx_mul(w, lx_rbf(lx_mul(bf(o1[k]), r1))));
+        h1 = lx_rb(lx_mul(u, lx_silu(lx_rbf(z[q].a1))));
+      }
+      on[(size_t)k * b.Tp / 2] = pack2(h0, h1);
+    }
   }
 }
 
@@ -524,22 +702,11 @@ __global__ void __launch_bounds__(128) lpf_add_rows(PV pv, int ptr_off,
   const int p0 = pv.i32[ptr_off + rr], p1 = pv.i32[ptr_off + rr + 1];
   if (p0 == p1) return;
   const int t = blockIdx.x * ROWT + 2 * threadIdx.x;
-  float s0 = 0.0f, s1 = 0.0f;
-  bool a0 = false, a1 = false;
-  for (int k = p0; k < p1; k++) {
-    const uint32_t e = __ldg(pv.ent + k);
-    const float w = bfhi(e);
-    const uint32_t xx = *reinterpret_cast<const uint32_t*>(in + (size_t)(e & 0xffffu) * b.Tp + t);
-    const float v0 = bflo(xx), v1 = bfhi(xx);
-    if (v0 != 0.0f) {
-      s0 = lx_add(s0, lx_mul(v0, w));
-      a0 = true;
-    }
-    if (v1 != 0.0f) {
-      s1 = lx_add(s1, lx_mul(v1, w));
-      a1 = true;
-    }
-  }
+  Acc2 acc[1];
+  bool any[2] = {false, false};
+  dots<1, true>(pv.ent + p0, (uint32_t)(p1 - p0), nullptr, 0, in, b.Tp, t, acc, any);
+  const float s0 = acc[0].a0, s1 = acc[0].a1;
+  const bool a0 = any[0], a1 = any[1];
   if (!a0 && !a1) return;
   uint32_t* xp = reinterpret_cast<uint32_t*>(b.x + (size_t)rr * b.Tp + t);
   const uint32_t xx = *xp;
@@ -549,16 +716,63 @@ __global__ void __launch_bounds__(128) lpf_add_rows(PV pv, int ptr_off,
   *xp = pack2(n0, n1);
 }
 
-// MLP units: h = bf16(bf16(silu(bf16(gate . xn))) * bf16(up . xn))
-__global__ void __launch_bounds__(128) lpf_mlp(PV pv, int unit0, Buf b) {
-  const int t = blockIdx.x * ROWT + 2 * threadIdx.x;
-  const lxb_pf_unit u = pv.units[unit0 + blockIdx.y];
-  float g0, g1, u0, u1;
-  dot2(pv.ent + u.g, u.ng, b.xn, b.Tp, t, g0, g1);
-  dot2(pv.ent + u.u, u.nu, b.xn, b.Tp, t, u0, u1);
-  const uint16_t h0 = lx_rb(lx_mul(lx_rbf(lx_silu(lx_rbf(g0))), lx_rbf(u0)));
-  const uint16_t h1 = lx_rb(lx_mul(lx_rbf(lx_silu(lx_rbf(g1))), lx_rbf(u1)));
-  *reinterpret_cast<uint32_t*>(b.hb + (size_t)blockIdx.y * b.Tp + t) = pack2(h0, h1);
+// --- stages over a shared-memory token tile ---------------------------------------------------
+// A block takes XT = 32 consecutive tokens and copies their whole normed input ([2560][32] bf16,
+// 160 KB) into shared memory; lane l of every warp is token t0 + l, and the warps share out the
+// rows (MLP units, head rows). A row's entries are uniform loads (one per warp), its inputs
+// conflict-free shared loads (two lanes per 32-bit word), so no input read waits on L2.
+constexpr int XT = 32;
+constexpr int XW = 16;  // warps per tile block
+constexpr int XSMEM = H * XT * 2;
+
+__device__ __forceinline__ void fill_tile(uint16_t* xs, const uint16_t* __restrict__ xn, int Tp,
+                                          int t0) {
+  for (int k = threadIdx.x; k < H * (XT / 8); k += XW * 32) {
+    const int c = k / (XT / 8), q = k % (XT / 8);
+    cp_async16(xs + c * XT + q * 8, xn + (size_t)c * Tp + t0 + q * 8);
+  }
+  cp_commit();
+  cp_wait<0>();
+  __syncthreads();
+}
+
+// sequential dot of a row's entries over the tile, lane = token; 8 entries per round
+__device__ __forceinline__ float tdot(const uint32_t* __restrict__ ent, uint32_t n,
+                                      const uint16_t* xs, int lane) {
+  float a = 0.0f;
+  for (uint32_t k = 0; k < n; k += 8) {
+    uint32_t e[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) e[q] = k + q < n ? __ldg(ent + k + q) : 0u;
+    float x[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) x[q] = bf(xs[(e[q] & 0xffffu) * XT + lane]);
+#pragma unroll
+    for (int q = 0; q < 8; q++)
+      if (k + q < n) a = lx_add(a, lx_mul(x[q], bfhi(e[q])));
+  }
+  return a;
+}
+
+// MLP units over a tile: h = bf16(bf16(silu(bf16(gate . xn))) * bf16(up . xn)); each warp takes
+// two units at a time (their loads together)
+__global__ void __launch_bounds__(XW * 32) lpf_mlp_tile(PV pv, int unit0, int n_units, Buf b) {
+  extern __shared__ __align__(16) uint16_t xs[];
+  const int t0 = blockIdx.x * XT;
+  fill_tile(xs, b.xn, b.Tp, t0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint16_t* hb = b.hb + t0 + lane;
+  for (int u = warp; u < n_units; u += 2 * XW) {
+    const int u2 = u + XW;
+    const lxb_pf_unit A = pv.units[unit0 + u];
+    const lxb_pf_unit B = u2 < n_units ? pv.units[unit0 + u2] : lxb_pf_unit{0, 0, 0, 0};
+    const float ga = tdot(pv.ent + A.g, A.ng, xs, lane);
+    const float ua = tdot(pv.ent + A.u, A.nu, xs, lane);
+    const float gb = tdot(pv.ent + B.g, B.ng, xs, lane);
+    const float ub = tdot(pv.ent + B.u, B.nu, xs, lane);
+    hb[(size_t)u * b.Tp] = lx_rb(lx_mul(lx_rbf(lx_silu(lx_rbf(ga))), lx_rbf(ua)));
+    if (u2 < n_units) hb[(size_t)u2 * b.Tp] = lx_rb(lx_mul(lx_rbf(lx_silu(lx_rbf(gb))), lx_rbf(ub)));
+  }
 }
 
 struct HeadArgs {
@@ -567,52 +781,73 @@ struct HeadArgs {
   int dense_cols[LXB_PF_MAXDENSE];
 };
 
-// The head over one slice of its rows, per token: logit = bf16(D + S), D the dense columns in
-// groups of 4 (each from +0, the groups summed in order from +0), S the other entries in order;
-// the first maximum (a later equal logit does not replace it).
-__global__ void __launch_bounds__(128) lpf_head(PV pv, HeadArgs ha, Buf b) {
-  const int t = blockIdx.x * 128 + threadIdx.x;
-  if (t >= b.T) return;
+// The head's logit of one row: bf16(D + S), D the dense columns in groups of 4 (each from +0,
+// the groups summed in order from +0), S the other entries in order; the prediction is the first
+// maximum (a later equal logit does not replace it).
+__device__ __forceinline__ float head_dense(const HeadArgs& ha, unsigned long long codes,
+                                            const float* xd) {
+  float D = 0.0f, grp = 0.0f;
+  int in = 0;
+#pragma unroll
+  for (int j = 0; j < LXB_PF_MAXDENSE; j++) {
+    if (j < ha.n_dense) {
+      grp = lx_add(grp, lx_mul(ha.htab[(codes >> (2 * j)) & 3ull], xd[j]));
+      if (++in == 4 || j == ha.n_dense - 1) {
+        D = lx_add(D, grp);
+        grp = 0.0f;
+        in = 0;
+      }
+    }
+  }
+  return D;
+}
+
+// The head over a tile: the block's rows (a slice) for its 32 tokens; each warp takes rows
+// w, w + XW, ... and keeps each lane's (token's) first maximum; the warps' maxima are combined in
+// row order (the slice's maximum is the first among the warps' by value, then by row).
+__global__ void __launch_bounds__(XW * 32) lpf_head_tile(PV pv, HeadArgs ha, Buf b) {
+  extern __shared__ __align__(16) uint16_t xs[];
+  __shared__ float s_best[XW][XT];
+  __shared__ int s_bi[XW][XT];
+  const int t0 = blockIdx.x * XT;
+  fill_tile(xs, b.xn, b.Tp, t0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int ns = gridDim.y, k = blockIdx.y;
   const int r0 = (int)((long long)ha.V * k / ns), r1 = (int)((long long)ha.V * (k + 1) / ns);
   float xd[LXB_PF_MAXDENSE];
 #pragma unroll
   for (int j = 0; j < LXB_PF_MAXDENSE; j++)
-    xd[j] = j < ha.n_dense ? bf(b.xn[(size_t)ha.dense_cols[j] * b.Tp + t]) : 0.0f;
+    xd[j] = j < ha.n_dense ? bf(xs[ha.dense_cols[j] * XT + lane]) : 0.0f;
+  const int32_t* hp = pv.i32 + ha.head_ptr;
   float best = 0.0f;
   int bi = -1;
-  const int32_t* hp = pv.i32 + ha.head_ptr;
-  for (int row = r0; row < r1; row++) {
-    float D = 0.0f;
-    if (ha.n_dense) {
-      const unsigned long long codes = __ldg(pv.hcodes + row);
-      float grp = 0.0f;
-      int in = 0;
-#pragma unroll
-      for (int j = 0; j < LXB_PF_MAXDENSE; j++) {
-        if (j < ha.n_dense) {
-          grp = lx_add(grp, lx_mul(ha.htab[(codes >> (2 * j)) & 3ull], xd[j]));
-          if (++in == 4 || j == ha.n_dense - 1) {
-            D = lx_add(D, grp);
-            grp = 0.0f;
-            in = 0;
-          }
-        }
-      }
-    }
-    float S = 0.0f;
+  for (int row = r0 + warp; row < r1; row += XW) {
     const int e0 = __ldg(hp + row), e1 = __ldg(hp + row + 1);
-    for (int q = e0; q < e1; q++) {
-      const uint32_t e = __ldg(pv.ent + q);
-      S = lx_add(S, lx_mul(bfhi(e), bf(b.xn[(size_t)(e & 0xffffu) * b.Tp + t])));
-    }
+    float D = 0.0f;
+    if (ha.n_dense) D = head_dense(ha, __ldg(pv.hcodes + row), xd);
+    const float S = tdot(pv.ent + e0, (uint32_t)(e1 - e0), xs, lane);
     const float lg = lx_rbf(lx_add(D, S));
     if (bi < 0 || lg > best) {
       best = lg;
       bi = row;
     }
   }
-  b.hp[(size_t)k * b.Tp + t] = make_uint2(__float_as_uint(best), (uint32_t)bi);
+  s_best[warp][lane] = best;
+  s_bi[warp][lane] = bi;
+  __syncthreads();
+  if (warp == 0) {
+    float v = 0.0f;
+    int vi = -1;
+    for (int w = 0; w < XW; w++) {  // equal logits: the lowest row wins (the first maximum)
+      const int wi = s_bi[w][lane];
+      const float wv = s_best[w][lane];
+      if (wi >= 0 && (vi < 0 || wv > v || (wv == v && wi < vi))) {
+        v = wv;
+        vi = wi;
+      }
+    }
+    b.hp[(size_t)k * b.Tp + t0 + lane] = make_uint2(__float_as_uint(v), (uint32_t)vi);
+  }
 }
 
 // the slices' maxima in row order -> the prediction; with tokens, the first position whose
@@ -889,12 +1124,22 @@ int run_layers(lxb_prefill_plan* p, const uint64_t* state_ptrs, const Buf& b, cu
       lpf_qk<<<dim3(nb128, ly.n_kh), 128, 0, st>>>(p->pv, dly, b);
       LPF_LAUNCHED();
       const int g = ly.n_kh * R;
-      if (ly.nl <= 4) lpf_recur<4><<<g, 128, 0, st>>>(p->pv, dly, L, sp, b);
-      else if (ly.nl <= 8) lpf_recur<8><<<g, 128, 0, st>>>(p->pv, dly, L, sp, b);
-      else if (ly.nl <= 16) lpf_recur<16><<<g, 128, 0, st>>>(p->pv, dly, L, sp, b);
-      else lpf_recur<32><<<g, 128, 0, st>>>(p->pv, dly, L, sp, b);
+      switch (ly.nl) {  // the register slots: the layer's most live rows, rounded up a little
+#define LPF_R(n) lpf_recur<n><<<g, 128, 0, st>>>(p->pv, dly, L, sp, b); break
+        case 1: case 2: LPF_R(2);
+        case 3: LPF_R(3);
+        case 4: LPF_R(4);
+        case 5: LPF_R(5);
+        case 6: LPF_R(6);
+        case 7: case 8: LPF_R(8);
+        case 9: case 10: case 11: case 12: LPF_R(12);
+        case 13: case 14: case 15: case 16: LPF_R(16);
+        case 17: case 18: case 19: case 20: case 21: case 22: case 23: case 24: LPF_R(24);
+        default: LPF_R(31);
+#undef LPF_R
+      }
       LPF_LAUNCHED();
-      lpf_gnorm<<<dim3(nb128, g), 128, 0, st>>>(p->pv, dly, h.eps, b);
+      lpf_gnorm<<<dim3(nbrow, g), 128, 0, st>>>(p->pv, dly, h.eps, b);
       LPF_LAUNCHED();
       lpf_add_rows<<<dim3(nbrow, H), 128, 0, st>>>(p->pv, ly.out_ptr, b.on, b);
       LPF_LAUNCHED();
@@ -902,7 +1147,7 @@ int run_layers(lxb_prefill_plan* p, const uint64_t* state_ptrs, const Buf& b, cu
     if (ly.n_units) {
       lpf_norm<<<nb128, 128, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_post, h.eps, b.xn);
       LPF_LAUNCHED();
-      lpf_mlp<<<dim3(nbrow, ly.n_units), 128, 0, st>>>(p->pv, ly.unit0, b);
+      lpf_mlp_tile<<<b.Tp / XT, XW * 32, XSMEM, st>>>(p->pv, ly.unit0, ly.n_units, b);
       LPF_LAUNCHED();
       lpf_add_rows<<<dim3(nbrow, H), 128, 0, st>>>(p->pv, ly.down_ptr, b.hb, b);
       LPF_LAUNCHED();
@@ -924,7 +1169,7 @@ int run_head(lxb_prefill_plan* p, const Buf& b, const Layout& l, int32_t* preds,
   ha.head_ptr = h.head_ptr;
   memcpy(ha.htab, h.htab, sizeof(ha.htab));
   memcpy(ha.dense_cols, h.dense_cols, sizeof(ha.dense_cols));
-  lpf_head<<<dim3(nb128, l.ns), 128, 0, st>>>(p->pv, ha, b);
+  lpf_head_tile<<<dim3(l.Tp / XT, l.ns), XW * 32, XSMEM, st>>>(p->pv, ha, b);
   LPF_LAUNCHED();
   if (first_wrong) {
     lpf_fw_init<<<1, 1, 0, st>>>(b.fw);
@@ -975,6 +1220,12 @@ extern "C" int lxb_prefill_plan_create(const void* image, size_t bytes, lxb_pref
   if ((e = cudaMemcpy(p->dimage, img, bytes, cudaMemcpyHostToDevice))) return fail(e);
   if ((e = cudaMalloc(&p->status, 16))) return fail(e);
   if ((e = cudaMemset(p->status, 0, 16))) return fail(e);
+  if ((e = cudaFuncSetAttribute(lpf_mlp_tile, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                XSMEM)))
+    return fail(e);
+  if ((e = cudaFuncSetAttribute(lpf_head_tile, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                XSMEM)))
+    return fail(e);
   int lo = 0, hi = 0;
   cudaDeviceGetStreamPriorityRange(&lo, &hi);
   if ((e = cudaStreamCreateWithPriority(&p->side, cudaStreamNonBlocking, lo))) return fail(e);
