@@ -154,6 +154,7 @@ void lxb_plan_destroy(lxb_plan* plan);
  * given stream (the plan also runs work on a stream of its own, joined back before the call's last
  * operation); the plan's device must be current; one call at a time per plan. */
 typedef struct lxb_prefill_plan lxb_prefill_plan;
+#define LXB_PF_MAX_T (1 << 23)  /* tokens per call at most (8,388,608) */
 
 /* Validate a prefill image on the host (every offset, count and index); 0 or LXB_E_IMAGE. */
 int lxb_prefill_check_image(const void* image, size_t bytes);
@@ -188,6 +189,32 @@ int lxb_prefill_layers(lxb_prefill_plan* plan, const uint64_t* state_ptrs, const
  * [T][2560]). Replaces Fast.head_argmax(h) (lx/lx/fast.py:544-550). */
 int lxb_prefill_head(lxb_prefill_plan* plan, const uint16_t* h, int T, int32_t* preds,
                      void* scratch, void* cuda_stream);
+
+/* Per-stage timing (the reference's prof counters have no prefill counterpart; its profiler is
+ * tools/profile_verify.py over torch.profiler): with timing on, every later call records a CUDA
+ * event pair around each kernel launch; lxb_prefill_timing waits for them and returns, per stage
+ * kind (index k, named by lxb_prefill_stage_name), the summed milliseconds and the launches since
+ * the last read (then clears them). The decay scans run on the plan's second stream beside the
+ * others; their time overlaps. */
+#define LXB_PF_ROWS 0
+#define LXB_PF_NORM 1
+#define LXB_PF_TAPS 2
+#define LXB_PF_GATES 3
+#define LXB_PF_SCAN 4
+#define LXB_PF_CONV 5
+#define LXB_PF_WINDOWS 6
+#define LXB_PF_QK 7
+#define LXB_PF_RECUR 8
+#define LXB_PF_GNORM 9
+#define LXB_PF_OUT 10
+#define LXB_PF_MLP 11
+#define LXB_PF_DOWN 12
+#define LXB_PF_HEAD 13
+#define LXB_PF_REDUCE 14
+#define LXB_PF_STAGES 15
+int lxb_prefill_set_timing(lxb_prefill_plan* plan, int on);
+int lxb_prefill_timing(lxb_prefill_plan* plan, double* ms, long long* launches, int n);
+const char* lxb_prefill_stage_name(int k);
 
 /* The prefill plan's status word (LXB_S_TOKEN), after the stream has synchronised. */
 int lxb_prefill_status(lxb_prefill_plan* plan, lxb_error* err);

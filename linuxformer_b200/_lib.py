@@ -58,6 +58,9 @@ SIGNATURES = {
     "lxb_prefill_status": (I, [P, P]),
     "lxb_prefill_status_clear": (I, [P]),
     "lxb_prefill_plan_destroy": (None, [P]),
+    "lxb_prefill_set_timing": (I, [P, I]),
+    "lxb_prefill_timing": (I, [P, P, P, I]),
+    "lxb_prefill_stage_name": (ctypes.c_char_p, [I]),
 }
 
 

@@ -179,9 +179,9 @@ __global__ void __launch_bounds__(128) lpf_norm(const uint16_t* __restrict__ x, 
 }
 
 // Sequential sums over a row's entries (index | bf16 << 16) for two consecutive tokens, from +0:
-// up to 8 entries at a time, their 8 input columns read at once (the loads first, then the adds
+// up to DW entries at a time, their input columns read at once (the loads first, then the adds
 // in order), so a row costs one or two memory round trips instead of one per entry.
-constexpr int DW = 8;
+constexpr int DW = 4;
 struct Acc2 {
   float a0 = 0.0f, a1 = 0.0f;
 };
@@ -646,10 +646,10 @@ __device__ __forceinline__ float o_rr(const uint16_t* orow, float eps, bool& nz)
 
 __global__ void __launch_bounds__(128) lpf_gnorm(PV pv, const lxb_pf_layer* lyp, float eps,
                                                  Buf b) {
-  const int t = blockIdx.x * ROWT + 2 * threadIdx.x;
+  const int t = blockIdx.y * ROWT + 2 * threadIdx.x;  // heads vary fastest (xn stays in L2)
   if (t >= b.T) return;
   const lxb_pf_layer ly = *lyp;
-  const int lvh = blockIdx.y;
+  const int lvh = blockIdx.x;
   const int ostride = ly.n_kh * R * VD;
   const uint16_t* o0 = b.o + (size_t)t * ostride + lvh * VD;
   const uint16_t* o1 = o0 + ostride;  // token t + 1 (inside the padded buffer)
@@ -698,10 +698,10 @@ __global__ void __launch_bounds__(128) lpf_gnorm(PV pv, const lxb_pf_layer* lyp,
 // from +0; where any, x = bf16(x + bf16(s)).
 __global__ void __launch_bounds__(128) lpf_add_rows(PV pv, int ptr_off,
                                                     const uint16_t* __restrict__ in, Buf b) {
-  const int rr = blockIdx.y;
+  const int rr = blockIdx.x;  // rows vary fastest: one token block's inputs stay in L2
   const int p0 = pv.i32[ptr_off + rr], p1 = pv.i32[ptr_off + rr + 1];
   if (p0 == p1) return;
-  const int t = blockIdx.x * ROWT + 2 * threadIdx.x;
+  const int t = blockIdx.y * ROWT + 2 * threadIdx.x;
   Acc2 acc[1];
   bool any[2] = {false, false};
   dots<1, true>(pv.ent + p0, (uint32_t)(p1 - p0), nullptr, 0, in, b.Tp, t, acc, any);
@@ -736,43 +736,87 @@ __device__ __forceinline__ void fill_tile(uint16_t* xs, const uint16_t* __restri
   __syncthreads();
 }
 
-// sequential dot of a row's entries over the tile, lane = token; 8 entries per round
-__device__ __forceinline__ float tdot(const uint32_t* __restrict__ ent, uint32_t n,
-                                      const uint16_t* xs, int lane) {
-  float a = 0.0f;
-  for (uint32_t k = 0; k < n; k += 8) {
-    uint32_t e[8];
+// Two units' gate and up sums over the tile (lane = token): each unit's gate entries then its up
+// entries as one list; both lists walked together four entries at a time (the eight loads
+// first, then the adds in order, each into its own sum).
+struct UnitSums {
+  float g, u;
+};
+__device__ __forceinline__ void gate_up2(const uint32_t* const* __restrict__ ge,
+                                         const uint32_t* ng, const uint32_t* const* __restrict__ ue,
+                                         const uint32_t* nn, const uint16_t* xs, int lane,
+                                         UnitSums* out) {
+  out[0] = out[1] = UnitSums{0.0f, 0.0f};
+  const uint32_t n = max(nn[0], nn[1]);
+  for (uint32_t k = 0; k < n; k += 4) {
+    uint32_t e[2][4];
 #pragma unroll
-    for (int q = 0; q < 8; q++) e[q] = k + q < n ? __ldg(ent + k + q) : 0u;
-    float x[8];
+    for (int r = 0; r < 2; r++)
 #pragma unroll
-    for (int q = 0; q < 8; q++) x[q] = bf(xs[(e[q] & 0xffffu) * XT + lane]);
+      for (int q = 0; q < 4; q++) {
+        const uint32_t i = k + q;
+        e[r][q] = i < ng[r] ? __ldg(ge[r] + i) : i < nn[r] ? __ldg(ue[r] + (i - ng[r])) : 0u;
+      }
+    float x[2][4];
 #pragma unroll
-    for (int q = 0; q < 8; q++)
-      if (k + q < n) a = lx_add(a, lx_mul(x[q], bfhi(e[q])));
+    for (int r = 0; r < 2; r++)
+#pragma unroll
+      for (int q = 0; q < 4; q++) x[r][q] = bf(xs[(e[r][q] & 0xffffu) * XT + lane]);
+#pragma unroll
+    for (int r = 0; r < 2; r++)
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const uint32_t i = k + q;
+        const float pr = lx_mul(x[r][q], bfhi(e[r][q]));
+        if (i < ng[r]) out[r].g = lx_add(out[r].g, pr);
+        else if (i < nn[r]) out[r].u = lx_add(out[r].u, pr);
+      }
   }
-  return a;
 }
 
 // MLP units over a tile: h = bf16(bf16(silu(bf16(gate . xn))) * bf16(up . xn)); each warp takes
-// two units at a time (their loads together)
+// two units at a time and fetches the next pair's descriptors while this pair runs
 __global__ void __launch_bounds__(XW * 32) lpf_mlp_tile(PV pv, int unit0, int n_units, Buf b) {
   extern __shared__ __align__(16) uint16_t xs[];
   const int t0 = blockIdx.x * XT;
-  fill_tile(xs, b.xn, b.Tp, t0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const lxb_pf_unit* units = pv.units + unit0;
+  auto unit = [&](int u) { return u < n_units ? units[u] : lxb_pf_unit{0, 0, 0, 0}; };
+  lxb_pf_unit A = unit(warp), B = unit(warp + XW);
+  fill_tile(xs, b.xn, b.Tp, t0);
   uint16_t* hb = b.hb + t0 + lane;
   for (int u = warp; u < n_units; u += 2 * XW) {
-    const int u2 = u + XW;
-    const lxb_pf_unit A = pv.units[unit0 + u];
-    const lxb_pf_unit B = u2 < n_units ? pv.units[unit0 + u2] : lxb_pf_unit{0, 0, 0, 0};
-    const float ga = tdot(pv.ent + A.g, A.ng, xs, lane);
-    const float ua = tdot(pv.ent + A.u, A.nu, xs, lane);
-    const float gb = tdot(pv.ent + B.g, B.ng, xs, lane);
-    const float ub = tdot(pv.ent + B.u, B.nu, xs, lane);
-    hb[(size_t)u * b.Tp] = lx_rb(lx_mul(lx_rbf(lx_silu(lx_rbf(ga))), lx_rbf(ua)));
-    if (u2 < n_units) hb[(size_t)u2 * b.Tp] = lx_rb(lx_mul(lx_rbf(lx_silu(lx_rbf(gb))), lx_rbf(ub)));
+    const lxb_pf_unit nA = unit(u + 2 * XW), nB = unit(u + 3 * XW);
+    const uint32_t* ge[2] = {pv.ent + A.g, pv.ent + B.g};
+    const uint32_t* ue[2] = {pv.ent + A.u, pv.ent + B.u};
+    const uint32_t ng[2] = {A.ng, B.ng}, nn[2] = {A.ng + A.nu, B.ng + B.nu};
+    UnitSums d[2];
+    gate_up2(ge, ng, ue, nn, xs, lane, d);
+    hb[(size_t)u * b.Tp] = lx_rb(lx_mul(lx_rbf(lx_silu(lx_rbf(d[0].g))), lx_rbf(d[0].u)));
+    if (u + XW < n_units)
+      hb[(size_t)(u + XW) * b.Tp] =
+          lx_rb(lx_mul(lx_rbf(lx_silu(lx_rbf(d[1].g))), lx_rbf(d[1].u)));
+    A = nA;
+    B = nB;
   }
+}
+
+// a row's dot over the tile (lane = token), four entries at a time
+__device__ __forceinline__ float tdot(const uint32_t* __restrict__ ent, uint32_t n,
+                                      const uint16_t* xs, int lane) {
+  float a = 0.0f;
+  for (uint32_t k = 0; k < n; k += 4) {
+    uint32_t e[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) e[q] = k + q < n ? __ldg(ent + k + q) : 0u;
+    float x[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) x[q] = bf(xs[(e[q] & 0xffffu) * XT + lane]);
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+      if (k + q < n) a = lx_add(a, lx_mul(x[q], bfhi(e[q])));
+  }
+  return a;
 }
 
 struct HeadArgs {
@@ -891,6 +935,14 @@ struct lxb_prefill_plan {
   cudaStream_t side;             // the decay scans run here, beside the layer stages
   cudaEvent_t* ev;               // per layer: gates done, scan done
   int n_ev;
+  // per-stage timing (lxb_prefill_set_timing): an event pair around every launch
+  int timing;
+  static const int TCAP = 1024;
+  cudaEvent_t tev[2 * TCAP];
+  int tstage[TCAP];
+  int n_t, n_tev;
+  double tms[LXB_PF_STAGES];
+  long long tcount[LXB_PF_STAGES];
 };
 
 namespace {
@@ -1091,6 +1143,26 @@ Buf buffers(const Layout& l, void* scratch, int T) {
   } while (0)
 #define LPF_LAUNCHED() LPF_TRY(cudaGetLastError())
 
+int timing_begin(lxb_prefill_plan* p, cudaStream_t s) {
+  if (!p->timing || p->n_t >= lxb_prefill_plan::TCAP || 2 * p->n_t + 1 >= p->n_tev) return -1;
+  if (cudaEventRecord(p->tev[2 * p->n_t], s)) return -1;
+  return p->n_t;
+}
+void timing_end(lxb_prefill_plan* p, int i, int stage, cudaStream_t s) {
+  if (i < 0) return;
+  if (cudaEventRecord(p->tev[2 * i + 1], s)) return;
+  p->tstage[i] = stage;
+  p->n_t = i + 1;
+}
+// one stage launch: the launch, its error check and, with timing on, an event pair around it
+#define LPF_STAGE(k, s, launch)            \
+  do {                                     \
+    const int ti_ = timing_begin(p, s);    \
+    launch;                                \
+    LPF_LAUNCHED();                        \
+    timing_end(p, ti_, k, s);              \
+  } while (0)
+
 // The chip layers over the chunk in b.x (feature-major), updating the state in place.
 int run_layers(lxb_prefill_plan* p, const uint64_t* state_ptrs, const Buf& b, cudaStream_t st) {
   const lxb_pf_header& h = p->hdr;
@@ -1100,32 +1172,25 @@ int run_layers(lxb_prefill_plan* p, const uint64_t* state_ptrs, const Buf& b, cu
   for (int L = 0; L < h.n_layers; L++) {
     const lxb_pf_layer& ly = p->hlayers[L];
     const lxb_pf_layer* dly = p->dlayers + L;
-    lpf_norm<<<nb128, 128, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_in, h.eps, b.xn);
-    LPF_LAUNCHED();
+    LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<nb128, 128, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_in, h.eps, b.xn)));
     if (ly.n_tap) {
-      lpf_taps<<<dim3(nbrow, ly.n_tap), 128, 0, st>>>(p->pv, ly.tap0, b);
-      LPF_LAUNCHED();
+      LPF_STAGE(LXB_PF_TAPS, st, (lpf_taps<<<dim3(nbrow, ly.n_tap), 128, 0, st>>>(p->pv, ly.tap0, b)));
     }
-    lpf_gates<<<dim3(nbrow, NV), 128, 0, st>>>(p->pv, L, b);
-    LPF_LAUNCHED();
+    LPF_STAGE(LXB_PF_GATES, st, (lpf_gates<<<dim3(nbrow, NV), 128, 0, st>>>(p->pv, L, b)));
     // the decay of the other rows, on the side stream from here on
     LPF_TRY(cudaEventRecord(p->ev[2 * L], st));
     LPF_TRY(cudaStreamWaitEvent(p->side, p->ev[2 * L], 0));
-    lpf_scan<<<dim3(NV, KD / 8), 256, 0, p->side>>>(p->pv, dly, L, sp, b);
-    LPF_LAUNCHED();
+    LPF_STAGE(LXB_PF_SCAN, p->side, (lpf_scan<<<dim3(NV, KD / 8), 256, 0, p->side>>>(p->pv, dly, L, sp, b)));
     LPF_TRY(cudaEventRecord(p->ev[2 * L + 1], p->side));
     if (ly.n_tap) {
-      lpf_conv<<<dim3(nbrow, ly.n_tap), 128, 0, st>>>(p->pv, ly.tap0, sp, L, b);
-      LPF_LAUNCHED();
+      LPF_STAGE(LXB_PF_CONV, st, (lpf_conv<<<dim3(nbrow, ly.n_tap), 128, 0, st>>>(p->pv, ly.tap0, sp, L, b)));
     }
-    lpf_windows<<<CONV / 128, 128, 0, st>>>(p->pv, dly, sp, L, b);
-    LPF_LAUNCHED();
+    LPF_STAGE(LXB_PF_WINDOWS, st, (lpf_windows<<<CONV / 128, 128, 0, st>>>(p->pv, dly, sp, L, b)));
     if (ly.n_kh) {
-      lpf_qk<<<dim3(nb128, ly.n_kh), 128, 0, st>>>(p->pv, dly, b);
-      LPF_LAUNCHED();
+      LPF_STAGE(LXB_PF_QK, st, (lpf_qk<<<dim3(nb128, ly.n_kh), 128, 0, st>>>(p->pv, dly, b)));
       const int g = ly.n_kh * R;
       switch (ly.nl) {  // the register slots: the layer's most live rows, rounded up a little
-#define LPF_R(n) lpf_recur<n><<<g, 128, 0, st>>>(p->pv, dly, L, sp, b); break
+#define LPF_R(n) LPF_STAGE(LXB_PF_RECUR, st, (lpf_recur<n><<<g, 128, 0, st>>>(p->pv, dly, L, sp, b))); break
         case 1: case 2: LPF_R(2);
         case 3: LPF_R(3);
         case 4: LPF_R(4);
@@ -1138,19 +1203,13 @@ int run_layers(lxb_prefill_plan* p, const uint64_t* state_ptrs, const Buf& b, cu
         default: LPF_R(31);
 #undef LPF_R
       }
-      LPF_LAUNCHED();
-      lpf_gnorm<<<dim3(nbrow, g), 128, 0, st>>>(p->pv, dly, h.eps, b);
-      LPF_LAUNCHED();
-      lpf_add_rows<<<dim3(nbrow, H), 128, 0, st>>>(p->pv, ly.out_ptr, b.on, b);
-      LPF_LAUNCHED();
+      LPF_STAGE(LXB_PF_GNORM, st, (lpf_gnorm<<<dim3(g, nbrow), 128, 0, st>>>(p->pv, dly, h.eps, b)));
+      LPF_STAGE(LXB_PF_OUT, st, (lpf_add_rows<<<dim3(H, nbrow), 128, 0, st>>>(p->pv, ly.out_ptr, b.on, b)));
     }
     if (ly.n_units) {
-      lpf_norm<<<nb128, 128, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_post, h.eps, b.xn);
-      LPF_LAUNCHED();
-      lpf_mlp_tile<<<b.Tp / XT, XW * 32, XSMEM, st>>>(p->pv, ly.unit0, ly.n_units, b);
-      LPF_LAUNCHED();
-      lpf_add_rows<<<dim3(nbrow, H), 128, 0, st>>>(p->pv, ly.down_ptr, b.hb, b);
-      LPF_LAUNCHED();
+      LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<nb128, 128, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_post, h.eps, b.xn)));
+      LPF_STAGE(LXB_PF_MLP, st, (lpf_mlp_tile<<<b.Tp / XT, XW * 32, XSMEM, st>>>(p->pv, ly.unit0, ly.n_units, b)));
+      LPF_STAGE(LXB_PF_DOWN, st, (lpf_add_rows<<<dim3(H, nbrow), 128, 0, st>>>(p->pv, ly.down_ptr, b.hb, b)));
     }
   }
   for (int L = 0; L < h.n_layers; L++) LPF_TRY(cudaStreamWaitEvent(st, p->ev[2 * L + 1], 0));
@@ -1161,22 +1220,19 @@ int run_head(lxb_prefill_plan* p, const Buf& b, const Layout& l, int32_t* preds,
              const int32_t* tok, int32_t* first_wrong, cudaStream_t st) {
   const lxb_pf_header& h = p->hdr;
   const int nb128 = (b.T + 127) / 128;
-  lpf_norm<<<nb128, 128, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + h.final_norm, h.eps, b.xn);
-  LPF_LAUNCHED();
+  LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<nb128, 128, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + h.final_norm, h.eps, b.xn)));
   HeadArgs ha;
   ha.V = h.n_vocab;
   ha.n_dense = h.n_dense;
   ha.head_ptr = h.head_ptr;
   memcpy(ha.htab, h.htab, sizeof(ha.htab));
   memcpy(ha.dense_cols, h.dense_cols, sizeof(ha.dense_cols));
-  lpf_head_tile<<<dim3(l.Tp / XT, l.ns), XW * 32, XSMEM, st>>>(p->pv, ha, b);
-  LPF_LAUNCHED();
+  LPF_STAGE(LXB_PF_HEAD, st, (lpf_head_tile<<<dim3(l.Tp / XT, l.ns), XW * 32, XSMEM, st>>>(p->pv, ha, b)));
   if (first_wrong) {
     lpf_fw_init<<<1, 1, 0, st>>>(b.fw);
     LPF_LAUNCHED();
   }
-  lpf_head_reduce<<<nb128, 128, 0, st>>>(l.ns, b, preds, first_wrong ? tok : nullptr);
-  LPF_LAUNCHED();
+  LPF_STAGE(LXB_PF_REDUCE, st, (lpf_head_reduce<<<nb128, 128, 0, st>>>(l.ns, b, preds, first_wrong ? tok : nullptr)));
   if (first_wrong) {
     lpf_fw_done<<<1, 1, 0, st>>>(b.fw, first_wrong);
     LPF_LAUNCHED();
@@ -1252,7 +1308,7 @@ extern "C" size_t lxb_prefill_scratch_bytes(const lxb_prefill_plan* p, int T) {
 }
 
 static int check_call(lxb_prefill_plan* p, void* scratch, int T) {
-  if (!p || !scratch || T < 1 || T > (1 << 26)) return LXB_E_INVAL;
+  if (!p || !scratch || T < 1 || T > LXB_PF_MAX_T) return LXB_E_INVAL;
   if (reinterpret_cast<uintptr_t>(scratch) & 255) return LXB_E_INVAL;
   int dev = -1;
   LPF_TRY(cudaGetDevice(&dev));
@@ -1268,10 +1324,9 @@ extern "C" int lxb_prefill(lxb_prefill_plan* p, const uint64_t* state_ptrs, cons
   cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
   const Layout l = layout(p->hdr, T);
   const Buf b = buffers(l, scratch, T);
-  lpf_rows_in<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(embed, tokens, p->hdr.offset,
-                                                       p->hdr.n_embed_rows, T, l.Tp, b.x,
-                                                       p->status);
-  LPF_LAUNCHED();
+  LPF_STAGE(LXB_PF_ROWS, st,
+            (lpf_rows_in<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(
+                embed, tokens, p->hdr.offset, p->hdr.n_embed_rows, T, l.Tp, b.x, p->status)));
   if ((rc = run_layers(p, state_ptrs, b, st))) return rc;
   return run_head(p, b, l, preds, tokens, first_wrong, st);
 }
@@ -1285,13 +1340,13 @@ extern "C" int lxb_prefill_layers(lxb_prefill_plan* p, const uint64_t* state_ptr
   cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
   const Layout l = layout(p->hdr, T);
   const Buf b = buffers(l, scratch, T);
-  lpf_rows_in<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(h_in, nullptr, 0, T, T, l.Tp, b.x,
-                                                       p->status);
-  LPF_LAUNCHED();
+  LPF_STAGE(LXB_PF_ROWS, st,
+            (lpf_rows_in<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(h_in, nullptr, 0, T, T, l.Tp,
+                                                                  b.x, p->status)));
   if ((rc = run_layers(p, state_ptrs, b, st))) return rc;
   if (h_out) {
-    lpf_rows_out<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(b.x, T, l.Tp, h_out);
-    LPF_LAUNCHED();
+    LPF_STAGE(LXB_PF_ROWS, st,
+              (lpf_rows_out<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(b.x, T, l.Tp, h_out)));
   }
   return LXB_OK;
 }
@@ -1304,9 +1359,9 @@ extern "C" int lxb_prefill_head(lxb_prefill_plan* p, const uint16_t* h, int T, i
   cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
   const Layout l = layout(p->hdr, T);
   const Buf b = buffers(l, scratch, T);
-  lpf_rows_in<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(h, nullptr, 0, T, T, l.Tp, b.x,
-                                                       p->status);
-  LPF_LAUNCHED();
+  LPF_STAGE(LXB_PF_ROWS, st,
+            (lpf_rows_in<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(h, nullptr, 0, T, T, l.Tp,
+                                                                  b.x, p->status)));
   return run_head(p, b, l, preds, nullptr, nullptr, st);
 }
 
@@ -1325,8 +1380,49 @@ extern "C" int lxb_prefill_status_clear(lxb_prefill_plan* p) {
   return cuda_rc(cudaMemset(p->status, 0, 16));
 }
 
+extern "C" int lxb_prefill_set_timing(lxb_prefill_plan* p, int on) {
+  if (!p) return LXB_E_INVAL;
+  if (on && !p->n_tev) {
+    for (int k = 0; k < 2 * lxb_prefill_plan::TCAP; k++) {
+      cudaError_t e = cudaEventCreate(&p->tev[k]);
+      if (e) return cuda_rc(e);
+      p->n_tev = k + 1;
+    }
+  }
+  p->timing = on ? 1 : 0;
+  return LXB_OK;
+}
+
+extern "C" int lxb_prefill_timing(lxb_prefill_plan* p, double* ms, long long* launches, int n) {
+  if (!p || n < 0 || (n && (!ms || !launches))) return LXB_E_INVAL;
+  for (int i = 0; i < p->n_t; i++) {
+    float t = 0.0f;
+    cudaError_t e = cudaEventSynchronize(p->tev[2 * i + 1]);
+    if (!e) e = cudaEventElapsedTime(&t, p->tev[2 * i], p->tev[2 * i + 1]);
+    if (e) return cuda_rc(e);
+    p->tms[p->tstage[i]] += t;
+    p->tcount[p->tstage[i]]++;
+  }
+  p->n_t = 0;
+  for (int k = 0; k < n && k < LXB_PF_STAGES; k++) {
+    ms[k] = p->tms[k];
+    launches[k] = p->tcount[k];
+    p->tms[k] = 0.0;
+    p->tcount[k] = 0;
+  }
+  return LXB_OK;
+}
+
+extern "C" const char* lxb_prefill_stage_name(int k) {
+  static const char* names[LXB_PF_STAGES] = {"rows", "norm", "taps", "gates", "scan", "conv",
+                                             "windows", "qk", "recur", "gnorm", "out", "mlp",
+                                             "down", "head", "reduce"};
+  return k >= 0 && k < LXB_PF_STAGES ? names[k] : "";
+}
+
 extern "C" void lxb_prefill_plan_destroy(lxb_prefill_plan* p) {
   if (!p) return;
+  for (int k = 0; k < p->n_tev; k++) cudaEventDestroy(p->tev[k]);
   if (p->ev)
     for (int k = 0; k < p->n_ev; k++)
       if (p->ev[k]) cudaEventDestroy(p->ev[k]);

@@ -81,6 +81,19 @@ class Prefill:
                                 first_wrong.data_ptr() if first_wrong is not None else None,
                                 sc.data_ptr(), self._stream(stream)), "lxb_prefill")
 
+    def set_timing(self, on: bool) -> None:
+        """Record a CUDA event pair around every later kernel launch (per-stage timing)."""
+        check(lib().lxb_prefill_set_timing(self.plan, int(on)), "lxb_prefill_set_timing")
+
+    def timing(self) -> dict:
+        """{stage: (milliseconds, launches)} since the last read (waits for the events)."""
+        n = 15
+        ms = (ctypes.c_double * n)()
+        cnt = (ctypes.c_longlong * n)()
+        check(lib().lxb_prefill_timing(self.plan, ms, cnt, n), "lxb_prefill_timing")
+        return {lib().lxb_prefill_stage_name(k).decode(): (ms[k], cnt[k]) for k in range(n)
+                if cnt[k]}
+
     def status(self) -> Err:
         e = Err()
         check(lib().lxb_prefill_status(self.plan, ctypes.byref(e)), "lxb_prefill_status")

@@ -41,3 +41,28 @@ def job_rate(units_per_rank: float, world: int, slowest_seconds: float) -> float
     if slowest_seconds <= 0:
         raise ValueError("a non-positive time")
     return units_per_rank * world / slowest_seconds
+
+
+def shard(n_streams: int, rank: int, world: int) -> list[int]:
+    """The streams rank ``rank`` runs when ``n_streams`` independent machines are split evenly
+    over ``world`` GPUs: a contiguous block of n_streams / world (config 4: 64 streams over
+    1/2/4/8 GPUs)."""
+    if world < 1 or not 0 <= rank < world or n_streams % world:
+        raise ValueError(f"{n_streams} streams do not split evenly over {world} ranks")
+    k = n_streams // world
+    return list(range(rank * k, (rank + 1) * k))
+
+
+def gather_digests(mine: dict[int, str], device=None) -> dict[int, str]:
+    """Every rank's {stream: digest}, merged on every rank (a host-side object gather after the
+    timed region; the decode path itself exchanges nothing)."""
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return dict(mine)
+    parts = [None] * dist.get_world_size()
+    dist.all_gather_object(parts, mine)
+    out: dict[int, str] = {}
+    for p in parts:
+        out.update(p)
+    return out
