@@ -145,6 +145,7 @@ struct __align__(16) Smem {
   float ob[R][VD];                 // o per value head (bf16 values)
   float beta[R], g[R];
   uint32_t dbm[R][8];              // a decaying item's nonzero-row bitmaps
+  uint32_t nzm[R][8];              // ... the rows still nonzero after this token's decay
   float red[40];
   int nq, nk;
   int qkn;                         // the q / k lists are l2-normed already (eager_block)
@@ -629,7 +630,8 @@ __device__ __forceinline__ void item_fire(const Dev& P, const Run& run, Smem& sm
 // The decay of a thread's two value heads rA and rA + 4 (SA, SB at row 0, its column): every row
 // that may be nonzero (the bitmaps, staged in sm.dbm) times exp(g), each head's rows gathered
 // across the bitmap words, 12 loads in flight per round.
-__device__ __forceinline__ void item_decay(const Smem& sm, float* SA, float* SB, int rA) {
+__device__ __forceinline__ void item_decay(Smem& sm, float* SA, float* SB, int rA) {
+  const int lane = threadIdx.x & 31;
   constexpr int HPT = 2, D = 6, HS = 4;
   float* S[HPT] = {SA, SB};
   float e[HPT];
@@ -665,8 +667,15 @@ __device__ __forceinline__ void item_decay(const Smem& sm, float* SA, float* SB,
 #pragma unroll
     for (int k = 0; k < HPT; k++)
 #pragma unroll
-      for (int q = 0; q < D; q++)
-        if (ix[k][q] >= 0) S[k][ix[k][q] * VD] = lx_mul(v[k][q], e[k]);
+      for (int q = 0; q < D; q++) {
+        const float nv = lx_mul(v[k][q], e[k]);
+        if (ix[k][q] >= 0) S[k][ix[k][q] * VD] = nv;
+        // the warp's 32 columns of the row (its rows are the same on every lane): a row whose
+        // 128 columns all decayed to zero leaves the bitmap (zero rows stay zero)
+        const unsigned nzb = __ballot_sync(0xffffffffu, ix[k][q] >= 0 && nv != 0.0f);
+        if (lane == 0 && nzb)
+          atomicOr(&sm.nzm[rA + k * HS][ix[k][q] >> 5], 1u << (ix[k][q] & 31));
+      }
   }
 }
 
@@ -899,8 +908,10 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
     if (warp == 0) qk_norm(sm, nq, nk);
     __syncthreads();
   }
-  if (anyg && t < R * 8)  // the decaying heads' nonzero-row bitmaps, for item_decay
+  if (anyg && t < R * 8) {  // the decaying heads' nonzero-row bitmaps, for item_decay
     sm.dbm[t >> 3][t & 7] = bm[(bi.kh * R + (t >> 3)) * 8 + (t & 7)];
+    sm.nzm[t >> 3][t & 7] = 0u;
+  }
   if (nk) item_fire(P, run, sm, B, bi, conv, s, L, step, w_in, r_in);  // (ends with a barrier)
   else if (anyg) __syncthreads();
   // the delta rule, thread = (state column j, value heads rA and rA + 4): the decay and the
@@ -911,7 +922,12 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
     const int rA = t >> 7;
     float* SA = rec + (size_t)(bi.kh * R + rA) * KD * VD + j;
     float* SB = SA + (size_t)4 * KD * VD;
-    if (anyg) item_decay(sm, SA, SB, rA);
+    if (anyg) {
+      item_decay(sm, SA, SB, rA);
+      __syncthreads();  // a decayed head's bitmap: the rows still nonzero (keys add theirs later)
+      if (t < R * 8 && sm.g[t >> 3] != 0.0f)
+        bm[(bi.kh * R + (t >> 3)) * 8 + (t & 7)] = sm.nzm[t >> 3][t & 7];
+    }
     if (nk) {
       item_write(sm, SA, rA, j, nk);
       item_write(sm, SB, rA + 4, j, nk);

@@ -133,6 +133,42 @@ class Prefill:
                 break
         return preds, first
 
+    def run_host(self, ptrs: torch.Tensor, tokens: np.ndarray, chunk: int) -> tuple:
+        """The host-buffer call: token ids from (pinned) host memory in, chunk by chunk, the
+        predictions back in host memory; returns (preds int32 [T], the first mismatch or -1)."""
+        tok = np.ascontiguousarray(tokens, np.int32)
+        T = tok.size
+        pin = getattr(self, "_pin", None)
+        if pin is None or pin[0].numel() < T:
+            pin = (torch.empty(T, dtype=torch.int32).pin_memory(),
+                   torch.empty(T, dtype=torch.int32).pin_memory())
+            self._pin = pin
+        th, ph = pin[0][:T], pin[1][:T]
+        th.numpy()[...] = tok
+        st = torch.cuda.current_stream(self.dev)
+        dtok = torch.empty(T, dtype=torch.int32, device=self.dev)
+        dpred = torch.empty(T, dtype=torch.int32, device=self.dev)
+        fws = torch.empty(-(-T // chunk), dtype=torch.int32, device=self.dev)
+        sc = self.scratch(min(chunk, T))
+        for k, a in enumerate(range(0, T, chunk)):
+            dtok[a:a + chunk].copy_(th[a:a + chunk], non_blocking=True)
+            self.launch(ptrs, dtok[a:a + chunk], dpred[a:a + chunk], fws[k:k + 1], scratch=sc)
+        ph.copy_(dpred, non_blocking=True)
+        fh = fws.cpu()  # syncs the stream
+        st.synchronize()
+        self._raise_status()
+        preds = ph.numpy().copy()
+        first = -1
+        for k, a in enumerate(range(0, T, chunk)):
+            if int(fh[k]) >= 0:
+                first = a + int(fh[k])
+                break
+            b = a + chunk
+            if b < T and preds[b - 1] != tok[b]:
+                first = b - 1
+                break
+        return preds, first
+
     def layers(self, ptrs: torch.Tensor, h: torch.Tensor, out: torch.Tensor | None = None,
                stream=None) -> torch.Tensor:
         """The chip layers on rows h (bf16 [T, 2560] on the device), state updated in place."""
