@@ -146,6 +146,8 @@ struct __align__(16) Smem {
   float beta[R], g[R];
   uint32_t dbm[R][8];              // a decaying item's nonzero-row bitmaps
   uint32_t nzm[R][8];              // ... the rows still nonzero after this token's decay
+  float ge[R];                     // ... exp(g) per value head (1: no decay now)
+  int drows;                       // ... the rows their bitmaps hold (decaying heads)
   float red[40];
   int nq, nk;
   int qkn;                         // the q / k lists are l2-normed already (eager_block)
@@ -625,12 +627,17 @@ __device__ __forceinline__ void item_fire(const Dev& P, const Run& run, Smem& sm
   __syncthreads();
 }
 
-// The state's change for value head r, column j (S points at row 0, column j): the decay of the
-// rows that may be nonzero (the others stay zero), then the key's delta-rule write.
-// The decay of a thread's two value heads rA and rA + 4 (SA, SB at row 0, its column): every row
-// that may be nonzero (the bitmaps, staged in sm.dbm) times exp(g), each head's rows gathered
-// across the bitmap words, 12 loads in flight per round.
-__device__ __forceinline__ void item_decay(Smem& sm, float* SA, float* SB, int rA) {
+// The decay of an item's value heads: every row that may be nonzero (the bitmaps, staged in
+// sm.dbm) times exp(g) (sm.ge), over the whole block: thread (group grp = t / 128, column j)
+// takes, for every decaying head, the rows r with r % 4 == grp, D rows' loads in flight per
+// round, so a head whose rows all stay nonzero (a slow decay holds its values at small
+// subnormals, which its factor rounds back to themselves) costs a quarter of what one thread
+// group alone would. A row whose 128 columns all decayed to zero leaves the bitmap (sm.nzm; zero
+// rows stay zero).
+// A thread's two value heads rA and rA + 4 (SA, SB at row 0, its column): each head's rows
+// gathered across its bitmap words, 12 loads in flight per round. The cheaper walk when the
+// bitmaps hold few rows (the block's threads then have little to share out).
+__device__ __forceinline__ void item_decay_pairs(Smem& sm, float* SA, float* SB, int rA) {
   const int lane = threadIdx.x & 31;
   constexpr int HPT = 2, D = 6, HS = 4;
   float* S[HPT] = {SA, SB};
@@ -640,9 +647,8 @@ __device__ __forceinline__ void item_decay(Smem& sm, float* SA, float* SB, int r
   bool on[HPT];
 #pragma unroll
   for (int k = 0; k < HPT; k++) {
-    const float g = sm.g[rA + k * HS];
-    on[k] = g != 0.0f;
-    e[k] = on[k] ? lx_exp(g) : 1.0f;
+    e[k] = sm.ge[rA + k * HS];
+    on[k] = e[k] != 1.0f;
     w[k] = 0;
     m[k] = on[k] ? sm.dbm[rA + k * HS][0] : 0u;
   }
@@ -670,12 +676,52 @@ __device__ __forceinline__ void item_decay(Smem& sm, float* SA, float* SB, int r
       for (int q = 0; q < D; q++) {
         const float nv = lx_mul(v[k][q], e[k]);
         if (ix[k][q] >= 0) S[k][ix[k][q] * VD] = nv;
-        // the warp's 32 columns of the row (its rows are the same on every lane): a row whose
-        // 128 columns all decayed to zero leaves the bitmap (zero rows stay zero)
         const unsigned nzb = __ballot_sync(0xffffffffu, ix[k][q] >= 0 && nv != 0.0f);
         if (lane == 0 && nzb)
           atomicOr(&sm.nzm[rA + k * HS][ix[k][q] >> 5], 1u << (ix[k][q] & 31));
       }
+  }
+}
+
+__device__ __forceinline__ void item_decay(Smem& sm, float* S0) {
+  const int t = threadIdx.x, lane = t & 31, grp = t >> 7;
+  constexpr int D = 8;
+  const uint32_t msel = 0x11111111u << grp;
+  int h = 0, w = 0;
+  uint32_t m = sm.ge[0] != 1.0f ? (sm.dbm[0][0] & msel) : 0u;
+  for (;;) {
+    int ix[D];  // head * KD + row, or -1
+    bool any = false;
+#pragma unroll
+    for (int q = 0; q < D; q++) {
+      while (!m && h < R) {
+        if (++w == 8) {
+          w = 0;
+          if (++h == R) break;
+          if (sm.ge[h] == 1.0f) {  // this head does not decay now: its bitmap stays
+            w = 7;
+            continue;
+          }
+        }
+        m = sm.dbm[h][w] & msel;
+      }
+      ix[q] = m ? h * KD + w * 32 + __ffs(m) - 1 : -1;
+      m &= m - 1;
+      any |= ix[q] >= 0;
+    }
+    if (!any) break;
+    float v[D];
+#pragma unroll
+    for (int q = 0; q < D; q++) v[q] = ix[q] >= 0 ? S0[(size_t)ix[q] * VD] : 0.0f;
+#pragma unroll
+    for (int q = 0; q < D; q++) {
+      const int hh = ix[q] >= 0 ? ix[q] / KD : 0, row = ix[q] & (KD - 1);
+      const float nv = lx_mul(v[q], sm.ge[hh]);
+      if (ix[q] >= 0) S0[(size_t)ix[q] * VD] = nv;
+      // the warp's 32 columns of the row (its rows are the same on every lane)
+      const unsigned nzb = __ballot_sync(0xffffffffu, ix[q] >= 0 && nv != 0.0f);
+      if (lane == 0 && nzb) atomicOr(&sm.nzm[hh][row >> 5], 1u << (row & 31));
+    }
   }
 }
 
@@ -776,6 +822,7 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const bool spec = lmeta != nullptr;
   if (spec && (bi.n_eager > 32 || (bi.flags & LXB_IT_NONRES))) return ITEM_UNTOUCHED;
+  if (t == 0) sm.drows = 0;  // (read after the barriers below)
   const uint4* ch = reinterpret_cast<const uint4*>(B + bi.eager);
   // the eager rows' products, all entries at once over the block (the entries of the item's
   // eager channels are contiguous in the blob, in channel order); whether any is nonzero comes
@@ -909,8 +956,15 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
     __syncthreads();
   }
   if (anyg && t < R * 8) {  // the decaying heads' nonzero-row bitmaps, for item_decay
-    sm.dbm[t >> 3][t & 7] = bm[(bi.kh * R + (t >> 3)) * 8 + (t & 7)];
+    const uint32_t word = bm[(bi.kh * R + (t >> 3)) * 8 + (t & 7)];
+    sm.dbm[t >> 3][t & 7] = word;
     sm.nzm[t >> 3][t & 7] = 0u;
+    const float g = sm.g[t >> 3];
+    const float e = g != 0.0f ? lx_exp(g) : 1.0f;
+    if ((t & 7) == 0) sm.ge[t >> 3] = e;
+    const int n = e != 1.0f ? __popc(word) : 0;  // (warps 0 and 1: the 64 words)
+    const int wn = __reduce_add_sync(0xffffffffu, n);
+    if (lane == 0) atomicAdd(&sm.drows, wn);
   }
   if (nk) item_fire(P, run, sm, B, bi, conv, s, L, step, w_in, r_in);  // (ends with a barrier)
   else if (anyg) __syncthreads();
@@ -923,9 +977,11 @@ __device__ int gdn_item(const Dev& P, const Run& run, Smem& sm, const unsigned c
     float* SA = rec + (size_t)(bi.kh * R + rA) * KD * VD + j;
     float* SB = SA + (size_t)4 * KD * VD;
     if (anyg) {
-      item_decay(sm, SA, SB, rA);
-      __syncthreads();  // a decayed head's bitmap: the rows still nonzero (keys add theirs later)
-      if (t < R * 8 && sm.g[t >> 3] != 0.0f)
+      if (sm.drows > 128) item_decay(sm, rec + (size_t)bi.kh * R * KD * VD + j);
+      else item_decay_pairs(sm, SA, SB, rA);
+      __syncthreads();  // the decay's rows are shared out over the block: all of it done first,
+                        // then a decayed head's bitmap (the rows still nonzero; keys add theirs)
+      if (t < R * 8 && sm.ge[t >> 3] != 1.0f)
         bm[(bi.kh * R + (t >> 3)) * 8 + (t & 7)] = sm.nzm[t >> 3][t & 7];
     }
     if (nk) {
