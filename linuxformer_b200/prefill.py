@@ -259,3 +259,40 @@ class Fast:
                                     conv_kernel_size=C.TAPS)
             cache.layers[L].update_recurrent_state(
                 torch.zeros(1, C.NV, C.KD, C.VD, dtype=torch.float32, device=dev))
+
+
+def _main(argv) -> None:
+    """python -m linuxformer_b200.prefill [T] [chunks]: config 1's stack from its seeded state,
+    `chunks` chunks of T token ids (uniform over the vocabulary, seed 2) through lxb_prefill, and
+    the time of the last chunk (CUDA events). A self-check and the profiling entry."""
+    T = int(argv[1]) if len(argv) > 1 else 65536
+    n = int(argv[2]) if len(argv) > 2 else 2
+    chip = C.c1(0)
+    st = C.c1_state(chip, 0)
+    pf = Prefill(chip)
+    dev = pf.dev
+    rec = torch.from_numpy(st.recurrent.copy()).to(dev)
+    conv = torch.from_numpy(st.conv.view(np.int16).copy()).to(dev)
+    ptrs = torch.tensor([[rec[L].data_ptr(), conv[L].data_ptr()] for L in range(chip.n_layers)],
+                        dtype=torch.int64, device=dev)
+    ids = torch.from_numpy(np.random.default_rng(2).integers(0, chip.n_vocab, n * T)
+                           .astype(np.int32)).to(dev)
+    preds = torch.empty(n * T, dtype=torch.int32, device=dev)
+    fw = torch.empty(n, dtype=torch.int32, device=dev)
+    sc = pf.scratch(T)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for k in range(n):
+        if k == n - 1:
+            e0.record()
+        pf.launch(ptrs, ids[k * T:(k + 1) * T], preds[k * T:(k + 1) * T], fw[k:k + 1], scratch=sc)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    pf._raise_status()
+    ms = e0.elapsed_time(e1)
+    print(f"{n} chunks of {T} tokens; the last: {ms:.2f} ms, {T / ms * 1e3:.0f} tok/s")
+
+
+if __name__ == "__main__":
+    import sys
+
+    _main(sys.argv)

@@ -16,12 +16,18 @@ its checkout, builds the seeded config-1 stack as a stock model, seeds fp32 recu
   verified mode), the argmax at every position, the same state summaries after each chunk;
 - ``c1_prefill8k.npz``: one 8,192-token chunk of config 3's ids (uniform over the vocabulary,
   seed 2) run as chunked prefill from the seeded state: the argmax and its top-2 margin at every
-  position, the final conv windows and state summaries.
+  position, the final conv windows and state summaries;
+- ``c2_decode.npz``: config 2 (the 37-layer chip-shaped stack, the full 459,982-row head, the
+  seeded RAM/ROM state) decoded greedily for 32 tokens from token 0 by the stock forward, one
+  token per call: the tokens, each step's top-2 margin, the final conv windows (all layers),
+  SHA-256 digests of every layer's conv windows and recurrent state (bits, -0 written as +0),
+  per-(layer, value head) sums and absolute sums of the final recurrent state, and the whole
+  final state of two memory value heads.
 
 Run where the reference's checkout is (its directory in LXB_REFERENCE); the tests only read the
 .npz files:
 
-    LXB_REFERENCE=<checkout> python tests/golden/make_golden.py [decode] [prefill] [prefill8k]
+    LXB_REFERENCE=<checkout> python tests/golden/make_golden.py [decode] [prefill] [prefill8k] [c2]
 """
 
 import os
@@ -81,6 +87,10 @@ def main(parts):
 
     torch.manual_seed(0)
     torch.set_num_threads(os.cpu_count())
+    if "c2" in parts:
+        c2_decode(ref_hf)
+    if not {"decode", "prefill", "prefill8k"} & set(parts):
+        return
     chip = C.c1(0)
     model = C.to_hf(chip)
     st0 = C.c1_state(chip, 0)
@@ -157,5 +167,68 @@ def prefill8k(ref_hf, chip, model, st0, n, emb):
     print(f"prefill 8k: {PRE_8K} tokens in {dt:.1f}s")
 
 
+N_C2 = 32
+
+
+def c2_heads(chip):
+    """Two memory value heads (layer, value head) whose whole final state the fixture keeps:
+    the first memory key head's first value head, and a later layer's fifth."""
+    mem = chip.meta["memory_heads"]
+    (l0, k0), (l1, k1) = mem[0], mem[len(mem) // 2]
+    return ((l0, k0 * 8), (l1, k1 * 8 + 5))
+
+
+def c2_digests(conv, rec):
+    """SHA-256 per layer of the conv windows' and the recurrent state's bits, with -0 written as
+    +0 (the stock forward and the sparse path may differ in a zero's sign only: a product with a
+    zero weight or input that the sparse path never forms)."""
+    import hashlib
+
+    cv = np.where((conv & 0x7FFF) == 0, 0, conv).astype(np.uint16)
+    rv = np.where(rec == 0, np.float32(0), rec).astype(np.float32)
+    cd = [hashlib.sha256(np.ascontiguousarray(cv[L]).tobytes()).hexdigest()
+          for L in range(conv.shape[0])]
+    rd = [hashlib.sha256(np.ascontiguousarray(rv[L]).view(np.uint32).tobytes()).hexdigest()
+          for L in range(rec.shape[0])]
+    return np.array(cd), np.array(rd)
+
+
+def c2_decode(ref_hf):
+    # --- config 2: the 37-layer stack with its full head, one token per call -------------
+    chip = C.c2(1)
+    st0 = C.c2_state(chip, 1)
+    t0 = time.time()
+    model = C.to_hf(chip)
+    print(f"c2 stock model built in {time.time() - t0:.0f}s")
+    n = chip.n_layers
+    emb = model.model.embed_tokens
+    cache = new_cache(model, st0)
+    tok, toks, preds, marg = 0, [], [], []
+    t0 = time.time()
+    for i in range(N_C2):
+        h = ref_hf.chip_forward(model, emb(torch.tensor([[tok]])), cache, n)[0]
+        logits = torch.nn.functional.linear(model.model.norm(h), model.lm_head.weight)
+        p = int(ref_hf.head_argmax(model, h)[0])
+        assert p == int(logits.argmax(-1)[0])
+        toks.append(tok)
+        preds.append(p)
+        marg.append(float(margins(logits)[0]))
+        tok = p
+    dt = time.time() - t0
+    conv = np.stack([cache.layers[L].conv_states[0].view(torch.int16).numpy().view(np.uint16)
+                     for L in range(n)])
+    rec = np.stack([cache.layers[L].recurrent_states[0].float().numpy() for L in range(n)])
+    cd, rd = c2_digests(conv, rec)
+    hid = c2_heads(chip)
+    np.savez_compressed(HERE / "c2_decode.npz", digest=chip.digest(), inputs=np.array(toks),
+                        preds=np.array(preds), margin=np.array(marg, np.float32),
+                        conv=conv, conv_sha=cd, rec_sha=rd,
+                        rec_vh_sum=rec.astype(np.float64).sum(axis=(2, 3)),
+                        rec_vh_abs=np.abs(rec.astype(np.float64)).sum(axis=(2, 3)),
+                        heads=np.stack([rec[L, vh] for L, vh in hid]), head_ids=np.array(hid),
+                        cpu_s=dt)
+    print(f"c2 decode: {N_C2} tokens in {dt:.1f}s, min margin {min(marg):.3g}")
+
+
 if __name__ == "__main__":
-    main(sys.argv[1:] or ["decode", "prefill", "prefill8k"])
+    main(sys.argv[1:] or ["decode", "prefill", "prefill8k", "c2"])
