@@ -412,7 +412,9 @@ def prefill_c3(a, rank, world, dev):
         "stages_ms_per_pass": {k: round(v[0], 3) for k, v in split.items()},
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
                      "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": None,
+                     "traffic": (profile_value("prefill_c3_ncu.md",
+                                               "mlp_tile_traffic_per_launch_65536")
+                                 if dom == "mlp" else None),
                      "note": f"peak of {peak_kind}; the dominant stage by CUDA events; "
                              "algorithmic bytes: its inputs and outputs once per token"},
         "cpu_baseline": {"value": round(cpu_v, 2), "unit": "tok/s", "cores": HOST_THREADS,

@@ -166,3 +166,22 @@ def test_two_plans_share_one_scratch(c1_chip):
         want, _, _ = o.decode(host, [first], len(got[k]))
         assert got[k] == want.tolist(), k
         _same_state(dss[k], 0, host)
+
+
+def test_c2_full_head_matches_stock_stream():
+    """The bench's config 2 (the full 459,982-row head) on the GPU: the 32 greedy tokens of the
+    reference's own stock forward (tests/golden/c2_decode.npz), and the final conv windows and
+    recurrent states bit for bit those of the CPU restatement on the same stream (which holds
+    them to the stock forward's within the tolerance test_oracle_golden states)."""
+    g = np.load(GOLD / "c2_decode.npz")
+    chip = C.c2(1)
+    assert str(g["digest"]) == chip.digest()
+    st0 = C.c2_state(chip, 1)
+    n = len(g["preds"])
+    dec = _decoder(chip, 16)
+    ds = dec.states([st0])
+    preds, _ = dec.run(ds, [[0]], n)
+    assert (preds[0].cpu().numpy() == g["preds"]).all()
+    host = st0.copy()
+    Oracle(chip).decode(host, [0], n)
+    _same_state(ds, 0, host)
