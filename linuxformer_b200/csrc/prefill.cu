@@ -138,41 +138,51 @@ __global__ void __launch_bounds__(256) lpf_rows_out(const uint16_t* x, int T, in
 // The canonical 2560-element sum of squares (lane l of 512 sums x[l + 512 i]^2, i = 0..4; an xor
 // butterfly over each 32 lanes; one over the 16 partial sums), taken by one thread per token; then
 // xn = bf16(x * rsqrt(ssq / 2560 + eps) * (1 + w)).
-__global__ void __launch_bounds__(128) lpf_norm(const uint16_t* __restrict__ x, int T, int Tp,
+// A block takes 32 tokens (lane = token) with 16 warps: warp g sums the canonical lanes
+// 32 g .. 32 g + 31 of its token (each 5 squares, then that group's butterfly) in one thread,
+// warp 0 folds the 16 group sums, and all 512 threads write the normed columns.
+__global__ void __launch_bounds__(512) lpf_norm(const uint16_t* __restrict__ x, int T, int Tp,
                                                 const uint16_t* __restrict__ w, float eps,
                                                 uint16_t* __restrict__ xn) {
-  const int t = blockIdx.x * 128 + threadIdx.x;
-  if (t >= T) return;
-  const uint16_t* xc = x + t;
-  float ws[16];
+  __shared__ float s_w[16][32];
+  __shared__ float s_r[32];
+  const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * 32, t = t0 + lane;
+  const uint16_t* xc = x + t;  // (t < Tp: the buffers are padded; tokens past T are not used)
+  float v[32];
 #pragma unroll
-  for (int g = 0; g < 16; g++) {
-    float v[32];
+  for (int l = 0; l < 32; l++) {
+    const int c = g * 32 + l;
+    float a = bf(xc[(size_t)c * Tp]);
+    float sq = lx_mul(a, a);
 #pragma unroll
-    for (int l = 0; l < 32; l++) {
-      const int lane = g * 32 + l;
-      float a = bf(xc[(size_t)lane * Tp]);
-      float s = lx_mul(a, a);
-#pragma unroll
-      for (int i = 1; i < 5; i++) {
-        a = bf(xc[(size_t)(lane + 512 * i) * Tp]);
-        s = lx_add(s, lx_mul(a, a));
-      }
-      v[l] = s;
+    for (int i = 1; i < 5; i++) {
+      a = bf(xc[(size_t)(c + 512 * i) * Tp]);
+      sq = lx_add(sq, lx_mul(a, a));
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-      for (int l = 0; l < off; l++) v[l] = lx_add(v[l], v[l + off]);
-    ws[g] = v[0];
+    v[l] = sq;
   }
 #pragma unroll
-  for (int off = 8; off > 0; off >>= 1)
+  for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-    for (int l = 0; l < off; l++) ws[l] = lx_add(ws[l], ws[l + off]);
-  const float r = lx_rsqrt(lx_add(lx_div(ws[0], (float)H), eps));
-#pragma unroll 16
-  for (int c = 0; c < H; c++) {
+    for (int l = 0; l < off; l++) v[l] = lx_add(v[l], v[l + off]);
+  s_w[g][lane] = v[0];
+  __syncthreads();
+  if (g == 0) {
+    float ws[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) ws[k] = s_w[k][lane];
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1)
+#pragma unroll
+      for (int k = 0; k < off; k++) ws[k] = lx_add(ws[k], ws[k + off]);
+    s_r[lane] = lx_rsqrt(lx_add(lx_div(ws[0], (float)H), eps));
+  }
+  __syncthreads();
+  if (t >= T) return;
+  const float r = s_r[lane];
+#pragma unroll 4
+  for (int c = g; c < H; c += 16) {
     const float w1 = lx_add(1.0f, bf(__ldg(w + c)));
     xn[(size_t)c * Tp + t] = lx_rb(lx_mul(lx_mul(bf(xc[(size_t)c * Tp]), r), w1));
   }
@@ -1172,7 +1182,7 @@ int run_layers(lxb_prefill_plan* p, const uint64_t* state_ptrs, const Buf& b, cu
   for (int L = 0; L < h.n_layers; L++) {
     const lxb_pf_layer& ly = p->hlayers[L];
     const lxb_pf_layer* dly = p->dlayers + L;
-    LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<nb128, 128, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_in, h.eps, b.xn)));
+    LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<(b.T + 31) / 32, 512, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_in, h.eps, b.xn)));
     if (ly.n_tap) {
       LPF_STAGE(LXB_PF_TAPS, st, (lpf_taps<<<dim3(nbrow, ly.n_tap), 128, 0, st>>>(p->pv, ly.tap0, b)));
     }
@@ -1207,7 +1217,7 @@ int run_layers(lxb_prefill_plan* p, const uint64_t* state_ptrs, const Buf& b, cu
       LPF_STAGE(LXB_PF_OUT, st, (lpf_add_rows<<<dim3(H, nbrow), 128, 0, st>>>(p->pv, ly.out_ptr, b.on, b)));
     }
     if (ly.n_units) {
-      LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<nb128, 128, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_post, h.eps, b.xn)));
+      LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<(b.T + 31) / 32, 512, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_post, h.eps, b.xn)));
       LPF_STAGE(LXB_PF_MLP, st, (lpf_mlp_tile<<<b.Tp / XT, XW * 32, XSMEM, st>>>(p->pv, ly.unit0, ly.n_units, b)));
       LPF_STAGE(LXB_PF_DOWN, st, (lpf_add_rows<<<dim3(H, nbrow), 128, 0, st>>>(p->pv, ly.down_ptr, b.hb, b)));
     }
@@ -1220,7 +1230,7 @@ int run_head(lxb_prefill_plan* p, const Buf& b, const Layout& l, int32_t* preds,
              const int32_t* tok, int32_t* first_wrong, cudaStream_t st) {
   const lxb_pf_header& h = p->hdr;
   const int nb128 = (b.T + 127) / 128;
-  LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<nb128, 128, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + h.final_norm, h.eps, b.xn)));
+  LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<(b.T + 31) / 32, 512, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + h.final_norm, h.eps, b.xn)));
   HeadArgs ha;
   ha.V = h.n_vocab;
   ha.n_dense = h.n_dense;
