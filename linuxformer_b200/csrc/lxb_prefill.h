@@ -91,8 +91,8 @@ typedef struct {
 } lxb_pf_vh;  // 32 bytes
 
 typedef struct {
-  uint32_t g, u;           // gate / up row entries
-  uint32_t ng, nu;
+  uint32_t g, u;           // gate / up row entries: the up entries follow the gate entries
+  uint32_t ng, nu;         // (u == g + ng), so a unit's two rows are one list
 } lxb_pf_unit;  // 16 bytes
 
 #ifdef __cplusplus

@@ -746,16 +746,15 @@ __device__ __forceinline__ void fill_tile(uint16_t* xs, const uint16_t* __restri
   __syncthreads();
 }
 
-// Two units' gate and up sums over the tile (lane = token): each unit's gate entries then its up
-// entries as one list; both lists walked together four entries at a time (the eight loads
-// first, then the adds in order, each into its own sum).
+// Two units' gate and up sums over the tile (lane = token): a unit's gate entries then its up
+// entries are one list in the plan; both units' lists walked together four entries at a time
+// (the eight loads first, then the adds in order, each into its own sum).
 struct UnitSums {
   float g, u;
 };
 __device__ __forceinline__ void gate_up2(const uint32_t* const* __restrict__ ge,
-                                         const uint32_t* ng, const uint32_t* const* __restrict__ ue,
-                                         const uint32_t* nn, const uint16_t* xs, int lane,
-                                         UnitSums* out) {
+                                         const uint32_t* ng, const uint32_t* nn,
+                                         const uint16_t* xs, int lane, UnitSums* out) {
   out[0] = out[1] = UnitSums{0.0f, 0.0f};
   const uint32_t n = max(nn[0], nn[1]);
   for (uint32_t k = 0; k < n; k += 4) {
@@ -763,10 +762,7 @@ __device__ __forceinline__ void gate_up2(const uint32_t* const* __restrict__ ge,
 #pragma unroll
     for (int r = 0; r < 2; r++)
 #pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const uint32_t i = k + q;
-        e[r][q] = i < ng[r] ? __ldg(ge[r] + i) : i < nn[r] ? __ldg(ue[r] + (i - ng[r])) : 0u;
-      }
+      for (int q = 0; q < 4; q++) e[r][q] = k + q < nn[r] ? __ldg(ge[r] + k + q) : 0u;
     float x[2][4];
 #pragma unroll
     for (int r = 0; r < 2; r++)
@@ -798,10 +794,9 @@ __global__ void __launch_bounds__(XW * 32) lpf_mlp_tile(PV pv, int unit0, int n_
   for (int u = warp; u < n_units; u += 2 * XW) {
     const lxb_pf_unit nA = unit(u + 2 * XW), nB = unit(u + 3 * XW);
     const uint32_t* ge[2] = {pv.ent + A.g, pv.ent + B.g};
-    const uint32_t* ue[2] = {pv.ent + A.u, pv.ent + B.u};
     const uint32_t ng[2] = {A.ng, B.ng}, nn[2] = {A.ng + A.nu, B.ng + B.nu};
     UnitSums d[2];
-    gate_up2(ge, ng, ue, nn, xs, lane, d);
+    gate_up2(ge, ng, nn, xs, lane, d);
     hb[(size_t)u * b.Tp] = lx_rb(lx_mul(lx_rbf(lx_silu(lx_rbf(d[0].g))), lx_rbf(d[0].u)));
     if (u + XW < n_units)
       hb[(size_t)(u + XW) * b.Tp] =
@@ -1078,7 +1073,8 @@ bool validate(const unsigned char* img, size_t bytes) {
       return false;
     for (int k = 0; k < ly.n_units; k++) {
       const lxb_pf_unit& u = units[ly.unit0 + k];
-      if (!ents_below(v, u.g, u.ng, H) || !ents_below(v, u.u, u.nu, H)) return false;
+      if ((uint64_t)u.u != (uint64_t)u.g + u.ng || !ents_below(v, u.g, (int64_t)u.ng + u.nu, H))
+        return false;
     }
     if (!ptrs_ok(v, ly.down_ptr, H, (uint32_t)ly.n_units)) return false;
   }

@@ -24,6 +24,7 @@ from __future__ import annotations
 import numpy as np
 
 from . import chip as C
+from .chip import _ranges
 from .tables import _Pool, _f32, _pack
 
 MAGIC = 0x46505A4C
@@ -145,11 +146,21 @@ def build_image(chip: C.Chip) -> tuple[bytes, dict]:
         d_col = np.bincount(ly.down.indices, minlength=C.INTER) if ly.down.nnz else \
             np.zeros(C.INTER, np.int64)
         live_u = np.nonzero((g_n > 0) & (u_n > 0) & (d_col > 0))[0]
-        g_off, _ = _row_ent(ly.gate, ent)
-        u_off, _ = _row_ent(ly.up, ent)
+        # each live unit's gate entries, then its up entries, contiguous (one list per unit)
+        gs, us = ly.gate.rows_subset(live_u), ly.up.rows_subset(live_u)
+        gu_cnt = gs.row_nnz() + us.row_nnz()
+        gu_ptr = np.zeros(len(live_u) + 1, np.int64)
+        np.cumsum(gu_cnt, out=gu_ptr[1:])
+        gu_idx = np.zeros(int(gu_ptr[-1]), np.int64)
+        gu_bits = np.zeros(int(gu_ptr[-1]), np.uint16)
+        g_pos = _ranges(gu_ptr[:-1], gs.row_nnz())
+        u_pos = _ranges(gu_ptr[:-1] + gs.row_nnz(), us.row_nnz())
+        gu_idx[g_pos], gu_bits[g_pos] = gs.indices, gs.data
+        gu_idx[u_pos], gu_bits[u_pos] = us.indices, us.data
+        base = ent.add(_pack(gu_idx, gu_bits))
         un = np.zeros(len(live_u), UNIT)
-        un["g"], un["ng"], un["u"], un["nu"] = g_off[live_u], g_n[live_u], u_off[live_u], \
-            u_n[live_u]
+        un["g"], un["ng"] = base + gu_ptr[:-1], gs.row_nnz()
+        un["u"], un["nu"] = base + gu_ptr[:-1] + gs.row_nnz(), us.row_nnz()
         rec["unit0"], rec["n_units"] = sum(len(x) for x in units), len(live_u)
         units.append(un)
         unit_of = np.full(C.INTER, -1, np.int64)
