@@ -69,7 +69,11 @@ struct PV {
 
 // Scratch buffers of one call (token stride Tp, a multiple of TPAD).
 struct Buf {
-  int T, Tp;
+  int T, Tp;        // tokens of this view; the token stride of every [..][Tp] buffer
+  int Te;           // this view's padded extent (a multiple of 256, at most Tp - its offset)
+  int t_off;        // this view's first token in the call
+  int T_call;       // the call's tokens (the mismatch check runs up to the call's end)
+  int os;           // the token stride of o (max live value heads x 128)
   uint16_t* x;      // [H][Tp] residual (bf16 values)
   uint16_t* xn;     // [H][Tp] the current norm's output
   uint16_t* P;      // [max_tap][Tp] tap channels' projections
@@ -84,7 +88,7 @@ struct Buf {
   uint16_t* on;     // [max_lvh * VD][Tp] gated-norm output
   uint16_t* hb;     // [max_units][Tp] MLP activations
   uint2* hp;        // [n_slices][Tp] head partial maxima (value bits, row)
-  uint32_t* flags;  // [n_layers][NV]: some exp(g) != 1 in this chunk
+  uint32_t* flags;  // [n_layers][NV]: some exp(g) != 1 in this view
   int* fw;          // the first mismatch (working value)
 };
 
@@ -492,7 +496,7 @@ __global__ void __launch_bounds__(128) lpf_recur(PV pv, const lxb_pf_layer* lyp,
   const float* ksv = b.ks + (size_t)s0 * b.Tp;
   const float* qsv = b.qs + (size_t)s0 * b.Tp;
   const uint4* vsrc = vt >= 0 ? reinterpret_cast<const uint4*>(b.Y + (size_t)vt * b.Tp) : nullptr;
-  const int ostride = ly.n_kh * R * VD;
+  const int ostride = b.os;
   uint16_t* op = b.o + lvh * VD + j;
   // the slots past the head's live rows stay zero in both buffers (nothing copies into them)
   for (int k = j; k < 2 * RT * NP; k += 128) {
@@ -587,8 +591,8 @@ __global__ void __launch_bounds__(256) lpf_scan(PV pv, const lxb_pf_layer* lyp, 
   const bool wrote = act;
   if (!__syncthreads_or(act)) return;
   const float* ev = b.e + ((size_t)L * NV + vh) * b.Tp;
-  auto issue = [&](int buf, int t0) {  // b.Tp is a multiple of 256: reads stay inside the row
-    for (int k = threadIdx.x; k < ST / 4 && t0 + 4 * k < b.Tp; k += 256)
+  auto issue = [&](int buf, int t0) {  // b.Te is a multiple of 256: reads stay inside the view
+    for (int k = threadIdx.x; k < ST / 4 && t0 + 4 * k < b.Te; k += 256)
       cp_async16(&s_e[buf][4 * k], ev + t0 + 4 * k);
     cp_commit();
   };
@@ -660,7 +664,7 @@ __global__ void __launch_bounds__(128) lpf_gnorm(PV pv, const lxb_pf_layer* lyp,
   if (t >= b.T) return;
   const lxb_pf_layer ly = *lyp;
   const int lvh = blockIdx.x;
-  const int ostride = ly.n_kh * R * VD;
+  const int ostride = b.os;
   const uint16_t* o0 = b.o + (size_t)t * ostride + lvh * VD;
   const uint16_t* o1 = o0 + ostride;  // token t + 1 (inside the padded buffer)
   uint32_t* on = reinterpret_cast<uint32_t*>(b.on + (size_t)lvh * VD * b.Tp + t);
@@ -917,7 +921,7 @@ __global__ void __launch_bounds__(128) lpf_head_reduce(int ns, Buf b, int32_t* _
     }
   }
   preds[t] = bi;
-  if (tok && t + 1 < b.T && bi != tok[t + 1]) atomicMin(b.fw, t);
+  if (tok && b.t_off + t + 1 < b.T_call && bi != tok[t + 1]) atomicMin(b.fw, b.t_off + t);
 }
 
 __global__ void lpf_fw_init(int* fw) { *fw = INT_MAX; }
@@ -938,8 +942,11 @@ struct lxb_prefill_plan {
   lxb_pf_layer* hlayers;         // host copy
   uint32_t* status;
   cudaStream_t side;             // the decay scans run here, beside the layer stages
-  cudaEvent_t* ev;               // per layer: gates done, scan done
-  int n_ev;
+  cudaEvent_t* ev;               // per layer: gates done, state done (the recurrence's rows and
+  int n_ev;                      // the conv windows, for the next view)
+  static const int NSUB = 4;     // a long chunk runs as this many views, one stream each
+  cudaStream_t sub[NSUB];
+  cudaEvent_t evx[2 + NSUB];     // fork, the scans' end, the views' ends
   // per-stage timing (lxb_prefill_set_timing): an event pair around every launch
   int timing;
   static const int TCAP = 1024;
@@ -1112,7 +1119,7 @@ Layout layout(const lxb_pf_header& h, int T) {
   l.on = take(2 * (size_t)h.max_lvh * VD * Tp);
   l.hb = take(2 * (size_t)h.max_units * Tp);
   l.hp = take(8 * (size_t)l.ns * Tp);
-  l.flags = take(4 * (size_t)h.n_layers * NV);
+  l.flags = take(4 * (size_t)lxb_prefill_plan::NSUB * h.n_layers * NV);
   l.fw = take(16);
   l.total = pos;
   return l;
@@ -1123,6 +1130,9 @@ Buf buffers(const Layout& l, void* scratch, int T) {
   Buf b;
   b.T = T;
   b.Tp = l.Tp;
+  b.Te = l.Tp;
+  b.t_off = 0;
+  b.T_call = T;
   b.x = reinterpret_cast<uint16_t*>(s + l.x);
   b.xn = reinterpret_cast<uint16_t*>(s + l.xn);
   b.P = reinterpret_cast<uint16_t*>(s + l.P);
@@ -1139,6 +1149,32 @@ Buf buffers(const Layout& l, void* scratch, int T) {
   b.hp = reinterpret_cast<uint2*>(s + l.hp);
   b.flags = reinterpret_cast<uint32_t*>(s + l.flags);
   b.fw = reinterpret_cast<int*>(s + l.fw);
+  b.os = 0;  // set by the caller (the plan's max_lvh x 128)
+  return b;
+}
+
+// The view of tokens [off, off + T) of a whole call's buffers (off a multiple of 256): the same
+// strides, every per-token pointer moved by off, its own flags (view k of NSUB).
+Buf view(const Buf& w, int off, int T, int k, int n_layers) {
+  Buf b = w;
+  b.T = T;
+  b.Te = (T + TPAD - 1) / TPAD * TPAD;
+  b.t_off = off;
+  b.x += off;
+  b.xn += off;
+  b.P += off;
+  b.Y += off;
+  b.e += off;
+  b.beta += off;
+  b.qs += off;
+  b.ks += off;
+  b.qm += off;
+  b.km += off;
+  b.o += (size_t)off * w.os;
+  b.on += off;
+  b.hb += off;
+  b.hp += off;
+  b.flags += (size_t)k * n_layers * NV;
   return b;
 }
 
@@ -1169,61 +1205,116 @@ void timing_end(lxb_prefill_plan* p, int i, int stage, cudaStream_t s) {
     timing_end(p, ti_, k, s);              \
   } while (0)
 
-// The chip layers over the chunk in b.x (feature-major), updating the state in place.
-int run_layers(lxb_prefill_plan* p, const uint64_t* state_ptrs, const Buf& b, cudaStream_t st) {
+// Layer L's stages over one view b on stream st: the decay scan forks to the plan's second stream
+// after the gates; with chained views, the state's part (conv windows, recurrence) waits for the
+// previous view's (wait_prev: ev[2L + 1]) and then marks its own done (mark_done).
+int layer_stages(lxb_prefill_plan* p, const uint64_t* sp, const Buf& b, cudaStream_t st, int L,
+                 bool wait_prev, bool mark_done) {
   const lxb_pf_header& h = p->hdr;
-  const int nb128 = (b.T + 127) / 128, nbrow = b.Tp / ROWT;
-  LPF_TRY(cudaMemsetAsync(b.flags, 0, 4 * (size_t)h.n_layers * NV, st));
-  const uint64_t* sp = state_ptrs;  // a device table: (recurrent, conv) per layer
-  for (int L = 0; L < h.n_layers; L++) {
-    const lxb_pf_layer& ly = p->hlayers[L];
-    const lxb_pf_layer* dly = p->dlayers + L;
-    LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<(b.T + 31) / 32, 512, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_in, h.eps, b.xn)));
-    if (ly.n_tap) {
-      LPF_STAGE(LXB_PF_TAPS, st, (lpf_taps<<<dim3(nbrow, ly.n_tap), 128, 0, st>>>(p->pv, ly.tap0, b)));
-    }
-    LPF_STAGE(LXB_PF_GATES, st, (lpf_gates<<<dim3(nbrow, NV), 128, 0, st>>>(p->pv, L, b)));
-    // the decay of the other rows, on the side stream from here on
-    LPF_TRY(cudaEventRecord(p->ev[2 * L], st));
-    LPF_TRY(cudaStreamWaitEvent(p->side, p->ev[2 * L], 0));
-    LPF_STAGE(LXB_PF_SCAN, p->side, (lpf_scan<<<dim3(NV, KD / 8), 256, 0, p->side>>>(p->pv, dly, L, sp, b)));
-    LPF_TRY(cudaEventRecord(p->ev[2 * L + 1], p->side));
-    if (ly.n_tap) {
-      LPF_STAGE(LXB_PF_CONV, st, (lpf_conv<<<dim3(nbrow, ly.n_tap), 128, 0, st>>>(p->pv, ly.tap0, sp, L, b)));
-    }
-    LPF_STAGE(LXB_PF_WINDOWS, st, (lpf_windows<<<CONV / 128, 128, 0, st>>>(p->pv, dly, sp, L, b)));
-    if (ly.n_kh) {
-      LPF_STAGE(LXB_PF_QK, st, (lpf_qk<<<dim3(nb128, ly.n_kh), 128, 0, st>>>(p->pv, dly, b)));
-      const int g = ly.n_kh * R;
-      switch (ly.nl) {  // the register slots: the layer's most live rows, rounded up a little
+  const int nb128 = (b.T + 127) / 128, nbrow = b.Te / ROWT;
+  const lxb_pf_layer& ly = p->hlayers[L];
+  const lxb_pf_layer* dly = p->dlayers + L;
+  LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<(b.T + 31) / 32, 512, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_in, h.eps, b.xn)));
+  if (ly.n_tap) {
+    LPF_STAGE(LXB_PF_TAPS, st, (lpf_taps<<<dim3(nbrow, ly.n_tap), 128, 0, st>>>(p->pv, ly.tap0, b)));
+  }
+  LPF_STAGE(LXB_PF_GATES, st, (lpf_gates<<<dim3(nbrow, NV), 128, 0, st>>>(p->pv, L, b)));
+  // the decay of the other rows, on the side stream from here on (in view order per layer)
+  LPF_TRY(cudaEventRecord(p->ev[2 * L], st));
+  LPF_TRY(cudaStreamWaitEvent(p->side, p->ev[2 * L], 0));
+  LPF_STAGE(LXB_PF_SCAN, p->side, (lpf_scan<<<dim3(NV, KD / 8), 256, 0, p->side>>>(p->pv, dly, L, sp, b)));
+  if (wait_prev) LPF_TRY(cudaStreamWaitEvent(st, p->ev[2 * L + 1], 0));
+  if (ly.n_tap) {
+    LPF_STAGE(LXB_PF_CONV, st, (lpf_conv<<<dim3(nbrow, ly.n_tap), 128, 0, st>>>(p->pv, ly.tap0, sp, L, b)));
+  }
+  LPF_STAGE(LXB_PF_WINDOWS, st, (lpf_windows<<<CONV / 128, 128, 0, st>>>(p->pv, dly, sp, L, b)));
+  if (ly.n_kh) {
+    LPF_STAGE(LXB_PF_QK, st, (lpf_qk<<<dim3(nb128, ly.n_kh), 128, 0, st>>>(p->pv, dly, b)));
+    const int g = ly.n_kh * R;
+    switch (ly.nl) {  // the register slots: the layer's most live rows, rounded up a little
 #define LPF_R(n) LPF_STAGE(LXB_PF_RECUR, st, (lpf_recur<n><<<g, 128, 0, st>>>(p->pv, dly, L, sp, b))); break
-        case 1: case 2: LPF_R(2);
-        case 3: LPF_R(3);
-        case 4: LPF_R(4);
-        case 5: LPF_R(5);
-        case 6: LPF_R(6);
-        case 7: case 8: LPF_R(8);
-        case 9: case 10: case 11: case 12: LPF_R(12);
-        case 13: case 14: case 15: case 16: LPF_R(16);
-        case 17: case 18: case 19: case 20: case 21: case 22: case 23: case 24: LPF_R(24);
-        default: LPF_R(31);
+      case 1: case 2: LPF_R(2);
+      case 3: LPF_R(3);
+      case 4: LPF_R(4);
+      case 5: LPF_R(5);
+      case 6: LPF_R(6);
+      case 7: case 8: LPF_R(8);
+      case 9: case 10: case 11: case 12: LPF_R(12);
+      case 13: case 14: case 15: case 16: LPF_R(16);
+      case 17: case 18: case 19: case 20: case 21: case 22: case 23: case 24: LPF_R(24);
+      default: LPF_R(31);
 #undef LPF_R
-      }
-      LPF_STAGE(LXB_PF_GNORM, st, (lpf_gnorm<<<dim3(g, nbrow), 128, 0, st>>>(p->pv, dly, h.eps, b)));
-      LPF_STAGE(LXB_PF_OUT, st, (lpf_add_rows<<<dim3(H, nbrow), 128, 0, st>>>(p->pv, ly.out_ptr, b.on, b)));
-    }
-    if (ly.n_units) {
-      LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<(b.T + 31) / 32, 512, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_post, h.eps, b.xn)));
-      LPF_STAGE(LXB_PF_MLP, st, (lpf_mlp_tile<<<b.Tp / XT, XW * 32, XSMEM, st>>>(p->pv, ly.unit0, ly.n_units, b)));
-      LPF_STAGE(LXB_PF_DOWN, st, (lpf_add_rows<<<dim3(H, nbrow), 128, 0, st>>>(p->pv, ly.down_ptr, b.hb, b)));
     }
   }
-  for (int L = 0; L < h.n_layers; L++) LPF_TRY(cudaStreamWaitEvent(st, p->ev[2 * L + 1], 0));
+  if (mark_done) LPF_TRY(cudaEventRecord(p->ev[2 * L + 1], st));
+  if (ly.n_kh) {
+    const int g = ly.n_kh * R;
+    LPF_STAGE(LXB_PF_GNORM, st, (lpf_gnorm<<<dim3(g, nbrow), 128, 0, st>>>(p->pv, dly, h.eps, b)));
+    LPF_STAGE(LXB_PF_OUT, st, (lpf_add_rows<<<dim3(H, nbrow), 128, 0, st>>>(p->pv, ly.out_ptr, b.on, b)));
+  }
+  if (ly.n_units) {
+    LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<(b.T + 31) / 32, 512, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + ly.ln_post, h.eps, b.xn)));
+    LPF_STAGE(LXB_PF_MLP, st, (lpf_mlp_tile<<<b.Te / XT, XW * 32, XSMEM, st>>>(p->pv, ly.unit0, ly.n_units, b)));
+    LPF_STAGE(LXB_PF_DOWN, st, (lpf_add_rows<<<dim3(H, nbrow), 128, 0, st>>>(p->pv, ly.down_ptr, b.hb, b)));
+  }
   return LXB_OK;
 }
 
 int run_head(lxb_prefill_plan* p, const Buf& b, const Layout& l, int32_t* preds,
-             const int32_t* tok, int32_t* first_wrong, cudaStream_t st) {
+             const int32_t* tok, cudaStream_t st);
+
+// The views of a chunk: a chunk of at least 4 x 4,096 tokens runs as NSUB views of equal size
+// (multiples of 256), view k on the plan's stream k. Per layer the views' state parts are chained
+// (view k's conv windows and recurrence wait for view k - 1's), everything else of a view is
+// its own, so layer L + 1 of view k runs beside layer L of view k + 1: the recurrences (a
+// dependent chain per token on few warps) overlap the token-parallel stages of other views.
+int n_views(int T) { return T >= lxb_prefill_plan::NSUB * 4096 ? lxb_prefill_plan::NSUB : 1; }
+
+// The chip layers over the call's rows in w.x (feature-major), updating the state in place;
+// with preds, also the head (tok: the call's token ids for the mismatch check, or NULL). Every
+// stream of the plan is joined back into st before it returns.
+int run_chunk(lxb_prefill_plan* p, const uint64_t* sp, const Buf& w, const Layout& l,
+              cudaStream_t st, int32_t* preds, const int32_t* tok) {
+  const lxb_pf_header& h = p->hdr;
+  const int nv = n_views(w.T);
+  LPF_TRY(cudaMemsetAsync(w.flags, 0, 4 * (size_t)nv * h.n_layers * NV, st));
+  if (nv == 1) {
+    for (int L = 0; L < h.n_layers; L++) {
+      int rc = layer_stages(p, sp, w, st, L, false, false);
+      if (rc) return rc;
+    }
+    if (preds) {
+      int rc = run_head(p, w, l, preds, tok, st);
+      if (rc) return rc;
+    }
+  } else {
+    const int per = (w.T / nv + TPAD - 1) / TPAD * TPAD;
+    LPF_TRY(cudaEventRecord(p->evx[0], st));
+    for (int k = 0; k < nv; k++) {
+      const int off = k * per, n = std::min(per, w.T - off);
+      if (n <= 0) break;
+      cudaStream_t sk = p->sub[k];
+      LPF_TRY(cudaStreamWaitEvent(sk, p->evx[0], 0));
+      const Buf b = view(w, off, n, k, h.n_layers);
+      for (int L = 0; L < h.n_layers; L++) {
+        int rc = layer_stages(p, sp, b, sk, L, k > 0, true);
+        if (rc) return rc;
+      }
+      if (preds) {
+        int rc = run_head(p, b, l, preds + off, tok ? tok + off : nullptr, sk);
+        if (rc) return rc;
+      }
+      LPF_TRY(cudaEventRecord(p->evx[2 + k], sk));
+      LPF_TRY(cudaStreamWaitEvent(st, p->evx[2 + k], 0));
+    }
+  }
+  LPF_TRY(cudaEventRecord(p->evx[1], p->side));
+  LPF_TRY(cudaStreamWaitEvent(st, p->evx[1], 0));
+  return LXB_OK;
+}
+
+int run_head(lxb_prefill_plan* p, const Buf& b, const Layout& l, int32_t* preds,
+             const int32_t* tok, cudaStream_t st) {
   const lxb_pf_header& h = p->hdr;
   const int nb128 = (b.T + 127) / 128;
   LPF_STAGE(LXB_PF_NORM, st, (lpf_norm<<<(b.T + 31) / 32, 512, 0, st>>>(b.x, b.T, b.Tp, p->pv.u16 + h.final_norm, h.eps, b.xn)));
@@ -1233,16 +1324,8 @@ int run_head(lxb_prefill_plan* p, const Buf& b, const Layout& l, int32_t* preds,
   ha.head_ptr = h.head_ptr;
   memcpy(ha.htab, h.htab, sizeof(ha.htab));
   memcpy(ha.dense_cols, h.dense_cols, sizeof(ha.dense_cols));
-  LPF_STAGE(LXB_PF_HEAD, st, (lpf_head_tile<<<dim3(l.Tp / XT, l.ns), XW * 32, XSMEM, st>>>(p->pv, ha, b)));
-  if (first_wrong) {
-    lpf_fw_init<<<1, 1, 0, st>>>(b.fw);
-    LPF_LAUNCHED();
-  }
-  LPF_STAGE(LXB_PF_REDUCE, st, (lpf_head_reduce<<<nb128, 128, 0, st>>>(l.ns, b, preds, first_wrong ? tok : nullptr)));
-  if (first_wrong) {
-    lpf_fw_done<<<1, 1, 0, st>>>(b.fw, first_wrong);
-    LPF_LAUNCHED();
-  }
+  LPF_STAGE(LXB_PF_HEAD, st, (lpf_head_tile<<<dim3(b.Te / XT, l.ns), XW * 32, XSMEM, st>>>(p->pv, ha, b)));
+  LPF_STAGE(LXB_PF_REDUCE, st, (lpf_head_reduce<<<nb128, 128, 0, st>>>(l.ns, b, preds, tok)));
   return LXB_OK;
 }
 
@@ -1293,6 +1376,10 @@ extern "C" int lxb_prefill_plan_create(const void* image, size_t bytes, lxb_pref
   if ((e = cudaStreamCreateWithPriority(&p->side, cudaStreamNonBlocking, lo))) return fail(e);
   for (int k = 0; k < p->n_ev; k++)
     if ((e = cudaEventCreateWithFlags(&p->ev[k], cudaEventDisableTiming))) return fail(e);
+  for (int k = 0; k < lxb_prefill_plan::NSUB; k++)
+    if ((e = cudaStreamCreateWithFlags(&p->sub[k], cudaStreamNonBlocking))) return fail(e);
+  for (int k = 0; k < 2 + lxb_prefill_plan::NSUB; k++)
+    if ((e = cudaEventCreateWithFlags(&p->evx[k], cudaEventDisableTiming))) return fail(e);
   const unsigned char* d = static_cast<const unsigned char*>(p->dimage);
   p->pv.layers = reinterpret_cast<const lxb_pf_layer*>(d + h.sec[LXB_PF_SEC_LAYERS].off);
   p->pv.ent = reinterpret_cast<const uint32_t*>(d + h.sec[LXB_PF_SEC_ENT].off);
@@ -1329,12 +1416,21 @@ extern "C" int lxb_prefill(lxb_prefill_plan* p, const uint64_t* state_ptrs, cons
   if (!state_ptrs || !embed || !tokens || !preds) return LXB_E_INVAL;
   cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
   const Layout l = layout(p->hdr, T);
-  const Buf b = buffers(l, scratch, T);
+  Buf b = buffers(l, scratch, T);
+  b.os = p->hdr.max_lvh * VD;
   LPF_STAGE(LXB_PF_ROWS, st,
             (lpf_rows_in<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(
                 embed, tokens, p->hdr.offset, p->hdr.n_embed_rows, T, l.Tp, b.x, p->status)));
-  if ((rc = run_layers(p, state_ptrs, b, st))) return rc;
-  return run_head(p, b, l, preds, tokens, first_wrong, st);
+  if (first_wrong) {
+    lpf_fw_init<<<1, 1, 0, st>>>(b.fw);
+    LPF_LAUNCHED();
+  }
+  if ((rc = run_chunk(p, state_ptrs, b, l, st, preds, first_wrong ? tokens : nullptr))) return rc;
+  if (first_wrong) {
+    lpf_fw_done<<<1, 1, 0, st>>>(b.fw, first_wrong);
+    LPF_LAUNCHED();
+  }
+  return LXB_OK;
 }
 
 extern "C" int lxb_prefill_layers(lxb_prefill_plan* p, const uint64_t* state_ptrs,
@@ -1345,11 +1441,12 @@ extern "C" int lxb_prefill_layers(lxb_prefill_plan* p, const uint64_t* state_ptr
   if (!state_ptrs || !h_in) return LXB_E_INVAL;
   cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
   const Layout l = layout(p->hdr, T);
-  const Buf b = buffers(l, scratch, T);
+  Buf b = buffers(l, scratch, T);
+  b.os = p->hdr.max_lvh * VD;
   LPF_STAGE(LXB_PF_ROWS, st,
             (lpf_rows_in<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(h_in, nullptr, 0, T, T, l.Tp,
                                                                   b.x, p->status)));
-  if ((rc = run_layers(p, state_ptrs, b, st))) return rc;
+  if ((rc = run_chunk(p, state_ptrs, b, l, st, nullptr, nullptr))) return rc;
   if (h_out) {
     LPF_STAGE(LXB_PF_ROWS, st,
               (lpf_rows_out<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(b.x, T, l.Tp, h_out)));
@@ -1364,11 +1461,12 @@ extern "C" int lxb_prefill_head(lxb_prefill_plan* p, const uint16_t* h, int T, i
   if (!h || !preds) return LXB_E_INVAL;
   cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
   const Layout l = layout(p->hdr, T);
-  const Buf b = buffers(l, scratch, T);
+  Buf b = buffers(l, scratch, T);
+  b.os = p->hdr.max_lvh * VD;
   LPF_STAGE(LXB_PF_ROWS, st,
             (lpf_rows_in<<<dim3(l.Tp / 32, H / 32), 256, 0, st>>>(h, nullptr, 0, T, T, l.Tp,
                                                                   b.x, p->status)));
-  return run_head(p, b, l, preds, nullptr, nullptr, st);
+  return run_head(p, b, l, preds, nullptr, st);
 }
 
 extern "C" int lxb_prefill_status(lxb_prefill_plan* p, lxb_error* err) {
@@ -1433,6 +1531,10 @@ extern "C" void lxb_prefill_plan_destroy(lxb_prefill_plan* p) {
     for (int k = 0; k < p->n_ev; k++)
       if (p->ev[k]) cudaEventDestroy(p->ev[k]);
   if (p->side) cudaStreamDestroy(p->side);
+  for (int k = 0; k < lxb_prefill_plan::NSUB; k++)
+    if (p->sub[k]) cudaStreamDestroy(p->sub[k]);
+  for (int k = 0; k < 2 + lxb_prefill_plan::NSUB; k++)
+    if (p->evx[k]) cudaEventDestroy(p->evx[k]);
   if (p->dimage) cudaFree(p->dimage);
   if (p->status) cudaFree(p->status);
   delete[] p->ev;

@@ -205,3 +205,53 @@ def test_fast_dropin_on_the_references_model(c1_chip):
         cache.layers[L].recurrent_states[0].copy_(rec[L])
     h2 = fast.forward(e, cache)[0]
     assert torch.equal(h1.view(torch.int16), h2.view(torch.int16))
+
+
+def test_layers_and_head_calls_equal_the_fused_call(c1_chip):
+    """lxb_prefill_layers (embedded rows in, rows out) followed by lxb_prefill_head gives what
+    lxb_prefill gives on the token ids: the same predictions and the same state; the per-stage
+    timing reports every stage of the chunk."""
+    ids = _ids(777, c1_chip.n_vocab, seed=9)
+    st0 = C.c1_state(c1_chip, 0)
+    pf = _prefill(c1_chip)
+    rec_a, conv_a, ptrs_a = _states(c1_chip, st0)
+    pf.set_timing(True)
+    pa, _ = pf.run(ptrs_a, ids)
+    split = pf.timing()
+    pf.set_timing(False)
+    assert {"rows", "norm", "gates", "scan", "recur", "gnorm", "out", "mlp", "down", "head",
+            "reduce"} <= set(split)
+    assert split["recur"][1] == c1_chip.n_layers and split["norm"][1] == 2 * c1_chip.n_layers + 1
+    rec_b, conv_b, ptrs_b = _states(c1_chip, st0)
+    emb = pf.embed.view(torch.bfloat16)[torch.from_numpy(ids).long().to(pf.dev)].contiguous()
+    h = pf.layers(ptrs_b, emb)
+    pb = pf.head(h)
+    torch.cuda.synchronize()
+    assert torch.equal(pa, pb)
+    assert torch.equal(conv_a, conv_b)
+    assert torch.equal(rec_a.view(torch.int32), rec_b.view(torch.int32))
+
+
+def test_c1_chunk_in_views_matches_the_forced_decode(c1_chip):
+    """A chunk long enough to run as four views on four streams (16,384 tokens: 4 x 4,096), each
+    view's state part chained to the previous one's, the decay scans ordered on the plan's second
+    stream. The trace is the decode's own greedy stream with one token changed just after the
+    first view boundary: the predictions and the final state equal the decode kernel's with every
+    input forced (itself bit-identical to the CPU restatement), and the first mismatch is the
+    position before the changed token, found across the views."""
+    from linuxformer_b200.runtime import Decoder
+
+    n = 16384
+    st0 = C.c1_state(c1_chip, 0)
+    dec = Decoder(c1_chip, cluster=16)
+    _, inputs = dec.run(dec.states([st0]), [[0]], n)
+    trace = inputs[0].cpu().numpy().copy()
+    trace[4097] = (trace[4097] + 1) % c1_chip.n_vocab
+    ds = dec.states([st0])
+    want, _ = dec.run(ds, [trace.tolist()], n)
+    pf = _prefill(c1_chip)
+    rec, conv, ptrs = _states(c1_chip, st0)
+    preds, first = pf.run(ptrs, trace)
+    assert (preds.cpu().numpy() == want[0].cpu().numpy()).all()
+    assert first == 4096
+    _same(rec, conv, ds.host(0))
