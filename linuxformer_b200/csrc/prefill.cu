@@ -1263,12 +1263,12 @@ int layer_stages(lxb_prefill_plan* p, const uint64_t* sp, const Buf& b, cudaStre
 int run_head(lxb_prefill_plan* p, const Buf& b, const Layout& l, int32_t* preds,
              const int32_t* tok, cudaStream_t st);
 
-// The views of a chunk: a chunk of at least 4 x 4,096 tokens runs as NSUB views of equal size
+// The views of a chunk: a chunk of at least 4 x 2,048 tokens runs as NSUB views of equal size
 // (multiples of 256), view k on the plan's stream k. Per layer the views' state parts are chained
 // (view k's conv windows and recurrence wait for view k - 1's), everything else of a view is
 // its own, so layer L + 1 of view k runs beside layer L of view k + 1: the recurrences (a
 // dependent chain per token on few warps) overlap the token-parallel stages of other views.
-int n_views(int T) { return T >= lxb_prefill_plan::NSUB * 4096 ? lxb_prefill_plan::NSUB : 1; }
+int n_views(int T) { return T >= lxb_prefill_plan::NSUB * 2048 ? lxb_prefill_plan::NSUB : 1; }
 
 // The chip layers over the call's rows in w.x (feature-major), updating the state in place;
 // with preds, also the head (tok: the call's token ids for the mismatch check, or NULL). Every
