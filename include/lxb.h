@@ -41,6 +41,8 @@ extern "C" {
 #define LXB_S_STAGE 2u       /* a staging copy did not land within 2 s: later steps skipped */
 #define LXB_S_HELPER 4u      /* a head helper cluster did not answer in time: the decoding cluster
                                 took its rows itself (informational: the stream is exact) */
+#define LXB_S_SYNC 8u        /* a grid barrier of the text decode did not complete within 2 s: the
+                                launch stopped early, its results are invalid */
 
 typedef struct lxb_plan lxb_plan;
 
@@ -220,6 +222,69 @@ const char* lxb_prefill_stage_name(int k);
 int lxb_prefill_status(lxb_prefill_plan* plan, lxb_error* err);
 int lxb_prefill_status_clear(lxb_prefill_plan* plan);
 void lxb_prefill_plan_destroy(lxb_prefill_plan* plan);
+
+/* ---- config 5: the Qwen3.5-4B-shaped text path, batch-1 decode ----------------------------
+ * The reference runs its text model (the chip layers merged into Qwen3.5-4B, whose Gated DeltaNet
+ * weights are zero-padded to the chip shape, lx/lx/merge.py:82-120) through the stock HF forward
+ * (`generate` on merge.text_view, lx/lx/chat.py:62-73, lx/lx/merge.py:251-280); here one
+ * persistent cooperative kernel per launch decodes it at batch 1, reading only the non-padding
+ * weights (packed by linuxformer_b200/text.py). Layer descriptors hold device addresses: */
+typedef struct {
+  int32_t type;          /* 0: Gated DeltaNet, 1: gated full attention */
+  int32_t pad;
+  uint64_t w1;           /* input projections, bf16 rows of 2560: GDN q k v z b a (12,352 rows),
+                            attention q+gate (per head 256 + 256), k, v (10,240 rows) */
+  uint64_t wo;           /* out_proj / o_proj over the live dims: 2560 x 4096 bf16 */
+  uint64_t wgu;          /* gate row u, then up row u: 18,432 x 2560 bf16 */
+  uint64_t wd;           /* down_proj: 2560 x 9216 bf16 */
+  uint64_t ln_in, ln_post;          /* RMSNorm weights [2560] bf16 */
+  uint64_t conv_w;       /* GDN: conv taps of the q, k, v channels [8192][4] bf16 */
+  uint64_t A_log, dt_bias;          /* GDN: [32] fp32 */
+  uint64_t gnorm;        /* GDN: the gated norm's weight [128] bf16 */
+  uint64_t qn, kn;       /* attention: q_norm / k_norm weights [256] bf16 */
+  uint64_t conv_state;   /* GDN: the stock cache's conv windows [24576][4] bf16 (in place) */
+  uint64_t rec_state;    /* GDN: the stock cache's recurrent state [128][256][128] fp32 (in place) */
+  uint64_t kc, vc;       /* attention: key / value rows [4][max_pos][256] bf16 */
+} lxb_text_layer;
+
+typedef struct lxb_text_plan_s lxb_text_plan;
+
+/* Copy the layer descriptors to the device and size the launch (one CTA per SM). embed: the
+ * embedding [n_embed][2560] bf16; head: the output head [n_vocab][2560] bf16 (the same memory
+ * when tied, as Qwen's head is its embedding's first rows, lx/lx/merge.py:251-280); final_norm
+ * [2560] bf16; rope: cos and sin of every position, [max_pos][2][64] bf16. LXB_E_INVAL for a
+ * null or misaligned address, LXB_E_DEVICE below compute capability 10 or without cooperative
+ * launch. */
+int lxb_text_plan_create(const lxb_text_layer* layers, int n_layers, const void* embed,
+                         int n_embed, const void* head, int n_vocab, const void* final_norm,
+                         const void* rope, int max_pos, float eps, int device,
+                         lxb_text_plan** out);
+size_t lxb_text_scratch_bytes(const lxb_text_plan* plan);
+/* n_tokens steps from position pos0 (pos0 + n_tokens <= max_pos): step t's input is forced[t]
+ * for t < n_forced, else step t-1's prediction; preds[t] = the first argmax of the head after
+ * step t; hidden (or null): [n_tokens][n_layers + 1][2560] fp32, at each step the residual after
+ * every layer, then the final norm's output (the stock model's last hidden state). Scratch (lxb_text_scratch_bytes, 256-byte aligned) holds
+ * the activations and the grid barrier; it needs no initialisation. Async on the stream. */
+int lxb_text_decode(lxb_text_plan* plan, const int32_t* forced, int n_forced, int n_tokens,
+                    int pos0, int32_t* preds, float* hidden, void* scratch,
+                    size_t scratch_bytes, void* cuda_stream);
+int lxb_text_status(lxb_text_plan* plan, uint32_t* status);   /* LXB_S_* bits (synchronises) */
+/* Per-section cycle counters of every CTA (the reference's prof counters, lx/csrc/mega.cu:717-737):
+ * with a DEVICE buffer of lxb_text_grid(plan) * LXB_TEXT_SECTIONS uint64, every later decode adds,
+ * per CTA, the clock64 cycles of each section and the tokens decoded. NULL turns it off. */
+#define LXB_TP_NORM 0     /* input vectors: RMSNorms, the gated norm, conv window shifts */
+#define LXB_TP_GEMV 1     /* dot products and their epilogues */
+#define LXB_TP_WAIT 2     /* waits for a weight chunk to land in shared memory */
+#define LXB_TP_SYNC 3     /* grid barriers */
+#define LXB_TP_GDN 4      /* the GDN step (conv, norms, gates, delta rule) */
+#define LXB_TP_ATT 5      /* attention partials and their combine */
+#define LXB_TP_HEAD 6     /* the argmax reduce of the head */
+#define LXB_TP_TOKENS 7   /* a count: tokens decoded */
+#define LXB_TEXT_SECTIONS 8
+int lxb_text_set_profile(lxb_text_plan* plan, unsigned long long* prof);
+int lxb_text_status_clear(lxb_text_plan* plan);
+int lxb_text_grid(const lxb_text_plan* plan);
+void lxb_text_plan_destroy(lxb_text_plan* plan);
 
 /* A short text for an error code. */
 const char* lxb_error_string(int code);

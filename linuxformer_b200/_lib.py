@@ -18,7 +18,7 @@ class LxbError(RuntimeError):
 
 
 # device status bits (include/lxb.h): the errors; LXB_S_HELPER (4) is informational
-S_TOKEN, S_STAGE, S_HELPER = 1, 2, 4
+S_TOKEN, S_STAGE, S_HELPER, S_SYNC = 1, 2, 4, 8
 S_ERRORS = S_TOKEN | S_STAGE
 
 
@@ -61,6 +61,14 @@ SIGNATURES = {
     "lxb_prefill_set_timing": (I, [P, I]),
     "lxb_prefill_timing": (I, [P, P, P, I]),
     "lxb_prefill_stage_name": (ctypes.c_char_p, [I]),
+    "lxb_text_plan_create": (I, [P, I, P, I, P, I, P, P, I, ctypes.c_float, I, P]),
+    "lxb_text_scratch_bytes": (ctypes.c_size_t, [P]),
+    "lxb_text_decode": (I, [P, P, I, I, I, P, P, P, ctypes.c_size_t, P]),
+    "lxb_text_status": (I, [P, P]),
+    "lxb_text_status_clear": (I, [P]),
+    "lxb_text_grid": (I, [P]),
+    "lxb_text_set_profile": (I, [P, P]),
+    "lxb_text_plan_destroy": (None, [P]),
 }
 
 

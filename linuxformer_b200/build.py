@@ -18,7 +18,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 OUT = PKG / "_build"
 LIB = OUT / "liblxb.so"
-SOURCES = [PKG / "csrc" / "decode.cu", PKG / "csrc" / "prefill.cu"]
+SOURCES = [PKG / "csrc" / "decode.cu", PKG / "csrc" / "prefill.cu", PKG / "csrc" / "text.cu"]
 HEADERS = [PKG / "csrc" / "lxb_math.h", PKG / "csrc" / "lxb_plan.h", PKG / "csrc" / "lxb_prefill.h",
            ROOT / "include" / "lxb.h"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-lineinfo",
