@@ -231,7 +231,7 @@ void lxb_prefill_plan_destroy(lxb_prefill_plan* plan);
  * weights (packed by linuxformer_b200/text.py). Layer descriptors hold device addresses: */
 typedef struct {
   int32_t type;          /* 0: Gated DeltaNet, 1: gated full attention */
-  int32_t pad;
+  int32_t flags;         /* LXB_TEXT_GNORM_F32: the gated norm's weight is an fp32 parameter */
   uint64_t w1;           /* input projections, bf16 rows of 2560: GDN q k v z b a (12,352 rows),
                             attention q+gate (per head 256 + 256), k, v (10,240 rows) */
   uint64_t wo;           /* out_proj / o_proj over the live dims: 2560 x 4096 bf16 */
@@ -240,12 +240,17 @@ typedef struct {
   uint64_t ln_in, ln_post;          /* RMSNorm weights [2560] bf16 */
   uint64_t conv_w;       /* GDN: conv taps of the q, k, v channels [8192][4] bf16 */
   uint64_t A_log, dt_bias;          /* GDN: [32] fp32 */
-  uint64_t gnorm;        /* GDN: the gated norm's weight [128] bf16 */
+  uint64_t gnorm;        /* GDN: the gated norm's weight [128] as fp32 values */
   uint64_t qn, kn;       /* attention: q_norm / k_norm weights [256] bf16 */
   uint64_t conv_state;   /* GDN: the stock cache's conv windows [24576][4] bf16 (in place) */
   uint64_t rec_state;    /* GDN: the stock cache's recurrent state [128][256][128] fp32 (in place) */
   uint64_t kc, vc;       /* attention: key / value rows [4][max_pos][256] bf16 */
 } lxb_text_layer;
+
+/* The gated norm multiplies by its weight in the weight's dtype (Qwen3_5RMSNormGated,
+ * modeling_qwen3_5.py:181-190): a bf16 weight rounds the product to bf16, an fp32 one (Qwen's
+ * stored dtype, kept by lx/lx/merge.py) does not. */
+#define LXB_TEXT_GNORM_F32 1
 
 typedef struct lxb_text_plan_s lxb_text_plan;
 

@@ -577,10 +577,12 @@ __device__ void gdn_windows(const TP& p, const lxb_text_layer& L) {
 }
 
 // P3 of a GDN layer: Qwen3_5RMSNormGated of the 32 heads' outputs into s.xb:
-// bf16(bf16(w * bf16(o * rsqrt(mean(o^2) + eps))) * silu(z))
+// bf16(bf16(w * bf16(o * rsqrt(mean(o^2) + eps))) * silu(z)), the product with w unrounded when w
+// is an fp32 parameter
 __device__ void gdn_gated_norm(const TP& p, TSm& s, const lxb_text_layer& L) {
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
-  const uint16_t* gw = (const uint16_t*)L.gnorm;
+  const float* gw = (const float*)L.gnorm;
+  const bool gf32 = L.flags & LXB_TEXT_GNORM_F32;
   for (int vh = w; vh < 32; vh += NCW) {
     float o[4], sq = 0.0f;
 #pragma unroll
@@ -594,7 +596,7 @@ __device__ void gdn_gated_norm(const TP& p, TSm& s, const lxb_text_layer& L) {
     for (int i = 0; i < 4; i++) {
       const int j = lane * 4 + i;
       const float hn = lx_rbf(lx_mul(o[i], rr));
-      const float u = lx_rbf(lx_mul(bfv(gw[j]), hn));
+      const float u = gf32 ? lx_mul(gw[j], hn) : lx_rbf(lx_mul(gw[j], hn));
       const float z = ldb(p.proj + ZOFF + vh * VD + j);
       s.xb[vh * VD + j] = lx_rb(lx_mul(u, lx_silu(z)));
     }

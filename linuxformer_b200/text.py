@@ -185,7 +185,9 @@ def pack(model, check_padding: bool = True) -> dict:
     """The kernel's weight tables from a config-5-shaped model (every tensor bf16 on the model's
     device, rows contiguous over the hidden dim):
       GDN layer: w1 [12,352 x 2560] = Qwen's q (key-head major), k, v, z, b, a rows; conv
-        [8192 x 4] (q, k, v channels); A_log, dt_bias as fp32 [32]; the gated norm [128];
+        [8192 x 4] (q, k, v channels); A_log, dt_bias and the gated norm's weight [128] as fp32
+        values (flags: 1 when that weight is an fp32 parameter, as in the reference's merged
+        model, so its product is not rounded to bf16);
       attention layer: w1 [10,240 x 2560] = q_proj (per head its 256 query then 256 gate rows),
         k_proj, v_proj; q_norm, k_norm [256];
       both: wo [2560 x 4096] (out_proj over the live value dims / o_proj); wgu [18,432 x 2560]
@@ -211,8 +213,9 @@ def pack(model, check_padding: bool = True) -> dict:
         d["ln_post"] = layer.post_attention_layernorm.weight.detach().to(bf).contiguous()
         if d["type"] == 0:
             ga = layer.linear_attn
-            if ga.norm.weight.dtype != bf:
-                raise Unsupported("the gated norm's weight must be bf16")
+            if ga.norm.weight.dtype not in (bf, torch.float32):
+                raise Unsupported("the gated norm's weight must be bf16 or fp32")
+            d["flags"] = 1 if ga.norm.weight.dtype == torch.float32 else 0
             qkv, z = ga.in_proj_qkv.weight.detach(), ga.in_proj_z.weight.detach()
             b, a = ga.in_proj_b.weight.detach(), ga.in_proj_a.weight.detach()
             out = ga.out_proj.weight.detach()
@@ -228,7 +231,7 @@ def pack(model, check_padding: bool = True) -> dict:
             d["conv"] = ga.conv1d.weight.detach().reshape(CONV, 4).index_select(0, rows).to(bf)
             d["A_log"] = ga.A_log.detach().float().index_select(0, heads).contiguous()
             d["dt_bias"] = ga.dt_bias.detach().float().index_select(0, heads).contiguous()
-            d["gnorm"] = ga.norm.weight.detach().to(bf).contiguous()
+            d["gnorm"] = ga.norm.weight.detach().float().contiguous()
             d["wo"] = out.index_select(1, vrows).to(bf).contiguous()
         else:
             at = layer.self_attn
@@ -295,6 +298,7 @@ class TextDecoder:
         for i, d in enumerate(self.t["layers"]):
             e = desc[i]
             e.type = d["type"]
+            e.flags = d.get("flags", 0)
             e.w1, e.wo, e.wgu, e.wd = (d[k].data_ptr() for k in ("w1", "wo", "wgu", "wd"))
             e.ln_in, e.ln_post = d["ln_in"].data_ptr(), d["ln_post"].data_ptr()
             if d["type"] == 0:
@@ -439,7 +443,7 @@ def _cut_at_stop(new, stop_strings, tok):
 
 class _TLayer(ctypes.Structure):
     """lxb_text_layer (include/lxb.h)."""
-    _fields_ = [("type", ctypes.c_int32), ("pad", ctypes.c_int32),
+    _fields_ = [("type", ctypes.c_int32), ("flags", ctypes.c_int32),
                 ("w1", ctypes.c_uint64), ("wo", ctypes.c_uint64), ("wgu", ctypes.c_uint64),
                 ("wd", ctypes.c_uint64), ("ln_in", ctypes.c_uint64), ("ln_post", ctypes.c_uint64),
                 ("conv_w", ctypes.c_uint64), ("A_log", ctypes.c_uint64),

@@ -17,6 +17,9 @@ its checkout, builds the seeded config-1 stack as a stock model, seeds fp32 recu
 - ``c1_prefill8k.npz``: one 8,192-token chunk of config 3's ids (uniform over the vocabulary,
   seed 2) run as chunked prefill from the seeded state: the argmax and its top-2 margin at every
   position, the final conv windows and state summaries;
+- ``c5_pad.npz``: config 5's Gated DeltaNet padding by the reference's own ``merge.pad_gdn``
+  (lx/lx/merge.py:82-120) applied to Qwen-shaped weights whose entries encode their own row (or
+  column): for every padded tensor, the Qwen row each padded row came from (-1: zero padding);
 - ``c2_decode.npz``: config 2 (the 37-layer chip-shaped stack, the full 459,982-row head, the
   seeded RAM/ROM state) decoded greedily for 32 tokens from token 0 by the stock forward, one
   token per call: the tokens, each step's top-2 margin, the final conv windows (all layers),
@@ -28,6 +31,7 @@ Run where the reference's checkout is (its directory in LXB_REFERENCE); the test
 .npz files:
 
     LXB_REFERENCE=<checkout> python tests/golden/make_golden.py [decode] [prefill] [prefill8k] [c2]
+        [c5pad]
 """
 
 import os
@@ -87,6 +91,8 @@ def main(parts):
 
     torch.manual_seed(0)
     torch.set_num_threads(os.cpu_count())
+    if "c5pad" in parts:
+        c5_pad()
     if "c2" in parts:
         c2_decode(ref_hf)
     if not {"decode", "prefill", "prefill8k"} & set(parts):
@@ -230,5 +236,34 @@ def c2_decode(ref_hf):
     print(f"c2 decode: {N_C2} tokens in {dt:.1f}s, min margin {min(marg):.3g}")
 
 
+def c5_pad():
+    from lx import merge as ref_merge
+
+    q = {"linear_num_key_heads": 16, "linear_key_head_dim": 128, "linear_num_value_heads": 32,
+         "linear_value_head_dim": 128}
+    hdim = 4  # the hidden size does not enter the padding
+
+    def rows(n, cols):  # every entry of row i is i + 1 (exact in fp32)
+        return (torch.arange(n, dtype=torch.float32) + 1)[:, None].expand(n, cols).contiguous()
+
+    w = {"in_proj_qkv.weight": rows(8192, hdim), "conv1d.weight": rows(8192, 4).view(8192, 1, 4),
+         "in_proj_z.weight": rows(4096, hdim), "in_proj_b.weight": rows(32, hdim),
+         "in_proj_a.weight": rows(32, hdim), "dt_bias": torch.arange(32.0) + 1,
+         "A_log": torch.arange(32.0) + 1, "norm.weight": torch.ones(128),
+         "out_proj.weight": rows(4096, hdim).t().contiguous()}
+    out = ref_merge.pad_gdn(w, q, nk=16, dk=256, nv=128, dv=128)
+
+    def src(t):
+        return (t[:, 0] if t.dim() > 1 else t).to(torch.int64).numpy() - 1
+
+    np.savez_compressed(
+        HERE / "c5_pad.npz",
+        qkv=src(out["in_proj_qkv.weight"]), conv=src(out["conv1d.weight"].reshape(-1, 4)),
+        z=src(out["in_proj_z.weight"]), b=src(out["in_proj_b.weight"]),
+        a=src(out["in_proj_a.weight"]), dt_bias=src(out["dt_bias"]), A_log=src(out["A_log"]),
+        out=src(out["out_proj.weight"].t()))
+    print("c5 pad: written")
+
+
 if __name__ == "__main__":
-    main(sys.argv[1:] or ["decode", "prefill", "prefill8k", "c2"])
+    main(sys.argv[1:] or ["decode", "prefill", "prefill8k", "c2", "c5pad"])
