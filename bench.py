@@ -1,7 +1,7 @@
 """Benchmark: the chip hot path on B200, one JSON line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl lxb|reference]
-                    [--mode all|decode|prefill|batched]
+                    [--mode all|decode|prefill|batched|text]
 
 BASELINE.json's metric has three parts; the default line carries all three:
 
@@ -21,6 +21,10 @@ BASELINE.json's metric has three parts; the default line carries all three:
   start token 0), sharded 64 / N per GPU (strong scaling over the 64 streams); a step is one
   launch of all of the rank's streams for --batched-tokens tokens each (8 steps are config 4's
   32,768 tokens). Per-stream SHA-256 digests are gathered on the host after the timed region.
+- ``text``: config 5's batch-1 decode (the Qwen3.5-4B-shaped model with zero-padded GDN layers,
+  seeded random weights): a 4,096-token random-id prompt (seed 4), then a step is 512 greedy
+  tokens from the state after the prompt (put back before every step, so every step decodes
+  positions 4,096-4,607). Every rank runs the whole config (replicas).
 
 Each part: ``value`` from CUDA events on the launch stream around the K timed steps (L2 flushed
 between decode steps; the prefill's and the batched decode's working sets are larger than L2),
@@ -58,6 +62,7 @@ BASELINE_PREFILL = 59236.0  # the reference's published lx.fast compiled verify-
 FALLBACK_HBM = 6650.0
 C3_TOKENS = 1 << 20
 C4_STREAMS = 64
+C5_PROMPT, C5_NEW = 4096, 512
 
 
 def _peaks():
@@ -542,6 +547,156 @@ def batched_c4(a, rank, world, dev):
     }
 
 
+# --- config 5: the text path's batch-1 decode -------------------------------------------------
+def text_bytes_per_token(dec, pos: int) -> float:
+    """Algorithmic bytes of one config-5 decode step at position pos: every non-padding weight
+    once (the packed tables, the head, the norms), the embedding row, the attention layers' key and
+    value rows up to pos plus the new ones, the GDN states' live rows (read and write) and the
+    conv windows of the live channels (read and write), a 4-byte prediction."""
+    from linuxformer_b200 import text as T
+
+    w = sum(v.numel() * v.element_size() for d in dec.t["layers"] for k, v in d.items()
+            if hasattr(v, "numel"))
+    w += dec.t["head"].numel() * 2 + dec.t["norm"].numel() * 2
+    kv = dec.n_att * T.NKV * (pos + 1) * T.HD * 2 * 2
+    gdn = dec.n_gdn * (T.QNV * T.QKD * T.VD * 4 * 2 + (2 * T.QNK * T.QKD + T.QNV * T.QVD) * 8 * 2)
+    return float(w + kv + gdn + T.H * 2 + 4)
+
+
+def text_c5(a, rank, world, dev):
+    import numpy as np
+    import torch
+
+    from linuxformer_b200 import text as T
+    from linuxformer_b200.streams import job_rate, slowest
+    from oracle.text_stock import cpu_copy, steps as stock_steps
+
+    model = T.random_model(seed=4, device=str(dev))
+    dec = T.TextDecoder(model, max_pos=C5_PROMPT + C5_NEW)
+    ids_h = np.random.default_rng(4).integers(0, T.VOCAB, C5_PROMPT).astype(np.int32)
+    ids = torch.from_numpy(ids_h).to(dev)
+    pp = torch.empty(C5_PROMPT, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    dec.launch(ids, C5_PROMPT, pp)
+    torch.cuda.synchronize(dev)
+    prompt_s = time.perf_counter() - t0
+    snap = (dec.conv.clone(), dec.rec.clone(), dec.kc[:, :, :C5_PROMPT].clone(),
+            dec.vc[:, :, :C5_PROMPT].clone())
+    first = pp[-1:].clone()
+    out = torch.empty(C5_NEW, dtype=torch.int32, device=dev)
+
+    def restore():
+        dec.conv.copy_(snap[0])
+        dec.rec.copy_(snap[1])
+        dec.kc[:, :, :C5_PROMPT].copy_(snap[2])
+        dec.vc[:, :, :C5_PROMPT].copy_(snap[3])
+        dec.pos = C5_PROMPT
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(a.warmup):
+        restore()
+        dec.launch(first, C5_NEW, out)
+    ref = out.clone()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    steps = max(1, min(a.steps, a.text_steps))
+    times, same = [], True
+    with Clocks(dev.index) as clk:
+        for _ in range(steps):
+            restore()  # outside the timed region
+            times.append(_event_time(lambda: dec.launch(first, C5_NEW, out), stream))
+            same &= bool(torch.equal(out, ref))
+    if dec.status():
+        raise RuntimeError(f"device status {dec.status():#x}")
+    tot = sum(times)
+    # e2e: the first token from pinned host memory, the predictions back into it
+    h_in = torch.tensor([int(first)], dtype=torch.int32).pin_memory()
+    h_out = torch.empty(C5_NEW, dtype=torch.int32).pin_memory()
+    restore()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    dec.launch(h_in.to(dev, non_blocking=True), C5_NEW, out)
+    h_out.copy_(out, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    e2e_tot = time.perf_counter() - t0
+    tot, e2e_tot = slowest([tot, e2e_tot], dev)
+    if rank != 0:
+        return None
+    # parity: 16 decode steps after the prompt against the stock forward (prompt as one chunk,
+    # then the same inputs token by token), teacher-forced with this stream
+    n_chk = 16
+    restore()
+    hid = torch.empty(n_chk, len(dec.t["layers"]) + 1, T.H, dtype=torch.float32, device=dev)
+    chk = torch.empty(n_chk, dtype=torch.int32, device=dev)
+    dec.launch(first, n_chk, chk, hid)
+    from transformers import DynamicCache
+
+    cache = DynamicCache(config=model.config)
+    with torch.no_grad():
+        model.model(input_ids=ids.long()[None], past_key_values=cache, use_cache=True)
+    inp = torch.cat([first, chk[:-1]]).long()
+    hs, lg = stock_steps(model, inp, cache)
+    top = lg.max(1)
+    gap = float((top.values - lg.gather(1, chk.long()[:, None])[:, 0]).max())
+    agree = float((top.indices.int() == chk).float().mean())
+    dh = float((hid[:, -1] - hs).abs().max())
+    # the CPU baseline: the reference's text path (the stock forward) on the host cores
+    cpu = cpu_copy(model)
+    del model
+    torch.cuda.empty_cache()
+    from oracle.text_stock import zero_cache
+
+    cc = zero_cache(cpu)
+    stock_steps(cpu, ids_h[:8], cc, logits=False)  # a short prompt, then timed decode steps
+    n_cpu = max(2, a.cpu_text_tokens)
+    t0 = time.perf_counter()
+    stock_steps(cpu, ids_h[8:8 + n_cpu], cc)
+    cpu_v = n_cpu / (time.perf_counter() - t0)
+    del cpu
+    value = job_rate(steps * C5_NEW, world, tot)
+    per_gpu = value / world
+    peak, peak_kind = _peaks()
+    btok = text_bytes_per_token(dec, C5_PROMPT + C5_NEW // 2)
+    achieved = btok * per_gpu / 1e9
+    return {
+        "metric": "text decode tok/s (config 5: batch 1 after a 4,096-token prompt)",
+        "value": round(value, 1), "unit": "tok/s", "steps": steps, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights, torch Philox on the device; seeded "
+                "random prompt ids)",
+        "ms_per_step": round(1000 * tot / steps, 3),
+        "config": {"workload": f"c5: Qwen3.5-4B-shaped random-init model (32 layers, GDN padded "
+                               f"to 128 value heads x 256 key dims, vocab {T.VOCAB}), "
+                               f"{C5_PROMPT}-token prompt (seed 4), {steps} steps of {C5_NEW} "
+                               "greedy tokens from the post-prompt state",
+                   "prompt_s": round(prompt_s, 2), "grid": dec.grid,
+                   "l2": "working set larger than L2 (8.4 GB of weights per token)"},
+        "scaling": "weak", "steps_identical": same,
+        "parity_sample": {"steps": n_chk, "argmax_agree": round(agree, 3),
+                          "max_logit_gap": round(gap, 4), "max_hidden_diff": round(dh, 4),
+                          "tolerance": {"logit_gap": 0.25, "hidden": 0.5},
+                          "against": "the stock HF forward on the GPU, prompt as one chunk, "
+                                     "then token by token"},
+        "e2e": {"value": round(job_rate(C5_NEW, world, e2e_tot), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * C5_NEW},
+        "roofline": {"bound": "hbm", "kernel": "lxb_text_kernel", "achieved": round(achieved, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": None,
+                     "note": f"peak of {peak_kind}; algorithmic {btok / 1e9:.3f} GB/token "
+                             "(non-padding weights, attention cache at the mean position, GDN "
+                             "live state rows and windows)"},
+        "cpu_baseline": {"value": round(cpu_v, 3), "unit": "tok/s", "cores": HOST_THREADS,
+                         "kind": "reference",
+                         "sample": f"the reference's text path (stock HF forward, transformers "
+                                   f"torch GDN) on the host: {n_cpu} decode steps after an "
+                                   "8-token prompt"},
+        "clocks": clk.summary(), "gpu_launches": steps,
+    }
+
+
 def reference_arm(a, rank, world, kw):
     """The reference's CPU path on the host cores (rank 0; the other ranks exit): config 2 by the
     CPU restatement (the reference's own stock model of config 2 is 16 GB of dense bf16 layers),
@@ -600,7 +755,35 @@ def reference_arm(a, rank, world, kw):
             line["batched"] = {"metric": "batched tok/s (config 4)", "value": round(bv, 2),
                                "unit": "tok/s", "kind": "reference", "cores": HOST_THREADS,
                                "sample": f"2 streams x {n} tokens, one after another"}
+    if a.mode in ("all", "text"):
+        line["text"] = reference_text(a)
     print(json.dumps(line))
+
+
+def reference_text(a):
+    """Config 5 by the reference's text path (the stock HF forward) on the host cores: the seeded
+    random-init model (made on the GPU when there is one, then copied to the host), an 8-token
+    prompt, then --steps decode steps timed."""
+    import numpy as np
+    import torch
+
+    from linuxformer_b200 import text as T
+    from oracle.text_stock import cpu_copy, steps as stock_steps, zero_cache
+
+    gpu = torch.cuda.is_available()
+    model = T.random_model(seed=4, device="cuda" if gpu else "cpu")
+    cpu = cpu_copy(model) if gpu else model
+    del model
+    ids = np.random.default_rng(4).integers(0, T.VOCAB, 8 + max(1, a.steps)).astype(np.int64)
+    cache = zero_cache(cpu)
+    stock_steps(cpu, ids[:8], cache, logits=False)
+    t0 = time.perf_counter()
+    stock_steps(cpu, ids[8:], cache)
+    v = (len(ids) - 8) / (time.perf_counter() - t0)
+    return {"metric": "text decode tok/s (config 5)", "value": round(v, 3), "unit": "tok/s",
+            "kind": "reference", "cores": HOST_THREADS,
+            "sample": f"{len(ids) - 8} decode steps after an 8-token prompt (the stock HF "
+                      "forward, transformers torch GDN)"}
 
 
 def main():
@@ -611,12 +794,15 @@ def main():
     ap.add_argument("--tokens", type=int, default=32768, help="decode tokens per step (launch)")
     ap.add_argument("--cluster", type=int, default=16)
     ap.add_argument("--impl", default="lxb", choices=["lxb", "reference"])
-    ap.add_argument("--mode", default="all", choices=["all", "decode", "prefill", "batched"])
+    ap.add_argument("--mode", default="all",
+                    choices=["all", "decode", "prefill", "batched", "text"])
     ap.add_argument("--cpu-tokens", type=int, default=400)
     ap.add_argument("--cpu-prefill-tokens", type=int, default=1024)
     ap.add_argument("--prefill-steps", type=int, default=4)
     ap.add_argument("--batched-tokens", type=int, default=4096)
     ap.add_argument("--cpu-batched-tokens", type=int, default=16)
+    ap.add_argument("--text-steps", type=int, default=4)
+    ap.add_argument("--cpu-text-tokens", type=int, default=4)
     ap.add_argument("--vocab", type=int, default=None, help="(tests) a smaller c2 head")
     a = ap.parse_args()
     assert a.warmup >= 3 or a.impl == "reference", "at least 3 warm-up steps"
@@ -645,11 +831,13 @@ def main():
         parts["prefill"] = prefill_c3(a, rank, world, dev)
     if a.mode in ("all", "batched"):
         parts["batched"] = batched_c4(a, rank, world, dev)
+    if a.mode in ("all", "text"):
+        parts["text"] = text_c5(a, rank, world, dev)
     if rank == 0:
         if line is None:  # a single part as the line itself
             (name, part), = parts.items()
-            line = dict(part, n_gpus=world, warmup=a.warmup, higher_is_better=True,
-                        dtype="fp32", data="synthetic (seeded c1 generator)", vs_baseline=None)
+            line = dict({"dtype": "fp32", "data": "synthetic (seeded c1 generator)"}, **part)
+            line.update(n_gpus=world, warmup=a.warmup, higher_is_better=True, vs_baseline=None)
         else:
             line.update(parts)
         print(json.dumps(line))

@@ -64,10 +64,10 @@ def cpu_copy(model, threads: int | None = None):
     with torch.device("meta"):
         m = Qwen3_5ForCausalLM(model.config).to(torch.bfloat16)
     m = m.to_empty(device="cpu")
-    src = dict(model.named_parameters())
-    for name, p in m.named_parameters():
-        p.data.copy_(src[name].data.to(p.dtype), non_blocking=False)
     m.tie_weights()
+    src = dict(model.named_parameters(remove_duplicate=False))
+    for name, p in m.named_parameters():  # a tied parameter once, under its first name
+        p.data.copy_(src[name].data.to(p.dtype), non_blocking=False)
     m.model.rotary_emb = type(model.model.rotary_emb)(config=model.config)
     from linuxformer_b200.text import force_torch_paths
 
