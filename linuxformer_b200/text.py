@@ -451,3 +451,30 @@ class _TLayer(ctypes.Structure):
                 ("qn", ctypes.c_uint64), ("kn", ctypes.c_uint64),
                 ("conv_state", ctypes.c_uint64), ("rec_state", ctypes.c_uint64),
                 ("kc", ctypes.c_uint64), ("vc", ctypes.c_uint64)]
+
+
+def _main(argv=None) -> None:
+    """python -m linuxformer_b200.text [n_layers] [vocab] [prompt] [tokens]: a seeded random-init
+    model (config 5's shape; fewer layers or a smaller vocabulary for small profiling cases), one
+    launch of the prompt, one launch of greedy tokens after it; prints the decode rate."""
+    import sys
+    import time
+
+    args = [int(x) for x in (sys.argv[1:] if argv is None else argv)]
+    n_layers, vocab, n_prompt, n_new = (args + [N_LAYERS, VOCAB, 64, 64][len(args):])[:4]
+    model = random_model(seed=4, n_layers=n_layers, vocab=vocab)
+    dec = TextDecoder(model, max_pos=n_prompt + n_new)
+    ids = torch.from_numpy(np.random.default_rng(4).integers(0, vocab, n_prompt).astype(np.int32))
+    preds = torch.empty(max(n_prompt, n_new), dtype=torch.int32, device=dec.dev)
+    dec.launch(ids.to(dec.dev), n_prompt, preds)
+    torch.cuda.synchronize(dec.dev)
+    t0 = time.perf_counter()
+    dec.launch(preds[n_prompt - 1:n_prompt].clone(), n_new, preds)
+    torch.cuda.synchronize(dec.dev)
+    dt = time.perf_counter() - t0
+    print(f"{n_layers} layers, vocab {vocab}: {n_new} tokens after a {n_prompt}-token prompt in "
+          f"{dt * 1e3:.1f} ms ({n_new / dt:.1f} tok/s), status {dec.status()}")
+
+
+if __name__ == "__main__":
+    _main()
