@@ -379,6 +379,7 @@ def prefill_c3(a, rank, world, dev):
     _, _, ptrs3 = fresh()
     tp, tfirst = pf.run(ptrs3, dinp[0].cpu().numpy(), chunk=1024)
     trace_ok = tfirst == -1 and bool((tp.cpu().numpy() == dp[0].cpu().numpy()).all())
+    draft = self_draft_c1(chip, st0, pf, dev)
     # the CPU baseline: the reference's stock chunked forward on the first ids
     from oracle.stock import StockCPU
 
@@ -427,7 +428,51 @@ def prefill_c3(a, rank, world, dev):
                          "sample": f"the reference's stock chunked forward (HF decoder layers, "
                                    f"transformers torch GDN) on the first {n_cpu} ids"},
         "gpu_launches": int(launches_per_pass * s64),
+        "self_draft": draft,
     }
+
+
+def self_draft_c1(chip, st0, pf, dev, n: int = 8192, D: int = 255) -> dict:
+    """Self-drafting verify (linuxformer_b200.draft) on config 1's greedy stream from token 0:
+    wall time of the whole host-driven loop (each round: draft on the host, one prefill call,
+    a device copy of the state, and a rollback when a draft token was wrong), against the decode
+    kernel's single-stream rate on the same stream; both streams compared token for token."""
+    import numpy as np
+    import torch
+
+    from linuxformer_b200.draft import SelfDraft
+    from linuxformer_b200.runtime import Decoder
+
+    def fresh():
+        rec = torch.from_numpy(st0.recurrent.copy()).to(dev)
+        conv = torch.from_numpy(st0.conv.view(np.int16).copy()).to(dev)
+        ptrs = torch.tensor([[rec[L].data_ptr(), conv[L].data_ptr()]
+                             for L in range(chip.n_layers)], dtype=torch.int64, device=dev)
+        return rec, conv, ptrs
+
+    sd = SelfDraft(pf, draft=D)
+    rec, conv, ptrs = fresh()
+    sd.run(ptrs, [rec, conv], 0, 512)  # warm-up
+    rec, conv, ptrs = fresh()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    got, stats = sd.run(ptrs, [rec, conv], 0, n)
+    torch.cuda.synchronize(dev)
+    t_sd = time.perf_counter() - t0
+    dec = Decoder(chip, cluster=16, device=dev)
+    ds = dec.states([st0])
+    dec.run(ds, [[0]], 64)
+    ds = dec.states([st0])
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    want, _ = dec.run(ds, [[0]], n)
+    torch.cuda.synchronize(dev)
+    t_dec = time.perf_counter() - t0
+    return {"metric": "self-drafting greedy decode tok/s (config 1, one stream)",
+            "value": round(n / t_sd, 1), "unit": "tok/s", "tokens": n, "draft": D,
+            "plain_decode": round(n / t_dec, 1), "speedup": round(t_dec / t_sd, 2),
+            "identical_to_decode": bool((got == want[0].cpu().numpy()).all()), **stats,
+            "timing": "wall clock of the host-driven loop (per-round host sync), both sides"}
 
 
 # --- config 4: batched independent machines -----------------------------------------------
