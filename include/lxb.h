@@ -123,6 +123,31 @@ int lxb_status_clear(lxb_plan* plan);
 int lxb_plan_set_profile(lxb_plan* plan, unsigned long long* prof);
 int lxb_profile_sections(void);
 
+/* The device typing queue (no counterpart in the reference's kernel: its host types a command into
+ * the model-alone machine between launches, Linux.run_alone, lx/lx/linux.py:254-289). With it
+ * set, every later lxb_decode types each stream's queued bytes itself, after any token: a batch of
+ * at most rx_slots bytes (the first as key0_base + byte, the others as key_base + byte) replaces
+ * the model's prediction as the next input once the current input is a record boundary and the
+ * machine has read every byte typed so far. The RX FIFO count is kept per token: an input of
+ * class LXB_T_TYPED adds one, an input of class LXB_T_RX takes one away. tstate holds, per
+ * stream, the bytes typed, the FIFO count, the bytes left in the current batch and the input
+ * after the launch's last step; the launch reads it first and writes it last, so the next
+ * launch takes &tstate[s * 4 + 3] as its forced first input. NULL (or keys NULL) turns it off. */
+#define LXB_T_FINAL 1u  /* a record boundary: a batch may follow this input */
+#define LXB_T_TYPED 2u  /* a typed key (enters the RX FIFO) */
+#define LXB_T_RX 4u     /* the machine reads a byte (leaves the RX FIFO) */
+typedef struct {
+  const int32_t* keys;    /* DEVICE [n_streams][max_keys]: the bytes to type */
+  const int32_t* n_keys;  /* DEVICE [n_streams]: bytes queued per stream */
+  int32_t max_keys;
+  int32_t key0_base, key_base;  /* token of a batch's first byte: key0_base + byte; others: key_base + byte */
+  int32_t rx_slots;       /* bytes per batch */
+  const uint8_t* tclass;  /* DEVICE [n_class]: LXB_T_* bits per token */
+  int32_t n_class;
+  int32_t* tstate;        /* DEVICE [n_streams][4], zeroed before the first launch */
+} lxb_typing;
+int lxb_plan_set_typing(lxb_plan* plan, const lxb_typing* typing);
+
 /* Head helpers: a single-stream launch also starts up to this many more clusters (default 7,
  * at most what the device holds beside the decoding cluster), each of which takes a slice of the
  * output head's rows per token and hands its maximum back through the scratch buffer, so the

@@ -27,6 +27,14 @@ class Caps(ctypes.Structure):
                 ("max_smem_optin", I), ("cluster_launch", I), ("max_clusters", I)]
 
 
+class Typing(ctypes.Structure):
+    """lxb_typing (include/lxb.h)."""
+    _fields_ = [("keys", P), ("n_keys", P), ("max_keys", ctypes.c_int32),
+                ("key0_base", ctypes.c_int32), ("key_base", ctypes.c_int32),
+                ("rx_slots", ctypes.c_int32), ("tclass", P), ("n_class", ctypes.c_int32),
+                ("tstate", P)]
+
+
 class Err(ctypes.Structure):
     _fields_ = [("status", ctypes.c_uint32), ("first_stream", ctypes.c_int32),
                 ("first_step", ctypes.c_int32)]
@@ -42,6 +50,7 @@ SIGNATURES = {
     "lxb_status": (I, [P, P]),
     "lxb_plan_set_profile": (I, [P, P]),
     "lxb_plan_set_head_helpers": (I, [P, I]),
+    "lxb_plan_set_typing": (I, [P, P]),
     "lxb_profile_sections": (I, []),
     "lxb_plan_staging": (I, [P, P, P, P]),
     "lxb_status_clear": (I, [P]),

@@ -113,6 +113,7 @@ struct Run {
   uint4* hpart;                // [slice * cluster + rank]: a helper's maximum {v, row, seq lo, hi}
   unsigned long long epoch;    // this launch's tag (launch count << 32): stale words never match
   int help_drill;              // the helpers start but never answer (the fallback's test)
+  lxb_typing typing;           // the device typing queue (keys == null: off)
 };
 
 // profile sections (lxb_plan_set_profile): cycles spent per CTA
@@ -193,6 +194,7 @@ struct __align__(16) Smem {
   int help_dead;                    // the helpers stopped answering: the cluster does every slice
   float cv, hv, gv;                 // the cluster's first maximum; with the helpers'; rank 0's
   int ci, hi, gi, hok;              // gathering; their rows; whether every helper answered
+  int tq_k, tq_wait, tq_left;       // typing: keys typed, the RX FIFO's count, keys left in a batch
 };
 
 // --- block reductions in the canonical orders -------------------------------------------------
@@ -1633,6 +1635,37 @@ __device__ void materialize(const Dev& P, const Run& run, Smem& sm, int s, int r
   }
 }
 
+// --- the device typing queue ---------------------------------------------------------------
+// The reference types a command into the model-alone machine from the host, a batch of at most
+// RX_SLOTS bytes at a time (KEY0 for the batch's first byte, KEY for the others), only at a record
+// boundary and only when the machine has read every byte typed so far; it sees both conditions
+// only at launch ends (lx/lx/linux.py:254-289). Here every CTA of the decoding cluster applies
+// the same rule after every token (each CTA computes the same, so no exchange is needed).
+__device__ __forceinline__ int type_class(const Run& run, int tok) {
+  return (tok >= 0 && tok < run.typing.n_class) ? run.typing.tclass[tok] : 0;
+}
+// an input token counted into the RX FIFO: a typed key enters it, an RX read leaves it
+__device__ __forceinline__ void type_count(const Run& run, Smem& sm, int tok) {
+  const int c = type_class(run, tok);
+  if (c & LXB_T_TYPED) sm.tq_wait++;
+  if (c & LXB_T_RX) sm.tq_wait--;
+}
+// the next input after the current one (sm.tok) whose prediction is bi
+__device__ __forceinline__ int type_next(const Run& run, Smem& sm, int s, int bi) {
+  const lxb_typing& ty = run.typing;
+  const int nk = ty.n_keys[s];
+  if (sm.tq_left == 0 && sm.tq_k < nk && sm.tq_wait == 0 &&
+      (type_class(run, sm.tok) & LXB_T_FINAL)) {
+    sm.tq_left = min(ty.rx_slots, nk - sm.tq_k) - 1;  // this batch's keys after the first
+    return ty.key0_base + ty.keys[(size_t)s * ty.max_keys + sm.tq_k++];
+  }
+  if (sm.tq_left > 0 && sm.tq_k < nk) {
+    sm.tq_left--;
+    return ty.key_base + ty.keys[(size_t)s * ty.max_keys + sm.tq_k++];
+  }
+  return bi;
+}
+
 __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
   extern __shared__ __align__(128) unsigned char dsm[];
   Smem& sm = *reinterpret_cast<Smem*>(dsm);
@@ -1659,6 +1692,13 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       tok = 0;
     }
     sm.tok = tok;
+    if (run.typing.keys) {
+      const int32_t* ts = run.typing.tstate + (size_t)s * 4;
+      sm.tq_k = ts[0];
+      sm.tq_wait = ts[1];
+      sm.tq_left = ts[2];
+      type_count(run, sm, tok);
+    }
     sm.broken = 0;
     for (int b = 0; b < P.nbuf; b++)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&sm.mbar[b])));
@@ -2147,11 +2187,15 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         const int bi = sm.ci;  // the token: the first maximum of the logits
         if (t == 0) {
           if (rank == 0) run.preds[(size_t)s * run.n_tokens + i] = bi;
-          int nt = (i + 1 < run.n_forced) ? run.forced[(size_t)s * run.n_forced + i + 1] : bi;
+          int nt = (i + 1 < run.n_forced) ? run.forced[(size_t)s * run.n_forced + i + 1]
+                                          : (run.typing.keys ? type_next(run, sm, s, bi) : bi);
           if (nt < 0 || (int64_t)nt + P.offset >= P.n_embed_rows) {
             if (i + 1 < run.n_tokens) set_status(P, LXB_S_TOKEN, s, i + 1);
             nt = 0;
           }
+          // the next input enters the RX FIFO count when it is embedded in this launch; the
+          // one after the last step is the next launch's first input and is counted there
+          if (run.typing.keys && i + 1 < run.n_tokens) type_count(run, sm, nt);
           sm.tok = nt;
         }
       }
@@ -2176,6 +2220,13 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
   }
   if (run.n_help > 0 && rank == 0 && t == 0)  // a helper still waiting for a token may leave
     st_release_u64(run.hseq, run.epoch | 0xffffffffull);
+  if (run.typing.keys && rank == 0 && t == 0) {  // the queue's state, and the next input
+    int32_t* ts = run.typing.tstate + (size_t)s * 4;
+    ts[0] = sm.tq_k;
+    ts[1] = sm.tq_wait;
+    ts[2] = sm.tq_left;
+    ts[3] = sm.tok;
+  }
   cluster.sync();  // every ring write of the launch is visible cluster-wide
   materialize(P, run, sm, s, rank, run.n_tokens);
   cluster.sync();  // no CTA leaves while another may still read its shared memory
@@ -2217,6 +2268,7 @@ struct lxb_plan {
   int help_drill;                // helpers that never answer (lxb_plan_set_head_helpers < 0)
   unsigned long long* prof;
   int smem;  // dynamic shared memory per CTA: Smem, then the staging buffers
+  lxb_typing typing;             // the device typing queue (keys == null: off)
 };
 
 static_assert(offsetof(Smem, own) % 16 == 0 && offsetof(Smem, on) % 16 == 0 && offsetof(Smem, xin) % 16 == 0 &&
@@ -2685,7 +2737,7 @@ static int decode_launch(lxb_plan* p, const uint64_t* state_ptrs, uint32_t* bitm
   Run run{state_ptrs, bitmaps, ring, ring_r, embed, forced, n_forced, n_tokens, preds, inputs,
           p->prof, n_streams, n_help, reinterpret_cast<float*>(xg),
           reinterpret_cast<unsigned long long*>(xg + (size_t)H * 4),
-          reinterpret_cast<uint4*>(xg + (size_t)H * 4 + 16), epoch, p->help_drill};
+          reinterpret_cast<uint4*>(xg + (size_t)H * 4 + 16), epoch, p->help_drill, p->typing};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -2775,6 +2827,19 @@ extern "C" int lxb_plan_set_profile(lxb_plan* p, unsigned long long* prof) {
 }
 
 extern "C" int lxb_profile_sections(void) { return PR_N; }
+
+extern "C" int lxb_plan_set_typing(lxb_plan* p, const lxb_typing* ty) {
+  if (!p) return LXB_E_INVAL;
+  if (!ty || !ty->keys) {
+    memset(&p->typing, 0, sizeof(p->typing));
+    return LXB_OK;
+  }
+  if (!ty->n_keys || !ty->tclass || !ty->tstate || ty->max_keys < 0 || ty->rx_slots < 1 ||
+      ty->n_class < 0)
+    return LXB_E_INVAL;
+  p->typing = *ty;
+  return LXB_OK;
+}
 
 extern "C" int lxb_plan_set_head_helpers(lxb_plan* p, int max_clusters) {
   if (!p || max_clusters < -(LXB_HEADSLICES - LXB_HEADMAIN)) return LXB_E_INVAL;

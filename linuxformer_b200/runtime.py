@@ -18,7 +18,7 @@ import torch
 
 from . import chip as C
 from . import tables
-from ._lib import S_ERRORS, Caps, Err, LxbError, check, lib
+from ._lib import S_ERRORS, Caps, Err, LxbError, Typing, check, lib
 
 
 def _u16(t: np.ndarray, dev) -> torch.Tensor:
@@ -127,6 +127,40 @@ class Decoder:
                                preds.data_ptr(),
                                inputs.data_ptr() if inputs is not None else None, st),
               "lxb_decode")
+
+    T_FINAL, T_TYPED, T_RX = 1, 2, 4  # lxb_typing token classes
+
+    def set_typing(self, keys, key0_base: int, key_base: int, rx_slots: int,
+                   tclass: np.ndarray | None) -> None:
+        """The device typing queue (lxb_plan_set_typing): keys, one byte sequence per stream;
+        tclass, T_* bits per token id (record boundary, typed key, RX read); None turns it off.
+        The queue state starts cleared; ``typing_state()`` reads it back and ``next_inputs()``
+        is the forced first input of each stream's next launch."""
+        if tclass is None:
+            check(lib().lxb_plan_set_typing(self.plan, None), "lxb_plan_set_typing")
+            self._typing = None
+            return
+        S = len(keys)
+        mk = max(1, max(len(k) for k in keys))
+        kt = torch.zeros((S, mk), dtype=torch.int32, device=self.dev)
+        for i, k in enumerate(keys):
+            if len(k):
+                kt[i, :len(k)] = torch.as_tensor(np.asarray(list(k), np.int32), device=self.dev)
+        nk = torch.tensor([len(k) for k in keys], dtype=torch.int32, device=self.dev)
+        tc = torch.as_tensor(np.asarray(tclass, np.uint8), device=self.dev)
+        ts = torch.zeros((S, 4), dtype=torch.int32, device=self.dev)
+        ty = Typing(kt.data_ptr(), nk.data_ptr(), mk, key0_base, key_base, rx_slots,
+                    tc.data_ptr(), tc.numel(), ts.data_ptr())
+        check(lib().lxb_plan_set_typing(self.plan, ctypes.byref(ty)), "lxb_plan_set_typing")
+        self._typing = (kt, nk, tc, ts)
+
+    def typing_state(self) -> np.ndarray:
+        """Per stream: bytes typed, the RX FIFO count, bytes left in the batch, next input."""
+        return self._typing[3].cpu().numpy()
+
+    def next_inputs(self) -> torch.Tensor:
+        """The first input of each stream's next launch (int32 [S, 1] on the device)."""
+        return self._typing[3][:, 3:4].contiguous()
 
     PROFILE = ("norm", "items", "mlp", "sync", "pull", "fixup", "head", "embed", "fixups",
                "tokens", "wait", "polls", "takesync")
