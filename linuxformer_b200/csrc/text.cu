@@ -102,7 +102,7 @@ struct __align__(128) TSm {
   float vv[32], dl[32];
   float aq[4][HD];
   float kn[HD], vn[HD];
-  float xres[64];  // the old residual of this CTA's out_proj / down_proj rows
+  float xres[64];  // this CTA's rows of the residual (it owns them in out_proj and down_proj)
   float bv[16];
   int bi[16];
   float scal[4];
@@ -399,8 +399,7 @@ __device__ void gemv(const TP& p, TSm& s, Prof& pf, uint32_t& cc, int ph, int ep
   int r0, r1;
   rows_of(d.n, d.q, blockIdx.x, gridDim.x, r0, r1);
   const int rp = rows_per_chunk(d.K, d.q), nsg = segs_of(d.K), V = d.K / (256 * nsg);
-  if (ep == EP_RESID && t < r1 - r0) s.xres[t] = ldb(p.xg + r0 + t);
-  csync();  // s.xb and s.xres complete
+  csync();  // s.xb complete
   const int wr = w / nsg, wsg = w - wr * nsg;
   uint4 xv[6];
   {
@@ -446,7 +445,9 @@ __device__ void gemv(const TP& p, TSm& s, Prof& pf, uint32_t& cc, int ph, int ep
       if (ep == EP_PROJ) {
         stb(p.proj + row, lx_rbf(y));
       } else if (ep == EP_RESID) {
-        stb(p.xg + row, lx_rbf(lx_add(s.xres[row - r0], lx_rbf(y))));
+        const float x = lx_rbf(lx_add(s.xres[row - r0], lx_rbf(y)));
+        s.xres[row - r0] = x;  // only this thread touches this row in the phase
+        stb(p.xg + row, x);
       } else {
         const float v = lx_rbf(y);
         if (v > bestv) bestv = v, besti = row;
@@ -859,8 +860,10 @@ __global__ void __launch_bounds__(NT, 1) lxb_text_kernel(const TP p) {
     for (int li = 0; li < p.n_layers; li++) {
       const lxb_text_layer& L = p.layers[li];
       if (li == 0) {
-        for (int r = wo0 + t; r < wo1; r += NCT)
+        for (int r = wo0 + t; r < wo1; r += NCT) {
           __stcg(reinterpret_cast<unsigned short*>(p.xg + r), erow[r]);
+          s.xres[r - wo0] = bfv(erow[r]);
+        }
         norm_to_xb(p, s, erow, (const uint16_t*)L.ln_in);
       } else {
         norm_to_xb(p, s, p.xg, (const uint16_t*)L.ln_in, hid ? hid + (size_t)(li - 1) * H : nullptr);
