@@ -19,7 +19,11 @@
 // split into fixed segments, one warp each, added in segment order, so every result is
 // independent of how rows are spread over CTAs.
 //
-// Phases per layer (a grid barrier after each):
+// Phases per layer (no grid barrier between them: every activation a phase reads from other CTAs
+// is stored with a 16-bit version tag in the same 32-bit word, and the reader polls the words it
+// needs until they carry the version it expects; the data dependencies between phases then order
+// every overwrite after every read of the version before, and the one grid barrier left is the
+// head's):
 //   P1  RMSNorm(x) -> the layer's input projections (GDN: q k v z b a; attention: q+gate k v)
 //   P2  GDN: conv, l2 norms, gates, the delta rule on the state's live rows (128 CTAs: 32 value
 //       heads x 4 column slices) / attention: q/k norm, rope, split-position partial softmax
@@ -54,7 +58,8 @@ constexpr int NS = LXB_TEXT_STAGES;               // ring stages (consumed in or
 #define LXB_TEXT_LOOKAHEAD 0
 #endif
 constexpr int LOOKAHEAD = LXB_TEXT_LOOKAHEAD;     // chunks prefetched into L2 beyond the ring
-constexpr int APART = 2 + HD;                     // an attention partial: m, l, acc[256]
+constexpr int APART = 4 + HD;                     // an attention partial: m, l, -, -, acc[256]
+constexpr int AACC = 4;                           // (acc 16-byte aligned)
 constexpr int NSUB = NCW / 4;                     // attention: position subsets per query head
 constexpr long long WAIT_CYCLES = 4000000000ll;   // ~2 s at the B200's clock
 
@@ -69,7 +74,8 @@ struct TP {
   const int32_t* forced;
   int32_t* preds;
   float* hidden;  // optional [n_tokens][n_layers + 1][2560]: each layer's residual, the final norm
-  uint16_t *xg, *proj, *vec, *act;  // bf16 activations: residual, projections, mixer out, act
+  uint32_t *xg, *proj, *vec, *act;  // tagged bf16 activations: residual, projections, mixer out,
+                                     // MLP activation (value bits | version tag << 16)
   float *apart, *amax;
   int* aidx;
   unsigned int* acnt;  // attention: arrivals per kv group (the last one combines)
@@ -131,12 +137,67 @@ __device__ __forceinline__ float bfv(uint16_t b) { return __uint_as_float((uint3
 __device__ __forceinline__ uint16_t bfbits(float bf_valued) {
   return (uint16_t)(__float_as_uint(bf_valued) >> 16);
 }
-// activations in global memory are bf16, written and read at L2 (other CTAs wrote them)
-__device__ __forceinline__ float ldb(const uint16_t* a) {
-  return bfv(__ldcg(reinterpret_cast<const unsigned short*>(a)));
+// Tagged activations: a bf16 value and its version's tag in one 32-bit word (single-copy atomic),
+// stored and loaded as relaxed gpu-scope operations. Tags are 1..65535 (the buffers are cleared
+// to 0 before every launch); a word is rewritten every token, so a stale word's tag is at most a
+// token's versions old and never equals the one a reader waits for.
+__device__ __forceinline__ uint32_t vtag(long long v) { return 1u + (uint32_t)(v % 65535); }
+__device__ __forceinline__ float wval(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ void st_tag(uint32_t* a, float bf_valued, uint32_t tag) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a),
+               "r"((__float_as_uint(bf_valued) >> 16) | (tag << 16))
+               : "memory");
 }
-__device__ __forceinline__ void stb(uint16_t* a, float bf_valued) {
-  __stcg(reinterpret_cast<unsigned short*>(a), bfbits(bf_valued));
+__device__ __forceinline__ uint32_t ld_rel(const uint32_t* a) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 ld_rel4(const uint32_t* a) {
+  uint4 v;
+  asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(a)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void poll_fail(const TP& p) {
+  atomicOr(p.status, LXB_S_SYNC);
+  atomicExch(p.abort_flag, 1);
+}
+// spin until the word carries tag (bounded: ~2 s, or earlier once another CTA aborted)
+__device__ __forceinline__ bool poll1(const TP& p, const uint32_t* a, uint32_t tag, float& x) {
+  long long t0 = 0;
+  for (int it = 0;; it++) {
+    const uint32_t v = ld_rel(a);
+    if ((v >> 16) == tag) {
+      x = wval(v);
+      return true;
+    }
+    if (it == 0) t0 = clock64();
+    else if ((it & 255) == 0 && *(volatile const int*)p.abort_flag) return false;
+    if (clock64() - t0 > WAIT_CYCLES) {
+      poll_fail(p);
+      return false;
+    }
+  }
+}
+// the same for 4 consecutive words (16-byte aligned)
+__device__ __forceinline__ bool poll4(const TP& p, const uint32_t* a, uint32_t tag, float (&x)[4]) {
+  long long t0 = 0;
+  for (int it = 0;; it++) {
+    const uint4 v = ld_rel4(a);
+    if ((v.x >> 16) == tag && (v.y >> 16) == tag && (v.z >> 16) == tag && (v.w >> 16) == tag) {
+      x[0] = wval(v.x), x[1] = wval(v.y), x[2] = wval(v.z), x[3] = wval(v.w);
+      return true;
+    }
+    if (it == 0) t0 = clock64();
+    else if ((it & 255) == 0 && *(volatile const int*)p.abort_flag) return false;
+    if (clock64() - t0 > WAIT_CYCLES) {
+      poll_fail(p);
+      return false;
+    }
+  }
 }
 __device__ __forceinline__ void bf8(uint4 v, float (&x)[8]) {
   const uint32_t u[4] = {v.x, v.y, v.z, v.w};
@@ -350,21 +411,31 @@ __device__ float block_sum(TSm& s, float v) {
 }
 
 // Qwen3_5RMSNorm of a 2560-vector into s.xb: bf16(x * rsqrt(mean(x^2) + eps) * (1 + w)).
-// src: bf16 (the embedding row, or the residual xg); thread t < 320 takes elements 8t .. 8t + 7.
-// dump (or null): where the input vector is copied (the per-layer residuals of `hidden`).
-__device__ void norm_to_xb(const TP& p, TSm& s, const uint16_t* src, const uint16_t* w,
-                           float* dump = nullptr) {
+// The vector: the embedding row erow (bf16), or the residual (tagged words of version tag).
+// Thread t < 320 takes elements 8t .. 8t + 7. dump (or null): where the vector is copied (the
+// per-layer residuals of `hidden`). Returns false (on every consumer thread) after a failed poll.
+__device__ bool norm_to_xb(const TP& p, TSm& s, const uint16_t* erow, uint32_t tag,
+                           const uint16_t* w, float* dump = nullptr) {
   const int t = threadIdx.x;
   float x[8], ss = 0.0f;
   const bool on = t < H / 8;
+  bool ok = true;
   if (on) {
-    bf8(__ldcg(reinterpret_cast<const uint4*>(src) + t), x);
+    if (erow) {
+      bf8(__ldg(reinterpret_cast<const uint4*>(erow) + t), x);
+    } else {
+      float a[4], b[4];
+      ok = poll4(p, p.xg + 8 * t, tag, a) && poll4(p, p.xg + 8 * t + 4, tag, b);
+#pragma unroll
+      for (int i = 0; i < 4; i++) x[i] = a[i], x[4 + i] = b[i];
+    }
 #pragma unroll
     for (int i = 0; i < 8; i++) ss = lx_add(ss, lx_mul(x[i], x[i]));
     if (dump)
 #pragma unroll
       for (int i = 0; i < 8; i++) dump[8 * t + i] = x[i];
   }
+  if (!csync_and(ok)) return false;
   const float tot = block_sum(s, ss);
   const float r = lx_rsqrt(lx_add(lx_div(tot, (float)H), p.eps));
   if (on) {
@@ -377,12 +448,20 @@ __device__ void norm_to_xb(const TP& p, TSm& s, const uint16_t* src, const uint1
              ((uint32_t)lx_rb(lx_mul(lx_mul(x[2 * i + 1], r), lx_add(1.0f, wf[2 * i + 1]))) << 16);
     reinterpret_cast<uint4*>(s.xb)[t] = make_uint4(o[0], o[1], o[2], o[3]);
   }
+  return true;
 }
 
-// a bf16 vector of n elements (n a multiple of 8) from global memory into s.xb
-__device__ __forceinline__ void copy_to_xb(TSm& s, const uint16_t* src, int n) {
-  for (int i = threadIdx.x; i < n / 8; i += NCT)
-    reinterpret_cast<uint4*>(s.xb)[i] = __ldcg(reinterpret_cast<const uint4*>(src) + i);
+// n tagged words (n a multiple of 4) of version tag into s.xb as bf16; false after a failed poll
+__device__ bool copy_to_xb(const TP& p, TSm& s, const uint32_t* src, int n, uint32_t tag) {
+  bool ok = true;
+  for (int i = threadIdx.x; ok && i < n / 4; i += NCT) {
+    float v[4];
+    ok = poll4(p, src + 4 * i, tag, v);
+    reinterpret_cast<uint2*>(s.xb)[i] =
+        make_uint2((__float_as_uint(v[0]) >> 16) | (__float_as_uint(v[1]) & 0xffff0000u),
+                   (__float_as_uint(v[2]) >> 16) | (__float_as_uint(v[3]) & 0xffff0000u));
+  }
+  return csync_and(ok);
 }
 
 enum { EP_PROJ = 0, EP_RESID = 1, EP_ACT = 2, EP_HEAD = 3 };
@@ -392,8 +471,8 @@ enum { EP_PROJ = 0, EP_RESID = 1, EP_ACT = 2, EP_HEAD = 3 };
 // same in every chunk of the phase, so its part of the input vector stays in registers. The
 // epilogue (segment sums, rounding, stores) runs on warp EW. A staging timeout sets the abort
 // flag, which the next grid barrier reads.
-__device__ void gemv(const TP& p, TSm& s, Prof& pf, uint32_t& cc, int ph, int ep, float& bestv,
-                     int& besti) {
+__device__ void gemv(const TP& p, TSm& s, Prof& pf, uint32_t& cc, int ph, int ep, uint32_t tag,
+                     float& bestv, int& besti) {
   const int t = threadIdx.x, lane = t & 31, w = t >> 5, et = t - EW * 32;
   const PhaseDesc d = pdesc(p, ph);
   int r0, r1;
@@ -436,18 +515,18 @@ __device__ void gemv(const TP& p, TSm& s, Prof& pf, uint32_t& cc, int ph, int ep
           yu = lx_add(yu, part[(2 * et + 1) * nsg + sg]);
         }
         const float g = lx_rbf(yg), u = lx_rbf(yu);
-        stb(p.act + a / 2 + et, lx_rbf(lx_mul(lx_rbf(lx_silu(g)), u)));
+        st_tag(p.act + a / 2 + et, lx_rbf(lx_mul(lx_rbf(lx_silu(g)), u)), tag);
       }
     } else if (et >= 0 && et < nr) {
       float y = 0.0f;
       for (int sg = 0; sg < nsg; sg++) y = lx_add(y, part[et * nsg + sg]);
       const int row = a + et;
       if (ep == EP_PROJ) {
-        stb(p.proj + row, lx_rbf(y));
+        st_tag(p.proj + row, lx_rbf(y), tag);
       } else if (ep == EP_RESID) {
         const float x = lx_rbf(lx_add(s.xres[row - r0], lx_rbf(y)));
         s.xres[row - r0] = x;  // only this thread touches this row in the phase
-        stb(p.xg + row, x);
+        st_tag(p.xg + row, x, tag);
       } else {
         const float v = lx_rbf(y);
         if (v > bestv) bestv = v, besti = row;
@@ -459,7 +538,7 @@ __device__ void gemv(const TP& p, TSm& s, Prof& pf, uint32_t& cc, int ph, int ep
 }
 
 // --- P2: the GDN step of one (value head, 32-column slice) --------------------------------------
-__device__ void gdn_p2(const TP& p, TSm& s, const lxb_text_layer& L, int task) {
+__device__ bool gdn_p2(const TP& p, TSm& s, const lxb_text_layer& L, int task, uint32_t tag) {
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int vh = task >> 2, sl = task & 3, kh = vh >> 1, ph = kh * PR + (vh & 1);
   const uint16_t* cw = (const uint16_t*)L.conv_w;
@@ -471,6 +550,11 @@ __device__ void gdn_p2(const TP& p, TSm& s, const lxb_text_layer& L, int task) {
   if (w < 8)
 #pragma unroll
     for (int i = 0; i < 16; i++) h[i] = __ldcg(S + (size_t)(w * 16 + i) * VD);
+  // the conv windows were written by other CTAs at earlier tokens: everything they stored before
+  // the tagged words this CTA has since seen from them is visible after this fence
+  __threadfence();
+  bool ok = true;
+  if (t == 288 || t == 289) ok = poll1(p, p.proj + (t == 288 ? BOFF : AOFF) + vh, tag, s.scal[t - 286]);
   // conv over the new window [w1 w2 w3 P] (torch_causal_conv1d_update), silu, bf16
   if (t < 288) {
     int prow, pch;
@@ -481,7 +565,8 @@ __device__ void gdn_p2(const TP& p, TSm& s, const lxb_text_layer& L, int task) {
       prow = VOFF + vh * VD + j;
       pch = 2 * 16 * KDP + ph * VD + j;
     }
-    const float P = ldb(p.proj + prow);
+    float P = 0.0f;
+    ok = poll1(p, p.proj + prow, tag, P);
     const uint2 win = __ldcg(reinterpret_cast<const uint2*>(cs + (size_t)pch * 4));
     const uint2 tap = *reinterpret_cast<const uint2*>(cw + (size_t)prow * 4);
     float y = 0.0f;
@@ -493,7 +578,7 @@ __device__ void gdn_p2(const TP& p, TSm& s, const lxb_text_layer& L, int task) {
     if (t < 256) s.qk[t] = o;
     else s.vv[t - 256] = o;
   }
-  csync();
+  if (!csync_and(ok)) return false;
   // l2norm in bf16 (q by warp 0, k by warp 1; q then times 256^-0.5, exact), beta and decay
   if (w < 2) {
     float x[4], sq = 0.0f;
@@ -511,7 +596,7 @@ __device__ void gdn_p2(const TP& p, TSm& s, const lxb_text_layer& L, int task) {
       s.qk[w * QKD + lane * 4 + i] = w == 0 ? lx_mul(n, 0.0625f) : n;
     }
   } else if (t == 64) {
-    const float b = ldb(p.proj + BOFF + vh), a = ldb(p.proj + AOFF + vh);
+    const float b = s.scal[2], a = s.scal[3];
     const float beta = lx_rbf(lx_sigmoid(b));
     const float A = -lx_exp(((const float*)L.A_log)[vh]);
     const float g = lx_mul(A, lx_softplus(lx_add(a, ((const float*)L.dt_bias)[vh])));
@@ -552,13 +637,15 @@ __device__ void gdn_p2(const TP& p, TSm& s, const lxb_text_layer& L, int task) {
   if (w == 0) {
     float o2 = 0.0f;
     for (int g2 = 0; g2 < 8; g2++) o2 = lx_add(o2, s.red[g2][lane]);
-    stb(p.vec + vh * VD + sl * 32 + lane, lx_rbf(o2));
+    st_tag(p.vec + vh * VD + sl * 32 + lane, lx_rbf(o2), tag);
   }
   csync();
+  return true;
 }
 
 // P3 of a GDN layer: the conv windows of this CTA's channels shift in the new projection
-__device__ void gdn_windows(const TP& p, const lxb_text_layer& L) {
+__device__ bool gdn_windows(const TP& p, const lxb_text_layer& L, uint32_t tag) {
+  bool ok = true;
   const int G = gridDim.x, c = blockIdx.x;
   const int c0 = (int)((long long)c * 8192 / G), c1 = (int)((long long)(c + 1) * 8192 / G);
   uint16_t* cs = (uint16_t*)L.conv_state;
@@ -572,25 +659,30 @@ __device__ void gdn_windows(const TP& p, const lxb_text_layer& L) {
     }
     uint2* wp = reinterpret_cast<uint2*>(cs + (size_t)pch * 4);
     const uint2 win = __ldcg(wp);
-    const uint32_t P = __ldcg(reinterpret_cast<const unsigned short*>(p.proj + ch));
+    float Pv;
+    if (!(ok = poll1(p, p.proj + ch, tag, Pv))) break;
+    const uint32_t P = __float_as_uint(Pv) >> 16;
     __stcg(wp, make_uint2((win.x >> 16) | (win.y << 16), (win.y >> 16) | (P << 16)));
   }
+  __threadfence();  // the windows before any tagged word this CTA stores later
+  return ok;
 }
 
 // P3 of a GDN layer: Qwen3_5RMSNormGated of the 32 heads' outputs into s.xb:
 // bf16(bf16(w * bf16(o * rsqrt(mean(o^2) + eps))) * silu(z)), the product with w unrounded when w
 // is an fp32 parameter
-__device__ void gdn_gated_norm(const TP& p, TSm& s, const lxb_text_layer& L) {
+__device__ bool gdn_gated_norm(const TP& p, TSm& s, const lxb_text_layer& L, uint32_t tag,
+                               bool ok) {
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
   const float* gw = (const float*)L.gnorm;
   const bool gf32 = L.flags & LXB_TEXT_GNORM_F32;
   for (int vh = w; vh < 32; vh += NCW) {
-    float o[4], sq = 0.0f;
+    float o[4], z4[4], sq = 0.0f;
+    ok = ok && poll4(p, p.vec + vh * VD + lane * 4, tag, o) &&
+         poll4(p, p.proj + ZOFF + vh * VD + lane * 4, tag, z4);
+    if (__any_sync(0xffffffffu, !ok)) break;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      o[i] = ldb(p.vec + vh * VD + lane * 4 + i);
-      sq = lx_add(sq, lx_mul(o[i], o[i]));
-    }
+    for (int i = 0; i < 4; i++) sq = lx_add(sq, lx_mul(o[i], o[i]));
     sq = warp_sum(sq);
     const float rr = lx_rsqrt(lx_add(lx_div(sq, 128.0f), p.eps));
 #pragma unroll
@@ -598,30 +690,30 @@ __device__ void gdn_gated_norm(const TP& p, TSm& s, const lxb_text_layer& L) {
       const int j = lane * 4 + i;
       const float hn = lx_rbf(lx_mul(o[i], rr));
       const float u = gf32 ? lx_mul(gw[j], hn) : lx_rbf(lx_mul(gw[j], hn));
-      const float z = ldb(p.proj + ZOFF + vh * VD + j);
-      s.xb[vh * VD + j] = lx_rb(lx_mul(u, lx_silu(z)));
+      s.xb[vh * VD + j] = lx_rb(lx_mul(u, lx_silu(z4[i])));
     }
   }
+  return csync_and(ok);
 }
 
 // --- P2 of an attention layer: one (kv head, position split) ------------------------------------
 // nh heads (nh <= 4), head k from src + k * stride into dst + k * HD, 64 threads a head (4 dims
 // each): RMSNorm over the head's 256 dims (q_norm / k_norm), then rope on the first 64 dims with
 // bf16 rounding after every tensor op (apply_rotary_pos_emb, modeling_qwen3_5.py:544-579)
-__device__ void head_norm_rope(const TP& p, TSm& s, float* dst, const uint16_t* src, int stride,
-                               const uint16_t* w, int pos, int nh) {
+__device__ bool head_norm_rope(const TP& p, TSm& s, float* dst, const uint32_t* src, int stride,
+                               const uint16_t* w, int pos, int nh, uint32_t tag) {
   const int t = threadIdx.x, grp = t >> 6, d0 = (t & 63) * 4;
   const bool on = t < nh * 64;
   float x[4] = {0.0f, 0.0f, 0.0f, 0.0f}, ss = 0.0f;
-  if (on)
+  bool ok = true;
+  if (on) {
+    ok = poll4(p, src + grp * stride + d0, tag, x);
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      x[i] = ldb(src + grp * stride + d0 + i);
-      ss = lx_add(ss, lx_mul(x[i], x[i]));
-    }
+    for (int i = 0; i < 4; i++) ss = lx_add(ss, lx_mul(x[i], x[i]));
+  }
   ss = warp_sum(ss);
   if ((t & 31) == 0 && t < 256) s.red[t >> 5][1] = ss;
-  csync();
+  if (!csync_and(ok)) return false;
   float* o = dst + grp * HD;
   if (on) {
     const float tot = lx_add(s.red[2 * grp][1], s.red[2 * grp + 1][1]);
@@ -647,12 +739,14 @@ __device__ void head_norm_rope(const TP& p, TSm& s, float* dst, const uint16_t* 
 #pragma unroll
     for (int i = 0; i < 4; i++) o[d0 + i] = nv[i];
   csync();
+  return true;
 }
 
 // The combine: kv group g's 4 query heads over all splits in order, softmax-normalised, times
 // sigmoid(gate) (every split's m and l staged in shared memory first, then each output's
 // accumulators with their loads in flight together)
-__device__ void att_combine(const TP& p, TSm& s, int g) {
+__device__ bool att_combine(const TP& p, TSm& s, int g, uint32_t tag) {
+  bool ok = true;
   const int t = threadIdx.x, ns = p.nsplit;
   float* ms = &s.aq[0][0];  // [4][ns]
   float* ls = ms + 4 * ns;
@@ -671,42 +765,60 @@ __device__ void att_combine(const TP& p, TSm& s, int g) {
     fs[k] = ms[k] == -INFINITY ? 0.0f : lx_exp(lx_sub(ms[k], M));
   }
   csync();
-  for (int k = t; k < 4 * HD; k += NCT) {
-    const int h4 = k / HD, d = k % HD;
-    float Ls = 0.0f, A = 0.0f;
+  // 4 heads x 64 groups of 4 dims, one a thread: every split's 4 accumulators as one 16-byte
+  // load, 8 splits' loads in flight together
+  for (int k = t; k < HD; k += NCT) {
+    const int h4 = k / (HD / 4), d = (k % (HD / 4)) * 4;
+    float Ls = 0.0f, A[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int s0 = 0; s0 < ns; s0 += 8) {
-      float v[8];
+      float4 v[8];
 #pragma unroll
       for (int j = 0; j < 8; j++)
-        v[j] = s0 + j < ns ? __ldcg(base + (size_t)((s0 + j) * 4 + h4) * APART + 2 + d) : 0.0f;
+        v[j] = s0 + j < ns ? __ldcg(reinterpret_cast<const float4*>(
+                                 base + (size_t)((s0 + j) * 4 + h4) * APART + AACC + d))
+                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
       for (int j = 0; j < 8; j++)
         if (s0 + j < ns) {
-          Ls = __fmaf_rn(ls[h4 * ns + s0 + j], fs[h4 * ns + s0 + j], Ls);
-          A = __fmaf_rn(v[j], fs[h4 * ns + s0 + j], A);
+          const float f = fs[h4 * ns + s0 + j];
+          Ls = __fmaf_rn(ls[h4 * ns + s0 + j], f, Ls);
+          A[0] = __fmaf_rn(v[j].x, f, A[0]);
+          A[1] = __fmaf_rn(v[j].y, f, A[1]);
+          A[2] = __fmaf_rn(v[j].z, f, A[2]);
+          A[3] = __fmaf_rn(v[j].w, f, A[3]);
         }
     }
     const int h = g * 4 + h4;
-    const float o = lx_rbf(lx_div(A, Ls));
-    const float gate = ldb(p.proj + h * 2 * HD + HD + d);
-    stb(p.vec + h * HD + d, lx_rbf(lx_mul(o, lx_rbf(lx_sigmoid(gate)))));
+    float gate[4];
+    ok = ok && poll4(p, p.proj + h * 2 * HD + HD + d, tag, gate);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float o = lx_rbf(lx_div(A[i], Ls));
+      st_tag(p.vec + h * HD + d + i, lx_rbf(lx_mul(o, lx_rbf(lx_sigmoid(gate[i])))), tag);
+    }
   }
-  csync();
+  return csync_and(ok);
 }
 
-__device__ void att_p2(const TP& p, TSm& s, const lxb_text_layer& L, int pos) {
+__device__ bool att_p2(const TP& p, TSm& s, const lxb_text_layer& L, int pos, uint32_t tag) {
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int ns = p.nsplit, g = blockIdx.x / ns, sp = blockIdx.x % ns;
   const long long n = pos + 1;
   const int b0 = (int)(sp * n / ns), b1 = (int)((sp + 1) * n / ns);
   const bool last = sp == ns - 1;
+  // the key/value rows were written by other CTAs at earlier tokens: visible after this fence
+  __threadfence();
   // the group's 4 query heads, then the new key and value (if this split holds pos)
-  head_norm_rope(p, s, &s.aq[0][0], p.proj + (g * 4) * 2 * HD, 2 * HD, (const uint16_t*)L.qn,
-                 pos, 4);
+  if (!head_norm_rope(p, s, &s.aq[0][0], p.proj + (g * 4) * 2 * HD, 2 * HD,
+                      (const uint16_t*)L.qn, pos, 4, tag))
+    return false;
   if (last) {
-    head_norm_rope(p, s, s.kn, p.proj + KVOFF + g * HD, 0, (const uint16_t*)L.kn, pos, 1);
-    if (t < HD) s.vn[t] = ldb(p.proj + VVOFF + g * HD + t);
-    csync();
+    if (!head_norm_rope(p, s, s.kn, p.proj + KVOFF + g * HD, 0, (const uint16_t*)L.kn, pos, 1,
+                        tag))
+      return false;
+    bool ok = true;
+    if (t < HD) ok = poll1(p, p.proj + VVOFF + g * HD + t, tag, s.vn[t]);
+    if (!csync_and(ok)) return false;
   }
   // warp w < 4 * NSUB: query head hh = w & 3 over the positions b0 + ss + NSUB * j
   // (ss = w >> 2), four of them per round with their loads in flight together; lane: dims
@@ -782,7 +894,7 @@ __device__ void att_p2(const TP& p, TSm& s, const lxb_text_layer& L, int pos) {
     }
     if (lane == 0) aw[w * APART] = m, aw[w * APART + 1] = l;
 #pragma unroll
-    for (int i = 0; i < 8; i++) aw[w * APART + 2 + lane * 8 + i] = acc[i];
+    for (int i = 0; i < 8; i++) aw[w * APART + AACC + lane * 8 + i] = acc[i];
   }
   csync();
   // the NSUB position subsets of each query head, in order, into this split's partial
@@ -797,11 +909,11 @@ __device__ void att_p2(const TP& p, TSm& s, const lxb_text_layer& L, int pos) {
         if (mq == -INFINITY) continue;
         const float f = lx_exp(lx_sub(mq, M));
         Ls = __fmaf_rn(aw[(q * 4 + h4) * APART + 1], f, Ls);
-        A = __fmaf_rn(aw[(q * 4 + h4) * APART + 2 + d], f, A);
+        A = __fmaf_rn(aw[(q * 4 + h4) * APART + AACC + d], f, A);
       }
     float* dst = p.apart + ((size_t)(g * ns + sp) * 4 + h4) * APART;
     if (d == 0) __stcg(dst, M), __stcg(dst + 1, Ls);
-    __stcg(dst + 2 + d, A);
+    __stcg(dst + AACC + d, A);
   }
   if (last && t < HD) {  // the new key and value join the cache for later tokens
     ((uint16_t*)L.kc)[((size_t)g * p.max_pos + pos) * HD + t] = bfbits(s.kn[t]);
@@ -815,8 +927,9 @@ __device__ void att_p2(const TP& p, TSm& s, const lxb_text_layer& L, int pos) {
   csync();
   if (s.tok_last) {
     __threadfence();
-    att_combine(p, s, g);
+    return att_combine(p, s, g, tag);
   }
+  return true;
 }
 
 // first maximum: larger value, or equal value at a lower index
@@ -857,58 +970,54 @@ __global__ void __launch_bounds__(NT, 1) lxb_text_kernel(const TP p) {
     float* hid = p.hidden && c == 0 ? p.hidden + (size_t)it * (p.n_layers + 1) * H : nullptr;
     float bestv = -INFINITY;
     int besti = 0x7fffffff;
+    // versions of this token: x at 2 li + 1 after layer li's out_proj, 2 li + 2 after its
+    // down_proj; the projections, the mixer output and the MLP activation at the layer's index
+    const long long xv0 = (long long)it * (2 * p.n_layers + 1);
     for (int li = 0; li < p.n_layers; li++) {
       const lxb_text_layer& L = p.layers[li];
-      if (li == 0) {
-        for (int r = wo0 + t; r < wo1; r += NCT) {
-          __stcg(reinterpret_cast<unsigned short*>(p.xg + r), erow[r]);
-          s.xres[r - wo0] = bfv(erow[r]);
-        }
-        norm_to_xb(p, s, erow, (const uint16_t*)L.ln_in);
+      const uint32_t tl = vtag((long long)it * p.n_layers + li);
+      bool ok;
+      if (li == 0) {  // the embedding row: this CTA's residual rows, and the input norm's source
+        for (int r = wo0 + t; r < wo1; r += NCT) s.xres[r - wo0] = bfv(erow[r]);
+        ok = norm_to_xb(p, s, erow, 0, (const uint16_t*)L.ln_in);
       } else {
-        norm_to_xb(p, s, p.xg, (const uint16_t*)L.ln_in, hid ? hid + (size_t)(li - 1) * H : nullptr);
+        ok = norm_to_xb(p, s, nullptr, vtag(xv0 + 2 * li), (const uint16_t*)L.ln_in,
+                        hid ? hid + (size_t)(li - 1) * H : nullptr);
       }
+      if (!ok) goto done;
       pf.mark(LXB_TP_NORM);
-      gemv(p, s, pf, cc, 4 * li, EP_PROJ, bestv, besti);
-      if (!grid_sync(p, s, target)) goto done;
-      pf.mark(LXB_TP_SYNC);
+      gemv(p, s, pf, cc, 4 * li, EP_PROJ, tl, bestv, besti);
       if (L.type == 0) {
-        for (int task = c; task < 128; task += G) gdn_p2(p, s, L, task);
+        for (int task = c; task < 128; task += G)
+          if (!gdn_p2(p, s, L, task, tl)) goto done;
         pf.mark(LXB_TP_GDN);
+        // the gated norm first: once this CTA has seen every head's output of the layer, every
+        // GDN step has read the old conv windows (its output depends on them), so they may shift
+        ok = gdn_gated_norm(p, s, L, tl, true) && csync_and(gdn_windows(p, L, tl));
       } else {
-        if (c < NKV * p.nsplit) att_p2(p, s, L, pos);
+        if (c < NKV * p.nsplit && !att_p2(p, s, L, pos, tl)) goto done;
         pf.mark(LXB_TP_ATT);
+        ok = copy_to_xb(p, s, p.vec, 4096, tl);
       }
-      if (!grid_sync(p, s, target)) goto done;
-      pf.mark(LXB_TP_SYNC);
-      if (L.type == 0) {
-        gdn_windows(p, L);
-        gdn_gated_norm(p, s, L);
-      } else {
-        copy_to_xb(s, p.vec, 4096);
-      }
+      if (!ok) goto done;
       pf.mark(LXB_TP_NORM);
-      gemv(p, s, pf, cc, 4 * li + 1, EP_RESID, bestv, besti);
-      if (!grid_sync(p, s, target)) goto done;
-      pf.mark(LXB_TP_SYNC);
-      norm_to_xb(p, s, p.xg, (const uint16_t*)L.ln_post);
+      gemv(p, s, pf, cc, 4 * li + 1, EP_RESID, vtag(xv0 + 2 * li + 1), bestv, besti);
+      if (!norm_to_xb(p, s, nullptr, vtag(xv0 + 2 * li + 1), (const uint16_t*)L.ln_post)) goto done;
       pf.mark(LXB_TP_NORM);
-      gemv(p, s, pf, cc, 4 * li + 2, EP_ACT, bestv, besti);
-      if (!grid_sync(p, s, target)) goto done;
-      pf.mark(LXB_TP_SYNC);
-      copy_to_xb(s, p.act, INTER);
+      gemv(p, s, pf, cc, 4 * li + 2, EP_ACT, tl, bestv, besti);
+      if (!copy_to_xb(p, s, p.act, INTER, tl)) goto done;
       pf.mark(LXB_TP_NORM);
-      gemv(p, s, pf, cc, 4 * li + 3, EP_RESID, bestv, besti);
-      if (!grid_sync(p, s, target)) goto done;
-      pf.mark(LXB_TP_SYNC);
+      gemv(p, s, pf, cc, 4 * li + 3, EP_RESID, vtag(xv0 + 2 * li + 2), bestv, besti);
     }
-    norm_to_xb(p, s, p.xg, p.fnorm, hid ? hid + (size_t)(p.n_layers - 1) * H : nullptr);
+    if (!norm_to_xb(p, s, nullptr, vtag(xv0 + 2 * p.n_layers), p.fnorm,
+                    hid ? hid + (size_t)(p.n_layers - 1) * H : nullptr))
+      goto done;
     if (hid) {
       csync();
       for (int i = t; i < H; i += NCT) hid[(size_t)p.n_layers * H + i] = bfv(s.xb[i]);
     }
     pf.mark(LXB_TP_NORM);
-    gemv(p, s, pf, cc, 4 * p.n_layers, EP_HEAD, bestv, besti);
+    gemv(p, s, pf, cc, 4 * p.n_layers, EP_HEAD, 0, bestv, besti);
     // this CTA's first maximum, then the grid's (CTAs hold ascending row ranges)
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -979,14 +1088,14 @@ Layout layout(const lxb_text_plan* P) {
   size_t o = 0;
   l.bar = o;  // bar (u64), abort flag, attention arrival counters [4]
   o = align256(o + 64);
-  l.xg = o;
-  o = align256(o + 2 * H);
+  l.xg = o;  // the tagged words (cleared before every launch): xg, proj, vec, act
+  o = align256(o + 4 * H);
   l.proj = o;
-  o = align256(o + 2 * W1G);
+  o = align256(o + 4 * W1G);
   l.vec = o;
-  o = align256(o + 2 * 4096);
+  o = align256(o + 4 * 4096);
   l.act = o;
-  o = align256(o + 2 * INTER);
+  o = align256(o + 4 * INTER);
   l.apart = o;
   o = align256(o + sizeof(float) * NKV * P->nsplit * 4 * APART);
   l.amax = o;
@@ -1075,7 +1184,7 @@ extern "C" int lxb_text_decode(lxb_text_plan* P, const int32_t* forced, int n_fo
   const Layout l = layout(P);
   if (scratch_bytes < l.total || ((uintptr_t)scratch & 255)) return LXB_E_INVAL;
   unsigned char* b = (unsigned char*)scratch;
-  cudaError_t e = cudaMemsetAsync(b + l.bar, 0, 64, stream);
+  cudaError_t e = cudaMemsetAsync(b + l.bar, 0, l.apart - l.bar, stream);
   if (e != cudaSuccess) return (int)e;
   TP p{};
   p.layers = P->d_layers;
@@ -1097,10 +1206,10 @@ extern "C" int lxb_text_decode(lxb_text_plan* P, const int32_t* forced, int n_fo
   p.hidden = hidden;
   p.bar = (unsigned long long*)(b + l.bar);
   p.abort_flag = (int*)(b + l.bar + 8);
-  p.xg = (uint16_t*)(b + l.xg);
-  p.proj = (uint16_t*)(b + l.proj);
-  p.vec = (uint16_t*)(b + l.vec);
-  p.act = (uint16_t*)(b + l.act);
+  p.xg = (uint32_t*)(b + l.xg);
+  p.proj = (uint32_t*)(b + l.proj);
+  p.vec = (uint32_t*)(b + l.vec);
+  p.act = (uint32_t*)(b + l.act);
   p.acnt = (unsigned int*)(b + l.bar + 16);
   p.apart = (float*)(b + l.apart);
   p.amax = (float*)(b + l.amax);
