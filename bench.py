@@ -230,6 +230,26 @@ def decode_c2(a, rank, world, dev, kw):
     tot, e2e_tot = slowest([tot, sum(e2e_t)], dev)
     if rank != 0:
         return None
+    # outside the timed region: the per-section split of a profiled launch continuing the
+    # stream, and the barrier floor (barriers per token x an empty cluster barrier's latency)
+    prof = torch.zeros((1, a.cluster, len(dec.PROFILE)), dtype=torch.int64, device=dev)
+    dec.set_profile(prof)
+    n_prof = 4096
+    pp = torch.empty((1, n_prof), dtype=torch.int32, device=dev)
+    dec.launch(states.ptrs, states.bitmaps, forced, n_prof, pp, None, sync_bitmaps=False,
+               stream=stream, scratch=states.scratch)
+    torch.cuda.synchronize(dev)
+    dec.set_profile(None)
+    pr = prof[0].cpu().numpy().astype(np.float64).mean(0)  # the cluster's CTAs
+    mhz = clk.summary().get("sm_mhz") or 1965.0
+    split = {n: round(pr[k] / n_prof / mhz, 3) for k, n in enumerate(dec.PROFILE)
+             if n not in dec.COUNTS}
+    bar_tok = pr[dec.PROFILE.index("barriers")] / n_prof
+    bar_ns = dec.barrier_cycles() / mhz * 1e3
+    us_tok = 1e6 * tot / (a.steps * T)
+    floor = {"barriers_per_token": round(bar_tok, 2), "empty_barrier_ns": round(bar_ns, 1),
+             "floor_us_per_token": round(bar_tok * bar_ns / 1e3, 2),
+             "floor_frac_of_step": round(bar_tok * bar_ns / 1e3 / us_tok, 4)}
     value = job_rate(a.steps * T, world, tot)
     e2e_value = job_rate(e2e_steps * T, world, e2e_tot)
     peak, peak_kind = _peaks()
@@ -262,6 +282,8 @@ def decode_c2(a, rank, world, dev, kw):
                          "to the CPU restatement",
         "activity_per_token": activity(counts),
         "us_per_token": round(1e6 * tot / (a.steps * T), 3),
+        "profile_us_per_token": split,
+        "barrier_floor": floor,
     }
 
 
@@ -435,8 +457,9 @@ def prefill_c3(a, rank, world, dev):
 def self_draft_c1(chip, st0, pf, dev, n: int = 8192, D: int = 255) -> dict:
     """Self-drafting verify (linuxformer_b200.draft) on config 1's greedy stream from token 0:
     wall time of the whole host-driven loop (each round: draft on the host, one prefill call,
-    a device copy of the state, and a rollback when a draft token was wrong), against the decode
-    kernel's single-stream rate on the same stream; both streams compared token for token."""
+    a device copy of the state, and a rollback when a draft token was wrong; bursts of the decode
+    kernel where nothing is drafted), against the decode kernel's single-stream rate on the same
+    stream; both streams compared token for token."""
     import numpy as np
     import torch
 
@@ -450,7 +473,7 @@ def self_draft_c1(chip, st0, pf, dev, n: int = 8192, D: int = 255) -> dict:
                              for L in range(chip.n_layers)], dtype=torch.int64, device=dev)
         return rec, conv, ptrs
 
-    sd = SelfDraft(pf, draft=D)
+    sd = SelfDraft(pf, draft=D, decoder=Decoder(chip, cluster=16, device=dev))
     rec, conv, ptrs = fresh()
     sd.run(ptrs, [rec, conv], 0, 512)  # warm-up
     rec, conv, ptrs = fresh()

@@ -123,6 +123,11 @@ int lxb_status_clear(lxb_plan* plan);
 int lxb_plan_set_profile(lxb_plan* plan, unsigned long long* prof);
 int lxb_profile_sections(void);
 
+/* An empty cluster barrier's latency in SM clock cycles (one cluster of `cluster` CTAs doing
+ * `iters` barriers and nothing else): with the profile's barrier count per token, the decode's
+ * barrier floor. Synchronises the device. */
+int lxb_cluster_sync_cycles(int cluster, int iters, double* cycles_per_barrier);
+
 /* The device typing queue (no counterpart in the reference's kernel: its host types a command into
  * the model-alone machine between launches, Linux.run_alone, lx/lx/linux.py:254-289). With it
  * set, every later lxb_decode types each stream's queued bytes itself, after any token: a batch of

@@ -52,6 +52,7 @@ SIGNATURES = {
     "lxb_plan_set_head_helpers": (I, [P, I]),
     "lxb_plan_set_typing": (I, [P, P]),
     "lxb_profile_sections": (I, []),
+    "lxb_cluster_sync_cycles": (I, [I, I, P]),
     "lxb_plan_staging": (I, [P, P, P, P]),
     "lxb_status_clear": (I, [P]),
     "lxb_plan_bytes": (ctypes.c_size_t, [P]),

@@ -131,6 +131,7 @@ enum {
   PR_WAIT,     // waiting for a staged blob
   PR_POLLS,    // count: staging polls that found the copy still in flight
   PR_TAKESYNC, // the block barrier after the staging wait
+  PR_BARRIERS, // count: cluster barriers in the token loop
   PR_N
 };
 
@@ -1907,6 +1908,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         }
       }
       cluster.sync();
+      pc[PR_BARRIERS]++;
       PROF(PR_SYNC);
       const int key = *reinterpret_cast<volatile int*>(&sm.gkey[gpar]);
       gp++;
@@ -1939,6 +1941,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         __syncthreads();
         push_rows(P, sm, sm.own[ph & 1], ph & 1, rank * P.blk, P.blk, cluster);
         cluster.sync();
+        pc[PR_BARRIERS]++;
         r_x = take_rows_norm(P, sm, ph & 1);
         x_new = false;
         ph++;
@@ -2038,6 +2041,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       if (wrote && t < C) *cluster.map_shared_rank(&sm.wflag[ph & 1], t) = 1;
       PROF(PR_ITEMS);
       cluster.sync();
+      pc[PR_BARRIERS]++;
       PROF(PR_SYNC);
       const int fl = *reinterpret_cast<volatile int*>(&sm.wflag[ph & 1]);
       __syncthreads();
@@ -2051,6 +2055,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         __syncthreads();
         push_rows(P, sm, sm.own[ph & 1], ph & 1, rank * P.blk, P.blk, cluster);
         cluster.sync();
+        pc[PR_BARRIERS]++;
         r_x = take_rows_norm(P, sm, ph & 1);
         x_new = false;
         ph++;
@@ -2062,6 +2067,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
           __syncthreads();
           push_rows(P, sm, sm.own[ph & 1], ph & 1, mr0, mnr, cluster);
           cluster.sync();
+          pc[PR_BARRIERS]++;
           if (P.nbuf == 1) issue_next(stp);
           r_x = take_rows_norm(P, sm, ph & 1, ly.mrow0, ly.mrow1);
           ph++;
@@ -2117,6 +2123,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         head_reduce(sm, bv, bi);
       }
       cluster.sync();
+      pc[PR_BARRIERS]++;
       cluster_max(sm, cluster, C);  // sm.cv / sm.ci: the cluster's first maximum
       if (helped) {
         // rank 0 gathers the helpers' maxima (each wait bounded) and tells every CTA
@@ -2153,6 +2160,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
           }
         }
         cluster.sync();
+        pc[PR_BARRIERS]++;
         if (sm.hok) {
           if (t == 0) {
             sm.cv = sm.hv;
@@ -2169,6 +2177,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
             head_rows(P, sm, P.headcta[rank * LXB_HEADSLICES + k], v2, i2);
           head_reduce(sm, v2, i2);
           cluster.sync();
+          pc[PR_BARRIERS]++;
           cluster_max(sm, cluster, C);
           if (t == 0) {
             if (bv > sm.cv || (bv == sm.cv && bi < sm.ci)) {
@@ -2827,6 +2836,44 @@ extern "C" int lxb_plan_set_profile(lxb_plan* p, unsigned long long* prof) {
 }
 
 extern "C" int lxb_profile_sections(void) { return PR_N; }
+
+// An empty cluster barrier's latency: one cluster of `cluster` CTAs (the decode's block size)
+// doing nothing but barrier.cluster, timed by rank 0's clock.
+__global__ void __launch_bounds__(NT, 1) lxb_cluster_sync_kernel(int iters,
+                                                                 unsigned long long* cycles) {
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  const long long t0 = clock64();
+  for (int i = 0; i < iters; i++) cluster.sync();
+  const long long t1 = clock64();
+  if (cluster.block_rank() == 0 && threadIdx.x == 0) *cycles = (unsigned long long)(t1 - t0);
+}
+
+extern "C" int lxb_cluster_sync_cycles(int cluster, int iters, double* cycles_per_barrier) {
+  if (cluster < 1 || cluster > 16 || iters < 1 || !cycles_per_barrier) return LXB_E_INVAL;
+  unsigned long long* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, sizeof(unsigned long long));
+  if (e) return cuda_rc(e);
+  if (cluster > 8)
+    cudaFuncSetAttribute(lxb_cluster_sync_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = cluster;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(cluster);
+  cfg.blockDim = dim3(NT);
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, lxb_cluster_sync_kernel, iters, d);
+  unsigned long long c = 0;
+  if (!e) e = cudaMemcpy(&c, d, sizeof(c), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (e) return cuda_rc(e);
+  *cycles_per_barrier = (double)c / iters;
+  return LXB_OK;
+}
 
 extern "C" int lxb_plan_set_typing(lxb_plan* p, const lxb_typing* ty) {
   if (!p) return LXB_E_INVAL;

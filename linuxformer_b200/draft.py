@@ -69,10 +69,16 @@ class CopyDrafter:
 class SelfDraft:
     """Greedy decode by draft-and-verify rounds on a Prefill plan (one stream)."""
 
-    def __init__(self, prefill: Prefill, draft: int = 64, ngram: int = 6, drafter=None) -> None:
+    def __init__(self, prefill: Prefill, draft: int = 64, ngram: int = 6, drafter=None,
+                 decoder=None, burst: int = 16) -> None:
         """drafter: a factory of drafters (objects with extend(tokens) and propose(D)); the
-        default is CopyDrafter(ngram)."""
+        default is CopyDrafter(ngram). decoder (a runtime.Decoder of the same chip, optional):
+        where the drafter has nothing to propose, the decode kernel runs ``burst`` tokens
+        instead of one-token prefill calls (its nonzero-row bitmaps rebuilt from the state
+        first, since the prefill does not keep them)."""
         self.pf = prefill
+        self.dec = decoder
+        self.burst = int(burst)
         self.make_drafter = drafter or (lambda: CopyDrafter(self.ngram))
         self.D = int(draft)
         self.ngram = int(ngram)
@@ -97,10 +103,29 @@ class SelfDraft:
         dr.extend([first])
         out: list[int] = []
         cur = int(first)
-        rounds = rollbacks = drafted = 0
+        rounds = rollbacks = drafted = bursts = burst_tokens = 0
+        if self.dec is not None:
+            L = self.pf.chip.n_layers
+            ptrs3 = ptrs.view(1, L, 2)
+            bitmaps = torch.zeros((1, L, 128, 8), dtype=torch.int32, device=dev)
+            dscratch = self.dec.scratch(1)
+            bf = torch.empty((1, 1), dtype=torch.int32, device=dev)
+            bp = torch.empty((1, max(1, self.burst)), dtype=torch.int32, device=dev)
         with torch.cuda.stream(st):
             while len(out) < n:
                 draft = dr.propose(min(self.D, n - len(out) - 1))
+                if not draft and self.dec is not None and n - len(out) > 1:
+                    k = min(self.burst, n - len(out))
+                    bf.fill_(cur)
+                    self.dec.launch(ptrs3, bitmaps, bf, k, bp[:, :k], None, sync_bitmaps=True,
+                                    stream=st, scratch=dscratch)
+                    new = bp[0, :k].tolist()  # syncs
+                    out.extend(new)
+                    dr.extend(new)
+                    cur = new[-1]
+                    bursts += 1
+                    burst_tokens += k
+                    continue
                 T = 1 + len(draft)
                 self.h_tok[0] = cur
                 if draft:
@@ -129,6 +154,8 @@ class SelfDraft:
                 rounds += 1
                 drafted += len(draft)
         self.pf._raise_status()
-        stats = {"rounds": rounds, "tokens_per_round": round(len(out) / max(rounds, 1), 2),
-                 "rollbacks": rollbacks, "drafted": drafted, "accepted": len(out) - rounds}
+        stats = {"rounds": rounds, "decode_bursts": bursts,
+                 "decoded_in_bursts": burst_tokens,
+                 "tokens_per_round": round((len(out) - burst_tokens) / max(rounds, 1), 2),
+                 "rollbacks": rollbacks, "drafted": drafted}
         return np.asarray(out[:n], dtype=np.int32), stats

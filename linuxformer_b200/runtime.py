@@ -163,7 +163,15 @@ class Decoder:
         return self._typing[3][:, 3:4].contiguous()
 
     PROFILE = ("norm", "items", "mlp", "sync", "pull", "fixup", "head", "embed", "fixups",
-               "tokens", "wait", "polls", "takesync")
+               "tokens", "wait", "polls", "takesync", "barriers")
+    COUNTS = ("fixups", "tokens", "polls", "barriers")  # counts; the others are clock cycles
+
+    def barrier_cycles(self, iters: int = 10000) -> float:
+        """An empty cluster barrier's latency (SM clock cycles) at this plan's cluster size."""
+        v = ctypes.c_double()
+        check(lib().lxb_cluster_sync_cycles(self.cluster, iters, ctypes.byref(v)),
+              "lxb_cluster_sync_cycles")
+        return v.value
 
     def set_profile(self, buf: torch.Tensor | None) -> None:
         """Accumulate per-section cycle counters into buf (int64 [S, cluster, 13]) on every

@@ -67,6 +67,23 @@ def test_rejected_drafts_roll_the_state_back(c1_chip):
     assert not (rec.cpu().numpy() != host.recurrent).any()
 
 
+def test_decode_bursts_where_nothing_is_drafted(c1_chip):
+    """With a Decoder, undrafted stretches run on the decode kernel: the stream and the state
+    stay the plain greedy decode's."""
+    chip = c1_chip
+    st0 = C.c1_state(chip, 0)
+    n = 900
+    rec, conv, ptrs = _state(chip, st0)
+    sd = SelfDraft(Prefill(chip), draft=64, decoder=Decoder(chip, cluster=16), burst=8)
+    got, stats = sd.run(ptrs, [rec, conv], 0, n)
+    host = st0.copy()
+    want, _, _ = Oracle(chip).decode(host, [0], n)
+    assert (got == want).all()
+    assert stats["decode_bursts"] > 0 and stats["rounds"] > 0
+    assert np.array_equal(conv.cpu().numpy().view(np.uint16), host.conv)
+    assert not (rec.cpu().numpy() != host.recurrent).any()
+
+
 def test_self_draft_matches_the_decode_kernel(c1_chip):
     chip = c1_chip
     st = C.c1_state(chip, 7)
