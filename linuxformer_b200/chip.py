@@ -479,3 +479,117 @@ def c2_state(chip: Chip, seed: int = 1) -> State:
         rec[L, vh, :n] = all_rows[k:k + n]
         k += n
     return State(rec, np.zeros((L_n, CONV, TAPS), np.uint16))
+
+
+# --- the real compiled circuit (a fixture made by the reference's own compiler) -----------------
+# (file key, the stock layer's weight name) of every projection / per-head vector in the fixture
+REAL_MATS = (("qkv", "linear_attn.in_proj_qkv.weight"), ("z", "linear_attn.in_proj_z.weight"),
+             ("b", "linear_attn.in_proj_b.weight"), ("a", "linear_attn.in_proj_a.weight"),
+             ("out", "linear_attn.out_proj.weight"), ("gate", "mlp.gate_proj.weight"),
+             ("up", "mlp.up_proj.weight"), ("down", "mlp.down_proj.weight"))
+REAL_VECS = (("A_log", "linear_attn.A_log"), ("dt_bias", "linear_attn.dt_bias"),
+             ("gnorm", "linear_attn.norm.weight"), ("ln_in", "input_layernorm.weight"),
+             ("ln_post", "post_attention_layernorm.weight"))
+
+
+def real_path():
+    from pathlib import Path
+
+    return Path(__file__).resolve().parents[1] / "tests" / "golden" / "real_chip.npz"
+
+
+def real(path=None, vocab: int | None = None) -> Chip:
+    """The real circuit's chip layers (the reference's compiler, ``lx.core.build(merge.config())``
+    emitted at hidden 2560 as the merged model has them, lx/lx/merge.py:123-157), the chip
+    vocabulary's embedding rows and, tied to them, the head (lx/lx/hf.py:63-93); final norm weight
+    0. ``vocab`` keeps only the first head rows (tests). The fixture's machine (program, RAM
+    seed, the RAM/ROM placement, the other tables' rows) and the reference machine's trace ride
+    along in ``meta``; ``real_state`` builds the state. Made by tests/golden/make_real.py."""
+    import json
+
+    z = np.load(path or real_path())
+    meta = json.loads(bytes(z["meta"]).decode())
+    layers = []
+    for L in range(meta["n_layers"]):
+        mats = {}
+        for f, _ in REAL_MATS:
+            cnt = z[f"L{L}.{f}.cnt"]
+            indptr = np.zeros(len(cnt) + 1, np.int64)
+            np.cumsum(cnt, out=indptr[1:])
+            shape = {"qkv": (CONV, H), "z": (ZD, H), "b": (NV, H), "a": (NV, H),
+                     "out": (H, ZD), "gate": (INTER, H), "up": (INTER, H), "down": (H, INTER)}[f]
+            assert len(cnt) == shape[0]
+            mats[f] = Sparse(shape, indptr, z[f"L{L}.{f}.idx"].astype(np.int32),
+                             z[f"L{L}.{f}.val"].astype(np.uint16))
+        vecs = {f: z[f"L{L}.{f}"].astype(np.uint16) for f, _ in REAL_VECS}
+        layers.append(Layer(conv=z[f"L{L}.conv"].astype(np.uint16), **mats, **vecs))
+    cols = z["emb_cols"].astype(np.int64)
+    vals = z["emb_vals"]
+    emb = np.zeros((vals.shape[0], H), np.uint16)
+    emb[:, cols] = vals
+    V = meta["vocab"] if vocab is None else vocab
+    r, k = np.nonzero(vals[:V] & 0x7FFF)
+    head = Sparse.from_coo((V, H), r, cols[k], vals[r, k])
+    fix = {k: z[k] for k in ("ram_map", "rom_map", "init_idx", "init_rows", "program", "trace")}
+    meta = dict(meta, config="real", fixture=fix)
+    return Chip(name="real circuit (merged config)" + (f", vocab={vocab}" if vocab else ""),
+                layers=layers, embed=emb, head=head, final_norm=np.zeros(H, np.uint16),
+                eps=float(meta["eps"]), meta=meta)
+
+
+def real_ram(chip: Chip) -> np.ndarray:
+    """The fixture machine's RAM bytes: seeded uniform random bytes, the program at the reset
+    address (checked against the fixture's digest)."""
+    m = chip.meta
+    ram = np.random.default_rng(m["ram_seed"]).integers(0, 256, m["ram_size"], dtype=np.uint8)
+    prog = m["fixture"]["program"]
+    ram[:len(prog)] = prog
+    assert hashlib.sha256(ram.tobytes()).hexdigest() == m["ram_sha256"], "RAM bytes"
+    return ram
+
+
+def real_state(chip: Chip, ram: np.ndarray | None = None) -> State:
+    """The machine's state in the GDN states, placed as the reference's ``lx.core.snapshot`` and
+    ``lx.hf.inject`` place it (lx/lx/core.py:1343-1414, lx/lx/hf.py:154-166):
+
+    - RAM block b (2048 words) lives in the value heads of key head j of layer L (the fixture's
+      map): word i of the block, if nonzero, is row i >> 3 of value head j * 8 + (i & 7): the
+      ballast a_ref in columns 0 and 1 and a_bit in column 2 + k for each set bit k;
+    - ROM head h (the first text_words words, 16384 a head): value head x of its key head holds
+      words [2048 x, 2048 (x + 1)) of the head's range, 8 words a row, the ballast in columns
+      0 and 1 and word k's 8 nibbles (low first) in columns 2 + 8 k ..;
+    - every other table's rows verbatim from the fixture.
+    Conv windows start at zero (a fresh session runs one zero step first, which leaves them so)."""
+    m, fx = chip.meta, chip.meta["fixture"]
+    ram = real_ram(chip) if ram is None else ram
+    rec = np.zeros((chip.n_layers, NV, KD, VD), np.float32)
+    a_ref, a_bit, rw = np.float32(m["a_ref"]), np.float32(m["a_bit"]), m["ram_head_words"]
+    refc = list(m["ref_cols"])
+    words = ram.view("<u4")
+    bitk = np.arange(32, dtype=np.uint32)
+    for blk, L, j in fx["ram_map"]:
+        seg = words[blk * rw:(blk + 1) * rw]
+        wi = np.nonzero(seg)[0]
+        rows = np.zeros((len(wi), VD), np.float32)
+        rows[:, refc] = a_ref
+        rows[:, 2:34] = ((seg[wi, None] >> bitk) & 1).astype(np.float32) * a_bit
+        rec[L, j * R + (wi & 7), wi >> 3] = rows
+    rom = words[:m["text_words"]]
+    hw = m["rom_head_words"]
+    nib = np.arange(8, dtype=np.uint32) * 4
+    for h, L, j in fx["rom_map"]:
+        for x in range(R):
+            base = h * hw + x * rw
+            blk = rom[base:base + rw] if base < len(rom) else rom[:0]
+            nr = -(-len(blk) // 8)
+            if nr == 0:
+                continue
+            pad = np.zeros(nr * 8, np.uint32)
+            pad[:len(blk)] = blk
+            rows = np.zeros((nr, VD), np.float32)
+            rows[:, refc] = a_ref
+            rows[:, 2:66] = ((pad.reshape(nr, 8)[:, :, None] >> nib) & 15).reshape(nr, 64)
+            rec[L, j * R + x, :nr] = rows
+    ii = fx["init_idx"]
+    rec[ii[:, 0], ii[:, 1], ii[:, 2]] = fx["init_rows"]
+    return State(rec, np.zeros((chip.n_layers, CONV, TAPS), np.uint16))

@@ -16,3 +16,11 @@ def c1_chip():
     from linuxformer_b200 import chip as C
 
     return C.c1(0)
+
+
+@pytest.fixture(scope="session")
+def real_chip():
+    """The real compiled circuit (tests/golden/real_chip.npz, made by the reference's compiler)."""
+    from linuxformer_b200 import chip as C
+
+    return C.real()
