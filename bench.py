@@ -1,7 +1,7 @@
 """Benchmark: the chip hot path on B200, one JSON line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl lxb|reference]
-                    [--mode all|decode|prefill|batched|text]
+                    [--mode all|decode|real|prefill|batched|text]
 
 BASELINE.json's metric has three parts; the default line carries all three:
 
@@ -12,6 +12,11 @@ BASELINE.json's metric has three parts; the default line carries all three:
   K x --tokens tokens of the stream (the reference's published figure runs 262,144 tokens a
   launch: 8 steps are one such chunk). Rank r decodes its own machine (state seed 1 + r): N
   GPUs decode N independent streams, no collective on the path (weak scaling).
+- ``real``: the same measurement on the real compiled circuit (tests/golden/real_chip.npz, made by
+  the reference's own compiler: the circuit behind the reference's published megakernel figure),
+  decoding the model alone from GO on the fixture's machine (a RISC-V program over 4.5 MiB of
+  seeded random RAM), --real-steps timed launches of --tokens after the warm-up launches; the
+  whole stream is checked against the reference machine's own trace.
 - ``prefill``: verify-prefill tok/s (config 3): 1,048,576 token ids uniform over the config-1
   vocabulary (seed 2) through the config-1 stack as chunked prefill (lxb_prefill), chunks of
   65,536 (the headline) and of 8,192; a step is one pass over all of them, continuing the state.
@@ -166,39 +171,81 @@ def _event_time(fn, stream) -> float:
 
 # --- config 2: single-stream decode (the headline) ---------------------------------------------
 def decode_c2(a, rank, world, dev, kw):
-    import numpy as np
-    import torch
-
     from linuxformer_b200 import chip as C
-    from linuxformer_b200._lib import S_ERRORS
-    from linuxformer_b200.runtime import Decoder
-    from linuxformer_b200.streams import job_rate, slowest, stream_seed
-    from oracle.oracle import Oracle
+    from linuxformer_b200.streams import stream_seed
 
     chip = C.c2(1, **kw)
     st0 = C.c2_state(chip, stream_seed(1, rank))
+    workload = (f"c2: 37-layer chip-shaped stack, greedy decode of {a.steps * a.tokens} tokens "
+                f"per stream as {a.steps} launches of {a.tokens}, one stream per GPU")
+    line = _decode_single(a, rank, world, dev, chip, st0, 0, None, "decode_c2_ncu.md")
+    if line is None:
+        return None
+    line.update(metric="chip decode tok/s (single stream per GPU)",
+                data="synthetic (seeded c2 generator)")
+    line["config"] = dict({"workload": workload, "seed": 1}, **line["config"])
+    return line
+
+
+def decode_real(a, rank, world, dev):
+    """The real compiled circuit (tests/golden/real_chip.npz: the reference's compiler, the
+    merged model's circuit at hidden 2560) decoding the model alone from GO on the fixture's
+    machine (a RISC-V program walking 4.5 MiB of seeded random RAM): the workload of the
+    reference's published megakernel figure (the same circuit, its own kernel image booting).
+    Every rank decodes its own copy of the machine (weak scaling); the stream is checked against
+    the reference machine's own token trace."""
+    from linuxformer_b200 import chip as C
+
+    chip = C.real()
+    st0 = C.real_state(chip)
+    tr = chip.meta["fixture"]["trace"]
+    line = _decode_single(a, rank, world, dev, chip, st0, int(tr[0]), tr, None)
+    if line is None:
+        return None
+    line.update(metric="chip decode tok/s, real circuit (single stream per GPU)",
+                data="the real circuit (reference compiler), seeded random RAM + program")
+    line["config"] = dict({"workload": (
+        f"real circuit: 37 compiled chip layers, 459,982-row head, greedy decode of "
+        f"{a.steps * a.tokens} tokens per stream as {a.steps} launches of {a.tokens} after "
+        f"{a.warmup} warm-up launches, from GO")}, **line["config"])
+    return line
+
+
+def _decode_single(a, rank, world, dev, chip, st0, first: int, trace, ncu_summary):
+    """One machine per GPU decoding greedily in launches of a.tokens; the line's common keys."""
+    import numpy as np
+    import torch
+
+    from linuxformer_b200._lib import S_ERRORS
+    from linuxformer_b200.runtime import Decoder
+    from linuxformer_b200.streams import job_rate, slowest
+    from oracle.oracle import Oracle
+
     dec = Decoder(chip, cluster=a.cluster, device=dev)
     states = dec.states([st0])
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     T = a.tokens
-    forced = torch.zeros((1, 1), dtype=torch.int32, device=dev)
+    forced = torch.full((1, 1), first, dtype=torch.int32, device=dev)
     preds = torch.empty((1, T), dtype=torch.int32, device=dev)
     cpu = None
     if rank == 0:  # the CPU restatement on the stream's first tokens; the GPU must agree
         st = st0.copy()
         t0 = time.perf_counter()
-        cpu_preds, _, _, counts = Oracle(chip).decode(st, [0], a.cpu_tokens, counts=True)
+        cpu_preds, _, _, counts = Oracle(chip).decode(st, [first], a.cpu_tokens, counts=True)
         cpu_v = a.cpu_tokens / (time.perf_counter() - t0)
         chk = dec.states([st0])
-        got, _ = dec.run(chk, [[0]], a.cpu_tokens)
+        got, _ = dec.run(chk, [[first]], a.cpu_tokens)
         same = bool((got[0].cpu().numpy() == cpu_preds).all())
         del chk
         cpu = (cpu_v, counts, same)
+    stream_all = []  # the stream, launch by launch (checked against the trace, if there is one)
     for w in range(a.warmup):
         dec.launch(states.ptrs, states.bitmaps, forced, T, preds, None, sync_bitmaps=(w == 0),
                    stream=stream, scratch=states.scratch)
         forced = preds[:, -1:].clone()
+        if trace is not None:
+            stream_all.append(preds[0].clone())
     torch.cuda.synchronize(dev)
     if world > 1:
         import torch.distributed as dist
@@ -213,6 +260,8 @@ def decode_c2(a, rank, world, dev, kw):
                                    sync_bitmaps=False, stream=stream, scratch=states.scratch),
                 stream))
             forced = preds[:, -1:].clone()
+            if trace is not None:
+                stream_all.append(preds[0].clone())  # outside the events
     torch.cuda.synchronize(dev)
     if dec.status().status & S_ERRORS:
         raise RuntimeError(f"device status {dec.status().status:#x}")
@@ -227,9 +276,19 @@ def decode_c2(a, rank, world, dev, kw):
         out = dec.run_host(states, np.array([[last]], np.int32), T, sync_bitmaps=False)
         e2e_t.append(time.perf_counter() - t0)
         last = int(out[0, -1])
+        if trace is not None:
+            stream_all.append(torch.from_numpy(np.asarray(out[0])))
     tot, e2e_tot = slowest([tot, sum(e2e_t)], dev)
     if rank != 0:
         return None
+    trace_check = None
+    if trace is not None:
+        got = torch.cat([x.cpu() for x in stream_all]).numpy()
+        n = min(len(got), len(trace) - 1)
+        bad = np.nonzero(got[:n] != trace[1:n + 1])[0]
+        trace_check = (f"first {n} tokens (warm-up, timed and e2e launches) "
+                       + ("identical to the reference machine's trace" if len(bad) == 0 else
+                          f"DIFFER from the reference machine's trace at token {bad[0] + 1}"))
     # outside the timed region: the per-section split of a profiled launch continuing the
     # stream, and the barrier floor (barriers per token x an empty cluster barrier's latency)
     prof = torch.zeros((1, a.cluster, len(dec.PROFILE)), dtype=torch.int64, device=dev)
@@ -256,17 +315,16 @@ def decode_c2(a, rank, world, dev, kw):
     cpu_v, counts, same = cpu
     btok = bytes_per_token(counts)
     achieved = btok * T / (tot / a.steps) / 1e9
-    tr = profile_value("decode_c2_ncu.md", "dram_bytes_per_token")
-    workload = (f"c2: 37-layer chip-shaped stack, greedy decode of {a.steps * a.tokens} tokens "
-                f"per stream as {a.steps} launches of {a.tokens}, one stream per GPU")
-    return {
-        "metric": "chip decode tok/s (single stream per GPU)", "value": round(value, 1),
+    tr = profile_value(ncu_summary, "dram_bytes_per_token") if ncu_summary else None
+    line = {
+        "metric": "", "value": round(value, 1),
         "unit": "tok/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": round(1000 * tot / a.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": round(value / BASELINE_TOKS, 3), "dtype": "fp32",
-        "data": "synthetic (seeded c2 generator)",
-        "config": {"workload": workload, "tokens_per_step": T, "cluster": a.cluster,
-                   "streams_per_gpu": 1, "seed": 1, "l2": "flushed between timed launches"},
+        "data": "",
+        "config": {"tokens_per_step": T, "cluster": a.cluster,
+                   "streams_per_gpu": 1, "l2": "flushed between timed launches",
+                   "staging": dec.staging()},
         "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * T},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
@@ -285,6 +343,9 @@ def decode_c2(a, rank, world, dev, kw):
         "profile_us_per_token": split,
         "barrier_floor": floor,
     }
+    if trace_check:
+        line["trace_check"] = trace_check
+    return line
 
 
 # --- config 3: verify-prefill ---------------------------------------------------------------
@@ -863,13 +924,14 @@ def main():
     ap.add_argument("--cluster", type=int, default=16)
     ap.add_argument("--impl", default="lxb", choices=["lxb", "reference"])
     ap.add_argument("--mode", default="all",
-                    choices=["all", "decode", "prefill", "batched", "text"])
+                    choices=["all", "decode", "real", "prefill", "batched", "text"])
     ap.add_argument("--cpu-tokens", type=int, default=400)
     ap.add_argument("--cpu-prefill-tokens", type=int, default=1024)
     ap.add_argument("--prefill-steps", type=int, default=4)
     ap.add_argument("--batched-tokens", type=int, default=4096)
     ap.add_argument("--cpu-batched-tokens", type=int, default=16)
     ap.add_argument("--text-steps", type=int, default=4)
+    ap.add_argument("--real-steps", type=int, default=4, help="timed launches, real circuit")
     ap.add_argument("--cpu-text-tokens", type=int, default=4)
     ap.add_argument("--vocab", type=int, default=None, help="(tests) a smaller c2 head")
     a = ap.parse_args()
@@ -895,6 +957,12 @@ def main():
     if a.mode in ("all", "decode"):
         line = decode_c2(a, rank, world, dev, kw)
     parts = {}
+    if a.mode in ("all", "real"):
+        import copy
+
+        ar = copy.copy(a)
+        ar.steps = a.real_steps if a.mode == "all" else a.steps
+        parts["real"] = decode_real(ar, rank, world, dev)
     if a.mode in ("all", "prefill"):
         parts["prefill"] = prefill_c3(a, rank, world, dev)
     if a.mode in ("all", "batched"):

@@ -86,13 +86,14 @@ struct Dev {
   int offset;
   float htab[4];
   int dense_cols[LXB_MAXDENSE];
+  const uint32_t* hsp;  // the head columns with sparse entries, a bitmask (null: none)
   uint32_t* status;  // [0] bits, [1] first stream, [2] first step
   const unsigned char* blobs;  // the step blobs
   const lxb_blobref* blobidx;  // [(n_layers + 1) * C]
   const int32_t* winmap;       // (layer, conv channel) pairs
   const int32_t* winidx;       // per CTA: (offset, count) into winmap
   int nbuf;                    // staging buffers in shared memory (1 or 2)
-  int stage;                   // bytes per staging buffer
+  int stage;                   // bytes per staging buffer: larger blobs are read where they are
 };
 
 struct Run {
@@ -187,6 +188,9 @@ struct __align__(16) Smem {
   int tok;
   int broken;                      // a staging wait gave up: blobs are not used any more
   alignas(8) unsigned long long mbar[2];  // staging buffers' transaction barriers
+  const unsigned char* bsrc[2];     // the blob each buffer's phase stands for: the buffer, or the
+                                    // blob in global memory when it is larger than a buffer
+  uint32_t hspm[H / 32];            // the head columns with sparse entries
   lxb_layer layers[LXB_MAXLAYERS];  // the layer descriptors
   uint64_t sptr[LXB_MAXLAYERS][2];  // this stream's state pointers per layer
   lxb_blobref bref[LXB_MAXLAYERS + 1];  // this CTA's step blobs (the head's last)
@@ -245,13 +249,17 @@ __device__ __forceinline__ void stage_issue(const Dev& P, Smem& sm, unsigned cha
   unsigned char* dst = stage + (size_t)buf * P.stage;
   const unsigned char* src = P.blobs + br.off;
   const uint32_t mb = smem_u32(&sm.mbar[buf]);
+  // a blob larger than a buffer is read in global memory: the phase completes on the arrival
+  // alone (no bytes expected), and the takers read the pointer published before it
+  const bool staged = br.bytes <= P.stage;
+  sm.bsrc[buf] = staged ? dst : src;
   // the buffer was last read through the generic proxy, by threads that have passed a block
   // barrier since: an async-proxy write after generic reads needs no proxy fence (the ordering
   // of the usual bulk-copy producer/consumer pipelines)
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mb),
-               "r"((uint32_t)br.bytes)
+               "r"(staged ? (uint32_t)br.bytes : 0u)
                : "memory");
-  for (int o = 0; o < br.bytes; o += 32768) {
+  for (int o = 0; staged && o < br.bytes; o += 32768) {
     const uint32_t n = (uint32_t)min(32768, br.bytes - o);
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -1422,7 +1430,10 @@ __device__ void load_embed(const Run& run, const Dev& P, Smem& sm, int tok) {
 
 // The head's per-group tables from sm.xm: htg[g][code] = the sum, in column order from +0, of the
 // group's 4 dense columns' weights (by their 2-bit codes) times xm. Ends with a block barrier.
-__device__ void head_tables(const Dev& P, Smem& sm) {
+// Returns (in every thread) whether xm is nonzero in some column with sparse entries: if not,
+// every sparse product is +-0 and a row's sparse sum stays +0, so head_rows skips the entries
+// (as the reference visits only sparse columns with x != 0, lx/csrc/mega.cu:584-595).
+__device__ int head_tables(const Dev& P, Smem& sm) {
   const int nd = P.n_dense, ng = (nd + 3) / 4;
   for (int k = threadIdx.x; k < ng * 256; k += NT) {
     const int g = k >> 8, code = k & 255;
@@ -1431,17 +1442,24 @@ __device__ void head_tables(const Dev& P, Smem& sm) {
       s = lx_add(s, lx_mul(P.htab[(code >> (2 * j)) & 3], sm.xm[P.dense_cols[4 * g + j]]));
     sm.htg[g][code] = s;
   }
-  __syncthreads();
+  int any = 0;
+#pragma unroll
+  for (int i = 0; i < H / NT; i++) {
+    const int c = threadIdx.x + NT * i;
+    any |= ((sm.hspm[c >> 5] >> (c & 31)) & 1u) && sm.xm[c] != 0.0f;
+  }
+  return __syncthreads_or(any);
 }
 
 // The head rows of one part, into this thread's running first maximum (bv, bi) of the bf16 logits
 // (a thread's rows ascend within a part, and parts are visited in ascending order).
-__device__ void head_rows(const Dev& P, const Smem& sm, const lxb_headcta hc, float& bv,
+__device__ void head_rows(const Dev& P, const Smem& sm, const lxb_headcta hc, int hsp, float& bv,
                           int& bi) {
   const int t = threadIdx.x;
   const int nd = P.n_dense, ng = (nd + 3) / 4;
   const int32_t* rp = P.i32 + hc.rowptr;
-  const bool sparse = rp[0] != rp[hc.r1 - hc.r0];  // any sparse entry in these rows
+  // any sparse entry in these rows, and a nonzero input in some sparse column (head_tables)
+  const bool sparse = hsp && rp[0] != rp[hc.r1 - hc.r0];
   constexpr int U = 4;  // rows in flight per thread
   for (int row0 = hc.r0 + t; row0 < hc.r1; row0 += NT * U) {
     uint64_t code[U];
@@ -1591,11 +1609,11 @@ __device__ void head_helper(const Dev& P, const Run& run, Smem& sm, int rank, in
     for (int k = t; k < H / 4; k += NT)
       reinterpret_cast<float4*>(sm.xm)[k] = __ldcg(reinterpret_cast<const float4*>(run.hx) + k);
     __syncthreads();
-    head_tables(P, sm);
+    const int hsp = head_tables(P, sm);
     float bv = -LXB_INF;
     int bi = 0x7fffffff;
     for (int k = LXB_HEADMAIN + hk - 1; k < LXB_HEADSLICES; k += run.n_help)
-      head_rows(P, sm, P.headcta[rank * LXB_HEADSLICES + k], bv, bi);
+      head_rows(P, sm, P.headcta[rank * LXB_HEADSLICES + k], hsp, bv, bi);
     head_reduce(sm, bv, bi);
     if (t == 0) {
       uint4* hp = run.hpart + part;
@@ -1676,6 +1694,8 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
   const int C = P.C;
   const int s = blockIdx.x / C;
   const int t = threadIdx.x;
+  // the head's sparse-column mask (read after the block barriers that precede every head step)
+  for (int k = t; k < H / 32; k += NT) sm.hspm[k] = P.hsp ? P.hsp[k] : 0u;
   if (s >= run.n_streams) {  // a head helper cluster
     head_helper(P, run, sm, rank, s - run.n_streams + 1);
     return;
@@ -1806,7 +1826,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     __syncthreads();
     PROF(PR_TAKESYNC);
     if (sm.broken) return nullptr;
-    return stage + (size_t)b * P.stage;
+    return sm.bsrc[b];
   };
   // A run of GDN-only layers [lo0, hi) as group steps, all on the residual as it was at the
   // step's start. That is exact as long as no layer before changes it. Each step first takes a
@@ -2110,15 +2130,15 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       }
       issue_next(stp);
       stp++;
-      head_tables(P, sm);
+      const int hsp = head_tables(P, sm);
       {  // this rank's first slices (helped), or its whole range
         float bv = -LXB_INF;
         int bi = 0x7fffffff;
         if (helped) {
           for (int k = 0; k < LXB_HEADMAIN; k++)
-            head_rows(P, sm, P.headcta[rank * LXB_HEADSLICES + k], bv, bi);
+            head_rows(P, sm, P.headcta[rank * LXB_HEADSLICES + k], hsp, bv, bi);
         } else {
-          head_rows(P, sm, P.headcta[C * LXB_HEADSLICES + rank], bv, bi);
+          head_rows(P, sm, P.headcta[C * LXB_HEADSLICES + rank], hsp, bv, bi);
         }
         head_reduce(sm, bv, bi);
       }
@@ -2174,7 +2194,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
           float v2 = -LXB_INF;
           int i2 = 0x7fffffff;
           for (int k = LXB_HEADMAIN; k < LXB_HEADSLICES; k++)
-            head_rows(P, sm, P.headcta[rank * LXB_HEADSLICES + k], v2, i2);
+            head_rows(P, sm, P.headcta[rank * LXB_HEADSLICES + k], hsp, v2, i2);
           head_reduce(sm, v2, i2);
           cluster.sync();
           pc[PR_BARRIERS]++;
@@ -2511,6 +2531,7 @@ int validate(const View& v, int cluster) {
   for (int j = 0; j < h->n_dense; j++)
     if (h->dense_cols[j] < 0 || h->dense_cols[j] >= H) return LXB_E_IMAGE;
   if (!u16_range(v, h->final_norm, H) || h->n_embed_rows < 1 || h->offset < 0) return LXB_E_IMAGE;
+  if (h->hsp_mask != -1 && !i32_range(v, h->hsp_mask, H / 32)) return LXB_E_IMAGE;
   const lxb_layer* layers = v.sec<lxb_layer>(LXB_SEC_LAYERS);
   const lxb_item* items = v.sec<lxb_item>(LXB_SEC_ITEMS);
   const lxb_chan* chans = v.sec<lxb_chan>(LXB_SEC_CHANS);
@@ -2604,9 +2625,12 @@ extern "C" int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb
   cudaDeviceGetAttribute(&cl, cudaDevAttrClusterLaunch, dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   const int base = (int)((sizeof(Smem) + 127) / 128 * 128);
-  const int stage = (v.h->blob_max + 127) / 128 * 128;
-  const int nbuf = base + 2 * stage <= optin ? 2 : 1;
-  if (major < 10 || !cl || base + nbuf * stage > optin) return LXB_E_DEVICE;
+  // two staging buffers; when the largest blob does not fit twice, buffers of what does fit,
+  // and the larger blobs are read in global memory (stage_issue)
+  int stage = (v.h->blob_max + 127) / 128 * 128;
+  if (base + 2 * stage > optin) stage = (optin - base) / 2 / 128 * 128;
+  const int nbuf = 2;
+  if (major < 10 || !cl || stage < (int)sizeof(lxb_bhdr)) return LXB_E_DEVICE;
   lxb_plan* p = new (std::nothrow) lxb_plan();
   if (!p) return LXB_E_INVAL;
   p->device = dev;
@@ -2648,6 +2672,7 @@ extern "C" int lxb_plan_create(const void* image, size_t bytes, int cluster, lxb
   d.offset = h->offset;
   memcpy(d.htab, h->htab, sizeof(d.htab));
   memcpy(d.dense_cols, h->dense_cols, sizeof(d.dense_cols));
+  d.hsp = h->hsp_mask >= 0 ? reinterpret_cast<const uint32_t*>(d.i32 + h->hsp_mask) : nullptr;
   d.status = p->status;
   d.blobs = b + h->sec[LXB_SEC_BLOBS].off;
   d.blobidx = reinterpret_cast<const lxb_blobref*>(b + h->sec[LXB_SEC_BLOBIDX].off);

@@ -80,7 +80,9 @@ typedef struct {
   float htab[4];         // the dense head columns' values, by code
   int32_t dense_cols[LXB_MAXDENSE];
   int32_t blob_max;      // the largest step blob, bytes
-  int32_t pad1[3];
+  int32_t hsp_mask;      // i32 pool offset: 80 words, bit c set if head column c has sparse
+                         // entries (-1: none)
+  int32_t pad1[2];
   lxb_sec sec[LXB_SEC_COUNT];
 } lxb_image_header;
 

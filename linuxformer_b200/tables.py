@@ -54,7 +54,8 @@ HEADER = np.dtype([("magic", "<u4"), ("version", "<u4"), ("n_layers", "<i4"), ("
                    ("n_vocab", "<i4"), ("hidden", "<i4"), ("n_items", "<i4"), ("n_dense", "<i4"),
                    ("n_embed_rows", "<i8"), ("offset", "<i4"), ("eps", "<f4"),
                    ("final_norm", "<i4"), ("pad0", "<i4"), ("htab", "<f4", (4,)),
-                   ("dense_cols", "<i4", (MAXDENSE,)), ("blob_max", "<i4"), ("pad1", "<i4", (3,)),
+                   ("dense_cols", "<i4", (MAXDENSE,)), ("blob_max", "<i4"), ("hsp_mask", "<i4"),
+                   ("pad1", "<i4", (2,)),
                    ("sec", "<i8", (len(SEC), 2))])
 BLOBREF = np.dtype([("off", "<i8"), ("bytes", "<i4"), ("pad", "<i4")])
 BHDR = np.dtype([("bytes", "<i4"), ("n_items", "<i4"), ("item", "<i4", (ITEMSLOTS,)),
@@ -412,6 +413,12 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
     sp_ptr = np.zeros(V + 1, np.int64)
     np.cumsum(np.bincount(sp_rows, minlength=V), out=sp_ptr[1:])
     sp_base = ent.add(_pack(sp_cols, sp_bits))
+    # the columns with sparse entries, as a bitmask: a token whose normed residual is zero in all
+    # of them adds only zeros there, and the kernel skips the rows' sparse entries
+    hsp = np.zeros(C.H // 32, np.uint32)
+    for c in np.unique(sp_cols):
+        hsp[c >> 5] |= np.uint32(1) << np.uint32(c & 31)
+    hsp_mask = i32.add(hsp.view(np.int32)) if len(sp_cols) else -1
     # the head rows: CTA rank c owns rows [V c / C, V (c + 1) / C) (entry C * HEADSLICES + c),
     # cut in HEADSLICES slices (entry c * HEADSLICES + k) for a launch with helper clusters: the
     # decoding cluster takes the first slices of its ranges, the helpers the others
@@ -459,6 +466,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
     hdr["htab"] = htab
     hdr["dense_cols"][:len(dense)] = dense
     hdr["blob_max"] = stats["blob_max"]
+    hdr["hsp_mask"] = hsp_mask
     blobs, pos = [], HEADER.itemsize
     for k, a in enumerate(secs):
         pos = -(-pos // 16) * 16

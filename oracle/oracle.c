@@ -460,8 +460,17 @@ static int head_argmax(lxo_run* st, float* margin_out) {
     if (k != w && cb[k] > second) second = cb[k];
   }
   if (margin_out) *margin_out = lx_sub(cb[w], second);
-  if (st->cnt)
-    st->cnt[LXO_C_HEAD_B] += (st->n_dense ? 8 * V : 0) + 4 * (hd->indptr[V] - (st->n_dense ? V * st->n_dense : 0));
+  if (st->cnt) {  // 8 bytes of codes per row; 4 per sparse entry whose column's input is nonzero
+    unsigned char dense[H];  // (the others add zeros: a kernel may skip them)
+    memset(dense, 0, sizeof(dense));
+    for (int j = 0; j < st->n_dense; j++) dense[st->dense_cols[j]] = 1;
+    int64_t sp = 0;
+    for (int64_t e = 0; e < hd->indptr[V]; e++) {
+      const int c = hd->indices[e];
+      sp += !dense[c] && xf[c] != 0.0f;
+    }
+    st->cnt[LXO_C_HEAD_B] += (st->n_dense ? 8 * V : 0) + 4 * sp;
+  }
   return ci[w];
 }
 
