@@ -15,8 +15,9 @@ BASELINE.json's metric has three parts; the default line carries all three:
 - ``real``: the same measurement on the real compiled circuit (tests/golden/real_chip.npz, made by
   the reference's own compiler: the circuit behind the reference's published megakernel figure),
   decoding the model alone from GO on the fixture's machine (a RISC-V program over 4.5 MiB of
-  seeded random RAM), --real-steps timed launches of --tokens after the warm-up launches; the
-  whole stream is checked against the reference machine's own trace.
+  seeded random RAM), --real-steps timed launches of --real-tokens after the warm-up launches
+  (--steps of --tokens with --mode real); the whole stream is checked against the reference
+  machine's own trace.
 - ``prefill``: verify-prefill tok/s (config 3): 1,048,576 token ids uniform over the config-1
   vocabulary (seed 2) through the config-1 stack as chunked prefill (lxb_prefill), chunks of
   65,536 (the headline) and of 8,192; a step is one pass over all of them, continuing the state.
@@ -932,6 +933,8 @@ def main():
     ap.add_argument("--cpu-batched-tokens", type=int, default=16)
     ap.add_argument("--text-steps", type=int, default=4)
     ap.add_argument("--real-steps", type=int, default=4, help="timed launches, real circuit")
+    ap.add_argument("--real-tokens", type=int, default=8192,
+                    help="tokens per launch of the real circuit's part in the default line")
     ap.add_argument("--cpu-text-tokens", type=int, default=4)
     ap.add_argument("--vocab", type=int, default=None, help="(tests) a smaller c2 head")
     a = ap.parse_args()
@@ -961,7 +964,8 @@ def main():
         import copy
 
         ar = copy.copy(a)
-        ar.steps = a.real_steps if a.mode == "all" else a.steps
+        if a.mode == "all":
+            ar.steps, ar.tokens = a.real_steps, a.real_tokens
         parts["real"] = decode_real(ar, rank, world, dev)
     if a.mode in ("all", "prefill"):
         parts["prefill"] = prefill_c3(a, rank, world, dev)
