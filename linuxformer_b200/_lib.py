@@ -4,6 +4,8 @@ library is missing or fails to load, every entry point raises."""
 from __future__ import annotations
 
 import ctypes
+import os
+from pathlib import Path
 
 from . import build as _build
 
@@ -86,7 +88,8 @@ def lib():
     """The loaded library (built first if it is missing or older than its sources)."""
     global _lib
     if _lib is None:
-        path = _build.LIB
+        # LXB_LIBRARY: another build of liblxb.so to load instead (A/B timing of two builds)
+        path = Path(os.environ["LXB_LIBRARY"]) if os.environ.get("LXB_LIBRARY") else _build.LIB
         if not path.exists():
             raise LxbError(f"{path} is not built: run `python -m linuxformer_b200.build`")
         L = ctypes.CDLL(str(path))

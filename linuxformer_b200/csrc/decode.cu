@@ -64,6 +64,8 @@ namespace cg = cooperative_groups;
 #define LXB_QTASKS (LXB_QLAYERS * LXB_ITEMSLOTS)
 #define LXB_QNONE 0xffffffffu
 #define LXB_QFULL 0x40000000u
+#define LXB_LONGROWS 64  // out_proj / down_proj rows of a CTA summed by a warp each (the rest by
+#define LXB_LONG 32      // a thread each): rows with more than LXB_LONG entries
 #define LXB_QOUT 0x80000000u   // (qinfo) the item's head has out_proj entries
 #ifndef LXB_GROUPS
 #define LXB_GROUPS 1    // runs of GDN-only layers as optimistic group steps
@@ -133,6 +135,11 @@ enum {
   PR_POLLS,    // count: staging polls that found the copy still in flight
   PR_TAKESYNC, // the block barrier after the staging wait
   PR_BARRIERS, // count: cluster barriers in the token loop
+  PR_GITEMS,   // group steps: quiet pass and items
+  PR_GSYNC,    // group steps: the cluster barrier
+  PR_GFIXUP,   // group steps: undo, out_proj fix-ups
+  PR_FXMLP,    // a paired step's fix-up: the MLP again, its barrier
+  PR_FXOUT,    // a paired step's fix-up: the out_proj rows (before their push and barrier)
   PR_N
 };
 
@@ -169,6 +176,16 @@ struct __align__(16) Smem {
   uint32_t qbad;                   // an MLP step's items with a nonzero key (or query) output
   int wflag[2];                    // some item of the step wrote (pushed by the writer)
   int kmask[LXB_NK];               // out_proj step: active value heads per key head
+  int lrows[LXB_LONGROWS];         // owned rows with many entries, summed by a warp each
+  int nlong;
+  unsigned long long bigm;         // layers whose every item is too big for a group step's
+                                   // speculation (many query/key channels, windows in global
+                                   // memory, or a decay): they run as steps of their own
+  unsigned long long pcs[PR_N];    // the profile's counters (thread 0's timeline)
+  unsigned long long upm;          // layers whose GDN wrote at the last token: their MLP waits
+                                   // for the out_proj rows instead of running beside the items
+  uint32_t kinfo[LXB_MAXLAYERS][LXB_NK];  // per layer and key head: its item's slot | cta << 8 |
+                                   // 1 << 16 (0: no item), for the out_proj step's gather
   alignas(16) uint16_t on[LXB_ITEMSLOTS][R * VD];  // the gated norm's output per item slot
   union {
     alignas(16) uint16_t onall[LXB_NK][R * VD];  // gathered for the out_proj step
@@ -1271,6 +1288,7 @@ __device__ uint32_t mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, co
                               qa.w, qb.x, qnw);
     if (v != 0.0f && (qout || (qa.y >> 16) >= KD)) atomicOr(&sm.qbad, 1u << qk);
   }
+  if (t == 0) sm.nlong = 0;
   __syncthreads();
   const int r0 = m.r0;
   const int32_t* rp = reinterpret_cast<const int32_t*>(B + m.down_ptr);
@@ -1281,6 +1299,13 @@ __device__ uint32_t mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, co
     float sd = 0.0f;
     bool any = false;
     const int e1 = rp[k + 1];
+    if (m.nlong && e1 - rp[k] > LXB_LONG) {  // a warp's, below (if the list has room)
+      const int q = atomicAdd(&sm.nlong, 1);
+      if (q < LXB_LONGROWS) {
+        sm.lrows[q] = k;
+        continue;
+      }
+    }
     for (int e = rp[k]; e < e1; e += 8) {  // 8 entries' loads in flight, then the sum in order
       uint32_t w[8];
       float hv[8];
@@ -1298,6 +1323,34 @@ __device__ uint32_t mlp_owner(const Dev& P, Smem& sm, const unsigned char* B, co
     if (any) res = lx_rbf(lx_add(xv, lx_rbf(sd)));
     own[k] = res;
   }
+  if (m.nlong) __syncthreads();  // (otherwise nothing was deferred; the plan counted them)
+  // the long rows, a warp each: 32 entries' products at once, summed in the entries' order
+  const int nlong = m.nlong ? min(sm.nlong, LXB_LONGROWS) : 0;
+  const int lane = t & 31;
+  for (int j = t >> 5; j < nlong; j += NT / 32) {
+    const int k = sm.lrows[j];
+    const int a = rp[k], b = rp[k + 1];
+    float sd = 0.0f;
+    bool any = false;
+    uint32_t w = a + lane < b ? de[a + lane] : 0u;
+    for (int e0 = a; e0 < b; e0 += 32) {
+      const uint32_t wn = e0 + 32 + lane < b ? de[e0 + 32 + lane] : 0u;  // the next
+      const float hv = e0 + lane < b ? sm.hbuf[w & 0xffffu] : 0.0f;
+      const float p = hv != 0.0f ? lx_mul(hv, lx_f((uint16_t)(w >> 16))) : 0.0f;
+      unsigned msk = __ballot_sync(0xffffffffu, hv != 0.0f);
+      any |= msk != 0u;
+      while (msk) {
+        const int l = __ffs(msk) - 1;
+        msk &= msk - 1u;
+        sd = lx_add(sd, __shfl_sync(0xffffffffu, p, l));
+      }
+      w = wn;
+    }
+    if (lane == 0) {
+      const float xv = sm.x[r0 + k];
+      own[k] = any ? lx_rbf(lx_add(xv, lx_rbf(sd))) : xv;
+    }
+  }
   const uint32_t bad = w_in ? sm.qbad : 0u;
   if (qk >= 0 && !((bad >> qk) & 1)) sm.win[qb.y] = qnw;  // a quiet item: its windows shift
   return full | bad;
@@ -1309,30 +1362,30 @@ __device__ void copy_owner(Smem& sm, int r0, int nr, float* own) {
 }
 
 // out_proj over this CTA's rows, from the layer's items' outputs (gathered over DSMEM)
-__device__ void out_owner(const Dev& P, Smem& sm, const lxb_layer& ly, const lxb_owner& ow,
+__device__ void out_owner(const Dev& P, Smem& sm, int L, const lxb_owner& ow,
                           int rank, int tok, float* own, cg::cluster_group& cluster) {
   const int t = threadIdx.x;
-  const int32_t* itemof = P.i32 + ly.itemof;
   if (t < LXB_NK) {
-    const int ii = itemof[t];
+    const uint32_t ki = sm.kinfo[L][t];
     uint32_t m = 0;
-    if (ii >= 0) {  // (a slot another layer's or token's item has set since holds none of this)
-      const lxb_item it = P.items[ii];
-      m = *cluster.map_shared_rank(&sm.vhmask[it.slot], it.cta);
-      if (*cluster.map_shared_rank(&sm.vhlay[it.slot], it.cta) != it.layer ||
-          *cluster.map_shared_rank(&sm.vhtok[it.slot], it.cta) != tok)
+    if (ki) {  // (a slot another layer's or token's item has set since holds none of this)
+      const int slot = (int)(ki & 0xffu), cta = (int)((ki >> 8) & 0xffu);
+      m = *cluster.map_shared_rank(&sm.vhmask[slot], cta);
+      if (*cluster.map_shared_rank(&sm.vhlay[slot], cta) != L ||
+          *cluster.map_shared_rank(&sm.vhtok[slot], cta) != tok)
         m = 0;
     }
     sm.kmask[t] = (int)m;
   }
+  if (t == 0) sm.nlong = 0;  // (the long rows' list, below)
   __syncthreads();
   // copy the active items' outputs: 16 key heads x 128 uint4
   for (int k = t; k < LXB_NK * (R * VD / 8); k += NT) {
     const int kh = k / (R * VD / 8), q = k % (R * VD / 8);
     if (!sm.kmask[kh]) continue;
-    const lxb_item it = P.items[itemof[kh]];
-    const uint4* src =
-        reinterpret_cast<const uint4*>(cluster.map_shared_rank(&sm.on[it.slot][0], it.cta));
+    const uint32_t ki = sm.kinfo[L][kh];
+    const uint4* src = reinterpret_cast<const uint4*>(
+        cluster.map_shared_rank(&sm.on[ki & 0xffu][0], (int)((ki >> 8) & 0xffu)));
     reinterpret_cast<uint4*>(&sm.onall[kh][0])[q] = src[q];
   }
   __syncthreads();
@@ -1343,6 +1396,13 @@ __device__ void out_owner(const Dev& P, Smem& sm, const lxb_layer& ly, const lxb
     float res = xv;
     if (rp) {
       const int a = rp[k], b = rp[k + 1];
+      if (ow.nlong && b - a > LXB_LONG) {  // a warp's, below (if the list has room)
+        const int q = atomicAdd(&sm.nlong, 1);
+        if (q < LXB_LONGROWS) {
+          sm.lrows[q] = k;
+          continue;
+        }
+      }
       float s = 0.0f;
       bool any = false;
       for (int e = a; e < b; e += 8) {
@@ -1365,6 +1425,47 @@ __device__ void out_owner(const Dev& P, Smem& sm, const lxb_layer& ly, const lxb
       if (any) res = lx_rbf(lx_add(xv, lx_rbf(s)));
     }
     own[k] = res;
+  }
+  if (!ow.nlong) return;  // (the plan counted them: nothing was deferred)
+  __syncthreads();
+  // the long rows, a warp each: 32 entries' loads and products at once, then their sum in the
+  // entries' order (the same additions as one thread's, in the same order: the same bits)
+  const int nlong = min(sm.nlong, LXB_LONGROWS);
+  const int lane = t & 31;
+  for (int j = t >> 5; j < nlong; j += NT / 32) {
+    const int k = sm.lrows[j];
+    const int a = rp[k], b = rp[k + 1];
+    float s = 0.0f;
+    bool any = false;
+    uint32_t w = a + lane < b ? __ldg(P.ent + a + lane) : 0u;
+    for (int e0 = a; e0 < b; e0 += 32) {
+      const uint32_t wn = e0 + 32 + lane < b ? __ldg(P.ent + e0 + 32 + lane) : 0u;  // the next
+      float p = 0.0f;
+      bool nz = false;
+      if (e0 + lane < b) {
+        const uint32_t vd = w & 0xffffu;
+        const int kh = (int)(vd >> 10);
+        if ((sm.kmask[kh] >> ((vd >> 7) & 7)) & 1) {
+          const float ov = lx_f(sm.onall[kh][vd & 1023u]);
+          if (ov != 0.0f) {
+            p = lx_mul(ov, lx_f((uint16_t)(w >> 16)));
+            nz = true;
+          }
+        }
+      }
+      unsigned m = __ballot_sync(0xffffffffu, nz);
+      any |= m != 0u;
+      while (m) {
+        const int l = __ffs(m) - 1;
+        m &= m - 1u;
+        s = lx_add(s, __shfl_sync(0xffffffffu, p, l));
+      }
+      w = wn;
+    }
+    if (lane == 0) {
+      const float xv = sm.x[r0 + k];
+      own[k] = any ? lx_rbf(lx_add(xv, lx_rbf(s))) : xv;
+    }
   }
 }
 
@@ -1756,6 +1857,30 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     }
     sm.qinfo[L][q] = v;
   }
+  for (int k = t; k < P.n_layers * LXB_NK; k += NT) {  // every layer's items: slot and CTA
+    const int L = k / LXB_NK, kh = k % LXB_NK;
+    const int ii = P.i32[sm.layers[L].itemof + kh];
+    uint32_t v = 0u;
+    if (ii >= 0) {
+      const lxb_item it = P.items[ii];
+      v = (uint32_t)it.slot | (uint32_t)it.cta << 8 | 0x10000u;
+    }
+    sm.kinfo[L][kh] = v;
+  }
+  if (t == 0) sm.upm = 0ull;
+  if (t < 64) {  // a lane per layer (from the plan's items: the same in every CTA)
+    bool big = false;
+    if (t < P.n_layers) {
+      const lxb_layer& ly = sm.layers[t];
+      big = ly.has_gdn && ly.n_items > 0;
+      for (int k = 0; big && k < ly.n_items; k++) {
+        const lxb_item it = P.items[ly.item0 + k];
+        big = it.n_eager > 32 || (it.flags & (LXB_IT_NONRES | LXB_IT_DECAYS));
+      }
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, big);
+    if ((t & 31) == 0) reinterpret_cast<unsigned*>(&sm.bigm)[t >> 5] = m;
+  }
   if (t < LXB_ITEMSLOTS) {  // no slot holds an output yet
     sm.vhmask[t] = 0;
     sm.vhlay[t] = -1;
@@ -1767,18 +1892,22 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
   int ph = 0;
   long long stp = 0;  // staged steps consumed
   uint32_t phases = 0u;  // bit b: the parity staging buffer b waits for next
-  unsigned long long pc[PR_N];
-#pragma unroll
-  for (int k = 0; k < PR_N; k++) pc[k] = 0;
+  // the profile (thread 0's sections and counts, in shared memory: no registers held for them)
+  if (t == 0)
+    for (int k = 0; k < PR_N; k++) sm.pcs[k] = 0ull;
   long long c0 = clock64();
   const bool prof = run.prof != nullptr;
-#define PROF(sec)                                \
-  do {                                           \
-    if (prof) {                                  \
-      const long long c1 = clock64();            \
-      pc[sec] += (unsigned long long)(c1 - c0);  \
-      c0 = c1;                                   \
-    }                                            \
+#define PROF(sec)                                     \
+  do {                                                \
+    if (prof && t == 0) {                             \
+      const long long c1 = clock64();                 \
+      sm.pcs[sec] += (unsigned long long)(c1 - c0);   \
+      c0 = c1;                                        \
+    }                                                 \
+  } while (0)
+#define COUNT(sec)                \
+  do {                            \
+    if (t == 0) sm.pcs[sec]++;    \
   } while (0)
   // the layer (or head, = n_layers) of global step k: k runs over the layers then the head
   int cur_layer = 0;  // the current step's layer (n_layers: the head)
@@ -1820,7 +1949,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     unsigned long long polls = 0;
     if (ok) ok = stage_wait(P, sm, b, (phases >> b) & 1u, s, i, polls);
     phases ^= 1u << b;
-    pc[PR_POLLS] += polls;
+    if (prof && t == 0) sm.pcs[PR_POLLS] += polls;
     if (!ok && t == 0) sm.broken = 1;
     PROF(PR_WAIT);
     __syncthreads();
@@ -1854,7 +1983,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       const int l0 = resume ? lo + 1 : lo;  // (J's other items are done)
       uint32_t vis;  // the layers l0 + b that still have items here (the same in every thread)
       const int qhi = quiet_pass(P, run, sm, s, rank, lo, l0, hi, i, r_x, vis);
-      PROF(PR_ITEMS);
+      PROF(PR_GITEMS);
       bool at_lo = resume && (rs_mask || held_out);  // J first: its pending items, its outputs
       auto peek = [&]() -> int { return at_lo ? lo : (vis ? l0 + __ffs(vis) - 1 : -1); };
       {
@@ -1918,7 +2047,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
           }
           stp++;
         }
-        PROF(PR_ITEMS);
+        PROF(PR_GITEMS);
         if (st_any) {
           sL = L;
           outL = st_any & 1;
@@ -1928,8 +2057,8 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         }
       }
       cluster.sync();
-      pc[PR_BARRIERS]++;
-      PROF(PR_SYNC);
+      COUNT(PR_BARRIERS);
+      PROF(PR_GSYNC);
       const int key = *reinterpret_cast<volatile int*>(&sm.gkey[gpar]);
       gp++;
       if (key == 0x7fffffff) {  // every layer of the step done, none wrote
@@ -1953,19 +2082,19 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         held_out = sL == J && outL;
         lo = J;
       } else {  // J wrote: its out_proj rows into the residual, then on from J + 1
-        pc[PR_FIXUPS]++;
+        COUNT(PR_FIXUPS);
         ph++;
         const lxb_layer& lyJ = sm.layers[J];
         const lxb_owner ow = P.owners[lyJ.owner0 + rank];
-        out_owner(P, sm, lyJ, ow, rank, i, sm.own[ph & 1], cluster);
+        out_owner(P, sm, J, ow, rank, i, sm.own[ph & 1], cluster);
         __syncthreads();
         push_rows(P, sm, sm.own[ph & 1], ph & 1, rank * P.blk, P.blk, cluster);
         cluster.sync();
-        pc[PR_BARRIERS]++;
+        COUNT(PR_BARRIERS);
         r_x = take_rows_norm(P, sm, ph & 1);
         x_new = false;
         ph++;
-        PROF(PR_FIXUP);
+        PROF(PR_GFIXUP);
         resume = false;
         rs_mask = 0;
         held_out = 0;
@@ -1981,10 +2110,15 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
     for (int L = 0; L < P.n_layers;) {
       const lxb_layer& ly = sm.layers[L];
 #if LXB_GROUPS
+      // a run of GDN-only layers as group steps, except the layers whose items are all too big
+      // to be speculated (each group step would take one of them, plus the pass's overhead)
+      const unsigned long long big = sm.bigm;
       if (P.nbuf == 2 && ly.has_gdn && !ly.has_mlp && L + 1 < P.n_layers &&
-          sm.layers[L + 1].has_gdn && !sm.layers[L + 1].has_mlp) {
+          sm.layers[L + 1].has_gdn && !sm.layers[L + 1].has_mlp && !((big >> L) & 3ull)) {
         int hi = L + 1;
-        while (hi < P.n_layers && sm.layers[hi].has_gdn && !sm.layers[hi].has_mlp) hi++;
+        while (hi < P.n_layers && sm.layers[hi].has_gdn && !sm.layers[hi].has_mlp &&
+               !((big >> hi) & 1ull))
+          hi++;
         group_run(L, hi, i);
         L = hi;
         continue;
@@ -2039,9 +2173,13 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       PROF(PR_NORM);
       // with an MLP the items are checked on its way and only the others run after it (they are
       // independent: the items read x, the MLP xm, and neither changes x before the barrier)
-      const bool merged = ly.has_gdn && B && mlp;
+      // a layer whose GDN wrote at the last token most likely writes again (the real circuit's
+      // first layers write at every token): its MLP runs once, after the out_proj rows, instead
+      // of beside the items and again after them (the same in every CTA: the flags are)
+      const bool unpair = ly.has_gdn && ly.has_mlp && B && ((sm.upm >> L) & 1ull);
+      const bool merged = ly.has_gdn && B && mlp && !unpair;
       uint32_t todo = ly.has_gdn && B && !merged ? 0xffffffffu : 0u;  // items for gdn_item
-      if (ly.has_mlp) {
+      if (ly.has_mlp && !unpair) {
         if (mlp) todo |= mlp_owner(P, sm, B, mh, sm.own[ph & 1], merged ? w_in : nullptr, r);
         else copy_owner(sm, mr0, mnr, sm.own[ph & 1]);
         __syncthreads();
@@ -2061,38 +2199,46 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       if (wrote && t < C) *cluster.map_shared_rank(&sm.wflag[ph & 1], t) = 1;
       PROF(PR_ITEMS);
       cluster.sync();
-      pc[PR_BARRIERS]++;
+      COUNT(PR_BARRIERS);
       PROF(PR_SYNC);
       const int fl = *reinterpret_cast<volatile int*>(&sm.wflag[ph & 1]);
       __syncthreads();
-      if (fl) {
-        pc[PR_FIXUPS]++;
-        if (t == 0) sm.wflag[ph & 1] = 0;
-        if (P.nbuf == 1 && !ly.has_mlp) issue_next(stp);  // the blob is no longer read
-        ph++;
-        const lxb_owner ow = P.owners[ly.owner0 + rank];
-        out_owner(P, sm, ly, ow, rank, i, sm.own[ph & 1], cluster);
-        __syncthreads();
-        push_rows(P, sm, sm.own[ph & 1], ph & 1, rank * P.blk, P.blk, cluster);
-        cluster.sync();
-        pc[PR_BARRIERS]++;
-        r_x = take_rows_norm(P, sm, ph & 1);
-        x_new = false;
-        ph++;
-        if (ly.has_mlp) {
-          norm_into(sm.xm, sm.x, w_post, r_x);
+      if (t == 0 && ly.has_gdn && ly.has_mlp)  // (read at this layer's next step, many barriers on)
+        sm.upm = fl ? sm.upm | 1ull << L : sm.upm & ~(1ull << L);
+      if (fl || unpair) {
+        if (fl) {  // the out_proj rows into the residual
+          COUNT(PR_FIXUPS);
+          if (t == 0) sm.wflag[ph & 1] = 0;
+          if (P.nbuf == 1 && !ly.has_mlp) issue_next(stp);  // the blob is no longer read
+          ph++;
+          const lxb_owner ow = P.owners[ly.owner0 + rank];
+          out_owner(P, sm, L, ow, rank, i, sm.own[ph & 1], cluster);
           __syncthreads();
+          PROF(PR_FXOUT);
+          push_rows(P, sm, sm.own[ph & 1], ph & 1, rank * P.blk, P.blk, cluster);
+          cluster.sync();
+          COUNT(PR_BARRIERS);
+          r_x = take_rows_norm(P, sm, ph & 1);
+          x_new = false;
+          ph++;
+          PROF(PR_FIXUP);
+        }
+        if (ly.has_mlp) {  // the MLP (again, or, unpaired and nothing written, now)
+          if (fl) {
+            norm_into(sm.xm, sm.x, w_post, r_x);
+            __syncthreads();
+          }
           if (mlp) mlp_owner(P, sm, B, mh, sm.own[ph & 1]);
           else copy_owner(sm, mr0, mnr, sm.own[ph & 1]);
           __syncthreads();
           push_rows(P, sm, sm.own[ph & 1], ph & 1, mr0, mnr, cluster);
           cluster.sync();
-          pc[PR_BARRIERS]++;
+          COUNT(PR_BARRIERS);
           if (P.nbuf == 1) issue_next(stp);
           r_x = take_rows_norm(P, sm, ph & 1, ly.mrow0, ly.mrow1);
           ph++;
         }
-        PROF(PR_FIXUP);
+        PROF(PR_FXMLP);
       } else {
         if (P.nbuf == 1) issue_next(stp);
         if (ly.has_mlp) r_x = take_rows_norm(P, sm, ph & 1, ly.mrow0, ly.mrow1);
@@ -2143,7 +2289,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
         head_reduce(sm, bv, bi);
       }
       cluster.sync();
-      pc[PR_BARRIERS]++;
+      COUNT(PR_BARRIERS);
       cluster_max(sm, cluster, C);  // sm.cv / sm.ci: the cluster's first maximum
       if (helped) {
         // rank 0 gathers the helpers' maxima (each wait bounded) and tells every CTA
@@ -2180,7 +2326,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
           }
         }
         cluster.sync();
-        pc[PR_BARRIERS]++;
+        COUNT(PR_BARRIERS);
         if (sm.hok) {
           if (t == 0) {
             sm.cv = sm.hv;
@@ -2197,7 +2343,7 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
             head_rows(P, sm, P.headcta[rank * LXB_HEADSLICES + k], hsp, v2, i2);
           head_reduce(sm, v2, i2);
           cluster.sync();
-          pc[PR_BARRIERS]++;
+          COUNT(PR_BARRIERS);
           cluster_max(sm, cluster, C);
           if (t == 0) {
             if (bv > sm.cv || (bv == sm.cv && bi < sm.ci)) {
@@ -2233,14 +2379,14 @@ __global__ void __launch_bounds__(NT, 1) lxb_decode_kernel(Dev P, Run run) {
       if (i + 1 < run.n_tokens) load_embed(run, P, sm, sm.tok);
       x_new = true;
       PROF(PR_EMBED);
-      pc[PR_TOKENS]++;
+      COUNT(PR_TOKENS);
     }
   }
 #undef PROF
+#undef COUNT
   if (prof && t == 0) {
     unsigned long long* d = run.prof + ((size_t)s * C + rank) * PR_N;
-#pragma unroll
-    for (int k = 0; k < PR_N; k++) d[k] += pc[k];
+    for (int k = 0; k < PR_N; k++) d[k] += sm.pcs[k];
   }
   for (int k = t; k < sm.nwin; k += NT) {  // the resident conv windows back into the state
     const int L = P.winmap[2 * (sm.win0 + k)], ch = P.winmap[2 * (sm.win0 + k) + 1];

@@ -15,7 +15,7 @@
 #include <stdint.h>
 
 #define LXB_MAGIC 0x50425a4cu  // "LZBP"
-#define LXB_IMAGE_VERSION 9
+#define LXB_IMAGE_VERSION 10
 
 #define LXB_H 2560
 #define LXB_KD 256
@@ -132,7 +132,7 @@ typedef struct {
 typedef struct {
   int32_t mr0, mr1;        // the MLP rows this CTA owns, [mr0, mr1): multiples of 8, at most
                            // H / LXB_MINC rows (the out_proj rows are rank * blk .. + blk)
-  int32_t pad;
+  int32_t nlong;           // owned out_proj rows with more than LXB_LONG entries (by warps)
   int32_t orow;            // i32 pool: blk + 1 entry pointers of the owned rows' out_proj
                            // entries (value dim | bf16 << 16), or -1
 } lxb_owner;  // 16 bytes
@@ -188,7 +188,8 @@ typedef struct {
   int32_t down_ptr;        // int32[nr + 1]: the owned rows' entries (indices into down_ent)
   int32_t down_ent;        // uint32 entries: local unit | bf16 << 16
   int32_t r0, nr;          // the owned MLP rows [r0, r0 + nr): the owner's mr0, mr1 - mr0
-  int32_t pad[2];
+  int32_t nlong;           // of them, rows with more than LXB_LONG entries (summed by warps)
+  int32_t pad;
 } lxb_bmlp;  // 32 bytes
 
 typedef struct {

@@ -163,7 +163,8 @@ class Decoder:
         return self._typing[3][:, 3:4].contiguous()
 
     PROFILE = ("norm", "items", "mlp", "sync", "pull", "fixup", "head", "embed", "fixups",
-               "tokens", "wait", "polls", "takesync", "barriers")
+               "tokens", "wait", "polls", "takesync", "barriers", "group_items", "group_sync",
+               "group_fixup", "fixup_mlp", "fixup_out")
     COUNTS = ("fixups", "tokens", "polls", "barriers")  # counts; the others are clock cycles
 
     def barrier_cycles(self, iters: int = 10000) -> float:

@@ -27,7 +27,7 @@ from . import chip as C
 from .chip import _ranges
 
 MAGIC = 0x50425A4C
-VERSION = 9
+VERSION = 10
 NSLOT, NOSLOT = 1536, 0xFFFF
 ITEMSLOTS, MAXDENSE, MAXUNITS, MAXWIN = 4, 32, 2048, 1024
 MINC = 4  # the smallest cluster: an owner holds at most H / MINC rows
@@ -48,7 +48,7 @@ CHAN = np.dtype([("ent", "<u4"), ("n", "<u2"), ("slot", "<u2"), ("conv_ch", "<u4
                  ("t01", "<u4"), ("t23", "<u4"), ("tapmask", "<u4"), ("win", "<u4"),
                  ("p2", "<u4")])
 UNIT = np.dtype([("g", "<u4"), ("u", "<u4"), ("ng", "<u2"), ("nu", "<u2"), ("pad", "<u4")])
-OWNER = np.dtype([("mr0", "<i4"), ("mr1", "<i4"), ("pad", "<i4"), ("orow", "<i4")])
+OWNER = np.dtype([("mr0", "<i4"), ("mr1", "<i4"), ("nlong", "<i4"), ("orow", "<i4")])
 HEADCTA = np.dtype([("r0", "<i4"), ("r1", "<i4"), ("rowptr", "<i4"), ("pad", "<i4")])
 HEADER = np.dtype([("magic", "<u4"), ("version", "<u4"), ("n_layers", "<i4"), ("cluster", "<i4"),
                    ("n_vocab", "<i4"), ("hidden", "<i4"), ("n_items", "<i4"), ("n_dense", "<i4"),
@@ -57,6 +57,7 @@ HEADER = np.dtype([("magic", "<u4"), ("version", "<u4"), ("n_layers", "<i4"), ("
                    ("dense_cols", "<i4", (MAXDENSE,)), ("blob_max", "<i4"), ("hsp_mask", "<i4"),
                    ("pad1", "<i4", (2,)),
                    ("sec", "<i8", (len(SEC), 2))])
+LONG = 32  # rows with more entries are summed by a warp each (LXB_LONG)
 BLOBREF = np.dtype([("off", "<i8"), ("bytes", "<i4"), ("pad", "<i4")])
 BHDR = np.dtype([("bytes", "<i4"), ("n_items", "<i4"), ("item", "<i4", (ITEMSLOTS,)),
                  ("ln_in", "<i4"), ("ln_post", "<i4"), ("mlp", "<i4"), ("pad", "<i4", (7,))])
@@ -65,7 +66,7 @@ BITEM = np.dtype([(n, "<i4") for n in ("item", "n_eager", "eager", "rows", "prm"
 BCHAN = np.dtype([("ent", "<i4"), ("n", "<u2"), ("slot", "<u2"), ("conv_ch", "<u4"),
                   ("t01", "<u4"), ("t23", "<u4"), ("win", "<u4"), ("p1", "<u4"), ("p2", "<u4")])
 BMLP = np.dtype([(n, "<i4") for n in ("n_units", "units", "down_ptr", "down_ent", "r0", "nr",
-                                      "p0", "p1")])
+                                      "nlong", "p1")])
 BUNIT = np.dtype([("g", "<i4"), ("u", "<i4"), ("ng", "<u2"), ("nu", "<u2"), ("pad", "<i4")])
 assert LAYER.itemsize == 48 and ITEM.itemsize == 48 and CHAN.itemsize == 32
 assert UNIT.itemsize == 16 and OWNER.itemsize == 16 and HEADCTA.itemsize == 16
@@ -371,6 +372,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
                 bm["units"] = blob.add(un)
                 bm["down_ptr"] = blob.add(ptr.astype(np.int32))
                 bm["down_ent"] = blob.add(_pack(loc, w))
+                bm["nlong"] = int((np.diff(ptr) > LONG).sum())  # rows the kernel sums by warps
                 bh["mlp"] = blob.add(np.array([bm], BMLP))
                 stats["unit_evals"] += len(need)
                 stats["down_nnz"] += int(keep.sum())
@@ -383,6 +385,7 @@ def build_image(chip: C.Chip, cluster: int = 16) -> tuple[bytes, dict]:
                 np.cumsum(np.bincount(rowid, minlength=blk), out=ptr[1:])
                 base = ent.add(_pack(sub.indices[keep], sub.data[keep]))
                 ow["orow"] = i32.add((ptr + base).astype(np.int32))
+                ow["nlong"] = int((np.diff(ptr) > LONG).sum())
                 stats["out_nnz"] += int(keep.sum())
             owners.append(ow)
     # --- the head ----------------------------------------------------------------------------
