@@ -200,7 +200,7 @@ def decode_real(a, rank, world, dev):
     chip = C.real()
     st0 = C.real_state(chip)
     tr = chip.meta["fixture"]["trace"]
-    line = _decode_single(a, rank, world, dev, chip, st0, int(tr[0]), tr, None)
+    line = _decode_single(a, rank, world, dev, chip, st0, int(tr[0]), tr, "decode_real_ncu.md")
     if line is None:
         return None
     line.update(metric="chip decode tok/s, real circuit (single stream per GPU)",
