@@ -85,7 +85,7 @@ SIGNATURES = {
 
 
 def lib():
-    """The loaded library (built first if it is missing or older than its sources)."""
+    """The loaded library (`python -m linuxformer_b200.build` builds it; a missing one raises)."""
     global _lib
     if _lib is None:
         # LXB_LIBRARY: another build of liblxb.so to load instead (A/B timing of two builds)
