@@ -120,3 +120,40 @@ def test_mlp_split_balances_the_work():
         # no contiguous split beats (total + bases) / Cn; a greedy one is within a chunk of it
         lower = max((rc[R[0]:R[-1]].sum() + base.sum()) / Cn, base.max())
         assert cost.max() <= lower + chunk + 1e-6, (Cn, cost.max(), lower, chunk)
+
+
+def test_real_circuit_head_mask_and_long_rows(real_chip):
+    """The real circuit's plan: the head's sparse-column mask holds exactly the 191 columns with
+    sparse entries (the kernel skips the rows' sparse entries when the normed residual is zero in
+    all of them), and every owner's and MLP blob's long-row count is the number of its rows with
+    more than LONG entries (the rows the kernel sums by warps)."""
+    Cn = 16
+    img, st = tables.build_image(real_chip, Cn)
+    im = Image(img)
+    i32 = im.sec("i32", np.dtype("<i4"))
+    mask = i32[int(im.h["hsp_mask"]):int(im.h["hsp_mask"]) + C.H // 32].view(np.uint32)
+    cols = np.nonzero((mask[np.arange(C.H) >> 5] >> (np.arange(C.H) & 31)) & 1)[0]
+    dense = set(int(c) for c in im.h["dense_cols"][:int(im.h["n_dense"])])
+    hd = real_chip.head
+    want = sorted(set(np.unique(hd.indices).tolist()) - dense)
+    assert cols.tolist() == want and len(want) == 191
+    owners = im.sec("owners", tables.OWNER).reshape(real_chip.n_layers, Cn)
+    layers = im.sec("layers", tables.LAYER)
+    n_long = 0
+    for L in range(real_chip.n_layers):
+        for c in range(Cn):
+            ow = owners[L, c]
+            if ow["orow"] >= 0:
+                ptr = i32[int(ow["orow"]):int(ow["orow"]) + C.H // Cn + 1]
+                assert ow["nlong"] == int((np.diff(ptr) > tables.LONG).sum())
+                n_long += int(ow["nlong"])
+            else:
+                assert ow["nlong"] == 0
+            if layers[L]["has_mlp"]:
+                b = im.blob(L, c, Cn)
+                bh = np.frombuffer(b[:tables.BHDR.itemsize], tables.BHDR)[0]
+                if bh["mlp"] >= 0:
+                    m = np.frombuffer(b[bh["mlp"]:bh["mlp"] + tables.BMLP.itemsize], tables.BMLP)[0]
+                    dp = np.frombuffer(b[m["down_ptr"]:m["down_ptr"] + 4 * (m["nr"] + 1)], "<i4")
+                    assert m["nlong"] == int((np.diff(dp) > tables.LONG).sum())
+    assert n_long > 0  # layer 2's memory-read rows (1,024 entries) among them
