@@ -25,13 +25,16 @@ its checkout, builds the seeded config-1 stack as a stock model, seeds fp32 recu
   token per call: the tokens, each step's top-2 margin, the final conv windows (all layers),
   SHA-256 digests of every layer's conv windows and recurrent state (bits, -0 written as +0),
   per-(layer, value head) sums and absolute sums of the final recurrent state, and the whole
-  final state of two memory value heads.
+  final state of two memory value heads;
+- ``real_decode.npz``: the real compiled circuit (``real_chip.npz``) decoded by the stock forward
+  from GO for 32 tokens, one per call (the predictions must be the reference machine's trace):
+  the tokens, their top-2 margins, the same per-layer digests and per-head sums.
 
 Run where the reference's checkout is (its directory in LXB_REFERENCE); the tests only read the
 .npz files:
 
     LXB_REFERENCE=<checkout> python tests/golden/make_golden.py [decode] [prefill] [prefill8k] [c2]
-        [c5pad]
+        [c5pad] [real]
 """
 
 import os
@@ -95,6 +98,8 @@ def main(parts):
         c5_pad()
     if "c2" in parts:
         c2_decode(ref_hf)
+    if "real" in parts:
+        real_decode(ref_hf)
     if not {"decode", "prefill", "prefill8k"} & set(parts):
         return
     chip = C.c1(0)
@@ -174,6 +179,7 @@ def prefill8k(ref_hf, chip, model, st0, n, emb):
 
 
 N_C2 = 32
+N_REAL = 32
 
 
 def c2_heads(chip):
@@ -236,6 +242,45 @@ def c2_decode(ref_hf):
     print(f"c2 decode: {N_C2} tokens in {dt:.1f}s, min margin {min(marg):.3g}")
 
 
+def real_decode(ref_hf):
+    # --- the real compiled circuit (real_chip.npz): the model alone from GO, one per call ----
+    chip = C.real()
+    st0 = C.real_state(chip)
+    tr = chip.meta["fixture"]["trace"]
+    t0 = time.time()
+    import dataclasses
+
+    # the stock model's vocabulary is the head's rows (the embedding's padding rows past them,
+    # PAD among them, are never an input)
+    model = C.to_hf(dataclasses.replace(chip, embed=chip.embed[:chip.n_vocab]))
+    print(f"real stock model built in {time.time() - t0:.0f}s")
+    n = chip.n_layers
+    emb = model.model.embed_tokens
+    cache = new_cache(model, st0)
+    tok, toks, preds, marg = int(tr[0]), [], [], []
+    t0 = time.time()
+    for i in range(N_REAL):
+        h = ref_hf.chip_forward(model, emb(torch.tensor([[tok]])), cache, n)[0]
+        logits = torch.nn.functional.linear(model.model.norm(h), model.lm_head.weight)
+        p = int(ref_hf.head_argmax(model, h)[0])
+        assert p == int(logits.argmax(-1)[0])
+        toks.append(tok)
+        preds.append(p)
+        marg.append(float(margins(logits)[0]))
+        tok = p
+    dt = time.time() - t0
+    assert preds == tr[1:N_REAL + 1].tolist(), "the stock forward left the machine's trace"
+    conv = np.stack([cache.layers[L].conv_states[0].view(torch.int16).numpy().view(np.uint16)
+                     for L in range(n)])
+    rec = np.stack([cache.layers[L].recurrent_states[0].float().numpy() for L in range(n)])
+    cd, rd = c2_digests(conv, rec)
+    np.savez_compressed(HERE / "real_decode.npz", inputs=np.array(toks), preds=np.array(preds),
+                        margin=np.array(marg, np.float32), conv_sha=cd, rec_sha=rd,
+                        rec_vh_sum=rec.astype(np.float64).sum(axis=(2, 3)),
+                        rec_vh_abs=np.abs(rec.astype(np.float64)).sum(axis=(2, 3)), cpu_s=dt)
+    print(f"real decode: {N_REAL} tokens in {dt:.1f}s, min margin {min(marg):.3g}")
+
+
 def c5_pad():
     from lx import merge as ref_merge
 
@@ -266,4 +311,4 @@ def c5_pad():
 
 
 if __name__ == "__main__":
-    main(sys.argv[1:] or ["decode", "prefill", "prefill8k", "c2", "c5pad"])
+    main(sys.argv[1:] or ["decode", "prefill", "prefill8k", "c2", "c5pad", "real"])

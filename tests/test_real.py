@@ -43,3 +43,25 @@ def test_oracle_reproduces_the_machine(real_chip):
     preds, inputs, _ = Oracle(real_chip).decode(st, [int(tr[0])], n)
     assert inputs[0] == real_chip.meta["go"]
     assert (preds == tr[1:n + 1]).all(), np.nonzero(preds != tr[1:n + 1])[0][:5]
+
+
+def test_oracle_matches_stock_bit_for_bit():
+    """The reference's own stock forward on the real circuit (tests/golden/real_decode.npz: the
+    HF decoder layers run as lx.hf.chip_forward runs them, 32 tokens from GO one per call, its
+    predictions the machine's trace): every token identical, and after them every layer's conv
+    windows and recurrent state identical bit for bit (-0 written as +0: a product with a zero
+    weight or input that the sparse path never forms can differ in a zero's sign only). Here the
+    stock CPU GEMM's summation order makes no difference: the circuit's sums are exact."""
+    from pathlib import Path
+
+    g = np.load(Path(__file__).parent / "golden" / "real_decode.npz")
+    chip = C.real()
+    st = C.real_state(chip)
+    preds, inputs, _ = Oracle(chip).decode(st, [int(g["inputs"][0])], len(g["preds"]))
+    assert (preds == g["preds"]).all() and (inputs == g["inputs"]).all()
+    cv = np.where((st.conv & 0x7FFF) == 0, 0, st.conv).astype(np.uint16)
+    rv = np.where(st.recurrent == 0, np.float32(0), st.recurrent).astype(np.float32)
+    for L in range(chip.n_layers):
+        assert hashlib.sha256(np.ascontiguousarray(cv[L]).tobytes()).hexdigest() == g["conv_sha"][L]
+        assert (hashlib.sha256(np.ascontiguousarray(rv[L]).view(np.uint32).tobytes()).hexdigest()
+                == g["rec_sha"][L]), f"layer {L}'s recurrent state"
