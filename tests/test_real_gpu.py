@@ -51,3 +51,27 @@ def test_real_reproduces_the_machine(real_chip):
     bad = np.nonzero(got != tr[1:n + 1])[0]
     assert len(bad) == 0, f"first difference at token {bad[0] + 1} of {n}"
     assert dec.status().status == 0
+
+
+def test_real_matches_stock_forward(real_chip):
+    """32 tokens from GO against the reference's stock forward (tests/golden/real_decode.npz):
+    the tokens and, after them, every layer's conv windows and recurrent state bit for bit (-0
+    written as +0)."""
+    import hashlib
+    from pathlib import Path
+
+    from linuxformer_b200.runtime import Decoder
+
+    g = np.load(Path(__file__).parent / "golden" / "real_decode.npz")
+    dec = Decoder(real_chip, cluster=16)
+    ds = dec.states([C.real_state(real_chip)])
+    preds, inputs = dec.run(ds, [[int(g["inputs"][0])]], len(g["preds"]))
+    assert (preds[0].cpu().numpy() == g["preds"]).all()
+    assert (inputs[0].cpu().numpy() == g["inputs"]).all()
+    st = ds.host(0)
+    cv = np.where((st.conv & 0x7FFF) == 0, 0, st.conv).astype(np.uint16)
+    rv = np.where(st.recurrent == 0, np.float32(0), st.recurrent).astype(np.float32)
+    for L in range(real_chip.n_layers):
+        assert hashlib.sha256(np.ascontiguousarray(cv[L]).tobytes()).hexdigest() == g["conv_sha"][L]
+        assert (hashlib.sha256(np.ascontiguousarray(rv[L]).view(np.uint32).tobytes()).hexdigest()
+                == g["rec_sha"][L]), f"layer {L}'s recurrent state"
