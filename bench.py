@@ -17,7 +17,8 @@ BASELINE.json's metric has three parts; the default line carries all three:
   decoding the model alone from GO on the fixture's machine (a RISC-V program over 4.5 MiB of
   seeded random RAM), --real-steps timed launches of --real-tokens after the warm-up launches
   (--steps of --tokens with --mode real); the whole stream is checked against the reference
-  machine's own trace.
+  machine's own trace. The default line carries it at N = 1 (the headline covers the scaling
+  runs); --mode real runs it on every rank.
 - ``prefill``: verify-prefill tok/s (config 3): 1,048,576 token ids uniform over the config-1
   vocabulary (seed 2) through the config-1 stack as chunked prefill (lxb_prefill), chunks of
   65,536 (the headline) and of 8,192; a step is one pass over all of them, continuing the state.
@@ -960,7 +961,8 @@ def main():
     if a.mode in ("all", "decode"):
         line = decode_c2(a, rank, world, dev, kw)
     parts = {}
-    if a.mode in ("all", "real"):
+    # (the default line carries the real circuit's part on one GPU; with --mode real, on every N)
+    if a.mode == "real" or (a.mode == "all" and world == 1):
         import copy
 
         ar = copy.copy(a)
