@@ -206,7 +206,16 @@ def cache_pointers(cache, n_chip: int, dev) -> torch.Tensor:
 class Fast:
     """lx.fast.Fast's interface (lx/lx/fast.py:172-550) on liblxb.so: the chip layers' forward
     over a chunk (``forward``), the head's argmax (``head_argmax``) and the single-token step
-    (``decode``, a chunk of one token)."""
+    (``decode``, a chunk of one token).
+
+    A circuit the prefill kernels do not take (a key head with more live query/key rows than
+    their register-resident recurrence holds: the real circuit's memory heads have 256) runs
+    through the decode kernel instead, every input forced: the same bits as the stock per-token
+    forward, at the decode's speed. The decode kernel keeps no hidden states, so ``forward`` and
+    ``decode`` then return NaN rows whose only use is ``head_argmax`` of that same tensor (the
+    predictions the kernel made); any other use of them shows up as NaN."""
+
+    FALLBACK_ROWS = 1 << 20  # the largest chunk the decode-kernel path takes
 
     compile = False     # the reference's flags, kept for its callers; nothing to compile here
     lean = False
@@ -223,7 +232,23 @@ class Fast:
         chip = chip_from_model(model, n_chip, rows, offset)
         emb = model.model.embed_tokens.weight
         chip.embed = chip.embed[:, :0]  # the kernels read the model's own embedding
-        self.pf = Prefill(chip, device=self.dev, embed=emb.view(torch.int16))
+        self.dec, self._last = None, None
+        try:
+            self.pf = Prefill(chip, device=self.dev, embed=emb.view(torch.int16))
+        except prefill_tables.PrefillUnsupported as e:
+            import dataclasses
+
+            from .runtime import Decoder
+
+            # the decode kernel over the chunk's own rows: its "embedding" is the chunk (row t
+            # is input t, offset 0), every input forced
+            self.pf, self.unsupported = None, str(e)
+            fc = dataclasses.replace(chip, embed=np.zeros((self.FALLBACK_ROWS, 0), np.uint16),
+                                     offset=0)
+            self.dec = Decoder(fc, cluster=16, device=self.dev,
+                               embed=torch.zeros((1, C.H), dtype=torch.int16, device=self.dev))
+            self._bm = torch.zeros((1, n_chip, C.NV, 8), dtype=torch.int32, device=self.dev)
+            self._scratch = self.dec.scratch(1)
         w = model.lm_head.weight if rows is None else model.lm_head.weight[rows]
         self.head_cols = (w != 0).any(0).nonzero()[:, 0]
         self.w_head = w[:, self.head_cols]
@@ -232,18 +257,47 @@ class Fast:
     def forward(self, h: torch.Tensor, cache) -> torch.Tensor:
         """h (1, T, hidden) -> (1, T, hidden), updating the cache's conv and recurrent states."""
         x = h[0].contiguous()
+        if self.pf is None:
+            return self._through_decode(x, cache)[None]
         out = self.pf.layers(cache_pointers(cache, self.n_chip, self.dev), x)
         return out[None]
 
     @torch.no_grad()
     def decode(self, h: torch.Tensor, cache) -> torch.Tensor:
         """One token: h (1, hidden) -> (1, hidden)."""
+        if self.pf is None:
+            return self._through_decode(h.contiguous(), cache)
         return self.pf.layers(cache_pointers(cache, self.n_chip, self.dev), h.contiguous())
 
     @torch.no_grad()
     def head_argmax(self, h: torch.Tensor, block: int | None = None) -> torch.Tensor:
         """The output head's argmax over the rows given at construction, for h (T, hidden)."""
+        if self.pf is None:
+            if self._last is None or h.untyped_storage().data_ptr() != self._last[0] \
+                    or h.shape[0] != self._last[1].shape[0]:
+                raise LxbError("this circuit runs through the decode kernel (" + self.unsupported
+                               + "): head_argmax takes only the rows forward/decode returned")
+            return self._last[1].long()
         return self.pf.head(h.contiguous()).long()
+
+    def _through_decode(self, x: torch.Tensor, cache) -> torch.Tensor:
+        """The chunk x (T, hidden) bf16 through the decode kernel, inputs forced; the
+        predictions are kept for head_argmax of the NaN rows returned."""
+        T = x.shape[0]
+        if not 0 < T <= self.FALLBACK_ROWS or x.dtype != torch.bfloat16:
+            raise LxbError(f"a chunk of 1..{self.FALLBACK_ROWS} bf16 rows, not {T} {x.dtype}")
+        self.dec.embed = x.view(torch.int16)
+        forced = torch.arange(T, dtype=torch.int32, device=self.dev).view(1, T)
+        preds = torch.empty((1, T), dtype=torch.int32, device=self.dev)
+        ptrs = cache_pointers(cache, self.n_chip, self.dev).view(1, self.n_chip, 2)
+        self.dec.launch(ptrs, self._bm, forced, T, preds, None, sync_bitmaps=True,
+                        scratch=self._scratch)
+        e = self.dec.status()
+        if e.status & S_ERRORS:
+            raise LxbError(f"decode kernel: device status {e.status:#x} at step {e.first_step}")
+        out = torch.full_like(x, float("nan"))
+        self._last = (out.untyped_storage().data_ptr(), preds[0])
+        return out
 
     def to(self, dev) -> "Fast":
         if torch.device(dev) != self.dev:

@@ -255,3 +255,45 @@ def test_c1_chunk_in_views_matches_the_forced_decode(c1_chip):
     assert (preds.cpu().numpy() == want[0].cpu().numpy()).all()
     assert first == 4096
     _same(rec, conv, ds.host(0))
+
+
+def test_fast_runs_unsupported_circuits_through_the_decode_kernel():
+    """A circuit the prefill kernels do not take (here config 1 with 40 tapped query rows in one
+    key head; the real circuit's memory heads have 256): Fast runs it through the decode kernel,
+    every input forced, so Session.verify's calls still work. Predictions, conv windows and
+    recurrent states equal the CPU restatement's forced decode bit for bit; head_argmax takes
+    only the rows forward returned."""
+    from transformers import DynamicCache
+
+    from linuxformer_b200._lib import LxbError
+    from linuxformer_b200.prefill import Fast
+
+    chip = C.c1(0)
+    ly = chip.layers[0]
+    ly.conv = ly.conv.copy()
+    ly.conv[:40, 3] = C.bf16_bits(np.float32(0.5))
+    model = C.to_hf(chip).to("cuda")
+    st0 = C.c1_state(chip, 0)
+    cache = DynamicCache(config=model.config)
+    for L in range(chip.n_layers):
+        cache.update_conv_state(torch.zeros((1, C.CONV, 4), dtype=torch.bfloat16, device="cuda"), L)
+        lay = cache.layers[L]
+        lay.recurrent_states = torch.from_numpy(st0.recurrent[L].copy())[None].to("cuda")
+        lay.is_recurrent_states_initialized = True
+    fast = Fast(model, chip.n_layers)
+    assert fast.pf is None and "live rows" in fast.unsupported
+    ids = np.random.default_rng(5).integers(0, chip.n_vocab, 96).astype(np.int32)
+    got = []
+    for a in (0, 64):  # two chunks, the state carried in the cache
+        e = model.model.embed_tokens(torch.from_numpy(ids[a:a + 64]).long().to("cuda")[None])
+        h = fast.forward(e, cache)[0]
+        got += fast.head_argmax(h).tolist()
+        with pytest.raises(LxbError):
+            fast.head_argmax(e[0])
+    host = st0.copy()
+    want, _, _ = Oracle(chip).decode(host, ids, len(ids))
+    assert got == want.tolist()
+    for L in range(chip.n_layers):
+        conv = cache.layers[L].conv_states[0].view(torch.int16).cpu().numpy().view(np.uint16)
+        assert np.array_equal(conv, host.conv[L])
+        assert not (cache.layers[L].recurrent_states[0].cpu().numpy() != host.recurrent[L]).any()
