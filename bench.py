@@ -3,7 +3,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl lxb|reference]
                     [--mode all|decode|real|prefill|batched|text]
 
-BASELINE.json's metric has three parts; the default line carries all three:
+BASELINE.json's metric has three parts (single-stream decode, verify-prefill, batched decode); the
+default line carries all three, the real circuit's decode and config 5's text decode:
 
 - headline (``value``): single-stream chip decode (config 2): the 37-layer chip-shaped stack
   (497 live key heads, 36,716 SwiGLU units, 459,982 head rows, 5.5 MB of RAM/ROM in the GDN
